@@ -1,0 +1,514 @@
+"""Benchmark of the INT8 weight-only MatMul path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one step): the decode GEMV set at GPT-2-small shapes -- QKV 768x2304,
+attn-out 768x768, FFN-up 768x3072, FFN-down 3072x768, LM head 768x50257 (tied),
+each at M = 1 and M = 8 token rows (10 MatMulQ calls), fp32 activations ~ N(0,1),
+int8 per-channel weights from N(0, 0.02), MTRTQ_MODE_BF16. Every call has 6
+device copies of its weights and consecutive steps rotate through them (548 MB
+of int8 weights in all, > 4x the 126 MB L2), so weights stream from HBM.
+
+metric/value: algorithmic bytes (int8 W + scales + fp32 X + fp32 Y) per second
+over the whole job, inputs resident in HBM, steps replayed as CUDA graphs, timed
+with CUDA events on the launching stream. e2e: the same bytes per second through
+the C ABI called from the host with pinned host buffers, host->device copy of
+each call's activations and device->host copy of each output inside the timed
+region. Secondary lines: the prefill tensor-core GEMM (TFLOP/s) at the large
+shapes, and the single-op FFN-up case.
+
+Multi-GPU (torchrun, one process per GPU): each rank runs its own full decode
+GEMV set (data-parallel replicas of the path, no collective on the data path);
+value = all ranks' bytes / the max over ranks of the timed region.
+
+--impl reference: the reference's own CPU MatMulQ (oracle/_ref, compiled from
+its sources) on the same workload, every call split into single-row calls
+(rows are independent in its loop) spread over all host threads; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "int8-W GEMM TFLOP/s & GEMV HBM GB/s vs peak; GPT-2 decode tok/s @1/2/4/8 GPU"
+UNIT = "GB/s"
+WEIGHT_COPIES = 6
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, None, "fallback"
+
+
+def committed_traffic(kernel_key: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f).get(kernel_key)
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- ours
+
+
+def build_decode_set(torch, dev, mode):
+    from mini_tensorrt_b200 import matmulq, workloads as wl
+    calls = []  # one entry per (M, shape): inputs, outputs, weight copies, workspace
+    for M in wl.DECODE_M:
+        for name, K, N in wl.DECODE_SHAPES:
+            W = wl.decode_weight(name, K, N)
+            q, s = matmulq.quantize_per_channel(W)
+            base = matmulq.PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), dev)
+            copies = [base] + [matmulq.PackedWeight(base.packed.clone(), base.scale.clone(), K, N)
+                               for _ in range(WEIGHT_COPIES - 1)]
+            x = torch.from_numpy(wl.activations(M, K, wl.shape_seed("x:" + name, M, K))).to(dev)
+            y = torch.empty((M, N), dtype=torch.float32, device=dev)
+            ws_bytes = matmulq.workspace_bytes(M, K, N, torch.float32, mode)
+            ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+            calls.append({"name": name, "M": M, "K": K, "N": N, "x": x, "y": y, "w": copies,
+                          "ws": ws, "bytes": wl.algorithmic_bytes(M, K, N, 4)})
+    return calls
+
+
+def launch_step(calls, step, mode, stream):
+    from mini_tensorrt_b200 import matmulq
+    for i, c in enumerate(calls):
+        w = c["w"][(step + i) % WEIGHT_COPIES]
+        matmulq.matmul_q8(c["x"], w, out=c["y"], mode=mode, workspace=c["ws"], stream=stream)
+
+
+def time_graphs(torch, graphs, steps, warmup, stream):
+    """Replays graphs round-robin on `stream`; returns seconds for `steps` replays."""
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            graphs[i % len(graphs)].replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            graphs[i % len(graphs)].replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3
+
+
+def run_ours(args, torch, rank, world, dev, dist):
+    from mini_tensorrt_b200 import _lib, matmulq, workloads as wl
+    hbm_peak, tc_peak, tc_sust, peak_kind = peaks()
+    stream = torch.cuda.Stream(dev)
+    calls = build_decode_set(torch, dev, args.mode)
+    step_bytes = sum(c["bytes"] for c in calls)
+
+    # Capture one CUDA graph per weight-copy rotation offset.
+    graphs = []
+    with torch.cuda.stream(stream):
+        launch_step(calls, 0, args.mode, stream)  # first launch outside capture
+        torch.cuda.synchronize()
+        for g in range(WEIGHT_COPIES):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                launch_step(calls, g, args.mode, stream)
+            graphs.append(graph)
+    torch.cuda.synchronize()
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        if world > 1:
+            dist.barrier()
+        secs = time_graphs(torch, graphs, args.steps, args.warmup, stream)
+        if world > 1:
+            dist.barrier()
+    torch.cuda.synchronize()
+    t = torch.tensor([secs], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    secs = float(t.item())
+    value = step_bytes * args.steps * world / secs / 1e9
+    assert matmulq.read_device_status() == 0, "a device wait timed out"
+
+    # Dominant kernel: the LM head GEMVs (most of the bytes). Time each alone,
+    # rotating its weight copies, with CUDA events on the launching stream.
+    per_kernel = {}
+    for c in calls:
+        if c["name"] != "lm_head":
+            continue
+        gs = []
+        with torch.cuda.stream(stream):
+            for g in range(WEIGHT_COPIES):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    matmulq.matmul_q8(c["x"], c["w"][g], out=c["y"], mode=args.mode,
+                                      workspace=c["ws"], stream=stream)
+                gs.append(graph)
+        reps = max(60, args.steps * 2)
+        s = time_graphs(torch, gs, reps, 6, stream)
+        per_kernel[c["M"]] = {"us": s / reps * 1e6, "bytes": c["bytes"],
+                              "plan": matmulq.plan_info(c["M"], c["K"], c["N"], mode=args.mode)}
+    # the LM head launch with the larger time is the dominant kernel
+    dom_m = max(per_kernel, key=lambda m: per_kernel[m]["us"])
+    dom = per_kernel[dom_m]
+    achieved = dom["bytes"] / (dom["us"] * 1e-6) / 1e9
+    traffic = committed_traffic(f"gemv_lm_head_m{dom_m}_{args.mode}")
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                "kernel": f"gemv_q8_kernel (LM head 768x50257, M={dom_m})",
+                "peak_kind": f"{peak_kind} hbm_gbs",
+                "per_launch_us": round(dom["us"], 3),
+                "algorithmic_bytes_per_launch": dom["bytes"]}
+
+    # End to end through the C ABI from the host (pinned buffers, copies timed).
+    e2e = run_e2e(torch, calls, args, dev, stream, dist, world)
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "i8w-f32acc",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantized per channel)",
+        "config": {"workload": "decode GEMV set, GPT-2-small shapes (QKV 768x2304, attn-out 768x768, "
+                               "FFN-up 768x3072, FFN-down 3072x768, LM head 768x50257) x M in {1,8}",
+                   "calls_per_step": len(calls), "algorithmic_bytes_per_step": step_bytes,
+                   "mode": args.mode, "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": f"weights rotated over {WEIGHT_COPIES} copies "
+                         f"({WEIGHT_COPIES * sum(c['K'] * c['N'] for c in calls) / 1e6:.0f} MB > 2x L2)",
+                   "timing": "CUDA graphs of one step, CUDA events on the launching stream"},
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": len(calls) * args.steps,
+        "clocks": clk.summary(),
+    }
+    return line, calls, stream
+
+
+def run_e2e(torch, calls, args, dev, stream, dist, world):
+    """Host-driven: per call, pinned H2D of X, mtrtq_matmul through ctypes, D2H of Y."""
+    from mini_tensorrt_b200 import _lib
+    from mini_tensorrt_b200.matmulq import MODES
+    lib = _lib.lib()
+    hx = [c["x"].cpu().pin_memory() for c in calls]
+    hy = [torch.empty_like(c["y"], device="cpu").pin_memory() for c in calls]
+    sp = stream.cuda_stream
+    mode = MODES[args.mode]
+    h2d = sum(c["M"] * c["K"] * 4 for c in calls)
+    d2h = sum(c["M"] * c["N"] * 4 for c in calls)
+    step_bytes = sum(c["bytes"] for c in calls)
+    ptrs = [(c["x"].data_ptr(), c["K"], c["y"].data_ptr(), c["N"], c["M"], c["ws"].data_ptr(),
+             c["ws"].numel(), [w.packed.data_ptr() for w in c["w"]], [w.scale.data_ptr() for w in c["w"]])
+            for c in calls]
+
+    def step(i):
+        for j, (xp, K, yp, N, M, wsp, wsn, wps, sps) in enumerate(ptrs):
+            calls[j]["x"].copy_(hx[j], non_blocking=True)
+            g = (i + j) % WEIGHT_COPIES
+            rc = lib.mtrtq_matmul(xp, 0, K, wps[g], sps[g], None, yp, N, M, K, N, mode, wsp, wsn, sp)
+            if rc != 0:
+                raise RuntimeError(_lib.last_error())
+            hy[j].copy_(calls[j]["y"], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    secs = e0.elapsed_time(e1) / 1e3
+    t = torch.tensor([secs], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    secs = float(t.item())
+    return {"value": round(step_bytes * args.steps * world / secs / 1e9, 1), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(secs / args.steps * 1e3, 4),
+            "how": "per call: pinned H2D of X, mtrtq_matmul via ctypes, pinned D2H of Y; CUDA events"}
+
+
+def run_extras(torch, dev, args, stream):
+    """Prefill tensor-core GEMM at the large shapes (M=2048, bf16 X) and the
+    single-op FFN-up case (M=64, fp32 X, bias), each timed alone."""
+    from mini_tensorrt_b200 import matmulq, workloads as wl
+    hbm_peak, tc_peak, tc_sust, peak_kind = peaks()
+    out = {}
+    for (K, N) in wl.LARGE_SHAPES:
+        M = 2048
+        W = wl.weights(K, N, wl.shape_seed(f"large_{K}x{N}", K, N))
+        q, s = matmulq.quantize_per_channel(W)
+        pw = matmulq.PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), dev)
+        x = torch.randn(M, K, device=dev, generator=torch.Generator(dev).manual_seed(1)).to(torch.bfloat16)
+        y = torch.empty(M, N, device=dev)
+        ws = torch.zeros(max(matmulq.workspace_bytes(M, K, N, torch.bfloat16, "bf16"), 256),
+                         dtype=torch.uint8, device=dev)
+        with torch.cuda.stream(stream):
+            matmulq.matmul_q8(x, pw, out=y, workspace=ws, stream=stream)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(5):
+                    matmulq.matmul_q8(x, pw, out=y, workspace=ws, stream=stream)
+        secs = time_graphs(torch, [graph], 10, 3, stream) / 5
+        tf = wl.flops(M, K, N) / (secs / 10) / 1e12
+        out[f"gemm_m{M}_{K}x{N}"] = {"tflops": round(tf, 1), "us": round(secs / 10 * 1e6, 2),
+                                     "frac_of_bf16_peak": round(tf / tc_peak, 4),
+                                     "plan": matmulq.plan_info(M, K, N, torch.bfloat16, "bf16")}
+        del pw, x, y, ws, graph
+    M, K, N = 64, 768, 3072
+    W = wl.weights(K, N, 7)
+    q, s = matmulq.quantize_per_channel(W)
+    copies = [matmulq.PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), dev)
+              for _ in range(60)]  # 141 MB of weights > L2
+    x = torch.randn(M, K, device=dev)
+    b = torch.randn(N, device=dev) * 0.02
+    y = torch.empty(M, N, device=dev)
+    ws = torch.zeros(max(matmulq.workspace_bytes(M, K, N, torch.float32, "bf16"), 256),
+                     dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        matmulq.matmul_q8(x, copies[0], bias=b, out=y, workspace=ws, stream=stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for c in copies:
+                matmulq.matmul_q8(x, c, bias=b, out=y, workspace=ws, stream=stream)
+    secs = time_graphs(torch, [graph], 5, 2, stream) / (5 * len(copies))
+    byts = wl.algorithmic_bytes(M, K, N, 4, True)
+    out["single_op_ffn_up_m64_bias"] = {"us": round(secs * 1e6, 2),
+                                        "gbs": round(byts / secs / 1e9, 1),
+                                        "tflops": round(wl.flops(M, K, N) / secs / 1e12, 2),
+                                        "plan": matmulq.plan_info(M, K, N, torch.float32, "bf16")}
+    return out
+
+
+# ---------------------------------------------------------------------- CPU legs
+
+
+def cpu_tasks():
+    """The decode GEMV set as single-row reference calls: (K, N, q, s, x_row)."""
+    from mini_tensorrt_b200 import matmulq, workloads as wl
+    tasks, step_bytes = [], 0
+    for M in wl.DECODE_M:
+        for name, K, N in wl.DECODE_SHAPES:
+            q, s = matmulq.quantize_per_channel(wl.decode_weight(name, K, N))
+            X = wl.activations(M, K, wl.shape_seed("x:" + name, M, K))
+            for r in range(M):
+                tasks.append((K, N, q, s, np.ascontiguousarray(X[r:r + 1])))
+            step_bytes += wl.algorithmic_bytes(M, K, N, 4)
+    return tasks, step_bytes
+
+
+def run_cpu_reference(tasks, threads, min_seconds=None, steps=None):
+    """Runs whole steps of `tasks` through the reference MatMulQ (oracle/_ref) on
+    `threads` host threads; returns (steps run, seconds)."""
+    import oracle
+    ref = oracle.ref()
+
+    def one(t):
+        K, N, q, s, x = t
+        C = np.empty((1, N), np.float32)
+        ref.ref_matmulq(x.ctypes.data_as(oracle._f32p), q.ctypes.data_as(oracle._i8p),
+                        s.ctypes.data_as(oracle._f32p), C.ctypes.data_as(oracle._f32p), 1, K, N)
+
+    # Longest calls first so the pool finishes together.
+    order = sorted(tasks, key=lambda t: -t[0] * t[1])
+
+    def run_step():
+        if threads == 1:
+            for t in order:
+                one(t)
+            return
+        idx = [0]
+        lock = threading.Lock()
+
+        def worker():
+            while True:
+                with lock:
+                    i = idx[0]
+                    idx[0] += 1
+                if i >= len(order):
+                    return
+                one(order[i])
+        ws = [threading.Thread(target=worker) for _ in range(threads)]
+        for w in ws:
+            w.start()
+        for w in ws:
+            w.join()
+
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run_step()
+        n += 1
+        el = time.perf_counter() - t0
+        if steps is not None and n >= steps:
+            break
+        if min_seconds is not None and el >= min_seconds:
+            break
+    return n, time.perf_counter() - t0
+
+
+def cpu_baseline_line():
+    import oracle
+    tasks, step_bytes = cpu_tasks()
+    kind = "reference" if oracle.ref_available() else "port"
+    if kind == "port":
+        return {"value": None, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": "oracle/_ref missing on this host"}
+    n, secs = run_cpu_reference(tasks, 1, min_seconds=10.0)
+    return {"value": round(step_bytes * n / secs / 1e9, 4), "unit": UNIT, "cores": 1,
+            "kind": "reference",
+            "sample": f"{n} full decode GEMV set steps (10 calls) through the reference MatMulQ "
+                      f"(oracle/_ref, registry lookup), single thread as the reference runs it, "
+                      f"{secs:.1f} s"}
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built"}))
+        return
+    threads = max(1, os.cpu_count() or 1)
+    tasks, step_bytes = cpu_tasks()
+    threads = min(threads, len(tasks))
+    run_cpu_reference(tasks, threads, steps=max(1, args.warmup))
+    n, secs = run_cpu_reference(tasks, threads, steps=args.steps)
+    value = step_bytes * n / secs / 1e9
+    sample = (f"each step: the full decode GEMV set as {len(tasks)} single-row MatMulQ calls "
+              f"through the reference kernel (oracle/_ref) on {threads} host threads")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+            "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
+            "ms_per_step": round(secs / n * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "i8w-f32acc", "data": "synthetic",
+            "config": {"workload": "decode GEMV set, GPT-2-small shapes x M in {1,8}", "mode": "fp32"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from mini_tensorrt_b200 import build as _b
+    _b.build()
+    line, calls, stream = run_ours(args, torch, rank, world, dev, dist)
+    del calls
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["extras"] = run_extras(torch, dev, args, stream)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_line()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * mtrtq -- B200 (sm_100a) INT8 weight-only MatMul, C ABI.
+ *
+ * Computes the reference's MatMulQ op, C[M,N] = A[M,K] x dequant(W_q8[K,N], scale[N]),
+ * with C[i,j] = scale[j] * sum_k A[i,k] * W[k,j]  (src/ops/kernels_matmul.cpp:42-74),
+ * optionally followed by the bias broadcast Add (src/ops/kernels_elementwise.cpp:31-35).
+ *
+ * The interface replaces, for this op, the reference's CPU kernel function
+ *   void matmul_q8_f32(const OpContext&)  registered as ("MatMulQ", DType::kF32)
+ *   (src/ops/kernels_matmul.cpp:78-81, include/mtrt/registry.h:19-22,
+ *    include/mtrt/op_context.h:13-20)
+ * and adds the device launcher the CUDA backend lacks (backends/cuda/kernels.h:11-76
+ * declares raw-device-pointer launchers for every other op; the CUDA executor throws
+ * on MatMulQ at backends/cuda/cuda_executor.cpp:152-154).
+ *
+ * Conventions
+ *  - Every entry point returns an int status (MTRTQ_OK == 0). None aborts or traps;
+ *    mtrtq_last_error() gives a message for the calling thread's last failure.
+ *  - Device pointers are plain CUDA device addresses. `stream` is a cudaStream_t
+ *    passed as void* (NULL = the legacy default stream), so the header needs no
+ *    CUDA include and binds from any FFI.
+ *  - Launch calls never allocate: scratch lives in a caller workspace sized by
+ *    mtrtq_workspace_bytes(). The workspace must be zero-filled once after it is
+ *    allocated; every call leaves it zero-filled again where that matters (split
+ *    counters). Calls that share a workspace must be ordered (same stream).
+ *  - Matrices are row-major and contiguous unless a leading dimension is given.
+ *  - No CPU fallback: without an sm_100 device the launch calls fail with
+ *    MTRTQ_ERR_NO_DEVICE.
+ */
+#ifndef MTRTQ_H_
+#define MTRTQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MTRTQ_VERSION 100 /* 1.0.0 */
+
+/* Status codes. The reference validates with MTRT_ASSERT (Debug abort, Release
+ * no-op, include/mtrt/support/assert.h:21-30) and aborts on CUDA errors
+ * (backends/cuda/kernels.cu:13-21); this ABI reports instead. */
+enum {
+  MTRTQ_OK = 0,
+  MTRTQ_ERR_INVALID_ARG = 1,  /* null pointer, non-positive or too-large size, bad enum */
+  MTRTQ_ERR_ALIGNMENT = 2,    /* a pointer or leading dimension breaks a stated alignment */
+  MTRTQ_ERR_WORKSPACE = 3,    /* workspace smaller than mtrtq_workspace_bytes() */
+  MTRTQ_ERR_NO_DEVICE = 4,    /* no CUDA device of compute capability 10.x */
+  MTRTQ_ERR_CUDA = 5,         /* a CUDA runtime call or launch failed */
+  MTRTQ_ERR_TIMEOUT = 6,      /* a bounded device-side wait gave up (see mtrtq_read_status) */
+  MTRTQ_ERR_ZERO_SCALE = 7    /* quantization met an all-zero column (see below) */
+};
+
+/* Activation element types accepted for A. */
+enum { MTRTQ_DTYPE_F32 = 0, MTRTQ_DTYPE_BF16 = 1 };
+
+/* Arithmetic modes.
+ *  MTRTQ_MODE_BF16: A is rounded to bf16 (round-to-nearest-even) once; the int8
+ *    weights are exact in bf16; products accumulate in fp32. M <= 8 runs the decode
+ *    GEMV on CUDA cores, M > 8 the tcgen05 tensor-core GEMM (TMEM accumulators).
+ *  MTRTQ_MODE_FP32: A stays fp32 and every product and sum is fp32 on CUDA cores,
+ *    the reference's arithmetic up to summation order. */
+enum { MTRTQ_MODE_BF16 = 0, MTRTQ_MODE_FP32 = 1 };
+
+/* Quantize-time policy for an all-zero weight column (the reference packer divides
+ * 0/0 there, tests/golden_kernel_test.cpp:166-169; numpy's packer uses scale 1,
+ * python/quantize_gpt2.py:32). */
+enum {
+  MTRTQ_ZERO_COLUMN_REJECT = 0, /* return MTRTQ_ERR_ZERO_SCALE */
+  MTRTQ_ZERO_COLUMN_ZERO = 1    /* scale 0, q 0: the bytes the reference's x86-64 build stores */
+};
+
+/* Library version (MTRTQ_VERSION of the build). */
+int mtrtq_version(void);
+
+/* Text for a status code; never NULL. */
+const char* mtrtq_status_string(int status);
+
+/* Message for the calling thread's last failing call ("" if none). */
+const char* mtrtq_last_error(void);
+
+/* ---- quantization (host) ------------------------------------------------------ */
+
+/* Host, single-threaded. W f32 [K,N] row-major -> q int8 [K,N] row-major and
+ * scale f32 [N], bit-exact with the reference packer (tests/golden_kernel_test.cpp:
+ * 163-170): amax = max_k |W|, s = amax / 127.0f, q = (int8) lround(W / s).
+ * zero_column_policy: MTRTQ_ZERO_COLUMN_*. */
+int mtrtq_quantize_per_channel(const float* W, int64_t K, int64_t N, int8_t* q, float* scale,
+                               int zero_column_policy);
+
+/* ---- weight pre-pack ------------------------------------------------------------ */
+
+/* Bytes of the device weight layout for a [K,N] int8 matrix:
+ * N_pad x K_pad with N_pad = ceil(N/128)*128 and K_pad = ceil(K/64)*64.
+ * The layout ("channel tiles of 16-k slabs"): for channel tile t (128 channels) and
+ * slab s (16 consecutive k), 2048 contiguous bytes hold, for each of the 128 channels
+ * in order, its 16 int8 weights. Padding is zero. Returns -1 for invalid sizes. */
+int64_t mtrtq_packed_bytes(int64_t K, int64_t N);
+
+/* Device: q_KN int8 [K,N] row-major (device memory, as the CUDA executor uploads a
+ * weight, backends/cuda/cuda_executor.cpp:61-72) -> packed (device, 256-byte
+ * aligned, packed_bytes >= mtrtq_packed_bytes). The int8 values are unchanged. */
+int mtrtq_prepack(const int8_t* q_KN, int64_t K, int64_t N, void* packed, size_t packed_bytes,
+                  void* stream);
+
+/* Host: the same layout transform on host memory (for upload with one copy). */
+int mtrtq_prepack_host(const int8_t* q_KN, int64_t K, int64_t N, void* packed,
+                       size_t packed_bytes);
+
+/* ---- the op ---------------------------------------------------------------------- */
+
+/* Workspace bytes mtrtq_matmul needs for this problem (0 is possible). */
+int64_t mtrtq_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int mode);
+
+/* Y[M,N] (+)= ... : Y[i*ldy + j] = scale[j] * sum_k X[i*ldx + k] * W[k,j] (+ bias[j]).
+ *   X       device, x_dtype elements, row stride ldx >= K (elements), 16-byte aligned
+ *   packed  device, from mtrtq_prepack for the same K, N, 256-byte aligned
+ *   scale   device f32 [N];  bias device f32 [N] or NULL
+ *   Y       device f32, row stride ldy >= N (elements), 4-byte aligned
+ *   workspace device, >= mtrtq_workspace_bytes(M,K,N,x_dtype,mode) bytes, 256-byte
+ *           aligned, zero-filled once after allocation (may be NULL if that size is 0)
+ * Asynchronous on `stream`. */
+int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                 const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N,
+                 int mode, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- options and diagnostics ----------------------------------------------------- */
+
+/* Process-wide options. Both change how a call is carried out, never its result
+ * beyond fp32 summation order; the workspace size depends on them, so set them
+ * before querying mtrtq_workspace_bytes. */
+enum {
+  MTRTQ_OPT_GEMM_A_SOURCE = 1, /* 0 (default): dequantized weights staged in TMEM
+                                  (tcgen05.mma A from tensor memory);
+                                  1: staged in 128-byte-swizzled shared memory */
+  MTRTQ_OPT_FORCE_PATH = 2     /* 0 (default): GEMV for M <= 8 or MTRTQ_MODE_FP32,
+                                  tcgen05 GEMM otherwise; 1: always GEMV;
+                                  2: always GEMM (MTRTQ_MODE_BF16 only) */
+};
+int mtrtq_set_option(int option, int64_t value);
+
+/* The plan mtrtq_matmul would use: info[0] path (0 GEMV, 1 GEMM), [1] token rows
+ * per tile, [2] token tiles, [3] channel tiles, [4] k splits, [5] k per split.
+ * n_info >= 6. */
+int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info,
+                    int n_info);
+
+/* Reads and clears the device status word the kernels set when a bounded wait gives
+ * up (MTRTQ_OK or MTRTQ_ERR_TIMEOUT). Synchronizes the current device. After a
+ * timeout the workspace of the failed call must be zero-filled again. */
+int mtrtq_read_status(int* device_status);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MTRTQ_H_ */

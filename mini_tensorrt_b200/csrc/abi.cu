@@ -1,0 +1,385 @@
+// C ABI of the INT8 weight-only MatMul library (include/mtrtq.h).
+//
+// Argument checking mirrors the MTRT_ASSERT preconditions of the reference
+// kernel (src/ops/kernels_matmul.cpp:43-60: ranks, inner dimensions, scale of
+// length N) but reports a status instead of aborting. Planning (GEMV vs tcgen05
+// GEMM, tile and split-K choice, workspace layout) is one pure function used by
+// both mtrtq_workspace_bytes and mtrtq_matmul, so the two always agree.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/mtrtq.h"
+#include "q8_common.cuh"
+#include "q8_internal.h"
+
+namespace mtrtq {
+
+// Device status word: a kernel whose bounded wait gives up stores
+// MTRTQ_ERR_TIMEOUT here (kernels get its address as a parameter).
+__device__ unsigned int g_device_status = 0;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MTRTQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Process-wide options (mtrtq_set_option).
+int g_opt_gemm_a_source = 0;  // 0: dequantized weights in TMEM, 1: in shared memory
+int g_opt_force_path = 0;     // 0 auto, 1 GEMV, 2 tcgen05 GEMM
+
+std::mutex g_dev_mu;
+DeviceInfo g_dev_cache[64];
+
+// Current device's properties; sm_count 148 when there is no device.
+int current_device(DeviceInfo* out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return fail(MTRTQ_ERR_NO_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+  }
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev_cache[dev];
+  if (d.device != dev) {
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    d.device = dev;
+    d.sm_count = prop.multiProcessorCount;
+    d.major = prop.major;
+    d.minor = prop.minor;
+    d.smem_optin = prop.sharedMemPerBlockOptin;
+  }
+  *out = d;
+  return MTRTQ_OK;
+}
+
+int sm_count_or_default() {
+  DeviceInfo d;
+  if (current_device(&d) == MTRTQ_OK) return d.sm_count;
+  g_last_error.clear();
+  return 148;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+constexpr int64_t kMaxDim = int64_t(1) << 30;
+
+int check_dims(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0)
+    return fail(MTRTQ_ERR_INVALID_ARG, "sizes must be positive (M=%lld K=%lld N=%lld)",
+                (long long)M, (long long)K, (long long)N);
+  if (M > kMaxDim || K > kMaxDim || N > kMaxDim)
+    return fail(MTRTQ_ERR_INVALID_ARG, "a size exceeds 2^30 (M=%lld K=%lld N=%lld)",
+                (long long)M, (long long)K, (long long)N);
+  const int64_t n_pad = round_up64(N, kTileN), k_pad = round_up64(K, kBlockK);
+  if (n_pad > (int64_t(1) << 62) / k_pad) return fail(MTRTQ_ERR_INVALID_ARG, "K*N overflows");
+  return MTRTQ_OK;
+}
+
+int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_count, Plan* out) {
+  if (int rc = check_dims(M, K, N)) return rc;
+  if (x_dtype != MTRTQ_DTYPE_F32 && x_dtype != MTRTQ_DTYPE_BF16)
+    return fail(MTRTQ_ERR_INVALID_ARG, "x_dtype must be MTRTQ_DTYPE_F32 or MTRTQ_DTYPE_BF16");
+  if (mode != MTRTQ_MODE_BF16 && mode != MTRTQ_MODE_FP32)
+    return fail(MTRTQ_ERR_INVALID_ARG, "mode must be MTRTQ_MODE_BF16 or MTRTQ_MODE_FP32");
+  if (mode == MTRTQ_MODE_FP32 && x_dtype == MTRTQ_DTYPE_BF16)
+    return fail(MTRTQ_ERR_INVALID_ARG, "MTRTQ_MODE_FP32 needs fp32 activations");
+  Plan p;
+  p.M = M;
+  p.K = K;
+  p.N = N;
+  p.n_pad = round_up64(N, kTileN);
+  p.k_pad = round_up64(K, kBlockK);
+  p.n_tiles = (int)(p.n_pad / kTileN);
+
+  bool gemm = (mode == MTRTQ_MODE_BF16) && M > 8;
+  if (g_opt_force_path == 1) gemm = false;
+  if (g_opt_force_path == 2) {
+    if (mode != MTRTQ_MODE_BF16)
+      return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core GEMM computes in MTRTQ_MODE_BF16 only");
+    gemm = true;
+  }
+
+  if (!gemm) {
+    p.kind = Plan::kGemv;
+    p.tile_m = 8;
+    p.m_tiles = (int)ceil_div64(M, 8);
+    if (p.m_tiles > 65535) return fail(MTRTQ_ERR_INVALID_ARG, "M too large for the GEMV path");
+    p.kunits = (int)(p.k_pad / kSlabK);
+    p.round_x = (mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32);
+    const int64_t base = (int64_t)p.n_tiles * p.m_tiles;
+    const int64_t target = (int64_t)sm_count * 6;
+    int64_t splits = base < target ? ceil_div64(target, base) : 1;
+    const int64_t max_by_len = p.kunits >= 4 ? p.kunits / 2 : 1;  // >= 2 slabs per split
+    if (splits > max_by_len) splits = max_by_len;
+    int64_t sps = ceil_div64(p.kunits, splits);
+    const int mt = (int)(M < 8 ? M : 8);
+    const int64_t sps_cap = (48 * 1024) / (kSlabK * 4 * mt);  // staged activations <= 48 KiB
+    if (sps > sps_cap) sps = sps_cap;
+    p.kunits_per_split = (int)sps;
+    p.splits = (int)ceil_div64(p.kunits, sps);
+    if (p.splits > 65535) return fail(MTRTQ_ERR_INVALID_ARG, "K too large for the GEMV path");
+  } else {
+    p.kind = Plan::kGemmTC;
+    int tm = 256;
+    if (M <= 16) tm = 16;
+    else if (M <= 32) tm = 32;
+    else if (M <= 64) tm = 64;
+    else if (M <= 128) tm = 128;
+    p.tile_m = tm;
+    p.m_tiles = (int)ceil_div64(M, tm);
+    if (p.n_tiles > 65535) return fail(MTRTQ_ERR_INVALID_ARG, "N too large for the GEMM path");
+    p.kunits = (int)(p.k_pad / kBlockK);
+    const int64_t base = (int64_t)p.n_tiles * p.m_tiles;
+    const int64_t target = (int64_t)sm_count * (tm >= 256 ? 1 : 2);
+    int64_t splits = base < target ? ceil_div64(target, base) : 1;
+    const int64_t max_by_len = p.kunits >= 4 ? p.kunits / 2 : 1;  // >= 2 blocks per split
+    if (splits > max_by_len) splits = max_by_len;
+    if (splits > 65535) splits = 65535;
+    const int64_t kbps = ceil_div64(p.kunits, splits);
+    p.kunits_per_split = (int)kbps;
+    p.splits = (int)ceil_div64(p.kunits, kbps);
+    p.x_to_bf16 = (x_dtype == MTRTQ_DTYPE_F32);
+    p.ldxb = round_up64(K, 8);
+  }
+
+  size_t off = 0;
+  p.off_counters = off;
+  off += round256((size_t)p.n_tiles * p.m_tiles * sizeof(unsigned));
+  p.off_partials = off;
+  if (p.splits > 1) off += round256((size_t)p.splits * (size_t)M * (size_t)p.n_pad * sizeof(float));
+  p.off_xb = off;
+  if (p.x_to_bf16) off += round256((size_t)M * (size_t)p.ldxb * 2);
+  // A single-split GEMV needs no workspace at all.
+  p.total = (p.splits > 1 || p.x_to_bf16) ? off : 0;
+  *out = p;
+  return MTRTQ_OK;
+}
+
+int check_device_sm100(DeviceInfo* d) {
+  if (int rc = current_device(d)) return rc;
+  if (d->major != 10)
+    return fail(MTRTQ_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a",
+                d->device, d->major, d->minor);
+  return MTRTQ_OK;
+}
+
+}  // namespace
+}  // namespace mtrtq
+
+using namespace mtrtq;
+
+extern "C" {
+
+int mtrtq_version(void) { return MTRTQ_VERSION; }
+
+const char* mtrtq_status_string(int status) {
+  switch (status) {
+    case MTRTQ_OK: return "ok";
+    case MTRTQ_ERR_INVALID_ARG: return "invalid argument";
+    case MTRTQ_ERR_ALIGNMENT: return "misaligned pointer or leading dimension";
+    case MTRTQ_ERR_WORKSPACE: return "workspace too small";
+    case MTRTQ_ERR_NO_DEVICE: return "no sm_100 CUDA device";
+    case MTRTQ_ERR_CUDA: return "CUDA error";
+    case MTRTQ_ERR_TIMEOUT: return "device wait timed out";
+    case MTRTQ_ERR_ZERO_SCALE: return "all-zero weight column";
+    default: return "unknown status";
+  }
+}
+
+const char* mtrtq_last_error(void) { return g_last_error.c_str(); }
+
+int mtrtq_set_option(int option, int64_t value) {
+  switch (option) {
+    case MTRTQ_OPT_GEMM_A_SOURCE:
+      if (value != 0 && value != 1) return fail(MTRTQ_ERR_INVALID_ARG, "GEMM A source is 0 or 1");
+      g_opt_gemm_a_source = (int)value;
+      return MTRTQ_OK;
+    case MTRTQ_OPT_FORCE_PATH:
+      if (value < 0 || value > 2) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0, 1 or 2");
+      g_opt_force_path = (int)value;
+      return MTRTQ_OK;
+    default:
+      return fail(MTRTQ_ERR_INVALID_ARG, "unknown option %d", option);
+  }
+}
+
+int mtrtq_quantize_per_channel(const float* W, int64_t K, int64_t N, int8_t* q, float* scale,
+                               int zero_column_policy) {
+  if (!W || !q || !scale) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  if (K <= 0 || N <= 0) return fail(MTRTQ_ERR_INVALID_ARG, "K and N must be positive");
+  if (zero_column_policy != MTRTQ_ZERO_COLUMN_REJECT && zero_column_policy != MTRTQ_ZERO_COLUMN_ZERO)
+    return fail(MTRTQ_ERR_INVALID_ARG, "unknown zero-column policy");
+  // Reference packer, tests/golden_kernel_test.cpp:163-170. The reference walks
+  // column by column; this walks rows (cache-friendly for [K,N] row-major). The
+  // bytes are identical: max is exact and order-free, and the division and
+  // lround are per element.
+  for (int64_t j = 0; j < N; ++j) scale[j] = 0.0f;  // running amax
+  for (int64_t k = 0; k < K; ++k) {
+    const float* row = W + k * N;
+    for (int64_t j = 0; j < N; ++j) {
+      const float a = std::fabs(row[j]);
+      scale[j] = scale[j] < a ? a : scale[j];
+    }
+  }
+  for (int64_t j = 0; j < N; ++j) {
+    if (scale[j] == 0.0f && zero_column_policy == MTRTQ_ZERO_COLUMN_REJECT)
+      return fail(MTRTQ_ERR_ZERO_SCALE, "weight column %lld is all zero", (long long)j);
+  }
+  for (int64_t j = 0; j < N; ++j) scale[j] = scale[j] / 127.0f;
+  for (int64_t k = 0; k < K; ++k) {
+    const float* row = W + k * N;
+    int8_t* qrow = q + k * N;
+    for (int64_t j = 0; j < N; ++j)
+      qrow[j] = scale[j] == 0.0f ? int8_t(0) : static_cast<int8_t>(std::lround(row[j] / scale[j]));
+  }
+  return MTRTQ_OK;
+}
+
+int64_t mtrtq_packed_bytes(int64_t K, int64_t N) {
+  if (K <= 0 || N <= 0 || K > kMaxDim || N > kMaxDim) return -1;
+  return round_up64(N, kTileN) * round_up64(K, kBlockK);
+}
+
+int mtrtq_prepack_host(const int8_t* q_KN, int64_t K, int64_t N, void* packed, size_t packed_bytes) {
+  if (!q_KN || !packed) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  const int64_t need = mtrtq_packed_bytes(K, N);
+  if (need < 0) return fail(MTRTQ_ERR_INVALID_ARG, "invalid K=%lld N=%lld", (long long)K, (long long)N);
+  if ((int64_t)packed_bytes < need)
+    return fail(MTRTQ_ERR_INVALID_ARG, "packed buffer %zu bytes < %lld", packed_bytes, (long long)need);
+  const int64_t KS = round_up64(K, kBlockK) / kSlabK;
+  const int64_t n_tiles = round_up64(N, kTileN) / kTileN;
+  uint8_t* out = static_cast<uint8_t*>(packed);
+  for (int64_t t = 0; t < n_tiles; ++t)
+    for (int64_t s = 0; s < KS; ++s)
+      for (int64_t r = 0; r < kTileN; ++r) {
+        uint8_t* dst = out + ((t * KS + s) * kTileN + r) * kSlabK;
+        const int64_t n = t * kTileN + r;
+        for (int b = 0; b < kSlabK; ++b) {
+          const int64_t k = s * kSlabK + b;
+          dst[b] = (n < N && k < K) ? static_cast<uint8_t>(q_KN[k * N + n]) : 0;
+        }
+      }
+  return MTRTQ_OK;
+}
+
+int mtrtq_prepack(const int8_t* q_KN, int64_t K, int64_t N, void* packed, size_t packed_bytes,
+                  void* stream) {
+  if (!q_KN || !packed) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  const int64_t need = mtrtq_packed_bytes(K, N);
+  if (need < 0) return fail(MTRTQ_ERR_INVALID_ARG, "invalid K=%lld N=%lld", (long long)K, (long long)N);
+  if ((int64_t)packed_bytes < need)
+    return fail(MTRTQ_ERR_INVALID_ARG, "packed buffer %zu bytes < %lld", packed_bytes, (long long)need);
+  if (!aligned(packed, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "packed weights must be 256-byte aligned");
+  DeviceInfo d;
+  if (int rc = check_device_sm100(&d)) return rc;
+  cudaError_t e = launch_prepack(q_KN, K, N, packed, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "prepack launch");
+  return MTRTQ_OK;
+}
+
+int64_t mtrtq_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int mode) {
+  Plan p;
+  if (plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p) != MTRTQ_OK) return -1;
+  return (int64_t)p.total;
+}
+
+int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                 const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (!X || !packed || !scale || !Y) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  if (ldx < K) return fail(MTRTQ_ERR_INVALID_ARG, "ldx (%lld) < K (%lld)", (long long)ldx, (long long)K);
+  if (ldy < N) return fail(MTRTQ_ERR_INVALID_ARG, "ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
+  DeviceInfo d;
+  if (int rc = check_device_sm100(&d)) return rc;
+  Plan p;
+  if (int rc = plan_matmul(M, K, N, x_dtype, mode, d.sm_count, &p)) return rc;
+  if (!aligned(packed, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "packed weights must be 256-byte aligned");
+  if (!aligned(scale, 4) || (bias && !aligned(bias, 4)) || !aligned(Y, 4))
+    return fail(MTRTQ_ERR_ALIGNMENT, "scale, bias and Y must be 4-byte aligned");
+  if (!aligned(X, 16)) return fail(MTRTQ_ERR_ALIGNMENT, "X must be 16-byte aligned");
+  if (p.total > 0) {
+    if (!workspace || workspace_bytes < p.total)
+      return fail(MTRTQ_ERR_WORKSPACE, "workspace %zu bytes < %zu", workspace_bytes, p.total);
+    if (!aligned(workspace, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (p.kind == Plan::kGemv) {
+    e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, workspace, st);
+    if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+    return MTRTQ_OK;
+  }
+  const void* xb = X;
+  int64_t ldxb = ldx;
+  if (p.x_to_bf16) {
+    xb = static_cast<char*>(workspace) + p.off_xb;
+    ldxb = p.ldxb;
+    e = launch_x_to_bf16(X, x_dtype, ldx, M, K, const_cast<void*>(xb), ldxb, st);
+    if (e != cudaSuccess) return cuda_fail(e, "activation staging launch");
+  } else if ((ldx * 2) % 16 != 0) {
+    return fail(MTRTQ_ERR_ALIGNMENT, "bf16 X on the GEMM path needs ldx %% 8 == 0 (ldx=%lld)",
+                (long long)ldx);
+  }
+  unsigned* status = nullptr;
+  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
+  if (e != cudaSuccess) return cuda_fail(e, "device status address");
+  CUtensorMap xmap;
+  const int rc = make_x_tensor_map(&xmap, xb, M, K, ldxb, p.tile_m);
+  if (rc != 0) return fail(MTRTQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", rc);
+  e = launch_gemm_tc(p, xb, ldxb, packed, scale, bias, Y, ldy, workspace, xmap,
+                     g_opt_gemm_a_source == 0 ? 1 : 0, status, st);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  return MTRTQ_OK;
+}
+
+int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info, int n_info) {
+  if (!info || n_info < 6) return fail(MTRTQ_ERR_INVALID_ARG, "info needs 6 slots");
+  Plan p;
+  if (int rc = plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p)) return rc;
+  info[0] = p.kind;
+  info[1] = p.tile_m;
+  info[2] = p.m_tiles;
+  info[3] = p.n_tiles;
+  info[4] = p.splits;
+  info[5] = p.kunits_per_split * (p.kind == Plan::kGemv ? kSlabK : kBlockK);
+  return MTRTQ_OK;
+}
+
+int mtrtq_read_status(int* device_status) {
+  if (!device_status) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  DeviceInfo d;
+  if (int rc = check_device_sm100(&d)) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "read device status");
+  const unsigned zero = 0;
+  e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero));
+  if (e != cudaSuccess) return cuda_fail(e, "clear device status");
+  *device_status = (int)v;
+  return MTRTQ_OK;
+}
+
+}  // extern "C"

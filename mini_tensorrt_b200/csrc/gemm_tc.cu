@@ -1,0 +1,391 @@
+// Prefill GEMM for the INT8 weight-only MatMul on 5th-generation tensor cores.
+//
+// Replaces, for M > 8 token rows, the reference's scalar MatMulQ loop
+// (src/ops/kernels_matmul.cpp:66-73). Swap-AB orientation: the MMA's M side is
+// 128 output channels (one channel tile of the packed weights), its N side is a
+// tile of TM tokens, K advances 64 at a time, so the per-channel scale and bias
+// are per-TMEM-lane constants in the epilogue and Y stores are coalesced along
+// channels.
+//
+// One CTA = 6 warps, warp-specialised, one output tile of 128 channels x TM
+// tokens over a k range:
+//   warp 0      producer: per stage one TMA tensor copy of the bf16 activation
+//               tile (128-byte swizzle) and one 8 KiB bulk copy of the int8 weight
+//               tile, both completing on the stage's `full` mbarrier;
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma (kind::f16, fp32
+//               accumulators in TMEM) and tcgen05.commit to release stages;
+//   warps 2..5  dequantize: each thread owns one channel row, reads its 64 int8
+//               weights of the stage from shared memory, converts them exactly to
+//               bf16 and writes them as the MMA's A operand -- into TMEM with
+//               tcgen05.st (A_TMEM) or into a 128-byte-swizzled shared tile;
+//               afterwards the same warps run the epilogue (tcgen05.ld, scale,
+//               bias, store or split-K partial).
+// Every mbarrier wait is bounded (~1 s); on timeout the kernel records
+// MTRTQ_ERR_TIMEOUT in the device status word, drains its own copies and MMAs,
+// frees TMEM and returns.
+#include "q8_common.cuh"
+#include "q8_internal.h"
+
+namespace mtrtq {
+
+struct GemmParams {
+  const uint8_t* W;       // packed weights
+  const float* scale;
+  const float* bias;
+  float* Y;
+  int64_t ldy;
+  int M, N, n_pad;
+  int KB;                 // k blocks of 64 in K_pad
+  int kb_per_split;
+  int splits;
+  int n_tiles, m_tiles;
+  float* partials;        // [splits][M][n_pad]
+  unsigned* counters;     // [m_tiles][n_tiles]
+  unsigned* status;       // device status word (MTRTQ_ERR_TIMEOUT on a failed wait)
+};
+
+template <int TM, bool A_TMEM, int STAGES>
+struct GemmCfg {
+  static constexpr int X_STAGE = TM * 128;                  // TM rows x 64 bf16
+  static constexpr int W_STAGE = kTileN * kBlockK;          // 8192 int8
+  static constexpr int A_STAGE = A_TMEM ? 0 : kTileN * 128; // 128 rows x 64 bf16
+  static constexpr int OFF_X = 0;
+  static constexpr int OFF_A = OFF_X + STAGES * X_STAGE;
+  static constexpr int OFF_W = OFF_A + STAGES * A_STAGE;
+  static constexpr int OFF_BAR = OFF_W + STAGES * W_STAGE;
+  static constexpr int NUM_BARS = 4 * STAGES + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 32 + 1024;   // + alignment slack
+  static constexpr int TMEM_A_COLS = A_TMEM ? STAGES * 32 : 0;
+  static constexpr int ACC_COL = TMEM_A_COLS;
+  static constexpr int NEED_COLS = TMEM_A_COLS + TM;
+  static constexpr int TMEM_COLS = NEED_COLS <= 32 ? 32 : NEED_COLS <= 64 ? 64
+                                 : NEED_COLS <= 128 ? 128 : NEED_COLS <= 256 ? 256 : 512;
+  static_assert(TM % 16 == 0 && TM >= 16 && TM <= 256, "MMA N must be 16..256, multiple of 16");
+  static_assert(X_STAGE % 1024 == 0, "swizzle atoms need 1024-byte aligned stages");
+  static_assert(NEED_COLS <= 512, "TMEM has 512 columns");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
+
+// Bounded wait by every lane of a warp; the result is warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned* status) {
+  const bool ok = mbar_wait_bounded(bar, parity, abort_flag, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Bounded wait that ignores the abort flag (used to drain in-flight work).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned* status) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kSpinLimitCycles) {
+      atomicExch(status, 6u);
+      return;
+    }
+  }
+}
+
+template <int TM, bool A_TMEM, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p) {
+  using C = GemmCfg<TM, A_TMEM, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;                    // TMA landed (X + W), count 1 + tx
+  uint64_t* empty = bars + STAGES;          // stage smem free: 4 converter warps + 1 commit
+  uint64_t* a_full = bars + 2 * STAGES;     // A operand written: 4 converter warps
+  uint64_t* a_empty = bars + 3 * STAGES;    // A operand consumed: 1 commit
+  uint64_t* acc_full = bars + 4 * STAGES;   // accumulator final: 1 commit
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  volatile unsigned* s_ticket = reinterpret_cast<volatile unsigned*>(smem + C::OFF_MISC + 8);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int mt = blockIdx.x;
+  const int nt = blockIdx.y;
+  const int split = blockIdx.z;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(kb0 + p.kb_per_split, p.KB);
+  const int nkb = kb1 - kb0;
+  const int m0 = mt * TM;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 5);
+      mbar_init(&a_full[s], 4);
+      mbar_init(&a_empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) prefetch_tensormap(&xmap);
+  if (warp == 1) {
+    tmem_alloc(s_tmem, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!mbar_wait_bounded(&empty[s], ph ^ 1, s_abort, p.status)) break;
+        mbar_arrive_expect_tx(&full[s], C::X_STAGE + C::W_STAGE);
+        const int kb = kb0 + i;
+        tma_load_2d(smem + C::OFF_X + s * C::X_STAGE, &xmap, kb * kBlockK, m0, &full[s]);
+        bulk_g2s(smem + C::OFF_W + s * C::W_STAGE,
+                 p.W + ((int64_t)nt * p.KB + kb) * (int64_t)C::W_STAGE, C::W_STAGE, &full[s]);
+        ++issued;
+      }
+      // No copy may still be in flight when the CTA exits.
+      for (int j = max(0, issued - STAGES); j < issued; ++j)
+        mbar_drain(&full[j % STAGES], (j / STAGES) & 1, p.status);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
+      const uint32_t acc = tmem_base + C::ACC_COL;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!mbar_wait_bounded(&a_full[s], ph, s_abort, p.status)) break;
+        if (!mbar_wait_bounded(&full[s], ph, s_abort, p.status)) break;
+        tc_fence_after();
+        const uint32_t xaddr = smem_u32(smem + C::OFF_X + s * C::X_STAGE);
+#pragma unroll
+        for (int k = 0; k < kBlockK / 16; ++k) {
+          const uint64_t bdesc = umma_desc_sw128(xaddr + k * 32);
+          const uint32_t accumulate = (i > 0 || k > 0) ? 1u : 0u;
+          if (A_TMEM) {
+            umma_ts(acc, tmem_base + s * 32 + k * 8, bdesc, idesc, accumulate);
+          } else {
+            const uint32_t aaddr = smem_u32(smem + C::OFF_A + s * C::A_STAGE);
+            umma_ss(acc, umma_desc_sw128(aaddr + k * 32), bdesc, idesc, accumulate);
+          }
+        }
+        umma_commit(&empty[s]);
+        umma_commit(&a_empty[s]);
+      }
+      umma_commit(acc_full);
+      if (*s_abort) mbar_drain(acc_full, 0, p.status);  // MMAs must finish before TMEM is freed
+    }
+    __syncwarp();
+  } else {
+    // ---------------- dequantizers, then epilogue ----------------
+    const int q = warp & 3;                 // TMEM lane quadrant of this warp
+    const int r = q * 32 + lane;            // channel row within the tile
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nkb && ok; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      if (!warp_wait(&full[s], ph, s_abort, p.status)) { ok = false; break; }
+      const uint8_t* wst = smem + C::OFF_W + s * C::W_STAGE;
+      uint4 wv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        wv[j] = *reinterpret_cast<const uint4*>(wst + j * kSlabBytes + r * 16);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      uint32_t a[32];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        i8x4_to_bf16x4(wv[j].x, a[8 * j + 0], a[8 * j + 1]);
+        i8x4_to_bf16x4(wv[j].y, a[8 * j + 2], a[8 * j + 3]);
+        i8x4_to_bf16x4(wv[j].z, a[8 * j + 4], a[8 * j + 5]);
+        i8x4_to_bf16x4(wv[j].w, a[8 * j + 6], a[8 * j + 7]);
+      }
+      if (!warp_wait(&a_empty[s], ph ^ 1, s_abort, p.status)) { ok = false; break; }
+      if (A_TMEM) {
+        tmem_st_32x32b_x32(tmem_base + lane_off + s * 32, a);
+        tmem_wait_st();
+      } else {
+        uint8_t* arow = smem + C::OFF_A + s * C::A_STAGE + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) =
+              make_uint4(a[4 * c], a[4 * c + 1], a[4 * c + 2], a[4 * c + 3]);
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[s]);
+    }
+
+    const int n = nt * kTileN + r;
+    const bool n_ok = n < p.N;
+    const float sc = n_ok ? p.scale[n] : 0.0f;
+    const float b = (n_ok && p.bias) ? p.bias[n] : 0.0f;
+    if (ok && warp_wait(acc_full, 0, s_abort, p.status)) {
+      tc_fence_after();
+      for (int c0 = 0; c0 < TM; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(tmem_base + lane_off + C::ACC_COL + c0, v);
+        tmem_wait_ld();
+        if (p.splits == 1) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (n_ok && m < p.M) {
+              float y = __fmul_rn(__uint_as_float(v[j]), sc);
+              if (p.bias) y = __fadd_rn(y, b);
+              p.Y[(int64_t)m * p.ldy + n] = y;
+            }
+          }
+        } else {
+          float* part = p.partials + ((int64_t)split * p.M) * p.n_pad + n;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < p.M) part[(int64_t)m * p.n_pad] = __uint_as_float(v[j]);
+          }
+        }
+      }
+    }
+    if (p.splits > 1) {
+      // Last CTA of this output tile sums the partials in split order. All four
+      // epilogue warps reach both named barriers whatever happened above, and the
+      // ticket is always taken, so the counter returns to zero even after a
+      // timeout (whose output is then flagged by the device status word).
+      __threadfence();
+      named_bar_sync(1, 128);
+      unsigned* counter = p.counters + (int64_t)mt * p.n_tiles + nt;
+      if (warp == 2 && lane == 0) *s_ticket = atomicAdd(counter, 1u);
+      named_bar_sync(1, 128);
+      if (*s_ticket == (unsigned)(p.splits - 1)) {
+        __threadfence();
+        if (n_ok) {
+          const int mend = min(m0 + TM, p.M);
+          for (int m = m0; m < mend; ++m) {
+            const float* src = p.partials + (int64_t)m * p.n_pad + n;
+            float sum = 0.0f;
+            for (int sp = 0; sp < p.splits; ++sp)
+              sum += __ldcg(src + (int64_t)sp * p.M * p.n_pad);
+            float y = __fmul_rn(sum, sc);
+            if (p.bias) y = __fadd_rn(y, b);
+            p.Y[(int64_t)m * p.ldy + n] = y;
+          }
+        }
+        if (warp == 2 && lane == 0) *counter = 0u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int TM, bool A_TMEM, int STAGES>
+static cudaError_t launch_cfg(const GemmParams& gp, const CUtensorMap& xmap, cudaStream_t st) {
+  using C = GemmCfg<TM, A_TMEM, STAGES>;
+  static bool attr_set = false;  // per instantiation; set before the first launch
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_q8_tc_kernel<TM, A_TMEM, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const dim3 grid((unsigned)gp.m_tiles, (unsigned)gp.n_tiles, (unsigned)gp.splits);
+  gemm_q8_tc_kernel<TM, A_TMEM, STAGES><<<grid, 192, C::SMEM_BYTES, st>>>(xmap, gp);
+  return cudaGetLastError();
+}
+
+template <bool A_TMEM>
+static cudaError_t launch_tm(int tm, const GemmParams& gp, const CUtensorMap& xmap, cudaStream_t st) {
+  switch (tm) {
+    case 16: return launch_cfg<16, A_TMEM, 4>(gp, xmap, st);
+    case 32: return launch_cfg<32, A_TMEM, 4>(gp, xmap, st);
+    case 64: return launch_cfg<64, A_TMEM, 4>(gp, xmap, st);
+    case 128: return launch_cfg<128, A_TMEM, 4>(gp, xmap, st);
+    case 256: return launch_cfg<256, A_TMEM, A_TMEM ? 4 : 3>(gp, xmap, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+bool gemm_tile_supported(int tile_m) {
+  return tile_m == 16 || tile_m == 32 || tile_m == 64 || tile_m == 128 || tile_m == 256;
+}
+
+cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const void* packed,
+                           const float* scale, const float* bias, float* Y, int64_t ldy,
+                           void* workspace, const CUtensorMap& xmap, int a_from_tmem,
+                           unsigned* status, cudaStream_t st) {
+  (void)Xb;
+  (void)ldxb;
+  GemmParams gp;
+  gp.W = static_cast<const uint8_t*>(packed);
+  gp.scale = scale;
+  gp.bias = bias;
+  gp.Y = Y;
+  gp.ldy = ldy;
+  gp.M = (int)p.M;
+  gp.N = (int)p.N;
+  gp.n_pad = (int)p.n_pad;
+  gp.KB = p.kunits;
+  gp.kb_per_split = p.kunits_per_split;
+  gp.splits = p.splits;
+  gp.n_tiles = p.n_tiles;
+  gp.m_tiles = p.m_tiles;
+  char* ws = static_cast<char*>(workspace);
+  gp.counters = ws ? reinterpret_cast<unsigned*>(ws + p.off_counters) : nullptr;
+  gp.partials = ws ? reinterpret_cast<float*>(ws + p.off_partials) : nullptr;
+  gp.status = status;
+  return a_from_tmem ? launch_tm<true>(p.tile_m, gp, xmap, st)
+                     : launch_tm<false>(p.tile_m, gp, xmap, st);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) ==
+            cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+int make_x_tensor_map(CUtensorMap* map, const void* Xb, int64_t M, int64_t K, int64_t ldx,
+                      int tile_m) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return -1;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBlockK, (cuuint32_t)tile_m};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(Xb), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+}  // namespace mtrtq

@@ -1,0 +1,58 @@
+// Host-side declarations shared by the launch files and the C ABI (abi.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mtrtq {
+
+// How one mtrtq_matmul call is carried out; computed by plan_matmul() from the
+// problem alone (and the device's SM count), so the workspace query and the
+// launch always agree.
+struct Plan {
+  enum Kind { kGemv = 0, kGemmTC = 1 } kind = kGemv;
+  int64_t M = 0, K = 0, N = 0;
+  int64_t n_pad = 0, k_pad = 0;    // packed weight extents
+  int n_tiles = 0;                 // channel tiles of 128
+  int m_tiles = 0;                 // token tiles (GEMV: chunks of 8 rows)
+  int tile_m = 0;                  // tokens per tile (GEMV: 8; GEMM: 16..256)
+  int splits = 1;                  // k splits
+  int kunits = 0;                  // k units (GEMV: slabs of 16; GEMM: blocks of 64)
+  int kunits_per_split = 0;
+  bool x_to_bf16 = false;          // GEMM: X is staged as a bf16 copy in the workspace
+  bool round_x = false;            // GEMV: round fp32 X to bf16 before the product
+  // workspace layout (byte offsets)
+  size_t off_counters = 0, off_partials = 0, off_xb = 0, total = 0;
+  int64_t ldxb = 0;                // row stride (elements) of the bf16 X copy
+};
+
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 148;
+  int major = 0, minor = 0;
+  size_t smem_optin = 0;
+};
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_prepack(const int8_t* q, int64_t K, int64_t N, void* packed, cudaStream_t st);
+cudaError_t launch_x_to_bf16(const void* X, int x_dtype, int64_t ldx, int64_t M, int64_t K,
+                             void* Xb, int64_t ldxb, cudaStream_t st);
+cudaError_t launch_gemv(const Plan& p, const void* X, int x_dtype, int64_t ldx, const void* packed,
+                        const float* scale, const float* bias, float* Y, int64_t ldy,
+                        void* workspace, cudaStream_t st);
+cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const void* packed,
+                           const float* scale, const float* bias, float* Y, int64_t ldy,
+                           void* workspace, const CUtensorMap& xmap, int a_from_tmem,
+                           unsigned* status, cudaStream_t st);
+
+// Builds the 2-D TMA descriptor for a bf16 [M, K] activation matrix with row
+// stride ldx elements, box = 64 k x tile_m rows, 128-byte swizzle.
+int make_x_tensor_map(CUtensorMap* map, const void* Xb, int64_t M, int64_t K, int64_t ldx,
+                      int tile_m);
+
+// GEMM tile sizes with a compiled kernel.
+bool gemm_tile_supported(int tile_m);
+
+}  // namespace mtrtq

@@ -1,0 +1,198 @@
+"""Torch-facing host API over the C ABI: device weight pre-pack and the MatMulQ launch.
+
+PyTorch supplies device memory, streams and pointers here; the arithmetic is
+the CUDA library's (libmtrtq.so). Nothing in this module computes on the CPU
+except the host quantizer, which is the library's own C function.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+MODES = {"bf16": _lib.MODE_BF16, "fp32": _lib.MODE_FP32}
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def quantize_per_channel(W, zero_columns: str = "reject"):
+    """Host quantization of W f32 [K,N] -> (q int8 [K,N], scale f32 [N]) with the
+    reference packer's rule (tests/golden_kernel_test.cpp:163-170), computed by the
+    library's C function. Accepts numpy arrays or CPU torch tensors; returns numpy."""
+    if isinstance(W, torch.Tensor):
+        W = W.detach().cpu().numpy()
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    if W.ndim != 2:
+        raise ValueError("W must be [K, N]")
+    K, N = W.shape
+    q = np.empty((K, N), dtype=np.int8)
+    s = np.empty((N,), dtype=np.float32)
+    policy = {"reject": _lib.ZERO_COLUMN_REJECT, "zero": _lib.ZERO_COLUMN_ZERO}[zero_columns]
+    check(lib().mtrtq_quantize_per_channel(W.ctypes.data, K, N, q.ctypes.data, s.ctypes.data,
+                                           policy), "mtrtq_quantize_per_channel")
+    return q, s
+
+
+def packed_bytes(K: int, N: int) -> int:
+    n = lib().mtrtq_packed_bytes(K, N)
+    if n < 0:
+        raise ValueError(f"invalid weight shape K={K} N={N}")
+    return n
+
+
+def prepack_host(q: np.ndarray) -> np.ndarray:
+    """Host layout transform int8 [K,N] -> packed bytes (uint8, 1-D)."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    K, N = q.shape
+    out = np.empty(packed_bytes(K, N), dtype=np.uint8)
+    check(lib().mtrtq_prepack_host(q.ctypes.data, K, N, out.ctypes.data, out.nbytes),
+          "mtrtq_prepack_host")
+    return out
+
+
+@dataclass
+class PackedWeight:
+    """One MatMulQ weight on the device: packed int8 bytes + per-channel scale [N].
+
+    Built once at load time (the CUDA executor's weight upload,
+    backends/cuda/cuda_executor.cpp:61-72), reused by every launch."""
+
+    packed: torch.Tensor  # uint8 [packed_bytes], 256-byte aligned
+    scale: torch.Tensor   # float32 [N]
+    K: int
+    N: int
+
+    @property
+    def device(self) -> torch.device:
+        return self.packed.device
+
+    @classmethod
+    def from_int8(cls, q, scale, device="cuda", stream=None) -> "PackedWeight":
+        """Pre-pack int8 [K,N] (row-major, the reference's W layout) on the device."""
+        q = torch.as_tensor(q)
+        if q.dtype != torch.int8 or q.dim() != 2:
+            raise ValueError("q must be int8 [K, N]")
+        K, N = q.shape
+        device = torch.device(device)
+        q_dev = q.to(device).contiguous()
+        scale = torch.as_tensor(scale, dtype=torch.float32).to(device).contiguous()
+        if scale.numel() != N:
+            raise ValueError("scale must be per-column [N]")
+        nbytes = packed_bytes(K, N)
+        packed = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        with torch.cuda.device(device):
+            check(lib().mtrtq_prepack(q_dev.data_ptr(), K, N, packed.data_ptr(), nbytes,
+                                      _stream_ptr(stream)), "mtrtq_prepack")
+        return cls(packed, scale, K, N)
+
+    @classmethod
+    def from_float(cls, W, device="cuda", zero_columns: str = "reject") -> "PackedWeight":
+        """Quantize on the host with the reference rule, then pre-pack on the device."""
+        q, s = quantize_per_channel(W, zero_columns)
+        return cls.from_int8(torch.from_numpy(q), torch.from_numpy(s), device)
+
+
+class Workspace:
+    """Zero-filled device scratch grown on demand (only when a call needs more)."""
+
+    def __init__(self, device="cuda"):
+        self.device = torch.device(device)
+        self.buf: torch.Tensor | None = None
+
+    def get(self, nbytes: int) -> torch.Tensor | None:
+        if nbytes <= 0:
+            return None
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+_workspaces: dict = {}
+
+
+def default_workspace(device) -> Workspace:
+    device = torch.device(device)
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    if key not in _workspaces:
+        _workspaces[key] = Workspace(torch.device(device.type, key[1]))
+    return _workspaces[key]
+
+
+def workspace_bytes(M: int, K: int, N: int, x_dtype: torch.dtype, mode: str) -> int:
+    xd = _lib.DTYPE_BF16 if x_dtype == torch.bfloat16 else _lib.DTYPE_F32
+    n = lib().mtrtq_workspace_bytes(M, K, N, xd, MODES[mode])
+    if n < 0:
+        raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_workspace_bytes", _lib.last_error())
+    return n
+
+
+def plan_info(M: int, K: int, N: int, x_dtype=torch.float32, mode: str = "bf16") -> dict:
+    xd = _lib.DTYPE_BF16 if x_dtype == torch.bfloat16 else _lib.DTYPE_F32
+    info = (ctypes.c_int64 * 6)()
+    check(lib().mtrtq_plan_info(M, K, N, xd, MODES[mode], info, 6), "mtrtq_plan_info")
+    return {"path": "gemm_tc" if info[0] == 1 else "gemv", "tile_m": info[1], "m_tiles": info[2],
+            "n_tiles": info[3], "splits": info[4], "k_per_split": info[5]}
+
+
+def matmul_q8(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None = None,
+              out: torch.Tensor | None = None, mode: str = "bf16",
+              workspace: Workspace | torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """out[M,N] = x[M,K] @ dequant(w) (+ bias): the reference MatMulQ (+ Add) on the GPU.
+
+    x: float32 or bfloat16 CUDA tensor [M, K] (row stride may exceed K).
+    mode: "bf16" (x rounded to bf16, tensor cores for M > 8) or "fp32" (CUDA cores).
+    """
+    if x.dim() != 2 or x.shape[1] != w.K:
+        raise ValueError(f"x must be [M, {w.K}], got {tuple(x.shape)}")
+    if x.stride(1) != 1:
+        raise ValueError("x must have unit stride along K")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("x must be float32 or bfloat16")
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, w.N), dtype=torch.float32, device=x.device)
+    if out.dtype != torch.float32 or out.shape != (M, w.N) or out.stride(1) != 1:
+        raise ValueError("out must be float32 [M, N] with unit stride along N")
+    xd = _lib.DTYPE_BF16 if x.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    need = lib().mtrtq_workspace_bytes(M, w.K, w.N, xd, MODES[mode])
+    if need < 0:
+        raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_workspace_bytes", _lib.last_error())
+    if isinstance(workspace, torch.Tensor):
+        ws = workspace
+    else:
+        ws = (workspace or default_workspace(x.device)).get(need)
+    ws_ptr = ws.data_ptr() if ws is not None else None
+    ws_bytes = ws.numel() * ws.element_size() if ws is not None else 0
+    with torch.cuda.device(x.device):
+        check(lib().mtrtq_matmul(x.data_ptr(), xd, x.stride(0), w.packed.data_ptr(),
+                                 w.scale.data_ptr(), _ptr(bias), out.data_ptr(), out.stride(0),
+                                 M, w.K, w.N, MODES[mode], ws_ptr, ws_bytes, _stream_ptr(stream)),
+              "mtrtq_matmul")
+    return out
+
+
+def set_option(option: int, value: int) -> None:
+    check(lib().mtrtq_set_option(option, value), "mtrtq_set_option")
+
+
+def read_device_status() -> int:
+    v = ctypes.c_int(0)
+    check(lib().mtrtq_read_status(ctypes.byref(v)), "mtrtq_read_status")
+    return v.value

@@ -1,0 +1,47 @@
+#!/usr/bin/env bash
+# Builds the oracle's two shared libraries. Test infrastructure only.
+#
+#   oracle/liboracle.so        the C restatement (matmulq_oracle.c), always built
+#   oracle/_ref/libmtrt_ref.so the reference's own MatMulQ path, compiled from its
+#                              unmodified sources where they lie, plus ref_shim.cpp
+#
+# The reference's CMake build needs network (FetchContent of gtest/nlohmann), so the
+# few sources on the MatMulQ path are compiled directly with g++. The JSON/ONNX
+# frontends, graph passes and executors are not needed by the path and are left out.
+# Release flags (-DNDEBUG) as the reference's own benchmarks use; -ffp-contract=off
+# keeps multiply and add separate in both libraries so they agree bit for bit.
+#
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+set -euo pipefail
+HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+REF="${1:-/root/reference}"
+CFLAGS="-O3 -fPIC -ffp-contract=off -fno-fast-math"
+
+gcc ${CFLAGS} -std=c11 -shared -o "${HERE}/liboracle.so" "${HERE}/matmulq_oracle.c" -lm
+
+if [[ ! -f "${REF}/src/ops/kernels_matmul.cpp" ]]; then
+  echo "build_ref: reference sources not found under ${REF}; keeping any prebuilt _ref" >&2
+  exit 0
+fi
+
+mkdir -p "${HERE}/_ref"
+SRCS=(
+  src/tensor/tensor.cpp
+  src/ops/registry.cpp
+  src/ops/kernels_matmul.cpp
+  src/ops/kernels_elementwise.cpp
+  src/ops/kernels_activation.cpp
+  src/ops/kernels_fused.cpp
+  src/ops/kernels_transformer.cpp
+  src/ops/kernels_gpt.cpp
+  src/graph/graph.cpp
+  src/optimizer/fusion.cpp
+  backends/cpu/gemm.cpp
+  backends/cpu/thread_pool.cpp
+)
+ABS=()
+for s in "${SRCS[@]}"; do ABS+=("${REF}/${s}"); done
+g++ -std=c++17 ${CFLAGS} -DNDEBUG -shared -pthread \
+  -I "${REF}/include" -I "${REF}" -I "${REF}/src" -I "${REF}/src/ops" \
+  -o "${HERE}/_ref/libmtrt_ref.so" "${HERE}/ref_shim.cpp" "${ABS[@]}"
+echo "build_ref: built ${HERE}/liboracle.so and ${HERE}/_ref/libmtrt_ref.so"

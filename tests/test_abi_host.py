@@ -1,0 +1,154 @@
+"""The C ABI without a GPU: the library loads, exports every declared symbol, validates
+its arguments, and its host functions (quantizer, pre-pack layout, planner) are right.
+No compute call reaches a device here."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from mini_tensorrt_b200 import _lib, matmulq, workloads as wl
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+HEADER = os.path.join(ROOT, "include", "mtrtq.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mtrtq_\w+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    names = declared_functions()
+    assert len(names) >= 12
+    lib = _lib.lib()
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/mtrtq.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    exported = set(re.findall(r"\b(mtrtq_\w+)\b", out))
+    assert set(names) == exported, f"exports differ from the header: {exported ^ set(names)}"
+
+
+def test_version_and_status_strings():
+    lib = _lib.lib()
+    assert lib.mtrtq_version() == 100
+    for code in range(8):
+        assert _lib.status_string(code)
+    assert _lib.status_string(99) == "unknown status"
+
+
+def test_header_compiles_as_c_and_cxx(tmp_path):
+    src = tmp_path / "use.c"
+    src.write_text('#include "mtrtq.h"\nint main(void){return mtrtq_version() == 100 ? 0 : 1;}\n')
+    for compiler, name in (("gcc", "use.c"), ("g++", "use.cpp")):
+        f = tmp_path / name
+        f.write_text(src.read_text())
+        exe = tmp_path / f"use_{compiler}"
+        r = subprocess.run([compiler, "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(f),
+                            "-o", str(exe), _lib.LIB_PATH, f"-Wl,-rpath,{os.path.dirname(_lib.LIB_PATH)}"],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        assert subprocess.run([str(exe)]).returncode == 0
+
+
+@pytest.mark.parametrize("K,N", [(1, 1), (3, 5), (48, 17), (768, 2304), (3072, 768), (100, 129)])
+def test_library_quantizer_bit_exact_with_oracle(K, N):
+    W = wl.weights(K, N, K * 7 + N)
+    q, s = matmulq.quantize_per_channel(W)
+    q2, s2 = oracle.quantize_per_channel(W)
+    assert np.array_equal(q, q2)
+    assert np.array_equal(s.view(np.uint32), s2.view(np.uint32))
+
+
+def test_library_quantizer_zero_column_policies():
+    W = np.zeros((4, 3), np.float32)
+    W[:, 1] = [1, -2, 3, -4]
+    with pytest.raises(_lib.MtrtqError) as e:
+        matmulq.quantize_per_channel(W, "reject")
+    assert e.value.status == _lib.ERR_ZERO_SCALE and "column 0" in str(e.value)
+    q, s = matmulq.quantize_per_channel(W, "zero")
+    q2, s2 = oracle.quantize_per_channel(W)
+    assert np.array_equal(q, q2) and np.array_equal(s, s2)
+
+
+def reference_layout(q: np.ndarray) -> np.ndarray:
+    """Packed layout restated in numpy: [tile][slab][row in tile][16 k]."""
+    K, N = q.shape
+    n_pad = -(-N // 128) * 128
+    k_pad = -(-K // 64) * 64
+    full = np.zeros((k_pad, n_pad), np.int8)
+    full[:K, :N] = q
+    t = full.reshape(k_pad // 16, 16, n_pad // 128, 128)  # [slab][b][tile][row]
+    return np.ascontiguousarray(t.transpose(2, 0, 3, 1)).view(np.uint8).ravel()
+
+
+@pytest.mark.parametrize("K,N", [(1, 1), (16, 128), (48, 17), (100, 300), (768, 2304), (768, 50257)])
+def test_prepack_host_layout(K, N):
+    q = np.random.default_rng(K + N).integers(-127, 128, size=(K, N), dtype=np.int8)
+    p = matmulq.prepack_host(q)
+    assert p.size == matmulq.packed_bytes(K, N)
+    assert np.array_equal(p, reference_layout(q))
+
+
+def test_invalid_arguments_are_rejected_without_a_device():
+    lib = _lib.lib()
+    assert lib.mtrtq_packed_bytes(0, 5) == -1 and lib.mtrtq_packed_bytes(5, -1) == -1
+    assert lib.mtrtq_quantize_per_channel(None, 2, 2, None, None, 0) == _lib.ERR_INVALID_ARG
+    buf = (ctypes.c_uint8 * 16)()
+    assert lib.mtrtq_prepack_host(buf, 64, 128, buf, 16) == _lib.ERR_INVALID_ARG  # too small
+    assert "packed buffer" in _lib.last_error()
+    assert lib.mtrtq_workspace_bytes(1, 64, 64, 7, 0) == -1                       # bad dtype
+    assert lib.mtrtq_workspace_bytes(1, 64, 64, _lib.DTYPE_BF16, _lib.MODE_FP32) == -1
+    assert lib.mtrtq_workspace_bytes(0, 64, 64, 0, 0) == -1
+    assert lib.mtrtq_workspace_bytes(1, 1 << 31, 64, 0, 0) == -1
+    assert lib.mtrtq_set_option(99, 0) == _lib.ERR_INVALID_ARG
+    assert lib.mtrtq_set_option(_lib.OPT_FORCE_PATH, 5) == _lib.ERR_INVALID_ARG
+    assert lib.mtrtq_matmul(None, 0, 64, None, None, None, None, 64, 1, 64, 64, 0, None, 0,
+                            None) == _lib.ERR_INVALID_ARG
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device status")
+def test_launch_without_device_fails_loudly():
+    lib = _lib.lib()
+    x = (ctypes.c_float * 64)()
+    rc = lib.mtrtq_matmul(x, 0, 64, x, x, None, x, 64, 1, 64, 64, 0, None, 0, None)
+    assert rc == _lib.ERR_NO_DEVICE
+    assert lib.mtrtq_prepack(x, 64, 64, x, 1 << 20, None) in (_lib.ERR_NO_DEVICE, _lib.ERR_ALIGNMENT)
+
+
+@pytest.mark.parametrize("M,K,N,mode,path", [
+    (1, 768, 50257, "bf16", "gemv"), (8, 768, 768, "fp32", "gemv"), (8, 3072, 768, "bf16", "gemv"),
+    (9, 768, 768, "bf16", "gemm_tc"), (64, 768, 3072, "bf16", "gemm_tc"),
+    (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv"),
+])
+def test_planner(M, K, N, mode, path):
+    info = matmulq.plan_info(M, K, N, torch.float32, mode)
+    assert info["path"] == path
+    assert info["n_tiles"] == -(-N // 128)
+    # every split has work, and the splits cover K
+    unit = 16 if path == "gemv" else 64
+    k_pad = -(-K // 64) * 64
+    assert (info["splits"] - 1) * info["k_per_split"] < k_pad <= info["splits"] * info["k_per_split"]
+    ws = matmulq.workspace_bytes(M, K, N, torch.float32, mode)
+    if info["splits"] > 1:
+        assert ws >= info["splits"] * M * (-(-N // 128) * 128) * 4
+    assert ws % 256 == 0 and ws >= 0
+
+
+def test_forced_paths_change_the_plan():
+    try:
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 2)
+        assert matmulq.plan_info(4, 768, 768)["path"] == "gemm_tc"
+        with pytest.raises(_lib.MtrtqError):
+            matmulq.plan_info(4, 768, 768, mode="fp32")
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 1)
+        assert matmulq.plan_info(64, 768, 768)["path"] == "gemv"
+    finally:
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
