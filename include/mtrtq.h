@@ -21,8 +21,9 @@
  *    CUDA include and binds from any FFI.
  *  - Launch calls never allocate: scratch lives in a caller workspace sized by
  *    mtrtq_workspace_bytes(). The workspace must be zero-filled once after it is
- *    allocated; every call leaves it zero-filled again where that matters (split
- *    counters). Calls that share a workspace must be ordered (same stream).
+ *    allocated: its first 4 KiB hold split-K ticket counters, which every call
+ *    leaves at zero again; the rest is per-call scratch. One workspace may serve
+ *    calls of any shapes, but calls that share it must be ordered (same stream).
  *  - Matrices are row-major and contiguous unless a leading dimension is given.
  *  - No CPU fallback: without an sm_100 device the launch calls fail with
  *    MTRTQ_ERR_NO_DEVICE.

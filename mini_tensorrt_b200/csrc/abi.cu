@@ -83,6 +83,8 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 constexpr int64_t kMaxDim = int64_t(1) << 30;
+constexpr size_t kCounterBytes = 4096;                       // fixed ticket region
+constexpr int64_t kMaxSplitTiles = kCounterBytes / sizeof(unsigned);
 
 int check_dims(int64_t M, int64_t K, int64_t N) {
   if (M <= 0 || K <= 0 || N <= 0)
@@ -132,13 +134,17 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
     int64_t splits = base < target ? ceil_div64(target, base) : 1;
     const int64_t max_by_len = p.kunits >= 4 ? p.kunits / 2 : 1;  // >= 2 slabs per split
     if (splits > max_by_len) splits = max_by_len;
-    int64_t sps = ceil_div64(p.kunits, splits);
-    const int mt = (int)(M < 8 ? M : 8);
-    const int64_t sps_cap = (48 * 1024) / (kSlabK * 4 * mt);  // staged activations <= 48 KiB
-    if (sps > sps_cap) sps = sps_cap;
+    if (splits > 65535) splits = 65535;
+    const int64_t sps = ceil_div64(p.kunits, splits);
     p.kunits_per_split = (int)sps;
     p.splits = (int)ceil_div64(p.kunits, sps);
-    if (p.splits > 65535) return fail(MTRTQ_ERR_INVALID_ARG, "K too large for the GEMV path");
+    // Activations are staged in shared memory a chunk at a time: <= 32 KiB,
+    // a multiple of the load unroll.
+    const int mt = (int)(M < 8 ? M : 8);
+    int64_t chunk = (32 * 1024) / (kSlabK * 4 * mt);
+    chunk = chunk / kGemvUnroll * kGemvUnroll;
+    const int64_t sps_r = round_up64(sps, kGemvUnroll);
+    p.chunk_units = (int)(chunk < sps_r ? chunk : sps_r);
   } else {
     p.kind = Plan::kGemmTC;
     int tm = 256;
@@ -163,9 +169,17 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
     p.ldxb = round_up64(K, 8);
   }
 
+  // Split-K tickets live in a fixed region at the start of every workspace (each
+  // call leaves its counters at zero). Its size is fixed so that the scratch of
+  // one call (partials) never overlaps the counters of another call that shares
+  // the workspace; a plan whose tiles do not fit runs unsplit.
+  if (p.splits > 1 && (int64_t)p.n_tiles * p.m_tiles > kMaxSplitTiles) {
+    p.splits = 1;
+    p.kunits_per_split = p.kunits;
+  }
   size_t off = 0;
   p.off_counters = off;
-  off += round256((size_t)p.n_tiles * p.m_tiles * sizeof(unsigned));
+  off += kCounterBytes;
   p.off_partials = off;
   if (p.splits > 1) off += round256((size_t)p.splits * (size_t)M * (size_t)p.n_pad * sizeof(float));
   p.off_xb = off;

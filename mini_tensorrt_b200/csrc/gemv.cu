@@ -36,6 +36,7 @@ struct GemvParams {
   int n_pad;
   int KS;               // slabs of 16 in K_pad
   int slabs_per_split;
+  int chunk_slabs;      // slabs of activations staged in shared memory at a time (% 8 == 0)
   int splits;
   int n_tiles;
   float* partials;      // [splits][M][n_pad]
@@ -74,8 +75,8 @@ __global__ void __launch_bounds__(128) gemv_q8_kernel(const GemvParams p) {
   const int s0 = split * p.slabs_per_split;
   const int s1 = min(s0 + p.slabs_per_split, p.KS);
   const int nsl = s1 - s0;
-  const int klen = p.slabs_per_split * kSlabK;
-  const int64_t k0 = (int64_t)s0 * kSlabK;
+  const int CH = p.chunk_slabs;   // multiple of U
+  const int klen = CH * kSlabK;   // staged activations per row
   const int m0 = mc * 8;
   const int mrem = min(MT, p.M - m0);
 
@@ -86,38 +87,47 @@ __global__ void __launch_bounds__(128) gemv_q8_kernel(const GemvParams p) {
   for (int u = 0; u < U; ++u)
     if (u < nsl) buf[u] = ldg_stream_v4(wp + (int64_t)u * kTileN);
 
-  // Stage this split's activations [MT][klen] as fp32 (zero beyond K and M).
-#pragma unroll
-  for (int m = 0; m < MT; ++m) {
-    for (int kk = tid; kk < klen; kk += 128) {
-      const int64_t k = k0 + kk;
-      float v = 0.0f;
-      if (m < mrem && k < p.K) {
-        if (X_BF16) {
-          v = __bfloat162float(static_cast<const __nv_bfloat16*>(p.X)[(int64_t)(m0 + m) * p.ldx + k]);
-        } else {
-          v = static_cast<const float*>(p.X)[(int64_t)(m0 + m) * p.ldx + k];
-          if (ROUND) v = round_bf16(v);
-        }
-      }
-      xs[m * klen + kk] = v;
-    }
-  }
-  __syncthreads();
-
   float2 acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = make_float2(0.0f, 0.0f);
 
+  int in_chunk = CH;  // slabs consumed from the staged chunk
   for (int s = 0; s < nsl; s += U) {
+    if (in_chunk == CH) {
+      // Stage activations for slabs [s0+s, s0+s+CH) as fp32 [MT][klen] (zero
+      // beyond K and M); the weight loads already in flight keep streaming.
+      if (s > 0) __syncthreads();
+      const int64_t k0 = (int64_t)(s0 + s) * kSlabK;
+      const int kn = min(CH, nsl - s) * kSlabK;
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        for (int kk = tid; kk < kn; kk += 128) {
+          const int64_t k = k0 + kk;
+          float v = 0.0f;
+          if (m < mrem && k < p.K) {
+            if (X_BF16) {
+              v = __bfloat162float(
+                  static_cast<const __nv_bfloat16*>(p.X)[(int64_t)(m0 + m) * p.ldx + k]);
+            } else {
+              v = static_cast<const float*>(p.X)[(int64_t)(m0 + m) * p.ldx + k];
+              if (ROUND) v = round_bf16(v);
+            }
+          }
+          xs[m * klen + kk] = v;
+        }
+      }
+      __syncthreads();
+      in_chunk = 0;
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (s + u < nsl) {
         const uint4 w = buf[u];
         if (s + u + U < nsl) buf[u] = ldg_stream_v4(wp + (int64_t)(s + u + U) * kTileN);
-        dot_slab<MT>(w, xs + (s + u) * kSlabK, klen, acc);
+        dot_slab<MT>(w, xs + (in_chunk + u) * kSlabK, klen, acc);
       }
     }
+    in_chunk += U;
   }
 
   const int n = nt * kTileN + tid;
@@ -170,14 +180,14 @@ __global__ void __launch_bounds__(128) gemv_q8_kernel(const GemvParams p) {
 
 template <int MT, bool X_BF16, bool ROUND>
 static cudaError_t launch_mt(const GemvParams& gp, dim3 grid, size_t smem, cudaStream_t st) {
-  constexpr int U = MT <= 2 ? 8 : 4;
+  constexpr int U = kGemvUnroll;
   gemv_q8_kernel<MT, X_BF16, ROUND, U><<<grid, 128, smem, st>>>(gp);
   return cudaGetLastError();
 }
 
 template <bool X_BF16, bool ROUND>
 static cudaError_t launch_by_mt(int mt, const GemvParams& gp, dim3 grid, cudaStream_t st) {
-  const size_t smem = (size_t)mt * gp.slabs_per_split * kSlabK * sizeof(float);
+  const size_t smem = (size_t)mt * gp.chunk_slabs * kSlabK * sizeof(float);
   switch (mt) {
     case 1: return launch_mt<1, X_BF16, ROUND>(gp, grid, smem, st);
     case 2: return launch_mt<2, X_BF16, ROUND>(gp, grid, smem, st);
@@ -207,6 +217,7 @@ cudaError_t launch_gemv(const Plan& p, const void* X, int x_dtype, int64_t ldx, 
   gp.n_pad = (int)p.n_pad;
   gp.KS = p.kunits;
   gp.slabs_per_split = p.kunits_per_split;
+  gp.chunk_slabs = p.chunk_units;
   gp.splits = p.splits;
   gp.n_tiles = p.n_tiles;
   char* ws = static_cast<char*>(workspace);

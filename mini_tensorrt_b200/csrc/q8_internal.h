@@ -21,12 +21,17 @@ struct Plan {
   int splits = 1;                  // k splits
   int kunits = 0;                  // k units (GEMV: slabs of 16; GEMM: blocks of 64)
   int kunits_per_split = 0;
+  int chunk_units = 0;             // GEMV: slabs of activations staged at a time
   bool x_to_bf16 = false;          // GEMM: X is staged as a bf16 copy in the workspace
   bool round_x = false;            // GEMV: round fp32 X to bf16 before the product
   // workspace layout (byte offsets)
   size_t off_counters = 0, off_partials = 0, off_xb = 0, total = 0;
   int64_t ldxb = 0;                // row stride (elements) of the bf16 X copy
 };
+
+// GEMV weight loads in flight per thread (16-byte slabs); the activation
+// staging chunk is a multiple of it.
+constexpr int kGemvUnroll = 8;
 
 struct DeviceInfo {
   int device = -1;

@@ -31,7 +31,8 @@ def run(X, q, s, mode, bias=None, x_dtype=torch.float32, dev="cuda"):
     pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), dev)
     xt = torch.from_numpy(X).to(dev).to(x_dtype)
     bt = torch.from_numpy(bias).to(dev) if bias is not None else None
-    y = matmul_q8(xt, pw, bias=bt, mode=mode)
+    y = torch.full((X.shape[0], q.shape[1]), float("nan"), device=dev)
+    matmul_q8(xt, pw, bias=bt, out=y, mode=mode)
     torch.cuda.synchronize()
     assert matmulq.read_device_status() == 0
     return y.cpu().numpy()
@@ -150,11 +151,11 @@ def test_strided_input_and_output(cuda_device):
         xbig[:, :K] = torch.from_numpy(X).to(cuda_device)
         ybig = torch.full((M, N + 20), 7.0, device=cuda_device)
         lib = _lib.lib()
+        ws = torch.zeros(max(256, matmulq.workspace_bytes(M, K, N, torch.float32, mode)),
+                         dtype=torch.uint8, device=cuda_device)
         rc = lib.mtrtq_matmul(xbig.data_ptr(), 0, K + 56, pw.packed.data_ptr(), pw.scale.data_ptr(),
                               None, ybig.data_ptr(), N + 20, M, K, N, matmulq.MODES[mode],
-                              matmulq.default_workspace(cuda_device).get(
-                                  matmulq.workspace_bytes(M, K, N, torch.float32, mode)).data_ptr(),
-                              1 << 30, None)
+                              ws.data_ptr(), ws.numel(), None)
         assert rc == 0, _lib.last_error()
         torch.cuda.synchronize()
         yb = ybig.cpu().numpy()
@@ -215,3 +216,31 @@ def test_argument_errors_on_device(cuda_device):
         rc = lib.mtrtq_matmul(x.data_ptr(), 0, 64, pw.packed.data_ptr(), pw.scale.data_ptr(), None,
                               y.data_ptr(), 64, 4, 64, 64, 0, None, 0, None)
         assert rc == _lib.ERR_WORKSPACE
+
+
+def test_one_workspace_serves_every_shape(cuda_device):
+    """Calls of different shapes share one workspace: split-K tickets of a call
+    with many channel tiles must not meet another call's leftover partials."""
+    ws = matmulq.Workspace(cuda_device)
+    seq = [(8, 768, 768), (1, 768, 50257), (64, 768, 3072), (1, 4096, 11008), (16, 4096, 11008),
+           (8, 3072, 768), (1, 768, 50257), (300, 200, 129), (2, 768, 50257)]
+    for i, (M, K, N) in enumerate(seq):
+        W = wl.weights(K, N, 100 + i)
+        q, s = matmulq.quantize_per_channel(W)
+        X = wl.activations(M, K, 200 + i)
+        pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+        for mode in ("fp32", "bf16"):
+            y = torch.full((M, N), float("nan"), device=cuda_device)
+            matmul_q8(torch.from_numpy(X).to(cuda_device), pw, out=y, mode=mode, workspace=ws)
+            check(y.cpu().numpy(), X, q, s, mode, tc=(mode == "bf16" and M > 8))
+
+
+@pytest.mark.parametrize("M", [3, 8, 24])
+def test_gemv_restages_activations_in_chunks(cuda_device, M):
+    # fp32 mode, K = 14336: each CTA's k range spans several staged chunks.
+    K, N = 14336, 512
+    W = wl.weights(K, N, 31)
+    q, s = matmulq.quantize_per_channel(W)
+    X = wl.activations(M, K, 32)
+    Y = run(X, q, s, "fp32")
+    check(Y, X, q, s, "fp32")
