@@ -57,6 +57,10 @@ def parse():
     ap.add_argument("--mode", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--workload", default="decode_set",
+                    help="decode_set (default) or shape:M,K,N (one MatMulQ shape timed alone)")
+    ap.add_argument("--x-dtype", choices=["f32", "bf16"], default="f32",
+                    help="activation type for --workload shape:M,K,N")
     return ap.parse_args()
 
 
@@ -367,6 +371,46 @@ def run_extras(torch, dev, args, stream):
     return out
 
 
+def run_shape(args, torch, dev):
+    """One MatMulQ shape timed alone: weights rotated over enough copies to exceed
+    2x L2, direct launches (no graph) so a profiler sees plain kernel launches."""
+    from mini_tensorrt_b200 import matmulq, workloads as wl
+    hbm_peak, tc_peak, _, peak_kind = peaks()
+    M, K, N = (int(v) for v in args.workload.split(":", 1)[1].split(","))
+    W = wl.weights(K, N, wl.shape_seed("shape", K, N))
+    q, s = matmulq.quantize_per_channel(W)
+    base = matmulq.PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), dev)
+    n_copies = max(2, -(-(260 << 20) // (K * N)))
+    copies = [base] + [matmulq.PackedWeight(base.packed.clone(), base.scale, K, N)
+                       for _ in range(n_copies - 1)]
+    xdt = torch.bfloat16 if args.x_dtype == "bf16" else torch.float32
+    x = torch.randn(M, K, device=dev, generator=torch.Generator(dev).manual_seed(1)).to(xdt)
+    y = torch.empty(M, N, device=dev)
+    ws = torch.zeros(max(matmulq.workspace_bytes(M, K, N, xdt, args.mode), 256), dtype=torch.uint8,
+                     device=dev)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            matmulq.matmul_q8(x, copies[i % n_copies], out=y, mode=args.mode, workspace=ws, stream=stream)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            matmulq.matmul_q8(x, copies[i % n_copies], out=y, mode=args.mode, workspace=ws, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    secs = e0.elapsed_time(e1) / 1e3 / args.steps
+    byts = wl.algorithmic_bytes(M, K, N, 2 if xdt == torch.bfloat16 else 4)
+    return {"workload": args.workload, "x_dtype": args.x_dtype, "mode": args.mode,
+            "us_per_call": round(secs * 1e6, 3), "gbs": round(byts / secs / 1e9, 1),
+            "hbm_frac": round(byts / secs / 1e9 / hbm_peak, 4),
+            "tflops": round(wl.flops(M, K, N) / secs / 1e12, 2),
+            "tc_frac": round(wl.flops(M, K, N) / secs / 1e12 / tc_peak, 4),
+            "peak_kind": peak_kind, "weight_copies": n_copies,
+            "plan": matmulq.plan_info(M, K, N, xdt, args.mode)}
+
+
 # ---------------------------------------------------------------------- CPU legs
 
 
@@ -496,6 +540,9 @@ def main():
     torch.cuda.set_device(dev)
     from mini_tensorrt_b200 import build as _b
     _b.build()
+    if args.workload.startswith("shape:"):
+        print(json.dumps(run_shape(args, torch, dev)))
+        return
     line, calls, stream = run_ours(args, torch, rank, world, dev, dist)
     del calls
     torch.cuda.empty_cache()

@@ -268,15 +268,33 @@ __global__ void __launch_bounds__(192, 1)
       if (*s_ticket == (unsigned)(p.splits - 1)) {
         __threadfence();
         if (n_ok) {
-          const int mend = min(m0 + TM, p.M);
-          for (int m = m0; m < mend; ++m) {
-            const float* src = p.partials + (int64_t)m * p.n_pad + n;
-            float sum = 0.0f;
-            for (int sp = 0; sp < p.splits; ++sp)
-              sum += __ldcg(src + (int64_t)sp * p.M * p.n_pad);
-            float y = __fmul_rn(sum, sc);
-            if (p.bias) y = __fadd_rn(y, b);
-            p.Y[(int64_t)m * p.ldy + n] = y;
+          // 8 tokens at a time: their loads (rows clamped to M-1, so always in
+          // bounds) for one split are independent and issued together; each output
+          // still sums splits 0, 1, 2, ... in order.
+          const int64_t split_stride = (int64_t)p.M * p.n_pad;
+          const float* base = p.partials + n;
+          for (int c0 = 0; c0 < TM && m0 + c0 < p.M; c0 += 8) {
+            int64_t off[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) off[j] = (int64_t)min(m0 + c0 + j, p.M - 1) * p.n_pad;
+            float sum[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sum[j] = 0.0f;
+            const float* src = base;
+#pragma unroll 2
+            for (int sp = 0; sp < p.splits; ++sp, src += split_stride) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) sum[j] += __ldcg(src + off[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int m = m0 + c0 + j;
+              if (m < p.M) {
+                float y = __fmul_rn(sum[j], sc);
+                if (p.bias) y = __fadd_rn(y, b);
+                p.Y[(int64_t)m * p.ldy + n] = y;
+              }
+            }
           }
         }
         if (warp == 2 && lane == 0) *counter = 0u;

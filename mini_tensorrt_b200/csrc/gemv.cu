@@ -166,13 +166,26 @@ __global__ void __launch_bounds__(128) gemv_q8_kernel(const GemvParams p) {
   if (n < p.N) {
     const float sc = p.scale[n];
     const float b = p.bias ? p.bias[n] : 0.0f;
-    for (int m = 0; m < mrem; ++m) {
-      const float* src = p.partials + (int64_t)(m0 + m) * p.n_pad + n;
-      float sum = 0.0f;
-      for (int sp = 0; sp < p.splits; ++sp) sum += __ldcg(src + (int64_t)sp * p.M * p.n_pad);
-      float y = __fmul_rn(sum, sc);
-      if (p.bias) y = __fadd_rn(y, b);
-      p.Y[(int64_t)(m0 + m) * p.ldy + n] = y;
+    // All rows' loads of one split are independent and issued together; the
+    // sum still runs split 0, 1, 2, ... for every output.
+    const float* src = p.partials + (int64_t)m0 * p.n_pad + n;
+    const int64_t split_stride = (int64_t)p.M * p.n_pad;
+    float sum[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) sum[m] = 0.0f;
+#pragma unroll 4
+    for (int sp = 0; sp < p.splits; ++sp) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+        if (m < mrem) sum[m] += __ldcg(src + sp * split_stride + (int64_t)m * p.n_pad);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m < mrem) {
+        float y = __fmul_rn(sum[m], sc);
+        if (p.bias) y = __fadd_rn(y, b);
+        p.Y[(int64_t)(m0 + m) * p.ldy + n] = y;
+      }
     }
   }
   if (tid == 0) *counter = 0u;

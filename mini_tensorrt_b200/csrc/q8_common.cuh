@@ -29,20 +29,11 @@ __device__ __forceinline__ float i8_lane_to_f32(uint32_t biased_word, uint32_t s
 // 4 int8 (one 32-bit word) -> 4 exact floats, as two float2 pairs (k, k+1), (k+2, k+3).
 __device__ __forceinline__ void i8x4_to_f32x4(uint32_t w, float2& lo, float2& hi) {
   const uint32_t u = w ^ 0x80808080u;
-  float2 a = make_float2(i8_lane_to_f32(u, 0x7540), i8_lane_to_f32(u, 0x7541));
-  float2 b = make_float2(i8_lane_to_f32(u, 0x7542), i8_lane_to_f32(u, 0x7543));
+  const float2 a = make_float2(i8_lane_to_f32(u, 0x7540), i8_lane_to_f32(u, 0x7541));
+  const float2 b = make_float2(i8_lane_to_f32(u, 0x7542), i8_lane_to_f32(u, 0x7543));
   const float2 bias = make_float2(-8388736.0f, -8388736.0f);
-  uint64_t ra, rb;
-  asm("{\n\t.reg .b64 x, y;\n\t"
-      "mov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
-      "add.rn.f32x2 %0, x, y;\n\t}"
-      : "=l"(ra) : "f"(a.x), "f"(a.y), "f"(bias.x), "f"(bias.y));
-  asm("{\n\t.reg .b64 x, y;\n\t"
-      "mov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
-      "add.rn.f32x2 %0, x, y;\n\t}"
-      : "=l"(rb) : "f"(b.x), "f"(b.y), "f"(bias.x), "f"(bias.y));
-  lo = make_float2(__uint_as_float((uint32_t)ra), __uint_as_float((uint32_t)(ra >> 32)));
-  hi = make_float2(__uint_as_float((uint32_t)rb), __uint_as_float((uint32_t)(rb >> 32)));
+  lo = __fadd2_rn(a, bias);  // packed fp32x2 add (sm_100)
+  hi = __fadd2_rn(b, bias);
 }
 
 // Two exact small-integer floats -> one bf16x2 word (element 0 in the low half).
@@ -58,16 +49,8 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& p0, uint32_
   p1 = pack_bf16x2_exact(hi.x, hi.y);
 }
 
-// d = a * b + c on both lanes (IEEE fp32 fma per lane).
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  uint64_t r;
-  asm("{\n\t.reg .b64 x, y, z;\n\t"
-      "mov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\tmov.b64 z, {%5, %6};\n\t"
-      "fma.rn.f32x2 %0, x, y, z;\n\t}"
-      : "=l"(r)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
-}
+// d = a * b + c on both lanes (IEEE fp32 fma per lane, packed fp32x2 on sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // fp32 -> bf16 (round to nearest even) -> fp32.
 __device__ __forceinline__ float round_bf16(float x) {
