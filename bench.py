@@ -372,8 +372,8 @@ def run_extras(torch, dev, args, stream):
 
 
 def run_shape(args, torch, dev):
-    """One MatMulQ shape timed alone: weights rotated over enough copies to exceed
-    2x L2, direct launches (no graph) so a profiler sees plain kernel launches."""
+    """One MatMulQ shape timed alone: one CUDA graph of back-to-back launches over
+    enough weight copies to exceed 2x L2, replayed --steps times."""
     from mini_tensorrt_b200 import matmulq, workloads as wl
     hbm_peak, tc_peak, _, peak_kind = peaks()
     M, K, N = (int(v) for v in args.workload.split(":", 1)[1].split(","))
@@ -390,17 +390,13 @@ def run_shape(args, torch, dev):
                      device=dev)
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            matmulq.matmul_q8(x, copies[i % n_copies], out=y, mode=args.mode, workspace=ws, stream=stream)
+        matmulq.matmul_q8(x, copies[0], out=y, mode=args.mode, workspace=ws, stream=stream)
         torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(args.steps):
-            matmulq.matmul_q8(x, copies[i % n_copies], out=y, mode=args.mode, workspace=ws, stream=stream)
-        e1.record(stream)
-        torch.cuda.synchronize()
-    secs = e0.elapsed_time(e1) / 1e3 / args.steps
+        graph = torch.cuda.CUDAGraph()   # one launch per weight copy, back to back
+        with torch.cuda.graph(graph, stream=stream):
+            for cpy in copies:
+                matmulq.matmul_q8(x, cpy, out=y, mode=args.mode, workspace=ws, stream=stream)
+    secs = time_graphs(torch, [graph], args.steps, args.warmup, stream) / (args.steps * n_copies)
     byts = wl.algorithmic_bytes(M, K, N, 2 if xdt == torch.bfloat16 else 4)
     return {"workload": args.workload, "x_dtype": args.x_dtype, "mode": args.mode,
             "us_per_call": round(secs * 1e6, 3), "gbs": round(byts / secs / 1e9, 1),

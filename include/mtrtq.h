@@ -59,8 +59,9 @@ enum { MTRTQ_DTYPE_F32 = 0, MTRTQ_DTYPE_BF16 = 1 };
 
 /* Arithmetic modes.
  *  MTRTQ_MODE_BF16: A is rounded to bf16 (round-to-nearest-even) once; the int8
- *    weights are exact in bf16; products accumulate in fp32. M <= 8 runs the decode
- *    GEMV on CUDA cores, M > 8 the tcgen05 tensor-core GEMM (TMEM accumulators).
+ *    weights are exact in bf16; products accumulate in fp32 on tcgen05 tensor cores
+ *    (TMEM accumulators): a stream-K kernel for M <= 64 (decode and small prefill),
+ *    a tiled GEMM above.
  *  MTRTQ_MODE_FP32: A stays fp32 and every product and sum is fp32 on CUDA cores,
  *    the reference's arithmetic up to summation order. */
 enum { MTRTQ_MODE_BF16 = 0, MTRTQ_MODE_FP32 = 1 };
@@ -136,15 +137,18 @@ enum {
   MTRTQ_OPT_GEMM_A_SOURCE = 1, /* 0 (default): dequantized weights staged in TMEM
                                   (tcgen05.mma A from tensor memory);
                                   1: staged in 128-byte-swizzled shared memory */
-  MTRTQ_OPT_FORCE_PATH = 2     /* 0 (default): GEMV for M <= 8 or MTRTQ_MODE_FP32,
-                                  tcgen05 GEMM otherwise; 1: always GEMV;
-                                  2: always GEMM (MTRTQ_MODE_BF16 only) */
+  MTRTQ_OPT_FORCE_PATH = 2     /* 0 (default): MTRTQ_MODE_FP32 -> CUDA-core GEMV;
+                                  MTRTQ_MODE_BF16 -> stream-K tcgen05 kernel for
+                                  M <= 64, tile tcgen05 GEMM above. 1: always the
+                                  CUDA-core GEMV; 2: always the tile GEMM; 3: always
+                                  the stream-K kernel (M <= 64). 2 and 3 need
+                                  MTRTQ_MODE_BF16. */
 };
 int mtrtq_set_option(int option, int64_t value);
 
-/* The plan mtrtq_matmul would use: info[0] path (0 GEMV, 1 GEMM), [1] token rows
- * per tile, [2] token tiles, [3] channel tiles, [4] k splits, [5] k per split.
- * n_info >= 6. */
+/* The plan mtrtq_matmul would use: info[0] path (0 CUDA-core GEMV, 1 tile GEMM,
+ * 2 stream-K kernel), [1] token rows per tile, [2] token tiles, [3] channel tiles,
+ * [4] k splits (stream-K: persistent CTAs), [5] k per split. n_info >= 6. */
 int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info,
                     int n_info);
 

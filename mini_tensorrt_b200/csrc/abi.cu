@@ -114,12 +114,38 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   p.k_pad = round_up64(K, kBlockK);
   p.n_tiles = (int)(p.n_pad / kTileN);
 
-  bool gemm = (mode == MTRTQ_MODE_BF16) && M > 8;
-  if (g_opt_force_path == 1) gemm = false;
-  if (g_opt_force_path == 2) {
-    if (mode != MTRTQ_MODE_BF16)
-      return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core GEMM computes in MTRTQ_MODE_BF16 only");
-    gemm = true;
+  // Path: fp32 mode -> CUDA-core GEMV; bf16 mode -> stream-K tensor-core kernel for
+  // M <= 64 (and at most kMaxSplitTiles channel tiles), tile GEMM above.
+  int path = 1;
+  if (mode == MTRTQ_MODE_BF16) path = (M <= 64 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
+  if (g_opt_force_path != 0) {
+    if (g_opt_force_path != 1 && mode != MTRTQ_MODE_BF16)
+      return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core kernels compute in MTRTQ_MODE_BF16 only");
+    if (g_opt_force_path == 3 && (M > 64 || p.n_tiles > kMaxSplitTiles))
+      return fail(MTRTQ_ERR_INVALID_ARG, "the stream-K kernel takes M <= 64 and N <= 131072");
+    path = g_opt_force_path;
+  }
+  const bool gemm = path == 2;
+
+  if (path == 3) {
+    p.kind = Plan::kSkinnyTC;
+    p.tile_m = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+    p.m_tiles = 1;
+    p.kunits = (int)(p.k_pad / kBlockK);
+    p.kunits_per_split = p.kunits;
+    const int64_t units = (int64_t)p.n_tiles * p.kunits;
+    p.grid = (int)(units < sm_count ? units : sm_count);
+    p.splits = 1;
+    p.ldxb = round_up64(K, 8);
+    size_t off = kCounterBytes;
+    p.off_counters = 0;
+    p.off_partials = off;
+    off += round256((size_t)p.grid * 2 * (size_t)M * kTileN * sizeof(float));
+    p.off_xb = off;  // bf16 copy of X, used only when X's layout does not suit TMA
+    off += round256((size_t)M * (size_t)p.ldxb * 2);
+    p.total = off;
+    *out = p;
+    return MTRTQ_OK;
   }
 
   if (!gemm) {
@@ -230,7 +256,7 @@ int mtrtq_set_option(int option, int64_t value) {
       g_opt_gemm_a_source = (int)value;
       return MTRTQ_OK;
     case MTRTQ_OPT_FORCE_PATH:
-      if (value < 0 || value > 2) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0, 1 or 2");
+      if (value < 0 || value > 3) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0, 1, 2 or 3");
       g_opt_force_path = (int)value;
       return MTRTQ_OK;
     default:
@@ -344,6 +370,31 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     return MTRTQ_OK;
   }
+  unsigned* status = nullptr;
+  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
+  if (e != cudaSuccess) return cuda_fail(e, "device status address");
+  if (p.kind == Plan::kSkinnyTC) {
+    // TMA reads X directly when its row stride is a multiple of 16 bytes; fp32 X
+    // is rounded to bf16 inside the kernel. Otherwise stage a bf16 copy first.
+    const int esz = x_dtype == MTRTQ_DTYPE_F32 ? 4 : 2;
+    const void* xsrc = X;
+    int64_t ldxs = ldx;
+    bool x_f32 = x_dtype == MTRTQ_DTYPE_F32;
+    if ((ldx * esz) % 16 != 0) {
+      void* xb = static_cast<char*>(workspace) + p.off_xb;
+      e = launch_x_to_bf16(X, x_dtype, ldx, M, K, xb, p.ldxb, st);
+      if (e != cudaSuccess) return cuda_fail(e, "activation staging launch");
+      xsrc = xb;
+      ldxs = p.ldxb;
+      x_f32 = false;
+    }
+    CUtensorMap xmap;
+    const int rc = make_x_tensor_map(&xmap, xsrc, M, K, ldxs, p.tile_m, x_f32);
+    if (rc != 0) return fail(MTRTQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", rc);
+    e = launch_skinny_tc(p, scale, bias, Y, ldy, packed, workspace, xmap, x_f32, status, st);
+    if (e != cudaSuccess) return cuda_fail(e, "stream-K kernel launch");
+    return MTRTQ_OK;
+  }
   const void* xb = X;
   int64_t ldxb = ldx;
   if (p.x_to_bf16) {
@@ -355,9 +406,6 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
     return fail(MTRTQ_ERR_ALIGNMENT, "bf16 X on the GEMM path needs ldx %% 8 == 0 (ldx=%lld)",
                 (long long)ldx);
   }
-  unsigned* status = nullptr;
-  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
-  if (e != cudaSuccess) return cuda_fail(e, "device status address");
   CUtensorMap xmap;
   const int rc = make_x_tensor_map(&xmap, xb, M, K, ldxb, p.tile_m);
   if (rc != 0) return fail(MTRTQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", rc);
@@ -371,11 +419,11 @@ int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int6
   if (!info || n_info < 6) return fail(MTRTQ_ERR_INVALID_ARG, "info needs 6 slots");
   Plan p;
   if (int rc = plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p)) return rc;
-  info[0] = p.kind;
+  info[0] = p.kind;  // 0 GEMV, 1 tile GEMM, 2 stream-K
   info[1] = p.tile_m;
   info[2] = p.m_tiles;
   info[3] = p.n_tiles;
-  info[4] = p.splits;
+  info[4] = p.kind == Plan::kSkinnyTC ? p.grid : p.splits;
   info[5] = p.kunits_per_split * (p.kind == Plan::kGemv ? kSlabK : kBlockK);
   return MTRTQ_OK;
 }

@@ -391,18 +391,19 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-int make_x_tensor_map(CUtensorMap* map, const void* Xb, int64_t M, int64_t K, int64_t ldx,
-                      int tile_m) {
+int make_x_tensor_map(CUtensorMap* map, const void* X, int64_t M, int64_t K, int64_t ldx,
+                      int tile_m, bool x_f32) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return -1;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  const cuuint64_t strides[1] = {(cuuint64_t)ldx * (x_f32 ? 4 : 2)};
   const cuuint32_t box[2] = {(cuuint32_t)kBlockK, (cuuint32_t)tile_m};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(Xb), dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r =
+      enc(map, x_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+          const_cast<void*>(X), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          x_f32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 

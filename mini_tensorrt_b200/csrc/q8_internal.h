@@ -12,7 +12,7 @@ namespace mtrtq {
 // problem alone (and the device's SM count), so the workspace query and the
 // launch always agree.
 struct Plan {
-  enum Kind { kGemv = 0, kGemmTC = 1 } kind = kGemv;
+  enum Kind { kGemv = 0, kGemmTC = 1, kSkinnyTC = 2 } kind = kGemv;
   int64_t M = 0, K = 0, N = 0;
   int64_t n_pad = 0, k_pad = 0;    // packed weight extents
   int n_tiles = 0;                 // channel tiles of 128
@@ -22,6 +22,7 @@ struct Plan {
   int kunits = 0;                  // k units (GEMV: slabs of 16; GEMM: blocks of 64)
   int kunits_per_split = 0;
   int chunk_units = 0;             // GEMV: slabs of activations staged at a time
+  int grid = 0;                    // stream-K kernel: persistent CTAs
   bool x_to_bf16 = false;          // GEMM: X is staged as a bf16 copy in the workspace
   bool round_x = false;            // GEMV: round fp32 X to bf16 before the product
   // workspace layout (byte offsets)
@@ -52,10 +53,16 @@ cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const vo
                            void* workspace, const CUtensorMap& xmap, int a_from_tmem,
                            unsigned* status, cudaStream_t st);
 
-// Builds the 2-D TMA descriptor for a bf16 [M, K] activation matrix with row
-// stride ldx elements, box = 64 k x tile_m rows, 128-byte swizzle.
-int make_x_tensor_map(CUtensorMap* map, const void* Xb, int64_t M, int64_t K, int64_t ldx,
-                      int tile_m);
+cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bias, float* Y,
+                             int64_t ldy, const void* packed, void* workspace,
+                             const CUtensorMap& xmap, bool x_f32, unsigned* status,
+                             cudaStream_t st);
+
+// Builds the 2-D TMA descriptor for an [M, K] activation matrix with row stride
+// ldx elements and box = 64 k x tile_m rows: bf16 with 128-byte swizzle
+// (x_f32 = false), or fp32 without swizzle (x_f32 = true).
+int make_x_tensor_map(CUtensorMap* map, const void* X, int64_t M, int64_t K, int64_t ldx,
+                      int tile_m, bool x_f32 = false);
 
 // GEMM tile sizes with a compiled kernel.
 bool gemm_tile_supported(int tile_m);

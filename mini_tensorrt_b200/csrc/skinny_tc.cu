@@ -1,0 +1,414 @@
+// Stream-K tensor-core kernel for skinny INT8 weight-only MatMuls: M <= 64 token
+// rows (decode GEMV and small prefill), MTRTQ_MODE_BF16.
+//
+// Replaces, for these shapes, the reference's scalar MatMulQ loop
+// (src/ops/kernels_matmul.cpp:66-73) and the decode loop's fp32 GEMV
+// (tools/run_gpt2.cpp:125-132, :189).
+//
+// Why stream-K: a skinny MatMul is a stream over the int8 weights (K*N bytes),
+// and the work is the same per 64-k block of a 128-channel tile (a "unit": 8 KiB
+// of packed weights, contiguous in memory because the packed layout is
+// [tile][slab]). The grid is one persistent CTA per SM; CTA c takes the units
+// [c*U/G, (c+1)*U/G), i.e. one contiguous byte range of the weights, so every SM
+// streams the same amount with no tail wave. A tile cut by a CTA boundary gets
+// one fp32 partial per CTA that touches it; the last of those CTAs to finish (an
+// atomic ticket per tile) sums them in CTA order -- deterministic -- and writes Y.
+//
+// Warp roles (14 warps):
+//   warp 0        producer: per unit, one 8 KiB bulk copy of the weights and one
+//                 TMA tensor copy of the activation tile (fp32 box 64 x TM, or bf16
+//                 with 128-byte swizzle) into a ring of shared-memory stages;
+//   warp 1        allocates TMEM; one lane issues tcgen05.mma (kind::f16, A from
+//                 TMEM, B = activations from shared memory) and tcgen05.commit;
+//   warps 2..5    dequantizer group 0 (even units), warps 6..9 group 1 (odd units):
+//                 each thread owns one channel row, converts its 64 int8 weights
+//                 exactly to bf16 and stores them into a TMEM A stage (tcgen05.st);
+//                 with fp32 activations the group also rounds the activation tile to
+//                 bf16 (round to nearest even) into the 128-byte-swizzled B tile;
+//   warps 10..13  epilogue: tcgen05.ld of a finished accumulator (double-buffered in
+//                 TMEM, so the next segment's MMAs proceed meanwhile), then scale and
+//                 bias into Y, or an fp32 partial plus the ticketed reduction.
+// Every wait is bounded (~1 s); on timeout the kernel records MTRTQ_ERR_TIMEOUT in
+// the device status word, drains its copies and MMAs, frees TMEM and returns.
+#include "q8_common.cuh"
+#include "q8_internal.h"
+
+namespace mtrtq {
+
+struct SkinnyParams {
+  const uint8_t* W;       // packed weights; unit u = (tile, k-block) lives at u * 8 KiB
+  const float* scale;
+  const float* bias;
+  float* Y;
+  int64_t ldy;
+  int M, N, n_pad;
+  int KB;                 // 64-k blocks per tile
+  int n_tiles;
+  long long units;        // n_tiles * KB
+  int grid;               // CTAs (G)
+  float* partials;        // [G][2][M][128]
+  unsigned* counters;     // [n_tiles]
+  unsigned* status;
+};
+
+constexpr int kSkinnyThreads = 14 * 32;
+constexpr int kSkinnyAStages = 4;   // TMEM A stages (even: groups alternate)
+
+template <int TM, bool X_F32>
+struct SkinnyCfg {
+  static constexpr int XB_BYTES = TM * 128;                  // bf16 B tile (SW128)
+  static constexpr int W_BYTES = kTileN * kBlockK;           // 8 KiB
+  static constexpr int XR_BYTES = X_F32 ? TM * kBlockK * 4 : 0;  // raw fp32 tile
+  static constexpr int STAGE = XB_BYTES + W_BYTES + XR_BYTES;
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE;
+  static constexpr int STAGES = (STAGES_RAW > 8 ? 8 : STAGES_RAW) & ~1;  // even, <= 8
+  static constexpr int OFF_XB = 0;
+  static constexpr int OFF_W = XB_BYTES;
+  static constexpr int OFF_XR = XB_BYTES + W_BYTES;
+  static constexpr int OFF_BAR = STAGES * STAGE;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * kSkinnyAStages + 5;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+  static constexpr int ACC_COL = kSkinnyAStages * 32;
+  static constexpr int NEED_COLS = ACC_COL + 2 * TM;
+  static constexpr int TMEM_COLS = NEED_COLS <= 256 ? 256 : 512;
+  static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(STAGES >= 2, "need at least two stages");
+  static_assert(TM % 16 == 0 && TM >= 16 && TM <= 64, "TM in {16, 32, 48, 64}");
+};
+
+__device__ __forceinline__ bool sk_warp_wait(uint64_t* bar, uint32_t parity, volatile int* ab,
+                                             unsigned* status) {
+  const bool ok = mbar_wait_bounded(bar, parity, ab, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void sk_drain(uint64_t* bar, uint32_t parity, unsigned* status) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kSpinLimitCycles) {
+      atomicExch(status, 6u);
+      return;
+    }
+  }
+}
+
+// CTA that owns unit u: r(c) = floor(c*U/G) <= u < r(c+1).
+__device__ __forceinline__ int sk_owner(long long u, long long U, int G) {
+  return (int)(((u + 1) * (long long)G - 1) / U);
+}
+
+template <int TM, bool X_F32>
+__global__ void __launch_bounds__(kSkinnyThreads, 1)
+    skinny_q8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const SkinnyParams p) {
+  using C = SkinnyCfg<TM, X_F32>;
+  constexpr int S = C::STAGES;
+  constexpr int SA = kSkinnyAStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;                   // [S]  producer tx
+  uint64_t* empty = bars + S;              // [S]  4 dequantizer warps + 1 commit
+  uint64_t* a_full = bars + 2 * S;         // [SA] 4 dequantizer warps
+  uint64_t* a_empty = bars + 2 * S + SA;   // [SA] 1 commit
+  uint64_t* acc_full = bars + 2 * S + 2 * SA;      // [2] 1 commit
+  uint64_t* acc_empty = acc_full + 2;              // [2] 4 epilogue warps
+  uint64_t* drain = acc_full + 4;                  // [1] abort drain, 1 commit
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  volatile unsigned* s_ticket = reinterpret_cast<volatile unsigned*>(smem + C::OFF_MISC + 8);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int c = blockIdx.x;
+  const long long U = p.units;
+  const int G = p.grid;
+  const long long u0 = (long long)c * U / G;
+  const long long u1 = (long long)(c + 1) * U / G;
+  const int n_units = (int)(u1 - u0);
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 5);
+    }
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&a_full[s], 4);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) prefetch_tensormap(&xmap);
+  if (warp == 1) {
+    tmem_alloc(s_tmem, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < n_units; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        if (!mbar_wait_bounded(&empty[s], ph ^ 1, s_abort, p.status)) break;
+        const long long u = u0 + i;
+        const int kb = (int)(u % p.KB);
+        uint8_t* st = smem + s * C::STAGE;
+        mbar_arrive_expect_tx(&full[s], C::W_BYTES + (X_F32 ? C::XR_BYTES : C::XB_BYTES));
+        bulk_g2s(st + C::OFF_W, p.W + u * (long long)C::W_BYTES, C::W_BYTES, &full[s]);
+        tma_load_2d(st + (X_F32 ? C::OFF_XR : C::OFF_XB), &xmap, kb * kBlockK, 0, &full[s]);
+        ++issued;
+      }
+      for (int j = max(0, issued - S); j < issued; ++j) sk_drain(&full[j % S], (j / S) & 1, p.status);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
+      int seg = -1;
+      bool ok = true;
+      for (int i = 0; i < n_units && ok; ++i) {
+        const long long u = u0 + i;
+        const int kb = (int)(u % p.KB);
+        const bool first = (i == 0) || kb == 0;
+        const bool last = (i == n_units - 1) || kb == p.KB - 1;
+        if (first) {
+          ++seg;
+          if (!mbar_wait_bounded(&acc_empty[seg & 1], ((seg >> 1) & 1) ^ 1, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+        }
+        const int s = i % S, sa = i % SA;
+        if (!mbar_wait_bounded(&a_full[sa], (i / SA) & 1, s_abort, p.status)) { ok = false; break; }
+        if (!mbar_wait_bounded(&full[s], (i / S) & 1, s_abort, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * TM;
+        const uint32_t xaddr = smem_u32(smem + s * C::STAGE + C::OFF_XB);
+#pragma unroll
+        for (int k = 0; k < kBlockK / 16; ++k)
+          umma_ts(acc, tmem_base + sa * 32 + k * 8, umma_desc_sw128(xaddr + k * 32), idesc,
+                  (first && k == 0) ? 0u : 1u);
+        umma_commit(&empty[s]);
+        umma_commit(&a_empty[sa]);
+        if (last) umma_commit(&acc_full[seg & 1]);
+      }
+      if (!ok) {
+        // Let every MMA already issued finish before TMEM is freed.
+        umma_commit(drain);
+        sk_drain(drain, 0, p.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 10) {
+    // ---------------- dequantizers (two groups alternate units) ----------------
+    const int group = (warp - 2) >> 2;     // 0: warps 2..5, 1: warps 6..9
+    const int q = warp & 3;                // TMEM lane quadrant
+    const int r = q * 32 + lane;           // channel row in the tile
+    const int gt = (warp - 2 - 4 * group) * 32 + lane;  // 0..127 within the group
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    for (int i = group; i < n_units; i += 2) {
+      const int s = i % S, sa = i % SA;
+      if (!sk_warp_wait(&full[s], (i / S) & 1, s_abort, p.status)) break;
+      uint8_t* st = smem + s * C::STAGE;
+      uint4 wv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        wv[j] = *reinterpret_cast<const uint4*>(st + C::OFF_W + j * kSlabBytes + r * 16);
+      if (X_F32) {
+        // Round the fp32 activation tile [TM][64] to bf16 into the swizzled B tile.
+        const float* xr = reinterpret_cast<const float*>(st + C::OFF_XR);
+        uint8_t* xb = st + C::OFF_XB;
+#pragma unroll
+        for (int cidx = gt; cidx < TM * 8; cidx += 128) {
+          const int row = cidx >> 3, ch = cidx & 7;
+          const float4 a = *reinterpret_cast<const float4*>(xr + row * 64 + ch * 8);
+          const float4 b = *reinterpret_cast<const float4*>(xr + row * 64 + ch * 8 + 4);
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(a.z, a.w);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(b.x, b.y);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(b.z, b.w);
+          uint4 v;
+          v.x = *reinterpret_cast<uint32_t*>(&h0);
+          v.y = *reinterpret_cast<uint32_t*>(&h1);
+          v.z = *reinterpret_cast<uint32_t*>(&h2);
+          v.w = *reinterpret_cast<uint32_t*>(&h3);
+          *reinterpret_cast<uint4*>(xb + row * 128 + ((ch ^ (row & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      uint32_t a[32];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        i8x4_to_bf16x4(wv[j].x, a[8 * j + 0], a[8 * j + 1]);
+        i8x4_to_bf16x4(wv[j].y, a[8 * j + 2], a[8 * j + 3]);
+        i8x4_to_bf16x4(wv[j].z, a[8 * j + 4], a[8 * j + 5]);
+        i8x4_to_bf16x4(wv[j].w, a[8 * j + 6], a[8 * j + 7]);
+      }
+      if (!sk_warp_wait(&a_empty[sa], ((i / SA) & 1) ^ 1, s_abort, p.status)) break;
+      tmem_st_32x32b_x32(tmem_base + lane_off + sa * 32, a);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[sa]);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int seg = -1;
+    long long u = u0;
+    while (u < u1) {
+      const int t = (int)(u / p.KB);
+      const long long seg_end = min(u1, (long long)(t + 1) * p.KB);
+      const bool full_tile = (u == (long long)t * p.KB) && (seg_end == (long long)(t + 1) * p.KB);
+      ++seg;
+      const int b = seg & 1;
+      float v[TM];
+      const bool ok = sk_warp_wait(&acc_full[b], (seg >> 1) & 1, s_abort, p.status);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < TM; c0 += 16) {
+          uint32_t raw[16];
+          tmem_ld_32x32b_x16(tmem_base + lane_off + C::ACC_COL + b * TM + c0, raw);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[c0 + j] = __uint_as_float(raw[j]);
+        }
+        tc_fence_before();
+      } else {
+#pragma unroll
+        for (int j = 0; j < TM; ++j) v[j] = 0.0f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+
+      const int n = t * kTileN + r;
+      const bool n_ok = n < p.N;
+      const float sc = n_ok ? p.scale[n] : 0.0f;
+      const float bi = (n_ok && p.bias) ? p.bias[n] : 0.0f;
+      if (full_tile) {
+        if (n_ok) {
+#pragma unroll
+          for (int j = 0; j < TM; ++j) {
+            if (j < p.M) {
+              float y = __fmul_rn(v[j], sc);
+              if (p.bias) y = __fadd_rn(y, bi);
+              p.Y[(int64_t)j * p.ldy + n] = y;
+            }
+          }
+        }
+      } else {
+        // Partial of tile t: this CTA's slot 0 if t is its first tile, else slot 1.
+        const int t_first = (int)(u0 / p.KB);
+        const int slot = (t == t_first) ? 0 : 1;
+        float* part = p.partials + ((int64_t)(c * 2 + slot) * p.M) * kTileN + r;
+#pragma unroll
+        for (int j = 0; j < TM; ++j)
+          if (j < p.M) part[(int64_t)j * kTileN] = v[j];
+        __threadfence();
+        named_bar_sync(1, 128);
+        const int c_first = sk_owner((long long)t * p.KB, U, G);
+        const int c_last = sk_owner((long long)(t + 1) * p.KB - 1, U, G);
+        const unsigned nslots = (unsigned)(c_last - c_first + 1);
+        unsigned* counter = p.counters + t;
+        if (warp == 10 && lane == 0) *s_ticket = atomicAdd(counter, 1u);
+        named_bar_sync(1, 128);
+        if (*s_ticket == nslots - 1) {
+          __threadfence();
+          if (n_ok) {
+            float sum[TM];
+#pragma unroll
+            for (int j = 0; j < TM; ++j) sum[j] = 0.0f;
+            for (int cc = c_first; cc <= c_last; ++cc) {
+              const int sl = ((int)((long long)cc * U / G / p.KB) == t) ? 0 : 1;
+              const float* src = p.partials + ((int64_t)(cc * 2 + sl) * p.M) * kTileN + r;
+#pragma unroll
+              for (int j = 0; j < TM; ++j)
+                if (j < p.M) sum[j] += __ldcg(src + (int64_t)j * kTileN);
+            }
+#pragma unroll
+            for (int j = 0; j < TM; ++j) {
+              if (j < p.M) {
+                float y = __fmul_rn(sum[j], sc);
+                if (p.bias) y = __fadd_rn(y, bi);
+                p.Y[(int64_t)j * p.ldy + n] = y;
+              }
+            }
+          }
+          if (warp == 10 && lane == 0) *counter = 0u;
+        }
+      }
+      u = seg_end;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int TM, bool X_F32>
+static cudaError_t sk_launch(const SkinnyParams& sp, const CUtensorMap& xmap, cudaStream_t st) {
+  using C = SkinnyCfg<TM, X_F32>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(skinny_q8_tc_kernel<TM, X_F32>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  skinny_q8_tc_kernel<TM, X_F32><<<sp.grid, kSkinnyThreads, C::SMEM_BYTES, st>>>(xmap, sp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bias, float* Y,
+                             int64_t ldy, const void* packed, void* workspace,
+                             const CUtensorMap& xmap, bool x_f32, unsigned* status,
+                             cudaStream_t st) {
+  SkinnyParams sp;
+  sp.W = static_cast<const uint8_t*>(packed);
+  sp.scale = scale;
+  sp.bias = bias;
+  sp.Y = Y;
+  sp.ldy = ldy;
+  sp.M = (int)p.M;
+  sp.N = (int)p.N;
+  sp.n_pad = (int)p.n_pad;
+  sp.KB = p.kunits;
+  sp.n_tiles = p.n_tiles;
+  sp.units = (long long)p.n_tiles * p.kunits;
+  sp.grid = p.grid;
+  char* ws = static_cast<char*>(workspace);
+  sp.counters = reinterpret_cast<unsigned*>(ws + p.off_counters);
+  sp.partials = reinterpret_cast<float*>(ws + p.off_partials);
+  sp.status = status;
+  switch (p.tile_m) {
+    case 16: return x_f32 ? sk_launch<16, true>(sp, xmap, st) : sk_launch<16, false>(sp, xmap, st);
+    case 32: return x_f32 ? sk_launch<32, true>(sp, xmap, st) : sk_launch<32, false>(sp, xmap, st);
+    case 64: return x_f32 ? sk_launch<64, true>(sp, xmap, st) : sk_launch<64, false>(sp, xmap, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace mtrtq

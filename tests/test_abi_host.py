@@ -124,14 +124,21 @@ def test_launch_without_device_fails_loudly():
 
 
 @pytest.mark.parametrize("M,K,N,mode,path", [
-    (1, 768, 50257, "bf16", "gemv"), (8, 768, 768, "fp32", "gemv"), (8, 3072, 768, "bf16", "gemv"),
-    (9, 768, 768, "bf16", "gemm_tc"), (64, 768, 3072, "bf16", "gemm_tc"),
+    (1, 768, 50257, "bf16", "stream_k_tc"), (8, 768, 768, "fp32", "gemv"),
+    (8, 3072, 768, "bf16", "stream_k_tc"), (9, 768, 768, "bf16", "stream_k_tc"),
+    (64, 768, 3072, "bf16", "stream_k_tc"), (65, 768, 3072, "bf16", "gemm_tc"),
     (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv"),
+    (1, 768, 200000, "bf16", "gemm_tc"),
 ])
 def test_planner(M, K, N, mode, path):
     info = matmulq.plan_info(M, K, N, torch.float32, mode)
     assert info["path"] == path
     assert info["n_tiles"] == -(-N // 128)
+    if path == "stream_k_tc":
+        units = info["n_tiles"] * (-(-K // 64))
+        assert info["ctas"] == min(units, 148)
+        assert matmulq.workspace_bytes(M, K, N, torch.float32, mode) >= 4096 + info["ctas"] * 2 * M * 512
+        return
     # every split has work, and the splits cover K
     unit = 16 if path == "gemv" else 64
     k_pad = -(-K // 64) * 64
@@ -150,5 +157,9 @@ def test_forced_paths_change_the_plan():
             matmulq.plan_info(4, 768, 768, mode="fp32")
         matmulq.set_option(_lib.OPT_FORCE_PATH, 1)
         assert matmulq.plan_info(64, 768, 768)["path"] == "gemv"
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 3)
+        assert matmulq.plan_info(8, 768, 768)["path"] == "stream_k_tc"
+        with pytest.raises(_lib.MtrtqError):
+            matmulq.plan_info(65, 768, 768)
     finally:
         matmulq.set_option(_lib.OPT_FORCE_PATH, 0)

@@ -74,22 +74,28 @@ def test_decode_gemv_set(cuda_device, case, mode):
     X, W, b = case_inputs(case)
     q, s = oracle.quantize_per_channel(W)
     Y = run(X, q, s, mode)
-    assert matmulq.plan_info(*X.shape, W.shape[1], mode=mode)["path"] == "gemv"
-    check(Y, X, q, s, mode)
+    path = matmulq.plan_info(*X.shape, W.shape[1], mode=mode)["path"]
+    assert path == ("gemv" if mode == "fp32" else "stream_k_tc")
+    check(Y, X, q, s, mode, tc=(mode == "bf16"))
 
 
-@pytest.mark.parametrize("a_source", [0, 1], ids=["A_tmem", "A_smem"])
+@pytest.mark.parametrize("path,a_source", [(0, 0), (2, 0), (2, 1), (3, 0), (1, 0)],
+                         ids=["auto", "tile_A_tmem", "tile_A_smem", "stream_k", "gemv"])
 @pytest.mark.parametrize("mode", ["bf16", "fp32"])
-def test_single_op_with_bias(cuda_device, mode, a_source):
+def test_single_op_with_bias(cuda_device, mode, path, a_source):
+    if mode == "fp32" and path in (2, 3):
+        pytest.skip("the tensor-core kernels compute in bf16 mode")
     case = SEEDED_CASES[0]
     X, W, b = case_inputs(case)
     q, s = oracle.quantize_per_channel(W)
     matmulq.set_option(_lib.OPT_GEMM_A_SOURCE, a_source)
+    matmulq.set_option(_lib.OPT_FORCE_PATH, path)
     try:
         Y = run(X, q, s, mode, bias=b)
     finally:
         matmulq.set_option(_lib.OPT_GEMM_A_SOURCE, 0)
-    check(Y, X, q, s, mode, bias=b, tc=(mode == "bf16"))
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
+    check(Y, X, q, s, mode, bias=b, tc=(mode == "bf16" and path != 1))
 
 
 LARGE = [(K, N, M) for (K, N) in wl.LARGE_SHAPES for M in wl.LARGE_M]
@@ -123,14 +129,14 @@ def test_ragged_shapes(cuda_device, M, K, N, mode):
     check(Y, X, q, s, mode, bias=b, tc=(mode == "bf16" and M > 8))
 
 
-@pytest.mark.parametrize("M", [1, 4, 8, 16, 64, 200])
-def test_forced_gemm_and_gemv_agree(cuda_device, M):
+@pytest.mark.parametrize("M", [1, 4, 8, 16, 40, 64, 200])
+def test_every_path_agrees(cuda_device, M):
     K, N = 768, 1000
     W = wl.weights(K, N, 5)
     q, s = oracle.quantize_per_channel(W)
     X = wl.activations(M, K, 6)
     outs = []
-    for path in (1, 2):
+    for path in ((1, 2, 3) if M <= 64 else (1, 2)):
         matmulq.set_option(_lib.OPT_FORCE_PATH, path)
         try:
             outs.append(run(X, q, s, "bf16"))
@@ -244,3 +250,30 @@ def test_gemv_restages_activations_in_chunks(cuda_device, M):
     X = wl.activations(M, K, 32)
     Y = run(X, q, s, "fp32")
     check(Y, X, q, s, "fp32")
+
+
+@pytest.mark.parametrize("x_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("K", [100, 77])
+def test_stream_k_with_unaligned_rows(cuda_device, x_dtype, K):
+    # Row strides that are not a multiple of 16 bytes cannot be read by TMA: the
+    # library stages a bf16 copy first. Same results either way.
+    M, N = 5, 300
+    W = wl.weights(K, N, 41)
+    q, s = oracle.quantize_per_channel(W)
+    X = oracle.round_bf16(wl.activations(M, K, 42))
+    Y = run(X, q, s, "bf16", x_dtype=x_dtype)
+    check(Y, X, q, s, "bf16", tc=True)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 64, 128), (3, 64, 50257), (8, 12288, 256), (64, 4096, 640),
+                                   (33, 192, 129), (16, 20000, 100)])
+def test_stream_k_partitions(cuda_device, M, K, N):
+    """Tiles cut by CTA boundaries in every way: one unit per CTA, many tiles per
+    CTA, tiles spread over many CTAs, ragged K and N."""
+    W = wl.weights(K, N, 51)
+    q, s = matmulq.quantize_per_channel(W)
+    X = wl.activations(M, K, 52)
+    b = wl.bias(N, 53)
+    Y = run(X, q, s, "bf16", bias=b)
+    assert matmulq.plan_info(M, K, N)["path"] == "stream_k_tc"
+    check(Y, X, q, s, "bf16", bias=b, tc=True)
