@@ -134,7 +134,14 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
     p.kunits = (int)(p.k_pad / kBlockK);
     p.kunits_per_split = p.kunits;
     const int64_t units = (int64_t)p.n_tiles * p.kunits;
-    p.grid = (int)(units < sm_count ? units : sm_count);
+    // One CTA per SM, but no tile shared by more than about 8 CTAs: every CTA
+    // takes at least ceil(KB/8) units, which bounds the partials a tile's last
+    // CTA has to sum.
+    const int64_t min_units = ceil_div64(p.kunits, 8);
+    int64_t g = units / min_units;
+    if (g > sm_count) g = sm_count;
+    if (g < 1) g = 1;
+    p.grid = (int)g;
     p.splits = 1;
     p.ldxb = round_up64(K, 8);
     size_t off = kCounterBytes;

@@ -334,22 +334,39 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         if (*s_ticket == nslots - 1) {
           __threadfence();
           if (n_ok) {
-            float sum[TM];
+            // Slots are summed in CTA order (= k order), 16 rows at a time; the
+            // loads of four slots are issued together.
+            constexpr int SL = 4;
+            for (int j0 = 0; j0 < TM && j0 < p.M; j0 += 16) {
+              float sum[16];
 #pragma unroll
-            for (int j = 0; j < TM; ++j) sum[j] = 0.0f;
-            for (int cc = c_first; cc <= c_last; ++cc) {
-              const int sl = ((int)((long long)cc * U / G / p.KB) == t) ? 0 : 1;
-              const float* src = p.partials + ((int64_t)(cc * 2 + sl) * p.M) * kTileN + r;
+              for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+              for (int cc0 = c_first; cc0 <= c_last; cc0 += SL) {
+                float v2[SL][16];
 #pragma unroll
-              for (int j = 0; j < TM; ++j)
-                if (j < p.M) sum[j] += __ldcg(src + (int64_t)j * kTileN);
-            }
+                for (int k = 0; k < SL; ++k) {
+                  const int cc = min(cc0 + k, c_last);
+                  const int sl = ((int)((long long)cc * U / G / p.KB) == t) ? 0 : 1;
+                  const float* src =
+                      p.partials + ((int64_t)(cc * 2 + sl) * p.M + j0) * kTileN + r;
 #pragma unroll
-            for (int j = 0; j < TM; ++j) {
-              if (j < p.M) {
-                float y = __fmul_rn(sum[j], sc);
-                if (p.bias) y = __fadd_rn(y, bi);
-                p.Y[(int64_t)j * p.ldy + n] = y;
+                  for (int j = 0; j < 16; ++j)
+                    v2[k][j] = (j0 + j < p.M) ? __ldcg(src + (int64_t)j * kTileN) : 0.0f;
+                }
+#pragma unroll
+                for (int k = 0; k < SL; ++k)
+                  if (cc0 + k <= c_last) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sum[j] += v2[k][j];
+                  }
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (j0 + j < p.M) {
+                  float y = __fmul_rn(sum[j], sc);
+                  if (p.bias) y = __fadd_rn(y, bi);
+                  p.Y[(int64_t)(j0 + j) * p.ldy + n] = y;
+                }
               }
             }
           }
