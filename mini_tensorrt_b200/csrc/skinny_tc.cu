@@ -61,7 +61,7 @@ struct SkinnyCfg {
   static constexpr int XR_BYTES = X_F32 ? TM * kBlockK * 4 : 0;  // raw fp32 tile
   static constexpr int STAGE = XB_BYTES + W_BYTES + XR_BYTES;
   static constexpr int STAGES_RAW = (200 * 1024) / STAGE;
-  static constexpr int STAGES = (STAGES_RAW > 8 ? 8 : STAGES_RAW) & ~1;  // even, <= 8
+  static constexpr int STAGES = (STAGES_RAW > 16 ? 16 : STAGES_RAW) & ~1;  // even, <= 16
   static constexpr int OFF_XB = 0;
   static constexpr int OFF_W = XB_BYTES;
   static constexpr int OFF_XR = XB_BYTES + W_BYTES;
@@ -69,12 +69,18 @@ struct SkinnyCfg {
   static constexpr int NUM_BARS = 2 * STAGES + 2 * kSkinnyAStages + 5;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+  // Independent accumulation chains per segment: unit j of a segment accumulates
+  // into sub-accumulator j % R, so consecutive units' MMAs do not wait on one
+  // another; the epilogue sums the R sub-accumulators in a fixed order.
+  static constexpr int R = TM <= 32 ? 4 : 2;
   static constexpr int ACC_COL = kSkinnyAStages * 32;
-  static constexpr int NEED_COLS = ACC_COL + 2 * TM;
+  static constexpr int ACC_BUF = R * TM;                     // columns per buffer
+  static constexpr int NEED_COLS = ACC_COL + 2 * ACC_BUF;
   static constexpr int TMEM_COLS = NEED_COLS <= 256 ? 256 : 512;
   static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(STAGES >= 2, "need at least two stages");
   static_assert(TM % 16 == 0 && TM >= 16 && TM <= 64, "TM in {16, 32, 48, 64}");
+  static_assert(NEED_COLS <= 512, "TMEM has 512 columns");
 };
 
 __device__ __forceinline__ bool sk_warp_wait(uint64_t* bar, uint32_t parity, volatile int* ab,
@@ -179,6 +185,7 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
       int seg = -1;
+      int seg_start = 0;
       bool ok = true;
       for (int i = 0; i < n_units && ok; ++i) {
         const long long u = u0 + i;
@@ -187,6 +194,7 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         const bool last = (i == n_units - 1) || kb == p.KB - 1;
         if (first) {
           ++seg;
+          seg_start = i;
           if (!mbar_wait_bounded(&acc_empty[seg & 1], ((seg >> 1) & 1) ^ 1, s_abort, p.status)) {
             ok = false;
             break;
@@ -196,12 +204,13 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         if (!mbar_wait_bounded(&a_full[sa], (i / SA) & 1, s_abort, p.status)) { ok = false; break; }
         if (!mbar_wait_bounded(&full[s], (i / S) & 1, s_abort, p.status)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * TM;
+        const int j = i - seg_start;  // unit index within the segment
+        const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * C::ACC_BUF + (j % C::R) * TM;
         const uint32_t xaddr = smem_u32(smem + s * C::STAGE + C::OFF_XB);
 #pragma unroll
         for (int k = 0; k < kBlockK / 16; ++k)
           umma_ts(acc, tmem_base + sa * 32 + k * 8, umma_desc_sw128(xaddr + k * 32), idesc,
-                  (first && k == 0) ? 0u : 1u);
+                  (j < C::R && k == 0) ? 0u : 1u);
         umma_commit(&empty[s]);
         umma_commit(&a_empty[sa]);
         if (last) umma_commit(&acc_full[seg & 1]);
@@ -284,13 +293,24 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
       const bool ok = sk_warp_wait(&acc_full[b], (seg >> 1) & 1, s_abort, p.status);
       if (ok) {
         tc_fence_after();
+        // Sub-accumulators that received units: min(R, units in the segment),
+        // summed 0, 1, 2, ... .
+        const int used = (int)min((long long)C::R, seg_end - u);
 #pragma unroll
-        for (int c0 = 0; c0 < TM; c0 += 16) {
-          uint32_t raw[16];
-          tmem_ld_32x32b_x16(tmem_base + lane_off + C::ACC_COL + b * TM + c0, raw);
-          tmem_wait_ld();
+        for (int j = 0; j < TM; ++j) v[j] = 0.0f;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[c0 + j] = __uint_as_float(raw[j]);
+        for (int sub = 0; sub < C::R; ++sub) {
+          if (sub < used) {
+#pragma unroll
+            for (int c0 = 0; c0 < TM; c0 += 16) {
+              uint32_t raw[16];
+              tmem_ld_32x32b_x16(tmem_base + lane_off + C::ACC_COL + b * C::ACC_BUF + sub * TM + c0,
+                                 raw);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[c0 + j] += __uint_as_float(raw[j]);
+            }
+          }
         }
         tc_fence_before();
       } else {
