@@ -61,6 +61,8 @@ def parse():
                     help="decode_set (default) or shape:M,K,N (one MatMulQ shape timed alone)")
     ap.add_argument("--x-dtype", choices=["f32", "bf16"], default="f32",
                     help="activation type for --workload shape:M,K,N")
+    ap.add_argument("--force-path", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="shape workload: 0 auto, 1 CUDA-core GEMV, 2 tile GEMM, 3 stream-K")
     return ap.parse_args()
 
 
@@ -377,6 +379,7 @@ def run_shape(args, torch, dev):
     from mini_tensorrt_b200 import matmulq, workloads as wl
     hbm_peak, tc_peak, _, peak_kind = peaks()
     M, K, N = (int(v) for v in args.workload.split(":", 1)[1].split(","))
+    matmulq.set_option(2, args.force_path)  # MTRTQ_OPT_FORCE_PATH
     W = wl.weights(K, N, wl.shape_seed("shape", K, N))
     q, s = matmulq.quantize_per_channel(W)
     base = matmulq.PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), dev)
@@ -398,13 +401,14 @@ def run_shape(args, torch, dev):
                 matmulq.matmul_q8(x, cpy, out=y, mode=args.mode, workspace=ws, stream=stream)
     secs = time_graphs(torch, [graph], args.steps, args.warmup, stream) / (args.steps * n_copies)
     byts = wl.algorithmic_bytes(M, K, N, 2 if xdt == torch.bfloat16 else 4)
+    plan = matmulq.plan_info(M, K, N, xdt, args.mode)
+    matmulq.set_option(2, 0)
     return {"workload": args.workload, "x_dtype": args.x_dtype, "mode": args.mode,
             "us_per_call": round(secs * 1e6, 3), "gbs": round(byts / secs / 1e9, 1),
             "hbm_frac": round(byts / secs / 1e9 / hbm_peak, 4),
             "tflops": round(wl.flops(M, K, N) / secs / 1e12, 2),
             "tc_frac": round(wl.flops(M, K, N) / secs / 1e12 / tc_peak, 4),
-            "peak_kind": peak_kind, "weight_copies": n_copies,
-            "plan": matmulq.plan_info(M, K, N, xdt, args.mode)}
+            "peak_kind": peak_kind, "weight_copies": n_copies, "plan": plan}
 
 
 # ---------------------------------------------------------------------- CPU legs

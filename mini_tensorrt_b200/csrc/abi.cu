@@ -117,19 +117,19 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   // Path: fp32 mode -> CUDA-core GEMV; bf16 mode -> stream-K tensor-core kernel for
   // M <= 64 (and at most kMaxSplitTiles channel tiles), tile GEMM above.
   int path = 1;
-  if (mode == MTRTQ_MODE_BF16) path = (M <= 64 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
+  if (mode == MTRTQ_MODE_BF16) path = (M <= 32 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
   if (g_opt_force_path != 0) {
     if (g_opt_force_path != 1 && mode != MTRTQ_MODE_BF16)
       return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core kernels compute in MTRTQ_MODE_BF16 only");
-    if (g_opt_force_path == 3 && (M > 64 || p.n_tiles > kMaxSplitTiles))
-      return fail(MTRTQ_ERR_INVALID_ARG, "the stream-K kernel takes M <= 64 and N <= 131072");
+    if (g_opt_force_path == 3 && (M > 32 || p.n_tiles > kMaxSplitTiles))
+      return fail(MTRTQ_ERR_INVALID_ARG, "the stream-K kernel takes M <= 32 and N <= 131072");
     path = g_opt_force_path;
   }
   const bool gemm = path == 2;
 
   if (path == 3) {
     p.kind = Plan::kSkinnyTC;
-    p.tile_m = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+    p.tile_m = M <= 16 ? 16 : 32;
     p.m_tiles = 1;
     p.kunits = (int)(p.k_pad / kBlockK);
     p.kunits_per_split = p.kunits;

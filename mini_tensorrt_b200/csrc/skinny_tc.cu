@@ -66,21 +66,23 @@ struct SkinnyCfg {
   static constexpr int OFF_W = XB_BYTES;
   static constexpr int OFF_XR = XB_BYTES + W_BYTES;
   static constexpr int OFF_BAR = STAGES * STAGE;
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * kSkinnyAStages + 5;
+  static constexpr int NUM_BARS = 2 * STAGES + kSkinnyAStages + 5;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
-  // Independent accumulation chains per segment: unit j of a segment accumulates
-  // into sub-accumulator j % R, so consecutive units' MMAs do not wait on one
-  // another; the epilogue sums the R sub-accumulators in a fixed order.
-  static constexpr int R = TM <= 32 ? 4 : 2;
+  // Independent accumulation chains: the k-th MMA (k = 0..3) of every unit of a
+  // segment accumulates into sub-accumulator k, so the four MMAs of a unit do not
+  // wait on one another in the tensor pipe; the epilogue sums the four
+  // sub-accumulators in a fixed order.
+  static constexpr int R = kBlockK / 16;
   static constexpr int ACC_COL = kSkinnyAStages * 32;
   static constexpr int ACC_BUF = R * TM;                     // columns per buffer
   static constexpr int NEED_COLS = ACC_COL + 2 * ACC_BUF;
   static constexpr int TMEM_COLS = NEED_COLS <= 256 ? 256 : 512;
   static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment");
-  static_assert(STAGES >= 2, "need at least two stages");
+  static_assert(STAGES >= kSkinnyAStages + 2, "the ring must be deeper than the TMEM A stages");
   static_assert(TM % 16 == 0 && TM >= 16 && TM <= 64, "TM in {16, 32, 48, 64}");
   static_assert(NEED_COLS <= 512, "TMEM has 512 columns");
+  static_assert(TM <= 32, "four sub-accumulators x two buffers fit TMEM for TM <= 32");
 };
 
 __device__ __forceinline__ bool sk_warp_wait(uint64_t* bar, uint32_t parity, volatile int* ab,
@@ -114,11 +116,13 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  // done[i % S] completes when unit i's MMAs have completed (one commit). That
+  // frees the unit's shared-memory stage (the dequantizers finished reading it
+  // before they signalled a_full) and its TMEM A stage.
   uint64_t* full = bars;                   // [S]  producer tx
-  uint64_t* empty = bars + S;              // [S]  4 dequantizer warps + 1 commit
+  uint64_t* done = bars + S;               // [S]  1 commit
   uint64_t* a_full = bars + 2 * S;         // [SA] 4 dequantizer warps
-  uint64_t* a_empty = bars + 2 * S + SA;   // [SA] 1 commit
-  uint64_t* acc_full = bars + 2 * S + 2 * SA;      // [2] 1 commit
+  uint64_t* acc_full = bars + 2 * S + SA;          // [2] 1 commit
   uint64_t* acc_empty = acc_full + 2;              // [2] 4 epilogue warps
   uint64_t* drain = acc_full + 4;                  // [1] abort drain, 1 commit
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
@@ -138,12 +142,9 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 5);
+      mbar_init(&done[s], 1);
     }
-    for (int s = 0; s < SA; ++s) {
-      mbar_init(&a_full[s], 4);
-      mbar_init(&a_empty[s], 1);
-    }
+    for (int s = 0; s < SA; ++s) mbar_init(&a_full[s], 4);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
@@ -166,17 +167,19 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     // ---------------- producer ----------------
     if (lane == 0) {
       int issued = 0;
+      int kb = (int)(u0 % p.KB);
+      int s = 0;
+      uint32_t ph = 0;
       for (int i = 0; i < n_units; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait_bounded(&empty[s], ph ^ 1, s_abort, p.status)) break;
+        if (!mbar_wait_bounded(&done[s], ph ^ 1, s_abort, p.status)) break;
         const long long u = u0 + i;
-        const int kb = (int)(u % p.KB);
         uint8_t* st = smem + s * C::STAGE;
         mbar_arrive_expect_tx(&full[s], C::W_BYTES + (X_F32 ? C::XR_BYTES : C::XB_BYTES));
         bulk_g2s(st + C::OFF_W, p.W + u * (long long)C::W_BYTES, C::W_BYTES, &full[s]);
         tma_load_2d(st + (X_F32 ? C::OFF_XR : C::OFF_XB), &xmap, kb * kBlockK, 0, &full[s]);
         ++issued;
+        if (++kb == p.KB) kb = 0;
+        if (++s == S) { s = 0; ph ^= 1; }
       }
       for (int j = max(0, issued - S); j < issued; ++j) sk_drain(&full[j % S], (j / S) & 1, p.status);
     }
@@ -185,16 +188,13 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
       int seg = -1;
-      int seg_start = 0;
       bool ok = true;
-      for (int i = 0; i < n_units && ok; ++i) {
-        const long long u = u0 + i;
-        const int kb = (int)(u % p.KB);
+      int kb = (int)(u0 % p.KB);
+      for (int i = 0; i < n_units && ok; ++i, kb = (kb + 1 == p.KB) ? 0 : kb + 1) {
         const bool first = (i == 0) || kb == 0;
         const bool last = (i == n_units - 1) || kb == p.KB - 1;
         if (first) {
           ++seg;
-          seg_start = i;
           if (!mbar_wait_bounded(&acc_empty[seg & 1], ((seg >> 1) & 1) ^ 1, s_abort, p.status)) {
             ok = false;
             break;
@@ -202,17 +202,20 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         }
         const int s = i % S, sa = i % SA;
         if (!mbar_wait_bounded(&a_full[sa], (i / SA) & 1, s_abort, p.status)) { ok = false; break; }
-        if (!mbar_wait_bounded(&full[s], (i / S) & 1, s_abort, p.status)) { ok = false; break; }
+        // bf16 activations arrive by TMA straight into the B tile: observe that copy.
+        // (fp32 activations are written by the dequantizers before a_full.)
+        if (!X_F32 && !mbar_wait_bounded(&full[s], (i / S) & 1, s_abort, p.status)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const int j = i - seg_start;  // unit index within the segment
-        const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * C::ACC_BUF + (j % C::R) * TM;
+        const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * C::ACC_BUF;
         const uint32_t xaddr = smem_u32(smem + s * C::STAGE + C::OFF_XB);
 #pragma unroll
         for (int k = 0; k < kBlockK / 16; ++k)
-          umma_ts(acc, tmem_base + sa * 32 + k * 8, umma_desc_sw128(xaddr + k * 32), idesc,
-                  (j < C::R && k == 0) ? 0u : 1u);
-        umma_commit(&empty[s]);
-        umma_commit(&a_empty[sa]);
+          umma_ts(acc + k * TM, tmem_base + sa * 32 + k * 8, umma_desc_sw128(xaddr + k * 32), idesc,
+                  first ? 0u : 1u);
+        umma_commit(&done[s]);
         if (last) umma_commit(&acc_full[seg & 1]);
       }
       if (!ok) {
@@ -259,8 +262,6 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         }
         fence_proxy_async_smem();
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
       uint32_t a[32];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -269,7 +270,8 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         i8x4_to_bf16x4(wv[j].z, a[8 * j + 4], a[8 * j + 5]);
         i8x4_to_bf16x4(wv[j].w, a[8 * j + 6], a[8 * j + 7]);
       }
-      if (!sk_warp_wait(&a_empty[sa], ((i / SA) & 1) ^ 1, s_abort, p.status)) break;
+      // A stage sa is free once unit i - SA's MMAs are done.
+      if (i >= SA && !sk_warp_wait(&done[(i - SA) % S], ((i - SA) / S) & 1, s_abort, p.status)) break;
       tmem_st_32x32b_x32(tmem_base + lane_off + sa * 32, a);
       tmem_wait_st();
       tc_fence_before();
@@ -293,23 +295,19 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
       const bool ok = sk_warp_wait(&acc_full[b], (seg >> 1) & 1, s_abort, p.status);
       if (ok) {
         tc_fence_after();
-        // Sub-accumulators that received units: min(R, units in the segment),
-        // summed 0, 1, 2, ... .
-        const int used = (int)min((long long)C::R, seg_end - u);
+        // The four sub-accumulators, summed 0, 1, 2, 3.
 #pragma unroll
         for (int j = 0; j < TM; ++j) v[j] = 0.0f;
 #pragma unroll
         for (int sub = 0; sub < C::R; ++sub) {
-          if (sub < used) {
 #pragma unroll
-            for (int c0 = 0; c0 < TM; c0 += 16) {
-              uint32_t raw[16];
-              tmem_ld_32x32b_x16(tmem_base + lane_off + C::ACC_COL + b * C::ACC_BUF + sub * TM + c0,
-                                 raw);
-              tmem_wait_ld();
+          for (int c0 = 0; c0 < TM; c0 += 16) {
+            uint32_t raw[16];
+            tmem_ld_32x32b_x16(tmem_base + lane_off + C::ACC_COL + b * C::ACC_BUF + sub * TM + c0,
+                               raw);
+            tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[c0 + j] += __uint_as_float(raw[j]);
-            }
+            for (int j = 0; j < 16; ++j) v[c0 + j] += __uint_as_float(raw[j]);
           }
         }
         tc_fence_before();
@@ -443,7 +441,6 @@ cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bia
   switch (p.tile_m) {
     case 16: return x_f32 ? sk_launch<16, true>(sp, xmap, st) : sk_launch<16, false>(sp, xmap, st);
     case 32: return x_f32 ? sk_launch<32, true>(sp, xmap, st) : sk_launch<32, false>(sp, xmap, st);
-    case 64: return x_f32 ? sk_launch<64, true>(sp, xmap, st) : sk_launch<64, false>(sp, xmap, st);
     default: return cudaErrorInvalidValue;
   }
 }
