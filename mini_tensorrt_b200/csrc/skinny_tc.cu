@@ -66,7 +66,7 @@ struct SkinnyCfg {
   static constexpr int OFF_W = XB_BYTES;
   static constexpr int OFF_XR = XB_BYTES + W_BYTES;
   static constexpr int OFF_BAR = STAGES * STAGE;
-  static constexpr int NUM_BARS = 2 * STAGES + kSkinnyAStages + 5;
+  static constexpr int NUM_BARS = STAGES + STAGES / 2 + 2 + 5;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
   // Independent accumulation chains: the k-th MMA (k = 0..3) of every unit of a
@@ -79,7 +79,7 @@ struct SkinnyCfg {
   static constexpr int NEED_COLS = ACC_COL + 2 * ACC_BUF;
   static constexpr int TMEM_COLS = NEED_COLS <= 256 ? 256 : 512;
   static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment");
-  static_assert(STAGES >= kSkinnyAStages + 2, "the ring must be deeper than the TMEM A stages");
+  static_assert(STAGES >= 2 * kSkinnyAStages, "the ring must hold more pairs than the A stages");
   static_assert(TM % 16 == 0 && TM >= 16 && TM <= 64, "TM in {16, 32, 48, 64}");
   static_assert(NEED_COLS <= 512, "TMEM has 512 columns");
   static_assert(TM <= 32, "four sub-accumulators x two buffers fit TMEM for TM <= 32");
@@ -116,15 +116,21 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  // done[i % S] completes when unit i's MMAs have completed (one commit). That
-  // frees the unit's shared-memory stage (the dequantizers finished reading it
-  // before they signalled a_full) and its TMEM A stage.
-  uint64_t* full = bars;                   // [S]  producer tx
-  uint64_t* done = bars + S;               // [S]  1 commit
-  uint64_t* a_full = bars + 2 * S;         // [SA] 4 dequantizer warps
-  uint64_t* acc_full = bars + 2 * S + SA;          // [2] 1 commit
-  uint64_t* acc_empty = acc_full + 2;              // [2] 4 epilogue warps
-  uint64_t* drain = acc_full + 4;                  // [1] abort drain, 1 commit
+  // Units are handled in pairs (units 2q and 2q+1 of this CTA, one per
+  // dequantizer group): one a_full wait, eight MMAs and one commit per pair for the
+  // MMA issuer, whose per-instruction bookkeeping is the scarce resource here.
+  //   full[i % S]        unit i's copies landed (producer tx)
+  //   done[q % (S/2)]    pair q's MMAs completed (one commit): frees both units'
+  //                      shared-memory stages (the dequantizers finished reading
+  //                      them before signalling a_full) and TMEM A stages
+  //   a_full[q % 2]      pair q's A operands written (4 warps of each group)
+  constexpr int SP = S / 2;
+  uint64_t* full = bars;                   // [S]
+  uint64_t* done = bars + S;               // [SP]
+  uint64_t* a_full = bars + S + SP;        // [2]
+  uint64_t* acc_full = a_full + 2;         // [2] 1 commit
+  uint64_t* acc_empty = acc_full + 2;      // [2] 4 epilogue warps
+  uint64_t* drain = acc_full + 4;          // [1] abort drain, 1 commit
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   volatile unsigned* s_ticket = reinterpret_cast<volatile unsigned*>(smem + C::OFF_MISC + 8);
@@ -138,13 +144,12 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   const long long u0 = (long long)c * U / G;
   const long long u1 = (long long)(c + 1) * U / G;
   const int n_units = (int)(u1 - u0);
+  const int n_pairs = (n_units + 1) >> 1;
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&done[s], 1);
-    }
-    for (int s = 0; s < SA; ++s) mbar_init(&a_full[s], 4);
+    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < SP; ++s) mbar_init(&done[s], 1);
+    for (int s = 0; s < 2; ++s) mbar_init(&a_full[s], 8);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
@@ -171,7 +176,10 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       for (int i = 0; i < n_units; ++i) {
-        if (!mbar_wait_bounded(&done[s], ph ^ 1, s_abort, p.status)) break;
+        const int q = i >> 1;
+        // Both stages of a pair are freed together by the pair's commit.
+        if (!(i & 1) && !mbar_wait_bounded(&done[q % SP], ((q / SP) & 1) ^ 1, s_abort, p.status))
+          break;
         const long long u = u0 + i;
         uint8_t* st = smem + s * C::STAGE;
         mbar_arrive_expect_tx(&full[s], C::W_BYTES + (X_F32 ? C::XR_BYTES : C::XB_BYTES));
@@ -190,33 +198,39 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
       int seg = -1;
       bool ok = true;
       int kb = (int)(u0 % p.KB);
-      for (int i = 0; i < n_units && ok; ++i, kb = (kb + 1 == p.KB) ? 0 : kb + 1) {
-        const bool first = (i == 0) || kb == 0;
-        const bool last = (i == n_units - 1) || kb == p.KB - 1;
-        if (first) {
-          ++seg;
-          if (!mbar_wait_bounded(&acc_empty[seg & 1], ((seg >> 1) & 1) ^ 1, s_abort, p.status)) {
-            ok = false;
-            break;
-          }
-        }
-        const int s = i % S, sa = i % SA;
-        if (!mbar_wait_bounded(&a_full[sa], (i / SA) & 1, s_abort, p.status)) { ok = false; break; }
-        // bf16 activations arrive by TMA straight into the B tile: observe that copy.
-        // (fp32 activations are written by the dequantizers before a_full.)
-        if (!X_F32 && !mbar_wait_bounded(&full[s], (i / S) & 1, s_abort, p.status)) {
-          ok = false;
-          break;
+      for (int q = 0; q < n_pairs && ok; ++q) {
+        if (!mbar_wait_bounded(&a_full[q & 1], (q >> 1) & 1, s_abort, p.status)) { ok = false; break; }
+        const int i_end = min(2 * q + 2, n_units);
+        // bf16 activations arrive by TMA straight into the B tile: observe those
+        // copies. (fp32 activations are written by the dequantizers before a_full.)
+        if (!X_F32) {
+          for (int i = 2 * q; i < i_end; ++i)
+            if (!mbar_wait_bounded(&full[i % S], (i / S) & 1, s_abort, p.status)) ok = false;
+          if (!ok) break;
         }
         tc_fence_after();
-        const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * C::ACC_BUF;
-        const uint32_t xaddr = smem_u32(smem + s * C::STAGE + C::OFF_XB);
+        for (int i = 2 * q; i < i_end; ++i, kb = (kb + 1 == p.KB) ? 0 : kb + 1) {
+          const bool first = (i == 0) || kb == 0;
+          const bool last = (i == n_units - 1) || kb == p.KB - 1;
+          if (first) {
+            ++seg;
+            if (!mbar_wait_bounded(&acc_empty[seg & 1], ((seg >> 1) & 1) ^ 1, s_abort, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * C::ACC_BUF;
+          const uint32_t xaddr = smem_u32(smem + (i % S) * C::STAGE + C::OFF_XB);
+          const uint32_t a_tm = tmem_base + (i % SA) * 32;
 #pragma unroll
-        for (int k = 0; k < kBlockK / 16; ++k)
-          umma_ts(acc + k * TM, tmem_base + sa * 32 + k * 8, umma_desc_sw128(xaddr + k * 32), idesc,
-                  first ? 0u : 1u);
-        umma_commit(&done[s]);
-        if (last) umma_commit(&acc_full[seg & 1]);
+          for (int k = 0; k < kBlockK / 16; ++k)
+            umma_ts(acc + k * TM, a_tm + k * 8, umma_desc_sw128(xaddr + k * 32), idesc,
+                    first ? 0u : 1u);
+          if (last) umma_commit(&acc_full[seg & 1]);
+        }
+        if (!ok) break;
+        umma_commit(&done[q % SP]);
       }
       if (!ok) {
         // Let every MMA already issued finish before TMEM is freed.
@@ -226,14 +240,14 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     }
     __syncwarp();
   } else if (warp < 10) {
-    // ---------------- dequantizers (two groups alternate units) ----------------
+    // ---------------- dequantizers (group g handles units i = g, g+2, ...) ----------------
     const int group = (warp - 2) >> 2;     // 0: warps 2..5, 1: warps 6..9
-    const int q = warp & 3;                // TMEM lane quadrant
-    const int r = q * 32 + lane;           // channel row in the tile
+    const int q4 = warp & 3;               // TMEM lane quadrant
+    const int r = q4 * 32 + lane;          // channel row in the tile
     const int gt = (warp - 2 - 4 * group) * 32 + lane;  // 0..127 within the group
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     for (int i = group; i < n_units; i += 2) {
-      const int s = i % S, sa = i % SA;
+      const int s = i % S, sa = i % SA, q = i >> 1;
       if (!sk_warp_wait(&full[s], (i / S) & 1, s_abort, p.status)) break;
       uint8_t* st = smem + s * C::STAGE;
       uint4 wv[4];
@@ -270,13 +284,14 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         i8x4_to_bf16x4(wv[j].z, a[8 * j + 4], a[8 * j + 5]);
         i8x4_to_bf16x4(wv[j].w, a[8 * j + 6], a[8 * j + 7]);
       }
-      // A stage sa is free once unit i - SA's MMAs are done.
-      if (i >= SA && !sk_warp_wait(&done[(i - SA) % S], ((i - SA) / S) & 1, s_abort, p.status)) break;
+      // A stage sa was last used by unit i - SA (pair q - 2): free once that pair is done.
+      if (q >= 2 && !sk_warp_wait(&done[(q - 2) % SP], ((q - 2) / SP) & 1, s_abort, p.status)) break;
       tmem_st_32x32b_x32(tmem_base + lane_off + sa * 32, a);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[sa]);
+      // A pair with one unit (the CTA's last, odd count) gets group 0's arrival twice.
+      if (lane == 0) mbar_arrive_cnt(&a_full[q & 1], (i == n_units - 1 && !(i & 1)) ? 2u : 1u);
     }
   } else {
     // ---------------- epilogue ----------------

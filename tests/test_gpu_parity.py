@@ -85,6 +85,15 @@ def test_decode_gemv_set(cuda_device, case, mode):
 def test_single_op_with_bias(cuda_device, mode, path, a_source):
     if mode == "fp32" and path in (2, 3):
         pytest.skip("the tensor-core kernels compute in bf16 mode")
+    if path == 3:
+        # M = 64 exceeds the stream-K kernel's token tile: the library refuses it.
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 3)
+        try:
+            with pytest.raises(_lib.MtrtqError):
+                matmulq.plan_info(64, 768, 3072)
+        finally:
+            matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
+        return
     case = SEEDED_CASES[0]
     X, W, b = case_inputs(case)
     q, s = oracle.quantize_per_channel(W)
@@ -136,7 +145,7 @@ def test_every_path_agrees(cuda_device, M):
     q, s = oracle.quantize_per_channel(W)
     X = wl.activations(M, K, 6)
     outs = []
-    for path in ((1, 2, 3) if M <= 64 else (1, 2)):
+    for path in ((1, 2, 3) if M <= 32 else (1, 2)):
         matmulq.set_option(_lib.OPT_FORCE_PATH, path)
         try:
             outs.append(run(X, q, s, "bf16"))
@@ -265,8 +274,8 @@ def test_stream_k_with_unaligned_rows(cuda_device, x_dtype, K):
     check(Y, X, q, s, "bf16", tc=True)
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 64, 128), (3, 64, 50257), (8, 12288, 256), (64, 4096, 640),
-                                   (33, 192, 129), (16, 20000, 100)])
+@pytest.mark.parametrize("M,K,N", [(1, 64, 128), (3, 64, 50257), (8, 12288, 256), (32, 4096, 640),
+                                   (17, 192, 129), (16, 20000, 100), (5, 64 * 23, 128 * 7)])
 def test_stream_k_partitions(cuda_device, M, K, N):
     """Tiles cut by CTA boundaries in every way: one unit per CTA, many tiles per
     CTA, tiles spread over many CTAs, ragged K and N."""
