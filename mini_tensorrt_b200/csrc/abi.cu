@@ -380,6 +380,14 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   unsigned* status = nullptr;
   e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
   if (e != cudaSuccess) return cuda_fail(e, "device status address");
+  if (p.kind == Plan::kSkinnyTC && skinny_x_resident(p.tile_m, p.k_pad)) {
+    CUtensorMap unused;
+    std::memset(&unused, 0, sizeof(unused));
+    e = launch_skinny_tc(p, scale, bias, Y, ldy, packed, workspace, unused, true, X, ldx, x_dtype,
+                         status, st);
+    if (e != cudaSuccess) return cuda_fail(e, "stream-K kernel launch");
+    return MTRTQ_OK;
+  }
   if (p.kind == Plan::kSkinnyTC) {
     // TMA reads X directly when its row stride is a multiple of 16 bytes; fp32 X
     // is rounded to bf16 inside the kernel. Otherwise stage a bf16 copy first.
@@ -398,7 +406,8 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
     CUtensorMap xmap;
     const int rc = make_x_tensor_map(&xmap, xsrc, M, K, ldxs, p.tile_m, x_f32);
     if (rc != 0) return fail(MTRTQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", rc);
-    e = launch_skinny_tc(p, scale, bias, Y, ldy, packed, workspace, xmap, x_f32, status, st);
+    e = launch_skinny_tc(p, scale, bias, Y, ldy, packed, workspace, xmap, x_f32, xsrc, ldxs,
+                         x_f32 ? MTRTQ_DTYPE_F32 : MTRTQ_DTYPE_BF16, status, st);
     if (e != cudaSuccess) return cuda_fail(e, "stream-K kernel launch");
     return MTRTQ_OK;
   }

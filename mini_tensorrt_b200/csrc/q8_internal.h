@@ -55,8 +55,11 @@ cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const vo
 
 cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bias, float* Y,
                              int64_t ldy, const void* packed, void* workspace,
-                             const CUtensorMap& xmap, bool x_f32, unsigned* status,
-                             cudaStream_t st);
+                             const CUtensorMap& xmap, bool x_f32, const void* X, int64_t ldx,
+                             int x_dtype, unsigned* status, cudaStream_t st);
+// True when the stream-K kernel keeps the whole bf16 activation matrix in shared
+// memory (it then reads X directly, at any stride, and needs no tensor map).
+bool skinny_x_resident(int tile_m, int64_t k_pad);
 
 // Builds the 2-D TMA descriptor for an [M, K] activation matrix with row stride
 // ldx elements and box = 64 k x tile_m rows: bf16 with 128-byte swizzle

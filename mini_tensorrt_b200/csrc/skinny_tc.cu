@@ -1,4 +1,4 @@
-// Stream-K tensor-core kernel for skinny INT8 weight-only MatMuls: M <= 64 token
+// Stream-K tensor-core kernel for skinny INT8 weight-only MatMuls: M <= 32 token
 // rows (decode GEMV and small prefill), MTRTQ_MODE_BF16.
 //
 // Replaces, for these shapes, the reference's scalar MatMulQ loop
@@ -14,20 +14,32 @@
 // one fp32 partial per CTA that touches it; the last of those CTAs to finish (an
 // atomic ticket per tile) sums them in CTA order -- deterministic -- and writes Y.
 //
+// Units travel in pairs (units 2q, 2q+1 of a CTA: 16 KiB contiguous in memory):
+// one bulk copy, one mbarrier round and one commit per pair. Measured on B200,
+// a single thread issues a small (N <= 64) tcgen05.mma only every ~50 cycles and
+// each completed-barrier check or commit costs ~50-100 more, so the per-unit
+// bookkeeping of the two single-thread roles, not bandwidth, is what bounds a
+// skinny kernel; pairing halves it.
+//
+// Activations: with X_RES the whole [TM x K] activation matrix is rounded to bf16
+// once per CTA into shared memory (128-byte-swizzled K-major tiles, one per 64-k
+// block) by the epilogue warps before their first epilogue; otherwise every unit
+// brings its own activation tile by TMA (fp32 rounded to bf16 by the dequantizers,
+// or bf16 straight into the swizzled tile).
+//
 // Warp roles (14 warps):
-//   warp 0        producer: per unit, one 8 KiB bulk copy of the weights and one
-//                 TMA tensor copy of the activation tile (fp32 box 64 x TM, or bf16
-//                 with 128-byte swizzle) into a ring of shared-memory stages;
+//   warp 0        producer: per pair, the weight bulk copy (and, without X_RES, the
+//                 activation tiles) into a ring of shared-memory stages;
 //   warp 1        allocates TMEM; one lane issues tcgen05.mma (kind::f16, A from
-//                 TMEM, B = activations from shared memory) and tcgen05.commit;
+//                 TMEM, B = activations from shared memory, four independent
+//                 sub-accumulators, one per 16-k step) and tcgen05.commit;
 //   warps 2..5    dequantizer group 0 (even units), warps 6..9 group 1 (odd units):
 //                 each thread owns one channel row, converts its 64 int8 weights
 //                 exactly to bf16 and stores them into a TMEM A stage (tcgen05.st);
-//                 with fp32 activations the group also rounds the activation tile to
-//                 bf16 (round to nearest even) into the 128-byte-swizzled B tile;
-//   warps 10..13  epilogue: tcgen05.ld of a finished accumulator (double-buffered in
-//                 TMEM, so the next segment's MMAs proceed meanwhile), then scale and
-//                 bias into Y, or an fp32 partial plus the ticketed reduction.
+//   warps 10..13  (X_RES) stage the activations, then the epilogue: tcgen05.ld of a
+//                 finished accumulator (double-buffered in TMEM, so the next
+//                 segment's MMAs proceed meanwhile), scale and bias into Y, or an
+//                 fp32 partial plus the ticketed reduction.
 // Every wait is bounded (~1 s); on timeout the kernel records MTRTQ_ERR_TIMEOUT in
 // the device status word, drains its copies and MMAs, frees TMEM and returns.
 #include "q8_common.cuh"
@@ -41,7 +53,10 @@ struct SkinnyParams {
   const float* bias;
   float* Y;
   int64_t ldy;
-  int M, N, n_pad;
+  const void* X;          // activations (X_RES staging), row stride ldx elements
+  int64_t ldx;
+  int x_bf16;             // X element type for X_RES staging
+  int M, N, K, n_pad;
   int KB;                 // 64-k blocks per tile
   int n_tiles;
   long long units;        // n_tiles * KB
@@ -52,21 +67,27 @@ struct SkinnyParams {
 };
 
 constexpr int kSkinnyThreads = 14 * 32;
-constexpr int kSkinnyAStages = 4;   // TMEM A stages (even: groups alternate)
+constexpr int kSkinnyAStages = 4;             // TMEM A stages: two pairs in flight
+constexpr int kSkinnyXResBytes = 96 * 1024;   // largest resident activation matrix
 
-template <int TM, bool X_F32>
+template <int TM, bool X_F32, bool X_RES>
 struct SkinnyCfg {
-  static constexpr int XB_BYTES = TM * 128;                  // bf16 B tile (SW128)
-  static constexpr int W_BYTES = kTileN * kBlockK;           // 8 KiB
-  static constexpr int XR_BYTES = X_F32 ? TM * kBlockK * 4 : 0;  // raw fp32 tile
-  static constexpr int STAGE = XB_BYTES + W_BYTES + XR_BYTES;
-  static constexpr int STAGES_RAW = (200 * 1024) / STAGE;
+  static constexpr int XB_BYTES = TM * 128;                           // bf16 B tile (SW128)
+  static constexpr int W_BYTES = kTileN * kBlockK;                    // 8 KiB
+  static constexpr int XR_BYTES = (!X_RES && X_F32) ? TM * kBlockK * 4 : 0;  // raw fp32 tile
+  static constexpr int STAGE = W_BYTES + (X_RES ? 0 : XB_BYTES + XR_BYTES);
+  static constexpr int X_REGION = X_RES ? kSkinnyXResBytes : 0;
+  static constexpr int STAGES_RAW = (200 * 1024 - X_REGION) / STAGE;
   static constexpr int STAGES = (STAGES_RAW > 16 ? 16 : STAGES_RAW) & ~1;  // even, <= 16
-  static constexpr int OFF_XB = 0;
-  static constexpr int OFF_W = XB_BYTES;
-  static constexpr int OFF_XR = XB_BYTES + W_BYTES;
-  static constexpr int OFF_BAR = STAGES * STAGE;
-  static constexpr int NUM_BARS = STAGES + STAGES / 2 + 2 + 5;
+  static constexpr int SP = STAGES / 2;                                // pair slots
+  // Per stage: [W 8 KiB][bf16 B tile][raw fp32 tile]; with X_RES a stage is just
+  // the 8 KiB of weights, so the two stages of a pair take one 16 KiB copy.
+  static constexpr int OFF_RING = X_REGION;
+  static constexpr int OFF_W = 0;
+  static constexpr int OFF_XB = W_BYTES;
+  static constexpr int OFF_XR = W_BYTES + XB_BYTES;
+  static constexpr int OFF_BAR = OFF_RING + STAGES * STAGE;
+  static constexpr int NUM_BARS = 2 * SP + 2 + 2 + 2 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
   // Independent accumulation chains: the k-th MMA (k = 0..3) of every unit of a
@@ -78,11 +99,11 @@ struct SkinnyCfg {
   static constexpr int ACC_BUF = R * TM;                     // columns per buffer
   static constexpr int NEED_COLS = ACC_COL + 2 * ACC_BUF;
   static constexpr int TMEM_COLS = NEED_COLS <= 256 ? 256 : 512;
-  static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(STAGE % 1024 == 0 && X_REGION % 1024 == 0, "1024-byte aligned tiles");
   static_assert(STAGES >= 2 * kSkinnyAStages, "the ring must hold more pairs than the A stages");
-  static_assert(TM % 16 == 0 && TM >= 16 && TM <= 64, "TM in {16, 32, 48, 64}");
+  static_assert(TM % 16 == 0 && TM >= 16 && TM <= 32, "TM in {16, 32}");
   static_assert(NEED_COLS <= 512, "TMEM has 512 columns");
-  static_assert(TM <= 32, "four sub-accumulators x two buffers fit TMEM for TM <= 32");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
 __device__ __forceinline__ bool sk_warp_wait(uint64_t* bar, uint32_t parity, volatile int* ab,
@@ -106,31 +127,58 @@ __device__ __forceinline__ int sk_owner(long long u, long long U, int G) {
   return (int)(((u + 1) * (long long)G - 1) / U);
 }
 
-template <int TM, bool X_F32>
+// 8 consecutive activations of row m starting at k (zero past K or M), rounded
+// to bf16 (round to nearest even) and packed as 4 bf16x2 words.
+__device__ __forceinline__ uint4 sk_load_x8(const SkinnyParams& p, int m, int k) {
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float x = 0.0f;
+    if (m < p.M && k + j < p.K) {
+      if (p.x_bf16)
+        x = __bfloat162float(static_cast<const __nv_bfloat16*>(p.X)[(int64_t)m * p.ldx + k + j]);
+      else
+        x = static_cast<const float*>(p.X)[(int64_t)m * p.ldx + k + j];
+    }
+    v[j] = x;
+  }
+  __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]);
+  __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 h2 = __floats2bfloat162_rn(v[4], v[5]);
+  __nv_bfloat162 h3 = __floats2bfloat162_rn(v[6], v[7]);
+  uint4 r;
+  r.x = *reinterpret_cast<uint32_t*>(&h0);
+  r.y = *reinterpret_cast<uint32_t*>(&h1);
+  r.z = *reinterpret_cast<uint32_t*>(&h2);
+  r.w = *reinterpret_cast<uint32_t*>(&h3);
+  return r;
+}
+
+template <int TM, bool X_F32, bool X_RES>
 __global__ void __launch_bounds__(kSkinnyThreads, 1)
     skinny_q8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const SkinnyParams p) {
-  using C = SkinnyCfg<TM, X_F32>;
+  using C = SkinnyCfg<TM, X_F32, X_RES>;
   constexpr int S = C::STAGES;
+  constexpr int SP = C::SP;
   constexpr int SA = kSkinnyAStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem + C::OFF_RING;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  // Units are handled in pairs (units 2q and 2q+1 of this CTA, one per
-  // dequantizer group): one a_full wait, eight MMAs and one commit per pair for the
-  // MMA issuer, whose per-instruction bookkeeping is the scarce resource here.
-  //   full[i % S]        unit i's copies landed (producer tx)
-  //   done[q % (S/2)]    pair q's MMAs completed (one commit): frees both units'
-  //                      shared-memory stages (the dequantizers finished reading
-  //                      them before signalling a_full) and TMEM A stages
-  //   a_full[q % 2]      pair q's A operands written (4 warps of each group)
-  constexpr int SP = S / 2;
-  uint64_t* full = bars;                   // [S]
-  uint64_t* done = bars + S;               // [SP]
-  uint64_t* a_full = bars + S + SP;        // [2]
+  //   full[q % SP]     pair q's copies landed (producer tx)
+  //   done[q % SP]     pair q's MMAs completed (one commit): frees both units'
+  //                    shared-memory stages (the dequantizers finished reading them
+  //                    before signalling a_full) and their TMEM A stages
+  //   a_full[q % 2]    pair q's A operands written (4 warps of each group)
+  //   x_ready          resident activations staged (4 epilogue warps)
+  uint64_t* full = bars;                   // [SP]
+  uint64_t* done = bars + SP;              // [SP]
+  uint64_t* a_full = bars + 2 * SP;        // [2]
   uint64_t* acc_full = a_full + 2;         // [2] 1 commit
   uint64_t* acc_empty = acc_full + 2;      // [2] 4 epilogue warps
-  uint64_t* drain = acc_full + 4;          // [1] abort drain, 1 commit
+  uint64_t* x_ready = acc_empty + 2;       // [1]
+  uint64_t* drain = x_ready + 1;           // [1] abort drain, 1 commit
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   volatile unsigned* s_ticket = reinterpret_cast<volatile unsigned*>(smem + C::OFF_MISC + 8);
@@ -147,18 +195,21 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   const int n_pairs = (n_units + 1) >> 1;
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
-    for (int s = 0; s < SP; ++s) mbar_init(&done[s], 1);
+    for (int s = 0; s < SP; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&done[s], 1);
+    }
     for (int s = 0; s < 2; ++s) mbar_init(&a_full[s], 8);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
     }
+    mbar_init(x_ready, 4);
     mbar_init(drain, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) prefetch_tensormap(&xmap);
+  if (!X_RES && warp == 0 && lane == 0) prefetch_tensormap(&xmap);
   if (warp == 1) {
     tmem_alloc(s_tmem, C::TMEM_COLS);
     tmem_relinquish();
@@ -169,46 +220,55 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   const uint32_t tmem_base = *s_tmem;
 
   if (warp == 0) {
-    // ---------------- producer ----------------
+    // ---------------- producer: one round per pair ----------------
     if (lane == 0) {
-      int issued = 0;
+      int issued = 0;  // pairs
       int kb = (int)(u0 % p.KB);
-      int s = 0;
-      uint32_t ph = 0;
-      for (int i = 0; i < n_units; ++i) {
-        const int q = i >> 1;
-        // Both stages of a pair are freed together by the pair's commit.
-        if (!(i & 1) && !mbar_wait_bounded(&done[q % SP], ((q / SP) & 1) ^ 1, s_abort, p.status))
-          break;
-        const long long u = u0 + i;
-        uint8_t* st = smem + s * C::STAGE;
-        mbar_arrive_expect_tx(&full[s], C::W_BYTES + (X_F32 ? C::XR_BYTES : C::XB_BYTES));
-        bulk_g2s(st + C::OFF_W, p.W + u * (long long)C::W_BYTES, C::W_BYTES, &full[s]);
-        tma_load_2d(st + (X_F32 ? C::OFF_XR : C::OFF_XB), &xmap, kb * kBlockK, 0, &full[s]);
+      for (int q = 0; q < n_pairs; ++q) {
+        const int pq = q % SP;
+        if (!mbar_wait_bounded(&done[pq], ((q / SP) & 1) ^ 1, s_abort, p.status)) break;
+        const int i0 = 2 * q;
+        const int nu = min(2, n_units - i0);
+        uint8_t* st = ring + (i0 % S) * C::STAGE;
+        const uint32_t x_bytes = X_RES ? 0u : (uint32_t)(X_F32 ? C::XR_BYTES : C::XB_BYTES);
+        mbar_arrive_expect_tx(&full[pq], (uint32_t)nu * (C::W_BYTES + x_bytes));
+        if (X_RES) {
+          // The two units' weights are adjacent in memory and in the ring.
+          bulk_g2s(st + C::OFF_W, p.W + (u0 + i0) * (long long)C::W_BYTES,
+                   (uint32_t)nu * C::W_BYTES, &full[pq]);
+        } else {
+          for (int j = 0; j < nu; ++j) {
+            uint8_t* sj = st + j * C::STAGE;
+            bulk_g2s(sj + C::OFF_W, p.W + (u0 + i0 + j) * (long long)C::W_BYTES, C::W_BYTES,
+                     &full[pq]);
+            tma_load_2d(sj + (X_F32 ? C::OFF_XR : C::OFF_XB), &xmap, kb * kBlockK, 0, &full[pq]);
+            if (++kb == p.KB) kb = 0;
+          }
+        }
         ++issued;
-        if (++kb == p.KB) kb = 0;
-        if (++s == S) { s = 0; ph ^= 1; }
       }
-      for (int j = max(0, issued - S); j < issued; ++j) sk_drain(&full[j % S], (j / S) & 1, p.status);
+      for (int j = max(0, issued - SP); j < issued; ++j)
+        sk_drain(&full[j % SP], (j / SP) & 1, p.status);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: one round per pair ----------------
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
       int seg = -1;
       bool ok = true;
       int kb = (int)(u0 % p.KB);
+      if (X_RES && !mbar_wait_bounded(x_ready, 0, s_abort, p.status)) ok = false;
       for (int q = 0; q < n_pairs && ok; ++q) {
         if (!mbar_wait_bounded(&a_full[q & 1], (q >> 1) & 1, s_abort, p.status)) { ok = false; break; }
-        const int i_end = min(2 * q + 2, n_units);
-        // bf16 activations arrive by TMA straight into the B tile: observe those
-        // copies. (fp32 activations are written by the dequantizers before a_full.)
-        if (!X_F32) {
-          for (int i = 2 * q; i < i_end; ++i)
-            if (!mbar_wait_bounded(&full[i % S], (i / S) & 1, s_abort, p.status)) ok = false;
-          if (!ok) break;
+        // bf16 activation tiles arrive by TMA straight into the B tile: observe
+        // those copies. (fp32 tiles are written by the dequantizers before a_full.)
+        if (!X_RES && !X_F32 &&
+            !mbar_wait_bounded(&full[q % SP], (q / SP) & 1, s_abort, p.status)) {
+          ok = false;
+          break;
         }
         tc_fence_after();
+        const int i_end = min(2 * q + 2, n_units);
         for (int i = 2 * q; i < i_end; ++i, kb = (kb + 1 == p.KB) ? 0 : kb + 1) {
           const bool first = (i == 0) || kb == 0;
           const bool last = (i == n_units - 1) || kb == p.KB - 1;
@@ -221,7 +281,9 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
             tc_fence_after();
           }
           const uint32_t acc = tmem_base + C::ACC_COL + (seg & 1) * C::ACC_BUF;
-          const uint32_t xaddr = smem_u32(smem + (i % S) * C::STAGE + C::OFF_XB);
+          const uint32_t xaddr =
+              X_RES ? smem_u32(smem + kb * C::XB_BYTES)
+                    : smem_u32(ring + (i % S) * C::STAGE + C::OFF_XB);
           const uint32_t a_tm = tmem_base + (i % SA) * 32;
 #pragma unroll
           for (int k = 0; k < kBlockK / 16; ++k)
@@ -248,13 +310,13 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     for (int i = group; i < n_units; i += 2) {
       const int s = i % S, sa = i % SA, q = i >> 1;
-      if (!sk_warp_wait(&full[s], (i / S) & 1, s_abort, p.status)) break;
-      uint8_t* st = smem + s * C::STAGE;
+      if (!sk_warp_wait(&full[q % SP], (q / SP) & 1, s_abort, p.status)) break;
+      uint8_t* st = ring + s * C::STAGE;
       uint4 wv[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         wv[j] = *reinterpret_cast<const uint4*>(st + C::OFF_W + j * kSlabBytes + r * 16);
-      if (X_F32) {
+      if (!X_RES && X_F32) {
         // Round the fp32 activation tile [TM][64] to bf16 into the swizzled B tile.
         const float* xr = reinterpret_cast<const float*>(st + C::OFF_XR);
         uint8_t* xb = st + C::OFF_XB;
@@ -294,10 +356,24 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
       if (lane == 0) mbar_arrive_cnt(&a_full[q & 1], (i == n_units - 1 && !(i & 1)) ? 2u : 1u);
     }
   } else {
-    // ---------------- epilogue ----------------
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    // ---------------- (X_RES: activation staging, then) epilogue ----------------
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    if (X_RES) {
+      // Round the whole [TM x K_pad] activation matrix to bf16 into one swizzled
+      // K-major tile per 64-k block: chunk (kb, row, ch) holds k = kb*64 + ch*8 .. +7.
+      const int et = (warp - 10) * 32 + lane;     // 0..127
+      const int chunks = p.KB * TM * 8;
+      for (int cidx = et; cidx < chunks; cidx += 128) {
+        const int ch = cidx & 7, row = (cidx >> 3) % TM, kb = cidx / (8 * TM);
+        const uint4 v = sk_load_x8(p, row, kb * kBlockK + ch * 8);
+        *reinterpret_cast<uint4*>(smem + kb * C::XB_BYTES + row * 128 + ((ch ^ (row & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(x_ready);
+    }
     int seg = -1;
     long long u = u0;
     while (u < u1) {
@@ -418,32 +494,40 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   }
 }
 
-template <int TM, bool X_F32>
+template <int TM, bool X_F32, bool X_RES>
 static cudaError_t sk_launch(const SkinnyParams& sp, const CUtensorMap& xmap, cudaStream_t st) {
-  using C = SkinnyCfg<TM, X_F32>;
+  using C = SkinnyCfg<TM, X_F32, X_RES>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(skinny_q8_tc_kernel<TM, X_F32>,
+    cudaError_t e = cudaFuncSetAttribute(skinny_q8_tc_kernel<TM, X_F32, X_RES>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  skinny_q8_tc_kernel<TM, X_F32><<<sp.grid, kSkinnyThreads, C::SMEM_BYTES, st>>>(xmap, sp);
+  skinny_q8_tc_kernel<TM, X_F32, X_RES><<<sp.grid, kSkinnyThreads, C::SMEM_BYTES, st>>>(xmap, sp);
   return cudaGetLastError();
+}
+
+bool skinny_x_resident(int tile_m, int64_t k_pad) {
+  return k_pad * tile_m * 2 <= kSkinnyXResBytes;
 }
 
 cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bias, float* Y,
                              int64_t ldy, const void* packed, void* workspace,
-                             const CUtensorMap& xmap, bool x_f32, unsigned* status,
-                             cudaStream_t st) {
+                             const CUtensorMap& xmap, bool x_f32, const void* X, int64_t ldx,
+                             int x_dtype, unsigned* status, cudaStream_t st) {
   SkinnyParams sp;
   sp.W = static_cast<const uint8_t*>(packed);
   sp.scale = scale;
   sp.bias = bias;
   sp.Y = Y;
   sp.ldy = ldy;
+  sp.X = X;
+  sp.ldx = ldx;
+  sp.x_bf16 = x_dtype == 1 ? 1 : 0;
   sp.M = (int)p.M;
   sp.N = (int)p.N;
+  sp.K = (int)p.K;
   sp.n_pad = (int)p.n_pad;
   sp.KB = p.kunits;
   sp.n_tiles = p.n_tiles;
@@ -453,10 +537,16 @@ cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bia
   sp.counters = reinterpret_cast<unsigned*>(ws + p.off_counters);
   sp.partials = reinterpret_cast<float*>(ws + p.off_partials);
   sp.status = status;
+  const bool res = skinny_x_resident(p.tile_m, p.k_pad);
   switch (p.tile_m) {
-    case 16: return x_f32 ? sk_launch<16, true>(sp, xmap, st) : sk_launch<16, false>(sp, xmap, st);
-    case 32: return x_f32 ? sk_launch<32, true>(sp, xmap, st) : sk_launch<32, false>(sp, xmap, st);
-    default: return cudaErrorInvalidValue;
+    case 16:
+      if (res) return sk_launch<16, true, true>(sp, xmap, st);
+      return x_f32 ? sk_launch<16, true, false>(sp, xmap, st) : sk_launch<16, false, false>(sp, xmap, st);
+    case 32:
+      if (res) return sk_launch<32, true, true>(sp, xmap, st);
+      return x_f32 ? sk_launch<32, true, false>(sp, xmap, st) : sk_launch<32, false, false>(sp, xmap, st);
+    default:
+      return cudaErrorInvalidValue;
   }
 }
 
