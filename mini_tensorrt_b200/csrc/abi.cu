@@ -98,7 +98,10 @@ int check_dims(int64_t M, int64_t K, int64_t N) {
   return MTRTQ_OK;
 }
 
-int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_count, Plan* out) {
+// force_path: 0 chooses by shape and mode; 1, 2, 3 select a kernel (see
+// MTRTQ_OPT_FORCE_PATH). Callers pass the process-wide option.
+int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_count, Plan* out,
+                int force_path) {
   if (int rc = check_dims(M, K, N)) return rc;
   if (x_dtype != MTRTQ_DTYPE_F32 && x_dtype != MTRTQ_DTYPE_BF16)
     return fail(MTRTQ_ERR_INVALID_ARG, "x_dtype must be MTRTQ_DTYPE_F32 or MTRTQ_DTYPE_BF16");
@@ -118,12 +121,12 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   // M <= 64 (and at most kMaxSplitTiles channel tiles), tile GEMM above.
   int path = 1;
   if (mode == MTRTQ_MODE_BF16) path = (M <= 32 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
-  if (g_opt_force_path != 0) {
-    if (g_opt_force_path != 1 && mode != MTRTQ_MODE_BF16)
+  if (force_path != 0) {
+    if (force_path != 1 && mode != MTRTQ_MODE_BF16)
       return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core kernels compute in MTRTQ_MODE_BF16 only");
-    if (g_opt_force_path == 3 && (M > 32 || p.n_tiles > kMaxSplitTiles))
+    if (force_path == 3 && (M > 32 || p.n_tiles > kMaxSplitTiles))
       return fail(MTRTQ_ERR_INVALID_ARG, "the stream-K kernel takes M <= 32 and N <= 131072");
-    path = g_opt_force_path;
+    path = force_path;
   }
   const bool gemm = path == 2;
 
@@ -347,7 +350,8 @@ int mtrtq_prepack(const int8_t* q_KN, int64_t K, int64_t N, void* packed, size_t
 
 int64_t mtrtq_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int mode) {
   Plan p;
-  if (plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p) != MTRTQ_OK) return -1;
+  if (plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p, g_opt_force_path) != MTRTQ_OK)
+    return -1;
   return (int64_t)p.total;
 }
 
@@ -360,7 +364,7 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   DeviceInfo d;
   if (int rc = check_device_sm100(&d)) return rc;
   Plan p;
-  if (int rc = plan_matmul(M, K, N, x_dtype, mode, d.sm_count, &p)) return rc;
+  if (int rc = plan_matmul(M, K, N, x_dtype, mode, d.sm_count, &p, g_opt_force_path)) return rc;
   if (!aligned(packed, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "packed weights must be 256-byte aligned");
   if (!aligned(scale, 4) || (bias && !aligned(bias, 4)) || !aligned(Y, 4))
     return fail(MTRTQ_ERR_ALIGNMENT, "scale, bias and Y must be 4-byte aligned");
@@ -434,7 +438,8 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
 int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info, int n_info) {
   if (!info || n_info < 6) return fail(MTRTQ_ERR_INVALID_ARG, "info needs 6 slots");
   Plan p;
-  if (int rc = plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p)) return rc;
+  if (int rc = plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p, g_opt_force_path))
+    return rc;
   info[0] = p.kind;  // 0 GEMV, 1 tile GEMM, 2 stream-K
   info[1] = p.tile_m;
   info[2] = p.m_tiles;

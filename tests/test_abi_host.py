@@ -126,7 +126,8 @@ def test_launch_without_device_fails_loudly():
 @pytest.mark.parametrize("M,K,N,mode,path", [
     (1, 768, 50257, "bf16", "stream_k_tc"), (8, 768, 768, "fp32", "gemv"),
     (8, 3072, 768, "bf16", "stream_k_tc"), (9, 768, 768, "bf16", "stream_k_tc"),
-    (64, 768, 3072, "bf16", "stream_k_tc"), (65, 768, 3072, "bf16", "gemm_tc"),
+    (32, 768, 3072, "bf16", "stream_k_tc"), (33, 768, 3072, "bf16", "gemm_tc"),
+    (64, 768, 3072, "bf16", "gemm_tc"),
     (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv"),
     (1, 768, 200000, "bf16", "gemm_tc"),
 ])
