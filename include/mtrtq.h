@@ -128,6 +128,31 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
                  const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N,
                  int mode, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Y = X x dequant(W) (+ bias) through the decode GEMV (CUDA cores, split-K), with
+ * the same arguments and results as mtrtq_matmul on its GEMV path, but without a
+ * caller workspace and without allocating anything.
+ *
+ * No counterpart in the reference (its CPU kernel needs no scratch). It is for
+ * callers that cannot allocate device memory at call time: a host runtime whose
+ * run() contract forbids allocation and whose arena was planned without room for
+ * this op's scratch, a plugin living inside a framework that owns every device
+ * allocation, or a real-time decode loop that must not risk the device-wide
+ * synchronization an allocation can cause.
+ *
+ * The scratch it uses instead is a fixed device array inside the library,
+ * MTRTQ_NOALLOC_SCRATCH_BYTES (8 MiB) on every GPU that loads the library, held
+ * until the process exits. Problems whose split-K scratch
+ * (mtrtq_workspace_bytes with MTRTQ_OPT_FORCE_PATH = 1) exceeds it are rejected
+ * with MTRTQ_ERR_WORKSPACE. The first call on a device looks up that device's
+ * array address (cudaGetSymbolAddress, with the device current); make that first
+ * call before any stream capture. Every call resets the array's split counters on
+ * `stream` before its kernel. All calls share the one array, so calls that overlap
+ * on the GPU (different streams, or other host threads) race: keep them ordered. */
+#define MTRTQ_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const void* packed,
+                              const float* scale, const float* bias, float* Y, int64_t ldy,
+                              int64_t M, int64_t K, int64_t N, int mode, void* stream);
+
 /* ---- options and diagnostics ----------------------------------------------------- */
 
 /* Process-wide options. Both change how a call is carried out, never its result

@@ -49,7 +49,10 @@ SIGNATURES = {
     "mtrtq_set_option": (_int, [_int, _i64]),
     "mtrtq_plan_info": (_int, [_i64, _i64, _i64, _int, _int, _vp, _int]),
     "mtrtq_read_status": (_int, [_vp]),
+    "mtrtq_matmul_gemv_noalloc": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                         _int, _vp]),
 }
+NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
 
 
 class MtrtqError(RuntimeError):

@@ -435,6 +435,68 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   return MTRTQ_OK;
 }
 
+}  // extern "C"
+
+namespace mtrtq {
+namespace {
+
+// Scratch of mtrtq_matmul_gemv_noalloc: split counters (first 4 KiB, zero at load)
+// then split partials. Host code may not use this name as a device address; the
+// address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MTRTQ_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// This device's address of g_noalloc_scratch (looked up on its first use here,
+// with the device current).
+int noalloc_scratch(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MTRTQ_OK;
+}
+
+}  // namespace
+}  // namespace mtrtq
+
+extern "C" {
+
+int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const void* packed,
+                              const float* scale, const float* bias, float* Y, int64_t ldy,
+                              int64_t M, int64_t K, int64_t N, int mode, void* stream) {
+  if (!X || !packed || !scale || !Y) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  if (ldx < K) return fail(MTRTQ_ERR_INVALID_ARG, "ldx (%lld) < K (%lld)", (long long)ldx, (long long)K);
+  if (ldy < N) return fail(MTRTQ_ERR_INVALID_ARG, "ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
+  DeviceInfo d;
+  if (int rc = check_device_sm100(&d)) return rc;
+  Plan p;
+  if (int rc = plan_matmul(M, K, N, x_dtype, mode, d.sm_count, &p, /*force_path=*/1)) return rc;
+  if (p.total > (size_t)MTRTQ_NOALLOC_SCRATCH_BYTES)
+    return fail(MTRTQ_ERR_WORKSPACE,
+                "problem needs %zu bytes of scratch; the no-allocation entry point holds %d",
+                p.total, MTRTQ_NOALLOC_SCRATCH_BYTES);
+  if (!aligned(packed, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "packed weights must be 256-byte aligned");
+  if (!aligned(scale, 4) || (bias && !aligned(bias, 4)) || !aligned(Y, 4))
+    return fail(MTRTQ_ERR_ALIGNMENT, "scale, bias and Y must be 4-byte aligned");
+  if (!aligned(X, 16)) return fail(MTRTQ_ERR_ALIGNMENT, "X must be 16-byte aligned");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(d.device, &scratch)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Counters must start at zero; a previous call leaves them at zero, but one that
+  // gave up on a timeout may not, so clear them (memset: no allocation).
+  cudaError_t e = cudaMemsetAsync(static_cast<char*>(scratch) + p.off_counters, 0, kCounterBytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "clear no-allocation counters");
+  e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, scratch, st);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+  return MTRTQ_OK;
+}
+
 int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info, int n_info) {
   if (!info || n_info < 6) return fail(MTRTQ_ERR_INVALID_ARG, "info needs 6 slots");
   Plan p;
