@@ -14,21 +14,21 @@
 // one fp32 partial per CTA that touches it; the last of those CTAs to finish (an
 // atomic ticket per tile) sums them in CTA order -- deterministic -- and writes Y.
 //
-// Units travel in pairs (units 2q, 2q+1 of a CTA: 16 KiB contiguous in memory):
-// one bulk copy, one mbarrier round and one commit per pair. Measured on B200,
-// a single thread issues a small (N <= 64) tcgen05.mma only every ~50 cycles and
-// each completed-barrier check or commit costs ~50-100 more, so the per-unit
-// bookkeeping of the two single-thread roles, not bandwidth, is what bounds a
-// skinny kernel; pairing halves it.
+// Units travel in batches of four (units 4b..4b+3 of a CTA: 32 KiB contiguous in
+// memory): one bulk copy, one mbarrier round and one commit per batch. Measured on
+// B200, a single thread issues a small (N <= 64) tcgen05.mma only every ~50-80
+// cycles, and a barrier wait with its tcgen05.fence costs ~400 cycles and a commit
+// ~100, so the single-thread roles' bookkeeping, not bandwidth, bounds a skinny
+// kernel; batching amortizes it over four units.
 //
 // Activations: with X_RES the whole [TM x K] activation matrix is rounded to bf16
 // once per CTA into shared memory (128-byte-swizzled K-major tiles, one per 64-k
-// block) by the epilogue warps before their first epilogue; otherwise every unit
+// block) by the twelve worker warps before their main loops; otherwise every unit
 // brings its own activation tile by TMA (fp32 rounded to bf16 by the dequantizers,
 // or bf16 straight into the swizzled tile).
 //
 // Warp roles (14 warps):
-//   warp 0        producer: per pair, the weight bulk copy (and, without X_RES, the
+//   warp 0        producer: per batch, the weight bulk copy (and, without X_RES, the
 //                 activation tiles) into a ring of shared-memory stages;
 //   warp 1        allocates TMEM; one lane issues tcgen05.mma (kind::f16, A from
 //                 TMEM, B = activations from shared memory, four independent
@@ -36,7 +36,7 @@
 //   warps 2..5    dequantizer group 0 (even units), warps 6..9 group 1 (odd units):
 //                 each thread owns one channel row, converts its 64 int8 weights
 //                 exactly to bf16 and stores them into a TMEM A stage (tcgen05.st);
-//   warps 10..13  (X_RES) stage the activations, then the epilogue: tcgen05.ld of a
+//   warps 10..13  the epilogue: tcgen05.ld of a
 //                 finished accumulator (double-buffered in TMEM, so the next
 //                 segment's MMAs proceed meanwhile), scale and bias into Y, or an
 //                 fp32 partial plus the ticketed reduction.
@@ -67,7 +67,8 @@ struct SkinnyParams {
 };
 
 constexpr int kSkinnyThreads = 14 * 32;
-constexpr int kSkinnyAStages = 4;             // TMEM A stages: two pairs in flight
+constexpr int kSkinnyBatch = 4;               // units per producer/MMA round (P)
+constexpr int kSkinnyAStages = 2 * kSkinnyBatch;  // TMEM A stages: two batches in flight
 constexpr int kSkinnyXResBytes = 96 * 1024;   // largest resident activation matrix
 
 template <int TM, bool X_F32, bool X_RES>
@@ -78,16 +79,16 @@ struct SkinnyCfg {
   static constexpr int STAGE = W_BYTES + (X_RES ? 0 : XB_BYTES + XR_BYTES);
   static constexpr int X_REGION = X_RES ? kSkinnyXResBytes : 0;
   static constexpr int STAGES_RAW = (200 * 1024 - X_REGION) / STAGE;
-  static constexpr int STAGES = (STAGES_RAW > 16 ? 16 : STAGES_RAW) & ~1;  // even, <= 16
-  static constexpr int SP = STAGES / 2;                                // pair slots
+  static constexpr int STAGES = (STAGES_RAW > 16 ? 16 : STAGES_RAW) / kSkinnyBatch * kSkinnyBatch;
+  static constexpr int SB = STAGES / kSkinnyBatch;                     // batch slots
   // Per stage: [W 8 KiB][bf16 B tile][raw fp32 tile]; with X_RES a stage is just
-  // the 8 KiB of weights, so the two stages of a pair take one 16 KiB copy.
+  // the 8 KiB of weights, so the four stages of a batch take one 32 KiB copy.
   static constexpr int OFF_RING = X_REGION;
   static constexpr int OFF_W = 0;
   static constexpr int OFF_XB = W_BYTES;
   static constexpr int OFF_XR = W_BYTES + XB_BYTES;
   static constexpr int OFF_BAR = OFF_RING + STAGES * STAGE;
-  static constexpr int NUM_BARS = 2 * SP + 2 + 2 + 2 + 2;
+  static constexpr int NUM_BARS = 2 * SB + 2 + 2 + 2 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
   // Independent accumulation chains: the k-th MMA (k = 0..3) of every unit of a
@@ -100,7 +101,7 @@ struct SkinnyCfg {
   static constexpr int NEED_COLS = ACC_COL + 2 * ACC_BUF;
   static constexpr int TMEM_COLS = NEED_COLS <= 256 ? 256 : 512;
   static_assert(STAGE % 1024 == 0 && X_REGION % 1024 == 0, "1024-byte aligned tiles");
-  static_assert(STAGES >= 2 * kSkinnyAStages, "the ring must hold more pairs than the A stages");
+  static_assert(SB >= 2, "the ring must hold two batches");
   static_assert(TM % 16 == 0 && TM >= 16 && TM <= 32, "TM in {16, 32}");
   static_assert(NEED_COLS <= 512, "TMEM has 512 columns");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
@@ -159,22 +160,23 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     skinny_q8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const SkinnyParams p) {
   using C = SkinnyCfg<TM, X_F32, X_RES>;
   constexpr int S = C::STAGES;
-  constexpr int SP = C::SP;
+  constexpr int SB = C::SB;
   constexpr int SA = kSkinnyAStages;
+  constexpr int P = kSkinnyBatch;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* ring = smem + C::OFF_RING;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  //   full[q % SP]     pair q's copies landed (producer tx)
-  //   done[q % SP]     pair q's MMAs completed (one commit): frees both units'
+  //   full[b % SB]     batch b's copies landed (producer tx)
+  //   done[b % SB]     batch b's MMAs completed (one commit): frees its units'
   //                    shared-memory stages (the dequantizers finished reading them
   //                    before signalling a_full) and their TMEM A stages
-  //   a_full[q % 2]    pair q's A operands written (4 warps of each group)
-  //   x_ready          resident activations staged (4 epilogue warps)
-  uint64_t* full = bars;                   // [SP]
-  uint64_t* done = bars + SP;              // [SP]
-  uint64_t* a_full = bars + 2 * SP;        // [2]
+  //   a_full[b % 2]    batch b's A operands written (4 arrivals per unit)
+  //   x_ready          resident activations staged (12 worker warps)
+  uint64_t* full = bars;                   // [SB]
+  uint64_t* done = bars + SB;              // [SB]
+  uint64_t* a_full = bars + 2 * SB;        // [2]
   uint64_t* acc_full = a_full + 2;         // [2] 1 commit
   uint64_t* acc_empty = acc_full + 2;      // [2] 4 epilogue warps
   uint64_t* x_ready = acc_empty + 2;       // [1]
@@ -192,19 +194,19 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   const long long u0 = (long long)c * U / G;
   const long long u1 = (long long)(c + 1) * U / G;
   const int n_units = (int)(u1 - u0);
-  const int n_pairs = (n_units + 1) >> 1;
+  const int n_batches = (n_units + P - 1) / P;
 
   if (tid == 0) {
-    for (int s = 0; s < SP; ++s) {
+    for (int s = 0; s < SB; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&done[s], 1);
     }
-    for (int s = 0; s < 2; ++s) mbar_init(&a_full[s], 8);
+    for (int s = 0; s < 2; ++s) mbar_init(&a_full[s], 4 * P);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
     }
-    mbar_init(x_ready, 4);
+    mbar_init(x_ready, 12);
     mbar_init(drain, 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -219,57 +221,86 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
 
+  // X_RES: the 12 worker warps (w = 0..11) round the whole [TM x K_pad] activation
+  // matrix to bf16 into one swizzled K-major tile per 64-k block (chunk (kb, row, ch)
+  // holds k = kb*64 + ch*8 .. +7), four chunks' loads in flight per thread.
+  auto stage_x = [&](int w) {
+    const int et = w * 32 + lane;                 // 0..383
+    const int chunks = p.KB * TM * 8;
+    for (int c0 = et; c0 < chunks; c0 += 4 * 384) {
+      uint4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int cidx = c0 + j * 384;
+        const int ch = cidx & 7, row = (cidx >> 3) % TM, kb = cidx / (8 * TM);
+        v[j] = cidx < chunks ? sk_load_x8(p, row, kb * kBlockK + ch * 8) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int cidx = c0 + j * 384;
+        if (cidx < chunks) {
+          const int ch = cidx & 7, row = (cidx >> 3) % TM, kb = cidx / (8 * TM);
+          *reinterpret_cast<uint4*>(smem + kb * C::XB_BYTES + row * 128 + ((ch ^ (row & 7)) << 4)) =
+              v[j];
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(x_ready);
+  };
+
   if (warp == 0) {
-    // ---------------- producer: one round per pair ----------------
+    // ---------------- producer: one round per batch ----------------
     if (lane == 0) {
-      int issued = 0;  // pairs
+      int issued = 0;  // batches
       int kb = (int)(u0 % p.KB);
-      for (int q = 0; q < n_pairs; ++q) {
-        const int pq = q % SP;
-        if (!mbar_wait_bounded(&done[pq], ((q / SP) & 1) ^ 1, s_abort, p.status)) break;
-        const int i0 = 2 * q;
-        const int nu = min(2, n_units - i0);
+      for (int b = 0; b < n_batches; ++b) {
+        const int sb = b % SB;
+        if (!mbar_wait_bounded(&done[sb], ((b / SB) & 1) ^ 1, s_abort, p.status)) break;
+        const int i0 = P * b;
+        const int nu = min(P, n_units - i0);
         uint8_t* st = ring + (i0 % S) * C::STAGE;
         const uint32_t x_bytes = X_RES ? 0u : (uint32_t)(X_F32 ? C::XR_BYTES : C::XB_BYTES);
-        mbar_arrive_expect_tx(&full[pq], (uint32_t)nu * (C::W_BYTES + x_bytes));
+        mbar_arrive_expect_tx(&full[sb], (uint32_t)nu * (C::W_BYTES + x_bytes));
         if (X_RES) {
-          // The two units' weights are adjacent in memory and in the ring.
+          // The batch's weights are adjacent in memory and in the ring.
           bulk_g2s(st + C::OFF_W, p.W + (u0 + i0) * (long long)C::W_BYTES,
-                   (uint32_t)nu * C::W_BYTES, &full[pq]);
+                   (uint32_t)nu * C::W_BYTES, &full[sb]);
         } else {
           for (int j = 0; j < nu; ++j) {
             uint8_t* sj = st + j * C::STAGE;
             bulk_g2s(sj + C::OFF_W, p.W + (u0 + i0 + j) * (long long)C::W_BYTES, C::W_BYTES,
-                     &full[pq]);
-            tma_load_2d(sj + (X_F32 ? C::OFF_XR : C::OFF_XB), &xmap, kb * kBlockK, 0, &full[pq]);
+                     &full[sb]);
+            tma_load_2d(sj + (X_F32 ? C::OFF_XR : C::OFF_XB), &xmap, kb * kBlockK, 0, &full[sb]);
             if (++kb == p.KB) kb = 0;
           }
         }
         ++issued;
       }
-      for (int j = max(0, issued - SP); j < issued; ++j)
-        sk_drain(&full[j % SP], (j / SP) & 1, p.status);
+      for (int j = max(0, issued - SB); j < issued; ++j)
+        sk_drain(&full[j % SB], (j / SB) & 1, p.status);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: one round per pair ----------------
+    // ---------------- MMA issuer: one round per batch ----------------
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
       int seg = -1;
       bool ok = true;
       int kb = (int)(u0 % p.KB);
       if (X_RES && !mbar_wait_bounded(x_ready, 0, s_abort, p.status)) ok = false;
-      for (int q = 0; q < n_pairs && ok; ++q) {
-        if (!mbar_wait_bounded(&a_full[q & 1], (q >> 1) & 1, s_abort, p.status)) { ok = false; break; }
+      for (int b = 0; b < n_batches && ok; ++b) {
+        if (!mbar_wait_bounded(&a_full[b & 1], (b >> 1) & 1, s_abort, p.status)) { ok = false; break; }
         // bf16 activation tiles arrive by TMA straight into the B tile: observe
         // those copies. (fp32 tiles are written by the dequantizers before a_full.)
         if (!X_RES && !X_F32 &&
-            !mbar_wait_bounded(&full[q % SP], (q / SP) & 1, s_abort, p.status)) {
+            !mbar_wait_bounded(&full[b % SB], (b / SB) & 1, s_abort, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int i_end = min(2 * q + 2, n_units);
-        for (int i = 2 * q; i < i_end; ++i, kb = (kb + 1 == p.KB) ? 0 : kb + 1) {
+        const int i_end = min(P * b + P, n_units);
+        for (int i = P * b; i < i_end; ++i, kb = (kb + 1 == p.KB) ? 0 : kb + 1) {
           const bool first = (i == 0) || kb == 0;
           const bool last = (i == n_units - 1) || kb == p.KB - 1;
           if (first) {
@@ -292,7 +323,7 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
           if (last) umma_commit(&acc_full[seg & 1]);
         }
         if (!ok) break;
-        umma_commit(&done[q % SP]);
+        umma_commit(&done[b % SB]);
       }
       if (!ok) {
         // Let every MMA already issued finish before TMEM is freed.
@@ -308,9 +339,10 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     const int r = q4 * 32 + lane;          // channel row in the tile
     const int gt = (warp - 2 - 4 * group) * 32 + lane;  // 0..127 within the group
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    if (X_RES) stage_x(warp - 2);
     for (int i = group; i < n_units; i += 2) {
-      const int s = i % S, sa = i % SA, q = i >> 1;
-      if (!sk_warp_wait(&full[q % SP], (q / SP) & 1, s_abort, p.status)) break;
+      const int s = i % S, sa = i % SA, b = i / P;
+      if (!sk_warp_wait(&full[b % SB], (b / SB) & 1, s_abort, p.status)) break;
       uint8_t* st = ring + s * C::STAGE;
       uint4 wv[4];
 #pragma unroll
@@ -346,34 +378,23 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         i8x4_to_bf16x4(wv[j].z, a[8 * j + 4], a[8 * j + 5]);
         i8x4_to_bf16x4(wv[j].w, a[8 * j + 6], a[8 * j + 7]);
       }
-      // A stage sa was last used by unit i - SA (pair q - 2): free once that pair is done.
-      if (q >= 2 && !sk_warp_wait(&done[(q - 2) % SP], ((q - 2) / SP) & 1, s_abort, p.status)) break;
+      // A stage sa was last used by unit i - SA (batch b - 2): free once that batch is done.
+      if (b >= 2 && !sk_warp_wait(&done[(b - 2) % SB], ((b - 2) / SB) & 1, s_abort, p.status)) break;
       tmem_st_32x32b_x32(tmem_base + lane_off + sa * 32, a);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      // A pair with one unit (the CTA's last, odd count) gets group 0's arrival twice.
-      if (lane == 0) mbar_arrive_cnt(&a_full[q & 1], (i == n_units - 1 && !(i & 1)) ? 2u : 1u);
+      // Four arrivals per unit; the CTA's last unit also stands in for the units its
+      // (short) final batch lacks, so every batch completes a_full with 4*P.
+      if (lane == 0)
+        mbar_arrive_cnt(&a_full[b & 1], i == n_units - 1 ? 1u + (uint32_t)(P * (b + 1) - n_units) : 1u);
     }
   } else {
     // ---------------- (X_RES: activation staging, then) epilogue ----------------
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    if (X_RES) {
-      // Round the whole [TM x K_pad] activation matrix to bf16 into one swizzled
-      // K-major tile per 64-k block: chunk (kb, row, ch) holds k = kb*64 + ch*8 .. +7.
-      const int et = (warp - 10) * 32 + lane;     // 0..127
-      const int chunks = p.KB * TM * 8;
-      for (int cidx = et; cidx < chunks; cidx += 128) {
-        const int ch = cidx & 7, row = (cidx >> 3) % TM, kb = cidx / (8 * TM);
-        const uint4 v = sk_load_x8(p, row, kb * kBlockK + ch * 8);
-        *reinterpret_cast<uint4*>(smem + kb * C::XB_BYTES + row * 128 + ((ch ^ (row & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(x_ready);
-    }
+    if (X_RES) stage_x(warp - 2);
     int seg = -1;
     long long u = u0;
     while (u < u1) {
