@@ -313,14 +313,9 @@ __global__ void __launch_bounds__(192, 1)
 template <int TM, bool A_TMEM, int STAGES>
 static cudaError_t launch_cfg(const GemmParams& gp, const CUtensorMap& xmap, cudaStream_t st) {
   using C = GemmCfg<TM, A_TMEM, STAGES>;
-  static bool attr_set = false;  // per instantiation; set before the first launch
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_q8_tc_kernel<TM, A_TMEM, STAGES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemm_q8_tc_kernel<TM, A_TMEM, STAGES>),
+                                         C::SMEM_BYTES))
+    return e;
   const dim3 grid((unsigned)gp.m_tiles, (unsigned)gp.n_tiles, (unsigned)gp.splits);
   gemm_q8_tc_kernel<TM, A_TMEM, STAGES><<<grid, 192, C::SMEM_BYTES, st>>>(xmap, gp);
   return cudaGetLastError();

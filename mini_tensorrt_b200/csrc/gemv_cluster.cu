@@ -1,0 +1,438 @@
+// Decode GEMV for the INT8 weight-only MatMul, M <= 8: split-K inside a thread-block
+// cluster, reduced through distributed shared memory.
+//
+// Replaces, for the decode sites, the reference's scalar MatMulQ loop
+// (src/ops/kernels_matmul.cpp:66-73) and the KV-cache decoder's fp32 GEMV
+// (tools/run_gpt2.cpp:125-132, :189).
+//
+// Work: one cluster of CS CTAs per 128-channel tile; CTA rank s takes the s-th of
+// CS equal ranges of the tile's 64-k units (8 KiB each, contiguous in the packed
+// layout). A producer warp streams the CTA's units into a ring of shared memory
+// stages with 1-D bulk async copies (TMA), so the bytes in flight are bounded by
+// shared memory, not registers.
+//
+// Arithmetic: the int8 weights are used as they are, as the A operand of integer
+// warp MMAs (m16n8k32, s8 x s8 -> s32, exact). Activations are re-expressed, per
+// CTA and token m, as three int8 digits over the CTA's k range:
+//     x = (s_m / 127) * (d0 + d1 / 2^7 + d2 / 2^14),   s_m = max |x[m, k range]|,
+// d0 in [-127, 127], d1, d2 in [-64, 64], so each x is represented to within
+// 2^-15 * s_m / 127 (about 2^-22 of the largest activation of the range; fp32
+// itself carries 24 bits). Each digit plane is one MMA B operand (8 columns =
+// the tokens); the three int32 accumulators are combined in fp32 at the end:
+//     partial = (s_m / 127) * (acc0 + acc1 / 2^7 + acc2 / 2^14).
+// In MTRTQ_MODE_BF16, fp32 activations are first rounded to bf16. Non-finite
+// activations make the token's outputs NaN.
+//
+// K order: an MMA sums over k in any order, so each lane loads the 16 bytes of
+// one 16-k slab row and feeds them to two k32 steps; the activation digits are
+// laid out with the same permutation.
+//
+// Partial sums never leave the SM cluster: each warp owns 16 channel rows, the CS
+// ranks' partials are exchanged through distributed shared memory after a cluster
+// barrier, and rank s sums rows [s*128/CS, (s+1)*128/CS) over the ranks in rank
+// order -- a fixed order, so results do not depend on timing -- then applies
+// y = sum * scale (+ bias), multiply then add, the reference's MatMulQ-then-Add
+// order. No workspace, no atomics, no device-wide fences.
+//
+// Every mbarrier wait is bounded: a wait that gives up records MTRTQ_ERR_TIMEOUT
+// in the device status word and stops the CTA's loops; the producer still waits
+// (bounded) for the copies it issued before the CTA leaves.
+#include "q8_common.cuh"
+#include "q8_internal.h"
+
+namespace mtrtq {
+
+namespace {
+
+constexpr int kClWarps = 8;                // consumers: one 16-row group each
+constexpr int kClThreads = kClWarps * 32;  // consumer threads
+constexpr int kClBlock = kClThreads + 32;  // + the producer warp
+constexpr uint32_t kUnitBytes = 8192;      // 64 k x 128 channels of int8
+constexpr int kDigits = 3;
+
+struct GemvClParams {
+  const void* X;
+  int64_t ldx;
+  const char* W;   // packed: tile t, unit u (64 k) at byte (t * KB + u) * 8192
+  const float* scale;
+  const float* bias;
+  float* Y;
+  int64_t ldy;
+  int M, K, N;
+  int KB;          // 64-k units per tile
+  int stages;      // shared memory ring stages (2..kGemvClMaxStages)
+  unsigned* status;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster rank `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// d[0..3] += A(16x32 s8) * B(32x8 s8), int32 accumulate (exact).
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Four consecutive activations of row m from k (zeros past K) as fp32; a vector
+// load when the row stride allows it and all four lie inside the row.
+template <bool X_BF16>
+__device__ __forceinline__ float4 cl_load_x4(const GemvClParams& p, int m, int k, bool vec) {
+  const int64_t off = (int64_t)m * p.ldx + k;
+  if (X_BF16) {
+    const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.X) + off;
+    if (vec && k + 3 < p.K) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(x));
+      return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                         __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+    }
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = k + i < p.K ? __bfloat162float(x[i]) : 0.0f;
+    return make_float4(v[0], v[1], v[2], v[3]);
+  }
+  const float* x = static_cast<const float*>(p.X) + off;
+  if (vec && k + 3 < p.K) return __ldg(reinterpret_cast<const float4*>(x));
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = k + i < p.K ? __ldg(x + i) : 0.0f;
+  return make_float4(v[0], v[1], v[2], v[3]);
+}
+
+template <bool ROUND>
+__device__ __forceinline__ float4 cl_round(float4 v) {
+  if (ROUND) {
+    v.x = round_bf16(v.x);
+    v.y = round_bf16(v.y);
+    v.z = round_bf16(v.z);
+    v.w = round_bf16(v.w);
+  }
+  return v;
+}
+
+// Three int8 digits of v (|v| <= 127): v ~ d0 + d1 / 2^7 + d2 / 2^14. Each
+// residual is exact in fp32 (it is the difference of two nearby values, then
+// scaled by a power of two); the last digit's rounding leaves |error| <= 2^-15.
+__device__ __forceinline__ void cl_digits(float v, int& d0, int& d1, int& d2) {
+  const float r0 = rintf(v);
+  const float v1 = (v - r0) * 128.0f;
+  const float r1 = rintf(v1);
+  const float r2 = rintf((v1 - r1) * 128.0f);
+  d0 = (int)r0;
+  d1 = (int)r1;
+  d2 = (int)r2;
+}
+
+// Activation digits over the CTA's units [u0, u0 + nu): plane d at xd + d * plane,
+// unit u, token m, k at ((u * mt + m) * 64 + k). Token m is staged by the consumer
+// warps w with w % mt == m, each taking an equal share of the range's 4-element
+// groups. s_max[m] gets max |x| over the range (atomically, as ordered bits) and
+// s_bad[m] flags a non-finite value. The first batch of each lane stays in
+// registers across the barrier that completes the maxima; longer shares read the
+// rest again (from the caches the first pass filled).
+template <bool X_BF16, bool ROUND>
+__device__ __forceinline__ void cl_stage_digits(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
+                                                int* s_bad, int u0, int nu, int warp, int lane) {
+  constexpr int kBatch = 6;  // 4-element loads in flight per lane
+  const int mt = p.M;
+  const int m = warp % mt;
+  const int share_warps = (kClWarps - 1 - m) / mt + 1;  // warps staging token m
+  const int j = warp / mt;
+  const int n4 = nu * 16;  // 4-element groups of the range
+  const int gbeg = (int)((int64_t)j * n4 / share_warps), gend = (int)((int64_t)(j + 1) * n4 / share_warps);
+  const int kbase = u0 * 64;
+  const bool vec = (p.ldx & 3) == 0;
+
+  float4 keep[kBatch];
+  float mx = 0.0f;
+  bool bad = false;
+  for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
+    float4 v[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int g = g0 + b * 32;
+      v[b] = g < gend ? cl_round<ROUND>(cl_load_x4<X_BF16>(p, m, kbase + g * 4, vec))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const float a = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
+      bad |= !(a <= 3.402823466e38f);  // NaN or infinity
+      mx = fmaxf(mx, a);
+    }
+    if (g0 == gbeg + lane) {
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) keep[b] = v[b];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    bad |= __shfl_xor_sync(0xffffffffu, (int)bad, o) != 0;
+  }
+  if (lane == 0) {
+    atomicMax(&s_max[m], __float_as_int(mx));  // mx >= 0: bit order is value order
+    if (bad) atomicOr(&s_bad[m], 1);
+  }
+  named_bar_sync(1, kClThreads);
+  const float smax = __int_as_float(s_max[m]);
+  const float inv = (smax > 0.0f && !s_bad[m]) ? 127.0f / smax : 0.0f;
+
+  for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
+    float4 v[kBatch];
+    if (g0 == gbeg + lane) {
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) v[b] = keep[b];
+    } else {
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int g = g0 + b * 32;
+        v[b] = g < gend ? cl_round<ROUND>(cl_load_x4<X_BF16>(p, m, kbase + g * 4, vec))
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int g = g0 + b * 32;
+      if (g < gend) {
+        int a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
+        cl_digits(v[b].x * inv, a0, a1, a2);
+        cl_digits(v[b].y * inv, b0, b1, b2);
+        cl_digits(v[b].z * inv, c0, c1, c2);
+        cl_digits(v[b].w * inv, e0, e1, e2);
+        const int u = g >> 4, k = (g & 15) * 4;
+        const int off = (u * mt + m) * 64 + k;
+        *reinterpret_cast<uint32_t*>(xd + off) =
+            (uint32_t)(a0 & 255) | ((uint32_t)(b0 & 255) << 8) | ((uint32_t)(c0 & 255) << 16) |
+            ((uint32_t)(e0 & 255) << 24);
+        *reinterpret_cast<uint32_t*>(xd + plane + off) =
+            (uint32_t)(a1 & 255) | ((uint32_t)(b1 & 255) << 8) | ((uint32_t)(c1 & 255) << 16) |
+            ((uint32_t)(e1 & 255) << 24);
+        *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) =
+            (uint32_t)(a2 & 255) | ((uint32_t)(b2 & 255) << 8) | ((uint32_t)(c2 & 255) << 16) |
+            ((uint32_t)(e2 & 255) << 24);
+      }
+    }
+  }
+}
+
+template <bool X_BF16, bool ROUND>
+__global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kernel(const GemvClParams p) {
+  // Shared memory: ring [stages][8 KiB] (the exchange buffer part[8][128] fp32
+  // reuses it at the end) | full[8], empty[8] barriers | digits [3][nu][M][64] s8.
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_abort;
+  __shared__ int s_max[8], s_bad[8];  // per token: max |x| (fp32 bits), non-finite flag
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const int CS = (int)gridDim.x;  // the cluster spans x
+  const int t = blockIdx.y;
+  const int nst = p.stages;
+  const int mt = p.M;
+
+  // This CTA's units [u0, u1) of tile t.
+  const int u0 = (int)((int64_t)rank * p.KB / CS), u1 = (int)((int64_t)(rank + 1) * p.KB / CS);
+  const int nu = u1 - u0;
+  unsigned char* ring = smem;
+  const size_t ring_bytes = max((size_t)nst * kUnitBytes, (size_t)8 * 128 * sizeof(float));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_bytes);
+  uint64_t* empty = full + kGemvClMaxStages;
+  int8_t* xd = reinterpret_cast<int8_t*>(empty + kGemvClMaxStages);
+  const int plane = nu * mt * 64;
+
+  if (tid == 0) {
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kClWarps);
+    }
+    s_abort = 0;
+    for (int i = 0; i < 8; ++i) s_max[i] = s_bad[i] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  int acc[kDigits][4];
+#pragma unroll
+  for (int d = 0; d < kDigits; ++d)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[d][j] = 0;
+
+  if (warp == kClWarps) {
+    // Producer: one thread keeps up to nst units in flight.
+    if (lane == 0) {
+      const char* src = p.W + ((int64_t)t * p.KB + u0) * kUnitBytes;
+      int issued = 0, st = 0;
+      uint32_t ph = 0;
+      for (int u = 0; u < nu; ++u) {
+        if (u >= nst && !mbar_wait_bounded(&empty[st], ph ^ 1u, &s_abort, p.status)) break;
+        mbar_arrive_expect_tx(&full[st], kUnitBytes);
+        bulk_g2s(ring + (size_t)st * kUnitBytes, src + (int64_t)u * kUnitBytes, kUnitBytes, &full[st]);
+        ++issued;
+        if (++st == nst) { st = 0; ph ^= 1u; }
+      }
+      // Every issued copy lands before the CTA moves on (and, on an abort, leaves).
+      volatile int no_abort = 0;
+      for (int u = issued > nst ? issued - nst : 0; u < issued; ++u)
+        mbar_wait_bounded(&full[u % nst], (uint32_t)(u / nst) & 1u, &no_abort, p.status);
+    }
+    __syncwarp();
+  } else {
+    // Consumers: activation digits first (the weights are already in flight).
+    cl_stage_digits<X_BF16, ROUND>(p, xd, plane, s_max, s_bad, u0, nu, warp, lane);
+    named_bar_sync(1, kClThreads);
+    // Warp w: channel rows w*16 + g and w*16 + g + 8 (g = lane / 4); lane's slab c
+    // (= lane % 4) of each unit. Step i of a unit takes words 2i, 2i+1 of the
+    // lane's 16-byte slab rows: k = 16c + 8i + 0..7.
+    const int g = lane >> 2, c = lane & 3;
+    const int ra = warp * 16 + g;
+    const bool has_x = g < mt;
+    const int8_t* xg = xd + g * 64 + c * 16;
+    int st = 0;
+    uint32_t ph = 0;
+    for (int u = 0; u < nu; ++u) {
+      if (!mbar_wait_bounded(&full[st], ph, &s_abort, p.status)) break;
+      const uint4* w = reinterpret_cast<const uint4*>(ring + (size_t)st * kUnitBytes);
+      const uint4 wa = w[c * 128 + ra];
+      const uint4 wb = w[c * 128 + ra + 8];
+      uint4 xv[kDigits];
+#pragma unroll
+      for (int d = 0; d < kDigits; ++d)
+        xv[d] = has_x ? *reinterpret_cast<const uint4*>(xg + d * plane + u * mt * 64)
+                      : make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);  // the weights are in registers
+#pragma unroll
+      for (int d = 0; d < kDigits; ++d) {
+        mma_s8(acc[d], wa.x, wb.x, wa.y, wb.y, xv[d].x, xv[d].y);
+        mma_s8(acc[d], wa.z, wb.z, wa.w, wb.w, xv[d].z, xv[d].w);
+      }
+      if (++st == nst) { st = 0; ph ^= 1u; }
+    }
+  }
+  __syncthreads();  // the ring is idle: every copy has landed and been read
+
+  // Accumulators -> fp32 partials part[token][row] in this CTA's shared memory.
+  // Element j of a warp's C fragment: row ra (j < 2) or ra + 8, token 2c + (j & 1).
+  float* part = reinterpret_cast<float*>(smem);  // [8][128], read by the other ranks
+  if (warp < kClWarps) {
+    const int g = lane >> 2, c = lane & 3;
+    const int ra = warp * 16 + g;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = 2 * c + (j & 1), row = ra + (j >> 1) * 8;
+      float v = 0.0f;
+      if (m < mt) {
+        const float sm = s_bad[m] ? __int_as_float(0x7fc00000) : __int_as_float(s_max[m]) * (1.0f / 127.0f);
+        v = sm * ((float)acc[0][j] + (float)acc[1][j] * (1.0f / 128.0f) +
+                  (float)acc[2][j] * (1.0f / 16384.0f));
+      }
+      part[m * 128 + row] = v;
+    }
+  }
+
+  // Rank s finishes rows [s * 128 / CS, (s + 1) * 128 / CS), summing the ranks'
+  // partials in rank order.
+  if (CS > 1) cluster_sync_all();
+  else __syncthreads();
+  const int r0 = (int)(rank * 128 / CS), r1 = (int)((rank + 1) * 128 / CS);
+  const int nr = r1 - r0;
+  for (int e = tid; e < nr * mt; e += kClBlock) {
+    const int m = e / nr, r = r0 + (e - m * nr);
+    const int n = t * kTileN + r;
+    float sum;
+    if (CS > 1) {
+      sum = 0.0f;
+      for (int q = 0; q < CS; ++q) sum += ld_dsmem_f32(dsmem_addr(part + m * 128 + r, (uint32_t)q));
+    } else {
+      sum = part[m * 128 + r];
+    }
+    if (n < p.N) {
+      float y = __fmul_rn(sum, p.scale[n]);
+      if (p.bias) y = __fadd_rn(y, p.bias[n]);
+      p.Y[(int64_t)m * p.ldy + n] = y;
+    }
+  }
+  // No CTA leaves while another rank may still read its shared memory.
+  if (CS > 1) cluster_sync_all();
+}
+
+template <bool X_BF16, bool ROUND>
+cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, cudaStream_t st) {
+  auto kern = gemv_cluster_kernel<X_BF16, ROUND>;
+  if (smem > 48 * 1024) {
+    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), (int)kGemvClSmemCap))
+      return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cs, (unsigned)n_tiles, 1);
+  cfg.blockDim = dim3(kClBlock, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, gp);
+}
+
+}  // namespace
+
+size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages) {
+  const int64_t nu = (units + cs - 1) / cs;  // the largest CTA range
+  const size_t ring = (size_t)stages * kUnitBytes;
+  const size_t exch = (size_t)8 * 128 * sizeof(float);  // reuses the ring
+  return (ring > exch ? ring : exch) + 2 * kGemvClMaxStages * sizeof(uint64_t) +
+         (size_t)kDigits * (size_t)nu * (size_t)m * 64;
+}
+
+cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,
+                                const void* packed, const float* scale, const float* bias, float* Y,
+                                int64_t ldy, unsigned* status, cudaStream_t st) {
+  GemvClParams gp;
+  gp.X = X;
+  gp.ldx = ldx;
+  gp.W = static_cast<const char*>(packed);
+  gp.scale = scale;
+  gp.bias = bias;
+  gp.Y = Y;
+  gp.ldy = ldy;
+  gp.M = (int)p.M;
+  gp.K = (int)p.K;
+  gp.N = (int)p.N;
+  gp.KB = p.kunits;
+  gp.stages = p.stages;
+  gp.status = status;
+  const size_t smem = gemv_cluster_smem_bytes((int)p.M, p.kunits, p.splits, p.stages);
+  if (x_dtype == 1) return cl_launch<true, false>(gp, p.splits, p.n_tiles, smem, st);
+  if (p.round_x) return cl_launch<false, true>(gp, p.splits, p.n_tiles, smem, st);
+  return cl_launch<false, false>(gp, p.splits, p.n_tiles, smem, st);
+}
+
+}  // namespace mtrtq

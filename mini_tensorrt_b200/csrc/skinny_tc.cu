@@ -518,13 +518,9 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
 template <int TM, bool X_F32, bool X_RES>
 static cudaError_t sk_launch(const SkinnyParams& sp, const CUtensorMap& xmap, cudaStream_t st) {
   using C = SkinnyCfg<TM, X_F32, X_RES>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(skinny_q8_tc_kernel<TM, X_F32, X_RES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(skinny_q8_tc_kernel<TM, X_F32, X_RES>),
+                                         C::SMEM_BYTES))
+    return e;
   skinny_q8_tc_kernel<TM, X_F32, X_RES><<<sp.grid, kSkinnyThreads, C::SMEM_BYTES, st>>>(xmap, sp);
   return cudaGetLastError();
 }

@@ -145,7 +145,7 @@ def test_every_path_agrees(cuda_device, M):
     q, s = oracle.quantize_per_channel(W)
     X = wl.activations(M, K, 6)
     outs = []
-    for path in ((1, 2, 3) if M <= 32 else (1, 2)):
+    for path in ((1, 2, 3, 4, 5) if M <= 8 else (1, 2, 3) if M <= 32 else (1, 2)):
         matmulq.set_option(_lib.OPT_FORCE_PATH, path)
         try:
             outs.append(run(X, q, s, "bf16"))
@@ -286,3 +286,53 @@ def test_stream_k_partitions(cuda_device, M, K, N):
     Y = run(X, q, s, "bf16", bias=b)
     assert matmulq.plan_info(M, K, N)["path"] == "stream_k_tc"
     check(Y, X, q, s, "bf16", bias=b, tc=True)
+
+
+GSK_CASES = [(1, 64, 128), (3, 64, 50257), (8, 12288, 256), (2, 4096, 14336), (1, 768, 50257),
+             (5, 64 * 23, 128 * 7), (7, 12000, 100), (8, 4096, 1000), (4, 100, 300), (6, 77, 129)]
+
+
+DECODE_PATHS = {4: "stream_k_gemv", 5: "cluster_gemv"}
+
+
+@pytest.mark.parametrize("M,K,N", GSK_CASES, ids=[f"{M}x{K}x{N}" for M, K, N in GSK_CASES])
+@pytest.mark.parametrize("mode", ["bf16", "fp32"])
+@pytest.mark.parametrize("path", sorted(DECODE_PATHS), ids=list(DECODE_PATHS.values()))
+def test_decode_gemv_partitions(cuda_device, M, K, N, mode, path):
+    """The CUDA-core decode GEMVs: one unit per CTA, tiles spread over many CTAs,
+    several tiles per CTA, ragged K and N, clusters of 1 to 8 CTAs."""
+    W = wl.weights(K, N, 61)
+    q, s = matmulq.quantize_per_channel(W)
+    X = wl.activations(M, K, 62)
+    b = wl.bias(N, 63)
+    matmulq.set_option(_lib.OPT_FORCE_PATH, path)
+    try:
+        assert matmulq.plan_info(M, K, N, mode=mode)["path"] == DECODE_PATHS[path]
+        Y = run(X, q, s, mode, bias=b)
+        Y2 = run(X, q, s, mode, bias=b)
+    finally:
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
+    rows = np.arange(M)
+    check(Y, X, q, s, mode, bias=b, rows=rows if N * K > 50_000_000 else None)
+    assert np.array_equal(Y, Y2), "stream-K GEMV results must not depend on CTA timing"
+
+
+@pytest.mark.parametrize("x_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("path", sorted(DECODE_PATHS), ids=list(DECODE_PATHS.values()))
+def test_decode_gemv_strided(cuda_device, x_dtype, path):
+    M, K, N = 6, 300, 700
+    W = wl.weights(K, N, 71)
+    q, s = matmulq.quantize_per_channel(W)
+    X = oracle.round_bf16(wl.activations(M, K, 72))
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), "cuda")
+    xbig = torch.zeros((M, K + 13), device="cuda", dtype=x_dtype)
+    xbig[:, :K] = torch.from_numpy(X).to(x_dtype)
+    ybig = torch.full((M, N + 5), float("nan"), device="cuda")
+    matmulq.set_option(_lib.OPT_FORCE_PATH, path)
+    try:
+        matmul_q8(xbig[:, :K], pw, out=ybig[:, :N], mode="bf16")
+    finally:
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
+    torch.cuda.synchronize()
+    assert torch.isnan(ybig[:, N:]).all()
+    check(ybig[:, :N].cpu().numpy(), X, q, s, "bf16")
