@@ -7,7 +7,9 @@ attn-out 768x768, FFN-up 768x3072, FFN-down 3072x768, LM head 768x50257 (tied),
 each at M = 1 and M = 8 token rows (10 MatMulQ calls), fp32 activations ~ N(0,1),
 int8 per-channel weights from N(0, 0.02), MTRTQ_MODE_BF16. Every call has 6
 device copies of its weights and consecutive steps rotate through them (548 MB
-of int8 weights in all, > 4x the 126 MB L2), so weights stream from HBM.
+of int8 weights in all, > 4x the 126 MB L2), so weights stream from HBM. The
+calls are launched with MTRTQ_OPT_OVERLAP_LAUNCH (each may start while the one
+ahead finishes; --no-overlap turns it off).
 
 metric/value: algorithmic bytes (int8 W + scales + fp32 X + fp32 Y) per second
 over the whole job, inputs resident in HBM, steps replayed as CUDA graphs, timed
@@ -61,8 +63,11 @@ def parse():
                     help="decode_set (default) or shape:M,K,N (one MatMulQ shape timed alone)")
     ap.add_argument("--x-dtype", choices=["f32", "bf16"], default="f32",
                     help="activation type for --workload shape:M,K,N")
-    ap.add_argument("--force-path", type=int, default=0, choices=[0, 1, 2, 3],
-                    help="shape workload: 0 auto, 1 CUDA-core GEMV, 2 tile GEMM, 3 stream-K")
+    ap.add_argument("--force-path", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
+                    help="shape workload: 0 auto, 1 CUDA-core GEMV, 2 tile GEMM, 3 stream-K tcgen05, "
+                         "4 stream-K GEMV, 5 cluster GEMV")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch every call only after the previous one has finished")
     return ap.parse_args()
 
 
@@ -73,6 +78,19 @@ def peaks():
             d = json.load(f)
         return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, None, "fallback"
+
+
+# Kernel (function name) that each plan path launches.
+PATH_KERNELS = {"gemv": "gemv_q8_kernel", "gemm_tc": "gemm_q8_tc_kernel",
+                "stream_k_tc": "skinny_q8_tc_kernel", "stream_k_gemv": "gemv_sk_kernel",
+                "cluster_gemv": "gemv_cluster_kernel"}
+
+# Arithmetic of each path: what the product is computed in.
+PATH_DTYPES = {"gemv": "int8 W -> fp32, fp32 FMA",
+               "gemm_tc": "int8 W -> bf16, bf16 x bf16 tcgen05, fp32 accumulate",
+               "stream_k_tc": "int8 W -> bf16, bf16 x bf16 tcgen05, fp32 accumulate",
+               "stream_k_gemv": "int8 W -> fp32, fp32 FMA",
+               "cluster_gemv": "int8 W x int8 activation digits (3 per value), int32 accumulate"}
 
 
 def committed_traffic(kernel_key: str):
@@ -186,6 +204,9 @@ def run_ours(args, torch, rank, world, dev, dist):
     from mini_tensorrt_b200 import _lib, matmulq, workloads as wl
     hbm_peak, tc_peak, tc_sust, peak_kind = peaks()
     stream = torch.cuda.Stream(dev)
+    # The decode set's weights are resident and never written inside the step, so
+    # each call may start while the one ahead finishes (MTRTQ_OPT_OVERLAP_LAUNCH).
+    matmulq.set_option(_lib.OPT_OVERLAP_LAUNCH, 0 if args.no_overlap else 1)
     calls = build_decode_set(torch, dev, args.mode)
     step_bytes = sum(c["bytes"] for c in calls)
 
@@ -243,7 +264,7 @@ def run_ours(args, torch, rank, world, dev, dist):
     traffic = committed_traffic(f"gemv_lm_head_m{dom_m}_{args.mode}")
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "kernel": f"gemv_q8_kernel (LM head 768x50257, M={dom_m})",
+                "kernel": f"{PATH_KERNELS[dom['plan']['path']]} (LM head 768x50257, M={dom_m})",
                 "peak_kind": f"{peak_kind} hbm_gbs",
                 "per_launch_us": round(dom["us"], 3),
                 "algorithmic_bytes_per_launch": dom["bytes"]}
@@ -255,7 +276,8 @@ def run_ours(args, torch, rank, world, dev, dist):
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "i8w-f32acc",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": PATH_DTYPES[per_kernel[dom_m]["plan"]["path"]],
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantized per channel)",
         "config": {"workload": "decode GEMV set, GPT-2-small shapes (QKV 768x2304, attn-out 768x768, "
                                "FFN-up 768x3072, FFN-down 3072x768, LM head 768x50257) x M in {1,8}",
@@ -263,7 +285,8 @@ def run_ours(args, torch, rank, world, dev, dist):
                    "mode": args.mode, "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": f"weights rotated over {WEIGHT_COPIES} copies "
                          f"({WEIGHT_COPIES * sum(c['K'] * c['N'] for c in calls) / 1e6:.0f} MB > 2x L2)",
-                   "timing": "CUDA graphs of one step, CUDA events on the launching stream"},
+                   "timing": "CUDA graphs of one step, CUDA events on the launching stream",
+                   "overlap_launch": not args.no_overlap},
         "roofline": roofline,
         "e2e": e2e,
         "gpu_launches": len(calls) * args.steps,

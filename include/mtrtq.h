@@ -162,12 +162,23 @@ enum {
   MTRTQ_OPT_GEMM_A_SOURCE = 1, /* 0 (default): dequantized weights staged in TMEM
                                   (tcgen05.mma A from tensor memory);
                                   1: staged in 128-byte-swizzled shared memory */
-  MTRTQ_OPT_FORCE_PATH = 2     /* 0 (default): MTRTQ_MODE_FP32 -> CUDA-core GEMV;
-                                  MTRTQ_MODE_BF16 -> stream-K tcgen05 kernel for
-                                  M <= 64, tile tcgen05 GEMM above. 1: always the
-                                  CUDA-core GEMV; 2: always the tile GEMM; 3: always
-                                  the stream-K kernel (M <= 64). 2 and 3 need
-                                  MTRTQ_MODE_BF16. */
+  MTRTQ_OPT_FORCE_PATH = 2,    /* 0 (default): chosen by shape and mode (see
+                                  mtrtq_plan_info). Otherwise one kernel for every
+                                  call: 1 CUDA-core split-K GEMV; 2 tile tcgen05 GEMM;
+                                  3 stream-K tcgen05 kernel (M <= 32); 4 stream-K
+                                  CUDA-core GEMV (M <= 8); 5 cluster GEMV (M <= 8).
+                                  2 and 3 need MTRTQ_MODE_BF16. A call the forced
+                                  kernel cannot take fails with
+                                  MTRTQ_ERR_INVALID_ARG. */
+  MTRTQ_OPT_OVERLAP_LAUNCH = 3 /* 0 (default) or 1: the cluster GEMV is launched with
+                                  programmatic stream serialization, so it may start
+                                  while the kernel ahead of it in the stream is still
+                                  running. It reads the packed weights, scales and
+                                  biases early and waits for that kernel before it
+                                  reads X or writes Y: set it only where the kernel
+                                  ahead never writes the weights, scales or biases
+                                  (for example, not right after mtrtq_prepack on the
+                                  same stream). */
 };
 int mtrtq_set_option(int option, int64_t value);
 

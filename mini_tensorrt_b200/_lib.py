@@ -29,6 +29,7 @@ ZERO_COLUMN_REJECT = 0
 ZERO_COLUMN_ZERO = 1
 OPT_GEMM_A_SOURCE = 1
 OPT_FORCE_PATH = 2
+OPT_OVERLAP_LAUNCH = 3
 
 # Every function the header declares, with its ctypes signature.
 _vp = ctypes.c_void_p

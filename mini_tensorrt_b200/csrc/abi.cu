@@ -44,7 +44,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 // Process-wide options (mtrtq_set_option).
 int g_opt_gemm_a_source = 0;  // 0: dequantized weights in TMEM, 1: in shared memory
-int g_opt_force_path = 0;     // 0 auto, 1 GEMV, 2 tcgen05 GEMM
+int g_opt_force_path = 0;     // 0 auto, else the kernel (MTRTQ_OPT_FORCE_PATH)
+int g_opt_overlap = 0;        // 1: programmatic dependent launch (MTRTQ_OPT_OVERLAP_LAUNCH)
 
 std::mutex g_dev_mu;
 DeviceInfo g_dev_cache[64];
@@ -178,10 +179,16 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   p.k_pad = round_up64(K, kBlockK);
   p.n_tiles = (int)(p.n_pad / kTileN);
 
-  // Path: fp32 mode -> CUDA-core GEMV; bf16 mode -> stream-K tensor-core kernel for
-  // M <= 64 (and at most kMaxSplitTiles channel tiles), tile GEMM above.
+  // Path: M <= 8 -> the cluster GEMV (either mode) when its shared memory allows;
+  // otherwise bf16 mode -> stream-K tcgen05 kernel for M <= 32 (and at most
+  // kMaxSplitTiles channel tiles), tile tcgen05 GEMM above; fp32 mode -> the
+  // CUDA-core split-K GEMV.
   int path = 1;
   if (mode == MTRTQ_MODE_BF16) path = (M <= 32 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
+  {
+    Plan q = p;
+    if (gemv_cluster_plan(M, sm_count, &q)) path = 5;
+  }
   if (force_path != 0) {
     if ((force_path == 2 || force_path == 3) && mode != MTRTQ_MODE_BF16)
       return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core kernels compute in MTRTQ_MODE_BF16 only");
@@ -366,6 +373,10 @@ int mtrtq_set_option(int option, int64_t value) {
       if (value < 0 || value > 5) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0 to 5");
       g_opt_force_path = (int)value;
       return MTRTQ_OK;
+    case MTRTQ_OPT_OVERLAP_LAUNCH:
+      if (value != 0 && value != 1) return fail(MTRTQ_ERR_INVALID_ARG, "overlap is 0 or 1");
+      g_opt_overlap = (int)value;
+      return MTRTQ_OK;
     default:
       return fail(MTRTQ_ERR_INVALID_ARG, "unknown option %d", option);
   }
@@ -487,7 +498,8 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
   if (e != cudaSuccess) return cuda_fail(e, "device status address");
   if (p.kind == Plan::kGemvCluster) {
-    e = launch_gemv_cluster(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, status, st);
+    e = launch_gemv_cluster(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, status,
+                            g_opt_overlap != 0, st);
     if (e != cudaSuccess) return cuda_fail(e, "cluster GEMV launch");
     return MTRTQ_OK;
   }

@@ -49,6 +49,10 @@ constexpr int kClThreads = kClWarps * 32;  // consumer threads
 constexpr int kClBlock = kClThreads + 32;  // + the producer warp
 constexpr uint32_t kUnitBytes = 8192;      // 64 k x 128 channels of int8
 constexpr int kDigits = 3;
+constexpr int kClEarlyUnits = 1;  // weight units issued before the activations land
+// Under programmatic dependent launch the first units are fetched while the grid
+// ahead finishes, before the activations can be read.
+constexpr int kClEarlyUnitsPdl = 2;
 
 struct GemvClParams {
   const void* X;
@@ -61,6 +65,7 @@ struct GemvClParams {
   int M, K, N;
   int KB;          // 64-k units per tile
   int stages;      // shared memory ring stages (2..kGemvClMaxStages)
+  int early_units; // weight units issued before the activations have arrived
   unsigned* status;
 };
 
@@ -73,6 +78,21 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n"
+               "barrier.cluster.wait.aligned;" ::: "memory");
+}
+
+// Programmatic dependent launch (no-ops unless the launch enabled it): wait for
+// the grids this one depends on to complete and their writes to be visible; let
+// the grids that depend on this one start launching.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Address of `p` (this CTA's shared memory) in the shared memory of cluster rank `rank`.
@@ -147,106 +167,136 @@ __device__ __forceinline__ void cl_digits(float v, int& d0, int& d1, int& d2) {
   d2 = (int)r2;
 }
 
-// Activation digits over the CTA's units [u0, u0 + nu): plane d at xd + d * plane,
-// unit u, token m, k at ((u * mt + m) * 64 + k). Token m is staged by the consumer
-// warps w with w % mt == m, each taking an equal share of the range's 4-element
-// groups. s_max[m] gets max |x| over the range (atomically, as ordered bits) and
-// s_bad[m] flags a non-finite value. The first batch of each lane stays in
-// registers across the barrier that completes the maxima; longer shares read the
-// rest again (from the caches the first pass filled).
-template <bool X_BF16, bool ROUND>
-__device__ __forceinline__ void cl_stage_digits(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
-                                                int* s_bad, int u0, int nu, int warp, int lane) {
-  constexpr int kBatch = 6;  // 4-element loads in flight per lane
-  const int mt = p.M;
-  const int m = warp % mt;
-  const int share_warps = (kClWarps - 1 - m) / mt + 1;  // warps staging token m
-  const int j = warp / mt;
-  const int n4 = nu * 16;  // 4-element groups of the range
-  const int gbeg = (int)((int64_t)j * n4 / share_warps), gend = (int)((int64_t)(j + 1) * n4 / share_warps);
-  const int kbase = u0 * 64;
-  const bool vec = (p.ldx & 3) == 0;
+// Loads groups g0, g0 + 32, ... (kB of them, those below gend) of token m's range
+// as fp32 (rounded to bf16 when ROUND); zeros elsewhere.
+template <int kB, bool X_BF16, bool ROUND>
+__device__ __forceinline__ void cl_load_groups(const GemvClParams& p, float4 (&v)[kB], int m, int kbase,
+                                               int g0, int gend, bool vec) {
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    const int g = g0 + b * 32;
+    v[b] = g < gend ? cl_round<ROUND>(cl_load_x4<X_BF16>(p, m, kbase + g * 4, vec))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
 
-  float4 keep[kBatch];
-  float mx = 0.0f;
-  bool bad = false;
-  for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
-    float4 v[kBatch];
+template <int kB>
+__device__ __forceinline__ void cl_max_groups(const float4 (&v)[kB], float& mx, bool& bad) {
 #pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const int g = g0 + b * 32;
-      v[b] = g < gend ? cl_round<ROUND>(cl_load_x4<X_BF16>(p, m, kbase + g * 4, vec))
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const float a = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
-      bad |= !(a <= 3.402823466e38f);  // NaN or infinity
-      mx = fmaxf(mx, a);
-    }
-    if (g0 == gbeg + lane) {
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) keep[b] = v[b];
-    }
+  for (int b = 0; b < kB; ++b) {
+    const float a = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
+    bad |= !(a <= 3.402823466e38f);  // NaN or infinity
+    mx = fmaxf(mx, a);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    bad |= __shfl_xor_sync(0xffffffffu, (int)bad, o) != 0;
-  }
-  if (lane == 0) {
-    atomicMax(&s_max[m], __float_as_int(mx));  // mx >= 0: bit order is value order
-    if (bad) atomicOr(&s_bad[m], 1);
-  }
-  named_bar_sync(1, kClThreads);
-  const float smax = __int_as_float(s_max[m]);
-  const float inv = (smax > 0.0f && !s_bad[m]) ? 127.0f / smax : 0.0f;
+}
 
-  for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
-    float4 v[kBatch];
-    if (g0 == gbeg + lane) {
+// Writes the three digit planes of groups g0, g0 + 32, ... (those below gend).
+template <int kB>
+__device__ __forceinline__ void cl_store_digits(const float4 (&v)[kB], float inv, int8_t* xd, int plane,
+                                                int mt, int m, int g0, int gend) {
 #pragma unroll
-      for (int b = 0; b < kBatch; ++b) v[b] = keep[b];
-    } else {
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const int g = g0 + b * 32;
-        v[b] = g < gend ? cl_round<ROUND>(cl_load_x4<X_BF16>(p, m, kbase + g * 4, vec))
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const int g = g0 + b * 32;
-      if (g < gend) {
-        int a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
-        cl_digits(v[b].x * inv, a0, a1, a2);
-        cl_digits(v[b].y * inv, b0, b1, b2);
-        cl_digits(v[b].z * inv, c0, c1, c2);
-        cl_digits(v[b].w * inv, e0, e1, e2);
-        const int u = g >> 4, k = (g & 15) * 4;
-        const int off = (u * mt + m) * 64 + k;
-        *reinterpret_cast<uint32_t*>(xd + off) =
-            (uint32_t)(a0 & 255) | ((uint32_t)(b0 & 255) << 8) | ((uint32_t)(c0 & 255) << 16) |
-            ((uint32_t)(e0 & 255) << 24);
-        *reinterpret_cast<uint32_t*>(xd + plane + off) =
-            (uint32_t)(a1 & 255) | ((uint32_t)(b1 & 255) << 8) | ((uint32_t)(c1 & 255) << 16) |
-            ((uint32_t)(e1 & 255) << 24);
-        *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) =
-            (uint32_t)(a2 & 255) | ((uint32_t)(b2 & 255) << 8) | ((uint32_t)(c2 & 255) << 16) |
-            ((uint32_t)(e2 & 255) << 24);
-      }
+  for (int b = 0; b < kB; ++b) {
+    const int g = g0 + b * 32;
+    if (g < gend) {
+      int a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
+      cl_digits(v[b].x * inv, a0, a1, a2);
+      cl_digits(v[b].y * inv, b0, b1, b2);
+      cl_digits(v[b].z * inv, c0, c1, c2);
+      cl_digits(v[b].w * inv, e0, e1, e2);
+      const int u = g >> 4, k = (g & 15) * 4;
+      const int off = (u * mt + m) * 64 + k;
+      *reinterpret_cast<uint32_t*>(xd + off) = (uint32_t)(a0 & 255) | ((uint32_t)(b0 & 255) << 8) |
+                                               ((uint32_t)(c0 & 255) << 16) | ((uint32_t)(e0 & 255) << 24);
+      *reinterpret_cast<uint32_t*>(xd + plane + off) =
+          (uint32_t)(a1 & 255) | ((uint32_t)(b1 & 255) << 8) | ((uint32_t)(c1 & 255) << 16) |
+          ((uint32_t)(e1 & 255) << 24);
+      *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) =
+          (uint32_t)(a2 & 255) | ((uint32_t)(b2 & 255) << 8) | ((uint32_t)(c2 & 255) << 16) |
+          ((uint32_t)(e2 & 255) << 24);
     }
   }
 }
 
+// Activation digits over the CTA's units [u0, u0 + nu): plane d at xd + d * plane,
+// unit u, token m, k at ((u * mt + m) * 64 + k). Token m is staged by the consumer
+// warps w with w % mt == m, each taking an equal share of the range's 4-element
+// groups. s_max[m] gets max |x| over the range (atomically, as ordered bits) and
+// s_bad[m] flags a non-finite value.
+//
+// begin() issues the loads of a share of up to 32 * kRes groups, which then stay
+// in registers (the kernel calls it before its barrier setup, so the load latency
+// overlaps that); finish() completes the maxima across warps (one named barrier)
+// and writes the digits. A longer share is read twice, in batches, in finish():
+// the second time from the caches the first pass filled.
+template <bool X_BF16, bool ROUND>
+struct ClStager {
+  static constexpr int kRes = 6;    // groups per lane held in registers
+  static constexpr int kBatch = 6;  // groups per lane per batch otherwise
+  int m, gbeg, gend, kbase;
+  bool vec, resident;
+  float4 v[kRes];
+
+  __device__ __forceinline__ void begin(const GemvClParams& p, int u0, int nu, int warp, int lane) {
+    const int mt = p.M;
+    m = warp % mt;
+    const int share_warps = (kClWarps - 1 - m) / mt + 1;  // warps staging token m
+    const int j = warp / mt;
+    const int n4 = nu * 16;  // 4-element groups of the range
+    gbeg = (int)((int64_t)j * n4 / share_warps);
+    gend = (int)((int64_t)(j + 1) * n4 / share_warps);
+    kbase = u0 * 64;
+    vec = (p.ldx & 3) == 0;
+    resident = gend - gbeg <= 32 * kRes;
+    if (resident) cl_load_groups<kRes, X_BF16, ROUND>(p, v, m, kbase, gbeg + lane, gend, vec);
+  }
+
+  __device__ __forceinline__ void finish(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
+                                         int* s_bad, int lane) {
+    const int mt = p.M;
+    float mx = 0.0f;
+    bool bad = false;
+    if (resident) {
+      cl_max_groups<kRes>(v, mx, bad);
+    } else {
+      for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
+        float4 w[kBatch];
+        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, m, kbase, g0, gend, vec);
+        cl_max_groups<kBatch>(w, mx, bad);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      bad |= __shfl_xor_sync(0xffffffffu, (int)bad, o) != 0;
+    }
+    if (lane == 0) {
+      atomicMax(&s_max[m], __float_as_int(mx));  // mx >= 0: bit order is value order
+      if (bad) atomicOr(&s_bad[m], 1);
+    }
+    named_bar_sync(1, kClThreads);
+    const float smax = __int_as_float(s_max[m]);
+    const float inv = (smax > 0.0f && !s_bad[m]) ? 127.0f / smax : 0.0f;
+    if (resident) {
+      cl_store_digits<kRes>(v, inv, xd, plane, mt, m, gbeg + lane, gend);
+      return;
+    }
+    for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
+      float4 w[kBatch];
+      cl_load_groups<kBatch, X_BF16, ROUND>(p, w, m, kbase, g0, gend, vec);
+      cl_store_digits<kBatch>(w, inv, xd, plane, mt, m, g0, gend);
+    }
+  }
+};
+
 template <bool X_BF16, bool ROUND>
 __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kernel(const GemvClParams p) {
   // Shared memory: ring [stages][8 KiB] (the exchange buffer part[8][128] fp32
-  // reuses it at the end) | full[8], empty[8] barriers | digits [3][nu][M][64] s8.
+  // reuses it at the end) | full[8], empty[8], xready (+ pad) barriers |
+  // digits [3][nu][M][64] s8.
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_abort;
   __shared__ int s_max[8], s_bad[8];  // per token: max |x| (fp32 bits), non-finite flag
+  __shared__ float s_sb[2][128];      // scale and bias of the rows this CTA finishes
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
   const int CS = (int)gridDim.x;  // the cluster spans x
@@ -261,17 +311,50 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
   const size_t ring_bytes = max((size_t)nst * kUnitBytes, (size_t)8 * 128 * sizeof(float));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_bytes);
   uint64_t* empty = full + kGemvClMaxStages;
-  int8_t* xd = reinterpret_cast<int8_t*>(empty + kGemvClMaxStages);
+  uint64_t* xready = empty + kGemvClMaxStages;
+  int8_t* xd = reinterpret_cast<int8_t*>(xready + 2);
   const int plane = nu * mt * 64;
+  const int r0 = (int)(rank * 128 / CS), r1 = (int)((rank + 1) * 128 / CS);  // rows finished here
 
-  if (tid == 0) {
-    for (int i = 0; i < nst; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kClWarps);
+  // Roles before the block barrier:
+  //  * producer thread: barrier setup, then the first weight units into the ring
+  //    (weights are never written by a kernel this launch may overlap);
+  //  * other producer lanes: the scales and biases of the rows finished here;
+  //  * consumers: wait for the grid this launch depends on (a no-op unless it was
+  //    launched with programmatic stream serialization), then issue the
+  //    activation loads, whose latency overlaps the rest of the setup.
+  ClStager<X_BF16, ROUND> stager;
+  const char* src = p.W + ((int64_t)t * p.KB + u0) * kUnitBytes;
+  int issued = 0, st_p = 0;
+  uint32_t ph_p = 0;
+  const int prefill = min(min(p.early_units, nst), nu);
+  if (tid == 0) grid_launch_dependents();
+  if (warp == kClWarps) {
+    if (lane == 0) {
+      for (int i = 0; i < nst; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], kClWarps);
+      }
+      mbar_init(xready, 1);
+      s_abort = 0;
+      for (int i = 0; i < 8; ++i) s_max[i] = s_bad[i] = 0;
+      fence_barrier_init();
+      for (; issued < prefill; ++issued) {
+        mbar_arrive_expect_tx(&full[st_p], kUnitBytes);
+        bulk_g2s(ring + (size_t)st_p * kUnitBytes, src + (int64_t)issued * kUnitBytes, kUnitBytes,
+                 &full[st_p]);
+        if (++st_p == nst) { st_p = 0; ph_p ^= 1u; }
+      }
+    } else {
+      for (int r = r0 + lane - 1; r < r1; r += 31) {
+        const int n = t * kTileN + r;
+        s_sb[0][r] = n < p.N ? p.scale[n] : 0.0f;
+        s_sb[1][r] = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
+      }
     }
-    s_abort = 0;
-    for (int i = 0; i < 8; ++i) s_max[i] = s_bad[i] = 0;
-    fence_barrier_init();
+  } else {
+    grid_dependency_wait();
+    stager.begin(p, u0, nu, warp, lane);
   }
   __syncthreads();
 
@@ -282,17 +365,17 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
     for (int j = 0; j < 4; ++j) acc[d][j] = 0;
 
   if (warp == kClWarps) {
-    // Producer: one thread keeps up to nst units in flight.
+    // Producer: one thread keeps up to nst units in flight. The activations are
+    // read while the memory system is quiet: after early_units units the weight
+    // stream waits until they have arrived.
     if (lane == 0) {
-      const char* src = p.W + ((int64_t)t * p.KB + u0) * kUnitBytes;
-      int issued = 0, st = 0;
-      uint32_t ph = 0;
-      for (int u = 0; u < nu; ++u) {
-        if (u >= nst && !mbar_wait_bounded(&empty[st], ph ^ 1u, &s_abort, p.status)) break;
-        mbar_arrive_expect_tx(&full[st], kUnitBytes);
-        bulk_g2s(ring + (size_t)st * kUnitBytes, src + (int64_t)u * kUnitBytes, kUnitBytes, &full[st]);
+      for (int u = issued; u < nu; ++u) {
+        if (u == p.early_units && !mbar_wait_bounded(xready, 0, &s_abort, p.status)) break;
+        if (u >= nst && !mbar_wait_bounded(&empty[st_p], ph_p ^ 1u, &s_abort, p.status)) break;
+        mbar_arrive_expect_tx(&full[st_p], kUnitBytes);
+        bulk_g2s(ring + (size_t)st_p * kUnitBytes, src + (int64_t)u * kUnitBytes, kUnitBytes, &full[st_p]);
         ++issued;
-        if (++st == nst) { st = 0; ph ^= 1u; }
+        if (++st_p == nst) { st_p = 0; ph_p ^= 1u; }
       }
       // Every issued copy lands before the CTA moves on (and, on an abort, leaves).
       volatile int no_abort = 0;
@@ -302,8 +385,9 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
     __syncwarp();
   } else {
     // Consumers: activation digits first (the weights are already in flight).
-    cl_stage_digits<X_BF16, ROUND>(p, xd, plane, s_max, s_bad, u0, nu, warp, lane);
+    stager.finish(p, xd, plane, s_max, s_bad, lane);
     named_bar_sync(1, kClThreads);
+    if (tid == 0) mbar_arrive(xready);
     // Warp w: channel rows w*16 + g and w*16 + g + 8 (g = lane / 4); lane's slab c
     // (= lane % 4) of each unit. Step i of a unit takes words 2i, 2i+1 of the
     // lane's 16-byte slab rows: k = 16c + 8i + 0..7.
@@ -358,7 +442,6 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
   // partials in rank order.
   if (CS > 1) cluster_sync_all();
   else __syncthreads();
-  const int r0 = (int)(rank * 128 / CS), r1 = (int)((rank + 1) * 128 / CS);
   const int nr = r1 - r0;
   for (int e = tid; e < nr * mt; e += kClBlock) {
     const int m = e / nr, r = r0 + (e - m * nr);
@@ -371,17 +454,19 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
       sum = part[m * 128 + r];
     }
     if (n < p.N) {
-      float y = __fmul_rn(sum, p.scale[n]);
-      if (p.bias) y = __fadd_rn(y, p.bias[n]);
+      float y = __fmul_rn(sum, s_sb[0][r]);
+      if (p.bias) y = __fadd_rn(y, s_sb[1][r]);
       p.Y[(int64_t)m * p.ldy + n] = y;
     }
   }
-  // No CTA leaves while another rank may still read its shared memory.
-  if (CS > 1) cluster_sync_all();
+  // No CTA leaves while another rank may still read its shared memory. Those
+  // reads have returned (their values are summed above), so the arrival needs
+  // no release ordering.
+  if (CS > 1) cluster_sync_relaxed();
 }
 
 template <bool X_BF16, bool ROUND>
-cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, cudaStream_t st) {
+cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, bool pdl, cudaStream_t st) {
   auto kern = gemv_cluster_kernel<X_BF16, ROUND>;
   if (smem > 48 * 1024) {
     if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), (int)kGemvClSmemCap))
@@ -392,13 +477,15 @@ cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, 
   cfg.blockDim = dim3(kClBlock, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)cs;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, gp);
 }
 
@@ -408,13 +495,13 @@ size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages) {
   const int64_t nu = (units + cs - 1) / cs;  // the largest CTA range
   const size_t ring = (size_t)stages * kUnitBytes;
   const size_t exch = (size_t)8 * 128 * sizeof(float);  // reuses the ring
-  return (ring > exch ? ring : exch) + 2 * kGemvClMaxStages * sizeof(uint64_t) +
+  return (ring > exch ? ring : exch) + (2 * kGemvClMaxStages + 2) * sizeof(uint64_t) +
          (size_t)kDigits * (size_t)nu * (size_t)m * 64;
 }
 
 cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,
                                 const void* packed, const float* scale, const float* bias, float* Y,
-                                int64_t ldy, unsigned* status, cudaStream_t st) {
+                                int64_t ldy, unsigned* status, bool pdl, cudaStream_t st) {
   GemvClParams gp;
   gp.X = X;
   gp.ldx = ldx;
@@ -428,11 +515,12 @@ cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64
   gp.N = (int)p.N;
   gp.KB = p.kunits;
   gp.stages = p.stages;
+  gp.early_units = pdl ? min(kClEarlyUnitsPdl, p.stages) : kClEarlyUnits;
   gp.status = status;
   const size_t smem = gemv_cluster_smem_bytes((int)p.M, p.kunits, p.splits, p.stages);
-  if (x_dtype == 1) return cl_launch<true, false>(gp, p.splits, p.n_tiles, smem, st);
-  if (p.round_x) return cl_launch<false, true>(gp, p.splits, p.n_tiles, smem, st);
-  return cl_launch<false, false>(gp, p.splits, p.n_tiles, smem, st);
+  if (x_dtype == 1) return cl_launch<true, false>(gp, p.splits, p.n_tiles, smem, pdl, st);
+  if (p.round_x) return cl_launch<false, true>(gp, p.splits, p.n_tiles, smem, pdl, st);
+  return cl_launch<false, false>(gp, p.splits, p.n_tiles, smem, pdl, st);
 }
 
 }  // namespace mtrtq

@@ -60,7 +60,7 @@ constexpr int kGemvClMaxStages = 8;
 size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages);
 cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,
                                 const void* packed, const float* scale, const float* bias, float* Y,
-                                int64_t ldy, unsigned* status, cudaStream_t st);
+                                int64_t ldy, unsigned* status, bool pdl, cudaStream_t st);
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_prepack(const int8_t* q, int64_t K, int64_t N, void* packed, cudaStream_t st);

@@ -124,12 +124,13 @@ def test_launch_without_device_fails_loudly():
 
 
 @pytest.mark.parametrize("M,K,N,mode,path", [
-    (1, 768, 50257, "bf16", "stream_k_tc"), (8, 768, 768, "fp32", "gemv"),
-    (8, 3072, 768, "bf16", "stream_k_tc"), (9, 768, 768, "bf16", "stream_k_tc"),
+    (1, 768, 50257, "bf16", "cluster_gemv"), (8, 768, 768, "fp32", "cluster_gemv"),
+    (8, 3072, 768, "bf16", "cluster_gemv"), (9, 768, 768, "bf16", "stream_k_tc"),
     (32, 768, 3072, "bf16", "stream_k_tc"), (33, 768, 3072, "bf16", "gemm_tc"),
     (64, 768, 3072, "bf16", "gemm_tc"),
     (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv"),
-    (1, 768, 200000, "bf16", "gemm_tc"),
+    (1, 768, 200000, "bf16", "cluster_gemv"), (9, 768, 200000, "bf16", "gemm_tc"),
+    (8, 24576, 128, "bf16", "stream_k_tc"), (8, 24576, 128, "fp32", "gemv"),
 ])
 def test_planner(M, K, N, mode, path):
     info = matmulq.plan_info(M, K, N, torch.float32, mode)
@@ -140,6 +141,13 @@ def test_planner(M, K, N, mode, path):
         kb = -(-K // 64)
         assert info["ctas"] == max(1, min(148, units // -(-kb // 8)))
         assert matmulq.workspace_bytes(M, K, N, torch.float32, mode) >= 4096 + info["ctas"] * 2 * M * 512
+        return
+    if path == "cluster_gemv":
+        # CS ranks take near-equal ranges of the 64-k units; no workspace
+        kb = -(-K // 64)
+        assert 1 <= info["splits"] <= min(8, kb)
+        assert info["k_per_split"] == -(-kb // info["splits"]) * 64
+        assert matmulq.workspace_bytes(M, K, N, torch.float32, mode) == 0
         return
     # every split has work, and the splits cover K
     unit = 16 if path == "gemv" else 64

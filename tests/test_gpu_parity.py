@@ -9,6 +9,8 @@ Tolerances (normwise relative error = max|y - ref| / max|ref|, tests/conftest.py
     are then identical and only fp32 summation order differs.
 Packing is checked bit for bit (device pre-pack vs the host layout transform).
 """
+import contextlib
+
 import numpy as np
 import pytest
 import torch
@@ -25,6 +27,16 @@ FP32_TOL = 1e-4
 BF16_SPEC_TOL = 2e-2
 BF16_SAME_INPUT_TOL_CORES = 1e-4
 BF16_SAME_INPUT_TOL_TC = 1e-3
+
+
+@contextlib.contextmanager
+def forced(path):
+    """Runs the block with MTRTQ_OPT_FORCE_PATH = path (0 restores the planner)."""
+    matmulq.set_option(_lib.OPT_FORCE_PATH, path)
+    try:
+        yield
+    finally:
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
 
 
 def run(X, q, s, mode, bias=None, x_dtype=torch.float32, dev="cuda"):
@@ -75,8 +87,8 @@ def test_decode_gemv_set(cuda_device, case, mode):
     q, s = oracle.quantize_per_channel(W)
     Y = run(X, q, s, mode)
     path = matmulq.plan_info(*X.shape, W.shape[1], mode=mode)["path"]
-    assert path == ("gemv" if mode == "fp32" else "stream_k_tc")
-    check(Y, X, q, s, mode, tc=(mode == "bf16"))
+    assert path == "cluster_gemv"
+    check(Y, X, q, s, mode)
 
 
 @pytest.mark.parametrize("path,a_source", [(0, 0), (2, 0), (2, 1), (3, 0), (1, 0)],
@@ -257,7 +269,8 @@ def test_gemv_restages_activations_in_chunks(cuda_device, M):
     W = wl.weights(K, N, 31)
     q, s = matmulq.quantize_per_channel(W)
     X = wl.activations(M, K, 32)
-    Y = run(X, q, s, "fp32")
+    with forced(1):
+        Y = run(X, q, s, "fp32")
     check(Y, X, q, s, "fp32")
 
 
@@ -270,7 +283,8 @@ def test_stream_k_with_unaligned_rows(cuda_device, x_dtype, K):
     W = wl.weights(K, N, 41)
     q, s = oracle.quantize_per_channel(W)
     X = oracle.round_bf16(wl.activations(M, K, 42))
-    Y = run(X, q, s, "bf16", x_dtype=x_dtype)
+    with forced(3):
+        Y = run(X, q, s, "bf16", x_dtype=x_dtype)
     check(Y, X, q, s, "bf16", tc=True)
 
 
@@ -283,8 +297,9 @@ def test_stream_k_partitions(cuda_device, M, K, N):
     q, s = matmulq.quantize_per_channel(W)
     X = wl.activations(M, K, 52)
     b = wl.bias(N, 53)
-    Y = run(X, q, s, "bf16", bias=b)
-    assert matmulq.plan_info(M, K, N)["path"] == "stream_k_tc"
+    with forced(3):
+        Y = run(X, q, s, "bf16", bias=b)
+        assert matmulq.plan_info(M, K, N)["path"] == "stream_k_tc"
     check(Y, X, q, s, "bf16", bias=b, tc=True)
 
 
@@ -336,3 +351,55 @@ def test_decode_gemv_strided(cuda_device, x_dtype, path):
     torch.cuda.synchronize()
     assert torch.isnan(ybig[:, N:]).all()
     check(ybig[:, :N].cpu().numpy(), X, q, s, "bf16")
+
+
+@pytest.mark.parametrize("graph", [False, True], ids=["stream", "graph"])
+def test_overlapped_launches_wait_for_their_inputs(cuda_device, graph):
+    """With MTRTQ_OPT_OVERLAP_LAUNCH a cluster GEMV may start before the kernel ahead
+    of it finishes. A chain where each call reads the previous call's output, whose
+    buffer another kernel has just refilled with NaN, must still see every input
+    complete."""
+    K = N = 768
+    M = 2
+    qs = []
+    for i in range(3):
+        q, s = oracle.quantize_per_channel(wl.weights(K, N, 80 + i))
+        qs.append((q, s, PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), "cuda")))
+    x = torch.from_numpy(wl.activations(M, K, 90)).cuda()
+    ys = [torch.empty((M, N), device="cuda") for _ in range(3)]
+
+    def chain():
+        for y in ys:
+            y.fill_(float("nan"))
+        inp = x
+        for (_, _, pw), y in zip(qs, ys):
+            matmul_q8(inp, pw, out=y, mode="fp32")
+            inp = y
+
+    matmulq.set_option(_lib.OPT_OVERLAP_LAUNCH, 1)
+    try:
+        with forced(5):
+            chain()  # first calls (per-device setup) outside any capture
+            torch.cuda.synchronize()
+            if graph:
+                g = torch.cuda.CUDAGraph()
+                st = torch.cuda.Stream()
+                with torch.cuda.stream(st):
+                    with torch.cuda.graph(g, stream=st):
+                        chain()
+                for _ in range(3):
+                    g.replay()
+            else:
+                for _ in range(3):
+                    chain()
+            torch.cuda.synchronize()
+    finally:
+        matmulq.set_option(_lib.OPT_OVERLAP_LAUNCH, 0)
+    assert matmulq.read_device_status() == 0
+    inp = x.cpu().numpy()
+    for (q, s, _), y in zip(qs, ys):
+        out = y.cpu().numpy()
+        assert np.all(np.isfinite(out)), "a call read its input before it was written"
+        err = normwise_rel_err(out, oracle.matmul_q8(inp, q, s))
+        assert err <= FP32_TOL, f"fp32 mode rel err {err:.3e}"
+        inp = out
