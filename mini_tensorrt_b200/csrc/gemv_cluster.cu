@@ -180,6 +180,50 @@ __device__ __forceinline__ void cl_load_groups(const GemvClParams& p, float4 (&v
   }
 }
 
+// Issues the loads of groups g0, g0 + 32, ... (kB of them, those below gend) that
+// a single vector load can fetch, keeping the raw bits; nothing else waits on them.
+template <int kB, bool X_BF16>
+__device__ __forceinline__ void cl_issue_groups(const GemvClParams& p, uint4 (&raw)[kB], int m, int kbase,
+                                                int g0, int gend, bool vec) {
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    const int g = g0 + b * 32, k = kbase + g * 4;
+    if (g < gend && vec && k + 3 < p.K) {
+      const int64_t off = (int64_t)m * p.ldx + k;
+      if (X_BF16) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.X) + off));
+        raw[b] = make_uint4(u.x, u.y, 0u, 0u);
+      } else {
+        raw[b] = __ldg(reinterpret_cast<const uint4*>(static_cast<const float*>(p.X) + off));
+      }
+    }
+  }
+}
+
+// The values of the groups cl_issue_groups covered, from their raw bits; the
+// others (past the row's end or at a stride that rules out vector loads) are
+// read here element by element. Rounded to bf16 when ROUND.
+template <int kB, bool X_BF16, bool ROUND>
+__device__ __forceinline__ void cl_decode_groups(const GemvClParams& p, const uint4 (&raw)[kB], float4 (&v)[kB],
+                                                 int m, int kbase, int g0, int gend, bool vec) {
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    const int g = g0 + b * 32, k = kbase + g * 4;
+    if (g >= gend) {
+      v[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else if (vec && k + 3 < p.K) {
+      const uint4 r = raw[b];
+      v[b] = X_BF16 ? make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xffff0000u),
+                                  __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xffff0000u))
+                    : make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z),
+                                  __uint_as_float(r.w));
+    } else {
+      v[b] = cl_load_x4<X_BF16>(p, m, k, vec);
+    }
+    v[b] = cl_round<ROUND>(v[b]);
+  }
+}
+
 template <int kB>
 __device__ __forceinline__ void cl_max_groups(const float4 (&v)[kB], float& mx, bool& bad) {
 #pragma unroll
@@ -223,18 +267,19 @@ __device__ __forceinline__ void cl_store_digits(const float4 (&v)[kB], float inv
 // groups. s_max[m] gets max |x| over the range (atomically, as ordered bits) and
 // s_bad[m] flags a non-finite value.
 //
-// begin() issues the loads of a share of up to 32 * kRes groups, which then stay
-// in registers (the kernel calls it before its barrier setup, so the load latency
-// overlaps that); finish() completes the maxima across warps (one named barrier)
-// and writes the digits. A longer share is read twice, in batches, in finish():
+// begin() issues the loads of a share of up to 32 * RES groups, whose raw bits
+// then stay in registers (the kernel calls it before its barrier setup, and
+// nothing waits on the loads until finish(), so their latency overlaps the
+// setup); finish() decodes them, completes the maxima across warps (one named
+// barrier) and writes the digits. A longer share is read twice, in batches, in finish():
 // the second time from the caches the first pass filled.
-template <bool X_BF16, bool ROUND>
+template <bool X_BF16, bool ROUND, int RES>
 struct ClStager {
-  static constexpr int kRes = 6;    // groups per lane held in registers
+  static constexpr int kRes = RES;  // groups per lane held in registers
   static constexpr int kBatch = 6;  // groups per lane per batch otherwise
   int m, gbeg, gend, kbase;
   bool vec, resident;
-  float4 v[kRes];
+  uint4 raw[kRes];
 
   __device__ __forceinline__ void begin(const GemvClParams& p, int u0, int nu, int warp, int lane) {
     const int mt = p.M;
@@ -247,7 +292,7 @@ struct ClStager {
     kbase = u0 * 64;
     vec = (p.ldx & 3) == 0;
     resident = gend - gbeg <= 32 * kRes;
-    if (resident) cl_load_groups<kRes, X_BF16, ROUND>(p, v, m, kbase, gbeg + lane, gend, vec);
+    if (resident) cl_issue_groups<kRes, X_BF16>(p, raw, m, kbase, gbeg + lane, gend, vec);
   }
 
   __device__ __forceinline__ void finish(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
@@ -255,7 +300,9 @@ struct ClStager {
     const int mt = p.M;
     float mx = 0.0f;
     bool bad = false;
+    float4 v[kRes];
     if (resident) {
+      cl_decode_groups<kRes, X_BF16, ROUND>(p, raw, v, m, kbase, gbeg + lane, gend, vec);
       cl_max_groups<kRes>(v, mx, bad);
     } else {
       for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
@@ -288,7 +335,7 @@ struct ClStager {
   }
 };
 
-template <bool X_BF16, bool ROUND>
+template <bool X_BF16, bool ROUND, int RES>
 __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kernel(const GemvClParams p) {
   // Shared memory: ring [stages][8 KiB] (the exchange buffer part[8][128] fp32
   // reuses it at the end) | full[8], empty[8], xready (+ pad) barriers |
@@ -319,11 +366,10 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
   // Roles before the block barrier:
   //  * producer thread: barrier setup, then the first weight units into the ring
   //    (weights are never written by a kernel this launch may overlap);
-  //  * other producer lanes: the scales and biases of the rows finished here;
   //  * consumers: wait for the grid this launch depends on (a no-op unless it was
   //    launched with programmatic stream serialization), then issue the
   //    activation loads, whose latency overlaps the rest of the setup.
-  ClStager<X_BF16, ROUND> stager;
+  ClStager<X_BF16, ROUND, RES> stager;
   const char* src = p.W + ((int64_t)t * p.KB + u0) * kUnitBytes;
   int issued = 0, st_p = 0;
   uint32_t ph_p = 0;
@@ -344,12 +390,6 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
         bulk_g2s(ring + (size_t)st_p * kUnitBytes, src + (int64_t)issued * kUnitBytes, kUnitBytes,
                  &full[st_p]);
         if (++st_p == nst) { st_p = 0; ph_p ^= 1u; }
-      }
-    } else {
-      for (int r = r0 + lane - 1; r < r1; r += 31) {
-        const int n = t * kTileN + r;
-        s_sb[0][r] = n < p.N ? p.scale[n] : 0.0f;
-        s_sb[1][r] = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
       }
     }
   } else {
@@ -381,6 +421,14 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
       volatile int no_abort = 0;
       for (int u = issued > nst ? issued - nst : 0; u < issued; ++u)
         mbar_wait_bounded(&full[u % nst], (uint32_t)(u / nst) & 1u, &no_abort, p.status);
+    } else {
+      // The other producer lanes fetch the epilogue's scales and biases meanwhile
+      // (weights-like data, as above).
+      for (int r = r0 + lane - 1; r < r1; r += 31) {
+        const int n = t * kTileN + r;
+        s_sb[0][r] = n < p.N ? p.scale[n] : 0.0f;
+        s_sb[1][r] = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
+      }
     }
     __syncwarp();
   } else {
@@ -465,9 +513,9 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
   if (CS > 1) cluster_sync_relaxed();
 }
 
-template <bool X_BF16, bool ROUND>
+template <bool X_BF16, bool ROUND, int RES>
 cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, bool pdl, cudaStream_t st) {
-  auto kern = gemv_cluster_kernel<X_BF16, ROUND>;
+  auto kern = gemv_cluster_kernel<X_BF16, ROUND, RES>;
   if (smem > 48 * 1024) {
     if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), (int)kGemvClSmemCap))
       return e;
@@ -518,9 +566,19 @@ cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64
   gp.early_units = pdl ? min(kClEarlyUnitsPdl, p.stages) : kClEarlyUnits;
   gp.status = status;
   const size_t smem = gemv_cluster_smem_bytes((int)p.M, p.kunits, p.splits, p.stages);
-  if (x_dtype == 1) return cl_launch<true, false>(gp, p.splits, p.n_tiles, smem, pdl, st);
-  if (p.round_x) return cl_launch<false, true>(gp, p.splits, p.n_tiles, smem, pdl, st);
-  return cl_launch<false, false>(gp, p.splits, p.n_tiles, smem, pdl, st);
+  // Activation groups a staging lane holds: 6 unless some warp's share needs
+  // more to be staged in one pass (a token has floor(8 / M) warps).
+  const int64_t nu_max = (p.kunits + p.splits - 1) / p.splits;
+  const int64_t share = (nu_max * 16 + kClWarps / p.M - 1) / (kClWarps / p.M);
+  const bool wide = share > 32 * 6;
+  if (x_dtype == 1)
+    return wide ? cl_launch<true, false, 12>(gp, p.splits, p.n_tiles, smem, pdl, st)
+                : cl_launch<true, false, 6>(gp, p.splits, p.n_tiles, smem, pdl, st);
+  if (p.round_x)
+    return wide ? cl_launch<false, true, 12>(gp, p.splits, p.n_tiles, smem, pdl, st)
+                : cl_launch<false, true, 6>(gp, p.splits, p.n_tiles, smem, pdl, st);
+  return wide ? cl_launch<false, false, 12>(gp, p.splits, p.n_tiles, smem, pdl, st)
+              : cl_launch<false, false, 6>(gp, p.splits, p.n_tiles, smem, pdl, st);
 }
 
 }  // namespace mtrtq
