@@ -63,9 +63,9 @@ def parse():
                     help="decode_set (default) or shape:M,K,N (one MatMulQ shape timed alone)")
     ap.add_argument("--x-dtype", choices=["f32", "bf16"], default="f32",
                     help="activation type for --workload shape:M,K,N")
-    ap.add_argument("--force-path", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
+    ap.add_argument("--force-path", type=int, default=0, choices=[0, 1, 2, 3, 4],
                     help="shape workload: 0 auto, 1 CUDA-core GEMV, 2 tile GEMM, 3 stream-K tcgen05, "
-                         "4 stream-K GEMV, 5 cluster GEMV")
+                         "4 cluster GEMV")
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch every call only after the previous one has finished")
     return ap.parse_args()
@@ -82,14 +82,12 @@ def peaks():
 
 # Kernel (function name) that each plan path launches.
 PATH_KERNELS = {"gemv": "gemv_q8_kernel", "gemm_tc": "gemm_q8_tc_kernel",
-                "stream_k_tc": "skinny_q8_tc_kernel", "stream_k_gemv": "gemv_sk_kernel",
-                "cluster_gemv": "gemv_cluster_kernel"}
+                "stream_k_tc": "skinny_q8_tc_kernel", "cluster_gemv": "gemv_cluster_kernel"}
 
 # Arithmetic of each path: what the product is computed in.
 PATH_DTYPES = {"gemv": "int8 W -> fp32, fp32 FMA",
                "gemm_tc": "int8 W -> bf16, bf16 x bf16 tcgen05, fp32 accumulate",
                "stream_k_tc": "int8 W -> bf16, bf16 x bf16 tcgen05, fp32 accumulate",
-               "stream_k_gemv": "int8 W -> fp32, fp32 FMA",
                "cluster_gemv": "int8 W x int8 activation digits (3 per value), int32 accumulate"}
 
 

@@ -165,8 +165,8 @@ enum {
   MTRTQ_OPT_FORCE_PATH = 2,    /* 0 (default): chosen by shape and mode (see
                                   mtrtq_plan_info). Otherwise one kernel for every
                                   call: 1 CUDA-core split-K GEMV; 2 tile tcgen05 GEMM;
-                                  3 stream-K tcgen05 kernel (M <= 32); 4 stream-K
-                                  CUDA-core GEMV (M <= 8); 5 cluster GEMV (M <= 8).
+                                  3 stream-K tcgen05 kernel (M <= 32); 4 cluster
+                                  GEMV (M <= 8).
                                   2 and 3 need MTRTQ_MODE_BF16. A call the forced
                                   kernel cannot take fails with
                                   MTRTQ_ERR_INVALID_ARG. */

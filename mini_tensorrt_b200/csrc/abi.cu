@@ -101,25 +101,6 @@ int check_dims(int64_t M, int64_t K, int64_t N) {
   return MTRTQ_OK;
 }
 
-// Stream-K GEMV geometry: units of one 64-k block of a 128-channel tile, spread
-// evenly over kGemvSkCtasPerSm CTAs per SM (never more CTAs than units).
-static void gemv_sk_plan(int64_t M, int sm_count, Plan* p) {
-  p->kind = Plan::kGemvSK;
-  p->tile_m = (int)M;
-  p->m_tiles = 1;
-  p->kunits = (int)(p->k_pad / kBlockK);
-  p->kunits_per_split = p->kunits;
-  const int64_t units = (int64_t)p->n_tiles * p->kunits;
-  int64_t g = (int64_t)sm_count * kGemvSkCtasPerSm;
-  if (g > units) g = units;
-  p->grid = (int)g;
-  p->splits = 1;
-  p->off_counters = 0;
-  p->off_partials = kCounterBytes;
-  p->total = kCounterBytes + round256((size_t)p->grid * 2 * (size_t)M * kTileN * sizeof(float));
-  p->off_xb = p->total;
-}
-
 // Cluster GEMV geometry: one cluster of CS CTAs (CS <= 8) per 128-channel tile,
 // each CTA streaming ceil(KB / CS) 64-k units through a ring of shared memory stages.
 // All clusters should be resident at once (kGemvClCtasPerSm CTAs per SM): CS is the
@@ -127,7 +108,7 @@ static void gemv_sk_plan(int64_t M, int sm_count, Plan* p) {
 // needed, until a CTA's staged activations leave room for two stages; the ring
 // then takes what the shared memory cap leaves (2 to 8 stages).
 static bool gemv_cluster_plan(int64_t M, int sm_count, Plan* p) {
-  if (M > kGemvSkMaxM || p->n_tiles > 65535) return false;
+  if (M > kGemvClMaxM || p->n_tiles > 65535) return false;
   const int64_t KB = p->k_pad / kBlockK;
   const int64_t capacity = (int64_t)sm_count * kGemvClCtasPerSm;
   int64_t cs = capacity / p->n_tiles;
@@ -149,15 +130,6 @@ static bool gemv_cluster_plan(int64_t M, int sm_count, Plan* p) {
   p->kunits_per_split = (int)ceil_div64(KB, cs);
   p->total = 0;  // no workspace
   return true;
-}
-
-static bool gemv_sk_fits(int64_t M, const Plan& base, int sm_count) {
-  if (M > kGemvSkMaxM) return false;
-  Plan p = base;
-  gemv_sk_plan(M, sm_count, &p);
-  return (size_t)p.grid * sizeof(unsigned) <= kCounterBytes &&
-         gemv_sk_smem_bytes((int)M, p.kunits, (long long)p.n_tiles * p.kunits, p.grid) <=
-             kGemvSkSmemCap;
 }
 
 // force_path: 0 chooses by shape and mode; 1, 2, 3, 4 select a kernel (see
@@ -187,17 +159,14 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   if (mode == MTRTQ_MODE_BF16) path = (M <= 32 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
   {
     Plan q = p;
-    if (gemv_cluster_plan(M, sm_count, &q)) path = 5;
+    if (gemv_cluster_plan(M, sm_count, &q)) path = 4;
   }
   if (force_path != 0) {
     if ((force_path == 2 || force_path == 3) && mode != MTRTQ_MODE_BF16)
       return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core kernels compute in MTRTQ_MODE_BF16 only");
     if (force_path == 3 && (M > 32 || p.n_tiles > kMaxSplitTiles))
       return fail(MTRTQ_ERR_INVALID_ARG, "the stream-K kernel takes M <= 32 and N <= 131072");
-    if (force_path == 4 && !gemv_sk_fits(M, p, sm_count))
-      return fail(MTRTQ_ERR_INVALID_ARG,
-                  "the stream-K GEMV takes M <= 8 and at most 48 KiB of staged activations");
-    if (force_path == 5) {
+    if (force_path == 4) {
       Plan q = p;
       if (!gemv_cluster_plan(M, sm_count, &q))
         return fail(MTRTQ_ERR_INVALID_ARG,
@@ -207,14 +176,8 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   }
   const bool gemm = path == 2;
 
-  if (path == 5) {
-    gemv_cluster_plan(M, sm_count, &p);
-    p.round_x = (mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32);
-    *out = p;
-    return MTRTQ_OK;
-  }
   if (path == 4) {
-    gemv_sk_plan(M, sm_count, &p);
+    gemv_cluster_plan(M, sm_count, &p);
     p.round_x = (mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32);
     *out = p;
     return MTRTQ_OK;
@@ -370,7 +333,7 @@ int mtrtq_set_option(int option, int64_t value) {
       g_opt_gemm_a_source = (int)value;
       return MTRTQ_OK;
     case MTRTQ_OPT_FORCE_PATH:
-      if (value < 0 || value > 5) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0 to 5");
+      if (value < 0 || value > 4) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0 to 4");
       g_opt_force_path = (int)value;
       return MTRTQ_OK;
     case MTRTQ_OPT_OVERLAP_LAUNCH:
@@ -487,11 +450,6 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   if (p.kind == Plan::kGemv) {
     e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, workspace, st);
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
-    return MTRTQ_OK;
-  }
-  if (p.kind == Plan::kGemvSK) {
-    e = launch_gemv_sk(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, workspace, st);
-    if (e != cudaSuccess) return cuda_fail(e, "stream-K GEMV launch");
     return MTRTQ_OK;
   }
   unsigned* status = nullptr;
@@ -621,11 +579,11 @@ int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int6
   Plan p;
   if (int rc = plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p, g_opt_force_path))
     return rc;
-  info[0] = p.kind;  // 0 GEMV, 1 tile GEMM, 2 stream-K tcgen05, 3 stream-K GEMV, 4 cluster GEMV
+  info[0] = p.kind;  // 0 GEMV, 1 tile GEMM, 2 stream-K tcgen05, 3 cluster GEMV
   info[1] = p.tile_m;
   info[2] = p.m_tiles;
   info[3] = p.n_tiles;
-  info[4] = (p.kind == Plan::kSkinnyTC || p.kind == Plan::kGemvSK) ? p.grid : p.splits;
+  info[4] = p.kind == Plan::kSkinnyTC ? p.grid : p.splits;
   info[5] = p.kunits_per_split * (p.kind == Plan::kGemv ? kSlabK : kBlockK);
   return MTRTQ_OK;
 }

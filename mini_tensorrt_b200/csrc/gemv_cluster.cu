@@ -496,8 +496,15 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
     const int n = t * kTileN + r;
     float sum;
     if (CS > 1) {
+      // All ranks' values are requested before the first is used.
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < CS) v[q] = ld_dsmem_f32(dsmem_addr(part + m * 128 + r, (uint32_t)q));
       sum = 0.0f;
-      for (int q = 0; q < CS; ++q) sum += ld_dsmem_f32(dsmem_addr(part + m * 128 + r, (uint32_t)q));
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < CS) sum += v[q];
     } else {
       sum = part[m * 128 + r];
     }

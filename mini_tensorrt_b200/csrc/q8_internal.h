@@ -12,7 +12,7 @@ namespace mtrtq {
 // problem alone (and the device's SM count), so the workspace query and the
 // launch always agree.
 struct Plan {
-  enum Kind { kGemv = 0, kGemmTC = 1, kSkinnyTC = 2, kGemvSK = 3, kGemvCluster = 4 } kind = kGemv;
+  enum Kind { kGemv = 0, kGemmTC = 1, kSkinnyTC = 2, kGemvCluster = 3 } kind = kGemv;
   int64_t M = 0, K = 0, N = 0;
   int64_t n_pad = 0, k_pad = 0;    // packed weight extents
   int n_tiles = 0;                 // channel tiles of 128
@@ -22,7 +22,7 @@ struct Plan {
   int kunits = 0;                  // k units (GEMV: slabs of 16; GEMM: blocks of 64)
   int kunits_per_split = 0;
   int chunk_units = 0;             // GEMV: slabs of activations staged at a time
-  int grid = 0;                    // stream-K kernels: persistent CTAs
+  int grid = 0;                    // stream-K kernel: persistent CTAs
   int stages = 0;                  // cluster GEMV: shared memory ring stages
   bool x_to_bf16 = false;          // GEMM: X is staged as a bf16 copy in the workspace
   bool round_x = false;            // GEMV: round fp32 X to bf16 before the product
@@ -35,11 +35,8 @@ struct Plan {
 // staging chunk is a multiple of it.
 constexpr int kGemvUnroll = 8;
 
-// Stream-K decode GEMV: rows it takes, CTAs per SM, and the cap on its staged
-// activations (the default dynamic shared memory limit, so four CTAs fit an SM).
-constexpr int kGemvSkMaxM = 8;
-constexpr int kGemvSkCtasPerSm = 4;
-constexpr size_t kGemvSkSmemCap = 48 * 1024;
+// Cluster GEMV: the most activation rows (tokens) it takes.
+constexpr int kGemvClMaxM = 8;
 
 struct DeviceInfo {
   int device = -1;
@@ -69,12 +66,6 @@ cudaError_t launch_x_to_bf16(const void* X, int x_dtype, int64_t ldx, int64_t M,
 cudaError_t launch_gemv(const Plan& p, const void* X, int x_dtype, int64_t ldx, const void* packed,
                         const float* scale, const float* bias, float* Y, int64_t ldy,
                         void* workspace, cudaStream_t st);
-cudaError_t launch_gemv_sk(const Plan& p, const void* X, int x_dtype, int64_t ldx, const void* packed,
-                           const float* scale, const float* bias, float* Y, int64_t ldy,
-                           void* workspace, cudaStream_t st);
-// Shared memory of the stream-K GEMV for m rows, KB k-blocks per tile, `units`
-// units over `grid` CTAs.
-size_t gemv_sk_smem_bytes(int m, int KB, long long units, int grid);
 cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const void* packed,
                            const float* scale, const float* bias, float* Y, int64_t ldy,
                            void* workspace, const CUtensorMap& xmap, int a_from_tmem,

@@ -109,7 +109,7 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.mtrtq_workspace_bytes(0, 64, 64, 0, 0) == -1
     assert lib.mtrtq_workspace_bytes(1, 1 << 31, 64, 0, 0) == -1
     assert lib.mtrtq_set_option(99, 0) == _lib.ERR_INVALID_ARG
-    assert lib.mtrtq_set_option(_lib.OPT_FORCE_PATH, 6) == _lib.ERR_INVALID_ARG
+    assert lib.mtrtq_set_option(_lib.OPT_FORCE_PATH, 5) == _lib.ERR_INVALID_ARG
     assert lib.mtrtq_matmul(None, 0, 64, None, None, None, None, 64, 1, 64, 64, 0, None, 0,
                             None) == _lib.ERR_INVALID_ARG
 
@@ -172,40 +172,12 @@ def test_forced_paths_change_the_plan():
         with pytest.raises(_lib.MtrtqError):
             matmulq.plan_info(65, 768, 768)
         matmulq.set_option(_lib.OPT_FORCE_PATH, 4)
-        assert matmulq.plan_info(8, 768, 768, mode="fp32")["path"] == "stream_k_gemv"
-        assert matmulq.plan_info(1, 768, 768)["path"] == "stream_k_gemv"
-        with pytest.raises(_lib.MtrtqError):
-            matmulq.plan_info(9, 768, 768)
-        matmulq.set_option(_lib.OPT_FORCE_PATH, 5)
         assert matmulq.plan_info(8, 768, 768, mode="fp32")["path"] == "cluster_gemv"
         assert matmulq.workspace_bytes(8, 768, 768, torch.float32, "fp32") == 0
         with pytest.raises(_lib.MtrtqError):
             matmulq.plan_info(9, 768, 768)
         with pytest.raises(_lib.MtrtqError):
-            matmulq.set_option(_lib.OPT_FORCE_PATH, 6)
-    finally:
-        matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
-
-
-@pytest.mark.parametrize("M,K,N", [(1, 64, 128), (3, 64, 50257), (8, 12288, 256), (8, 4096, 14336),
-                                   (1, 768, 50257), (5, 1472, 896), (8, 65536, 200000)])
-def test_stream_k_gemv_plan(M, K, N):
-    """Units of 64 k x 128 channels over at most four CTAs per SM, one or more units
-    each; staged activations within 48 KiB, else the plan is refused."""
-    kb = -(-K // 64)
-    units = -(-N // 128) * kb
-    ctas = min(4 * 148, units)
-    per_cta = -(-units // ctas)
-    smem = min(kb, per_cta) * M * 64 * 4
-    matmulq.set_option(_lib.OPT_FORCE_PATH, 4)
-    try:
-        if smem > 48 * 1024:
-            with pytest.raises(_lib.MtrtqError):
-                matmulq.plan_info(M, K, N)
-            return
-        info = matmulq.plan_info(M, K, N)
-        assert info["path"] == "stream_k_gemv" and info["ctas"] == ctas
-        assert matmulq.workspace_bytes(M, K, N, torch.float32, "bf16") >= 4096 + ctas * 2 * M * 512
+            matmulq.set_option(_lib.OPT_FORCE_PATH, 5)
     finally:
         matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
 
@@ -219,7 +191,7 @@ def test_cluster_gemv_plan(M, K, N, cs):
     all clusters resident at three CTAs per SM where the tiles allow; refused when
     a CTA's activation digits (3 bytes per activation) and two 8 KiB ring stages
     exceed 74 KiB."""
-    matmulq.set_option(_lib.OPT_FORCE_PATH, 5)
+    matmulq.set_option(_lib.OPT_FORCE_PATH, 4)
     try:
         if cs is None:
             with pytest.raises(_lib.MtrtqError):
