@@ -157,14 +157,28 @@ __device__ __forceinline__ float4 cl_round(float4 v) {
 // Three int8 digits of v (|v| <= 127): v ~ d0 + d1 / 2^7 + d2 / 2^14. Each
 // residual is exact in fp32 (it is the difference of two nearby values, then
 // scaled by a power of two); the last digit's rounding leaves |error| <= 2^-15.
-__device__ __forceinline__ void cl_digits(float v, int& d0, int& d1, int& d2) {
-  const float r0 = rintf(v);
-  const float v1 = (v - r0) * 128.0f;
-  const float r1 = rintf(v1);
-  const float r2 = rintf((v1 - r1) * 128.0f);
-  d0 = (int)r0;
-  d1 = (int)r1;
-  d2 = (int)r2;
+//
+// Rounding to the nearest integer (ties to even) is an add of 1.5 * 2^23: for
+// |v| < 2^22 the sum's spacing is 1, so the sum holds round(v) as a two's
+// complement offset in its low mantissa bits, and the low byte of its bit
+// pattern is the int8 digit. Plain adds and multiplies, where a float-to-integer
+// conversion would run on the narrower conversion pipe. w0, w1, w2 receive the
+// three sums' bit patterns.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+__device__ __forceinline__ void cl_digits(float v, uint32_t& w0, uint32_t& w1, uint32_t& w2) {
+  const float t0 = __fadd_rn(v, kRoundMagic);
+  const float v1 = __fmul_rn(__fsub_rn(v, __fsub_rn(t0, kRoundMagic)), 128.0f);
+  const float t1 = __fadd_rn(v1, kRoundMagic);
+  const float v2 = __fmul_rn(__fsub_rn(v1, __fsub_rn(t1, kRoundMagic)), 128.0f);
+  const float t2 = __fadd_rn(v2, kRoundMagic);
+  w0 = __float_as_uint(t0);
+  w1 = __float_as_uint(t1);
+  w2 = __float_as_uint(t2);
+}
+
+// The low bytes of a, b, c, e as one word (a in byte 0).
+__device__ __forceinline__ uint32_t cl_pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t e) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, e, 0x0040), 0x5410);
 }
 
 // Loads groups g0, g0 + 32, ... (kB of them, those below gend) of token m's range
@@ -242,21 +256,16 @@ __device__ __forceinline__ void cl_store_digits(const float4 (&v)[kB], float inv
   for (int b = 0; b < kB; ++b) {
     const int g = g0 + b * 32;
     if (g < gend) {
-      int a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
-      cl_digits(v[b].x * inv, a0, a1, a2);
-      cl_digits(v[b].y * inv, b0, b1, b2);
-      cl_digits(v[b].z * inv, c0, c1, c2);
-      cl_digits(v[b].w * inv, e0, e1, e2);
+      uint32_t a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
+      cl_digits(__fmul_rn(v[b].x, inv), a0, a1, a2);
+      cl_digits(__fmul_rn(v[b].y, inv), b0, b1, b2);
+      cl_digits(__fmul_rn(v[b].z, inv), c0, c1, c2);
+      cl_digits(__fmul_rn(v[b].w, inv), e0, e1, e2);
       const int u = g >> 4, k = (g & 15) * 4;
       const int off = (u * mt + m) * 64 + k;
-      *reinterpret_cast<uint32_t*>(xd + off) = (uint32_t)(a0 & 255) | ((uint32_t)(b0 & 255) << 8) |
-                                               ((uint32_t)(c0 & 255) << 16) | ((uint32_t)(e0 & 255) << 24);
-      *reinterpret_cast<uint32_t*>(xd + plane + off) =
-          (uint32_t)(a1 & 255) | ((uint32_t)(b1 & 255) << 8) | ((uint32_t)(c1 & 255) << 16) |
-          ((uint32_t)(e1 & 255) << 24);
-      *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) =
-          (uint32_t)(a2 & 255) | ((uint32_t)(b2 & 255) << 8) | ((uint32_t)(c2 & 255) << 16) |
-          ((uint32_t)(e2 & 255) << 24);
+      *reinterpret_cast<uint32_t*>(xd + off) = cl_pack_low_bytes(a0, b0, c0, e0);
+      *reinterpret_cast<uint32_t*>(xd + plane + off) = cl_pack_low_bytes(a1, b1, c1, e1);
+      *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) = cl_pack_low_bytes(a2, b2, c2, e2);
     }
   }
 }
