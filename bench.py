@@ -432,6 +432,76 @@ def run_shape(args, torch, dev):
             "peak_kind": peak_kind, "weight_copies": n_copies, "plan": plan}
 
 
+def run_sharded(args, torch, rank, world, dev, dist):
+    """One large MatMulQ split across the ranks (strong scaling: the total work is
+    fixed): --workload sharded:M,K,N,S with S = N (column split + all-gather) or
+    K (row split + all-reduce). Each rank rotates through copies of its shard
+    (> 2x L2 per GPU); a call is the local product plus the collective, timed with
+    CUDA events on the rank's stream, max over ranks. Also times the local product
+    alone, and gives the collective's NVLink lower bound (770 GB/s per direction)."""
+    from mini_tensorrt_b200 import matmulq, sharded, workloads as wl
+    hbm_peak, tc_peak, _, peak_kind = peaks()
+    M, K, N, split = args.workload.split(":", 1)[1].split(",")
+    M, K, N = int(M), int(K), int(N)
+    W = wl.weights(K, N, wl.shape_seed("sharded", K, N))
+    q, s = matmulq.quantize_per_channel(W)
+    op = sharded.ShardedMatMulQ(q, s, None, split=split, device=dev, mode=args.mode)
+    b, e = op.shard.begin, op.shard.end
+    shard_bytes = max(1, op.w.packed.numel())
+    n_copies = max(2, -(-(260 << 20) // shard_bytes))
+    copies = [op.w] + [matmulq.PackedWeight(op.w.packed.clone(), op.w.scale, op.w.K, op.w.N)
+                       for _ in range(n_copies - 1)]
+    xdt = torch.bfloat16 if args.x_dtype == "bf16" else torch.float32
+    x = torch.randn(M, K, device=dev, generator=torch.Generator(dev).manual_seed(1)).to(xdt)
+
+    def timed(fn, steps, warmup):
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / 1e3 / steps], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def full(i):
+        op.w = copies[i % n_copies]
+        op(x)
+
+    xs = x[:, b:e] if split == "K" else x
+
+    def local(i):
+        matmulq.matmul_q8(xs, copies[i % n_copies], mode=args.mode)
+
+    steps = max(args.steps, 2 * n_copies)
+    t_call = timed(full, steps, max(args.warmup, n_copies))
+    t_local = timed(local, steps, max(args.warmup, n_copies))
+    out_bytes = M * N * 4
+    if world == 1:
+        comm_bytes = 0
+    elif split == "N":
+        comm_bytes = out_bytes * (world - 1) / world      # each GPU receives the other shards
+    else:
+        comm_bytes = 2 * out_bytes * (world - 1) / world  # ring all-reduce, per GPU
+    byts = wl.algorithmic_bytes(M, K, N, 2 if xdt == torch.bfloat16 else 4)
+    return {"metric": METRIC, "impl": "ours", "workload": args.workload, "n_gpus": world,
+            "scaling": "strong", "split": split, "mode": args.mode, "x_dtype": args.x_dtype,
+            "us_per_call": round(t_call * 1e6, 3), "us_local_product": round(t_local * 1e6, 3),
+            "tflops": round(wl.flops(M, K, N) / t_call / 1e12, 2),
+            "gbs": round(byts / t_call / 1e9, 1),
+            "comm_lower_bound_us": round(comm_bytes / 770e9 * 1e6, 3),
+            "shard": [b, e], "weight_copies_per_gpu": n_copies, "peak_kind": peak_kind,
+            "timing": "CUDA events around eager calls (product + collective), max over ranks"}
+
+
 # ---------------------------------------------------------------------- CPU legs
 
 
@@ -563,6 +633,14 @@ def main():
     _b.build()
     if args.workload.startswith("shape:"):
         print(json.dumps(run_shape(args, torch, dev)))
+        return
+    if args.workload.startswith("sharded:"):
+        line = run_sharded(args, torch, rank, world, dev, dist)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(line))
         return
     line, calls, stream = run_ours(args, torch, rank, world, dev, dist)
     del calls

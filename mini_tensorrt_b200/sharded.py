@@ -78,8 +78,9 @@ class ShardedMatMulQ:
         if split not in ("N", "K"):
             raise ValueError("split must be 'N' or 'K'")
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        # Without an initialized process group this is the unsplit op on one GPU.
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.mode = mode
         self.device = torch.device(device) if device is not None else (
             torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
@@ -111,6 +112,8 @@ class ShardedMatMulQ:
         if x.shape[1] != self.K:
             raise ValueError(f"x must be [M, {self.K}]")
         sh = self.shard
+        if self.world == 1:
+            return self.local_matmul(x, self.w, self.bias, self.mode)
         if sh.split == "N":
             widths = [e - b for b, e in self.ranges]
             wmax = max(widths)
