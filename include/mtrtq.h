@@ -183,8 +183,9 @@ enum {
 int mtrtq_set_option(int option, int64_t value);
 
 /* The plan mtrtq_matmul would use: info[0] path (0 CUDA-core GEMV, 1 tile GEMM,
- * 2 stream-K kernel), [1] token rows per tile, [2] token tiles, [3] channel tiles,
- * [4] k splits (stream-K: persistent CTAs), [5] k per split. n_info >= 6. */
+ * 2 stream-K tcgen05 kernel, 3 cluster GEMV), [1] token rows per tile, [2] token
+ * tiles, [3] channel tiles, [4] k splits (stream-K: persistent CTAs; cluster GEMV:
+ * CTAs per cluster), [5] k per split. n_info >= 6. */
 int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info,
                     int n_info);
 
@@ -192,6 +193,51 @@ int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int6
  * up (MTRTQ_OK or MTRTQ_ERR_TIMEOUT). Synchronizes the current device. After a
  * timeout the workspace of the failed call must be zero-filled again. */
 int mtrtq_read_status(int* device_status);
+
+/* ---- KV-cache decode loop helpers --------------------------------------------
+ * The steps of the reference's KVDecoder::step (tools/run_gpt2.cpp:135-191) around
+ * its MatMulQ calls, as device launches on `stream`, so that a whole decode step
+ * (embedding, 12 x {LayerNorm, QKV, attention, out-proj, residual, LayerNorm, FFN-up,
+ * gelu_new, FFN-down, residual}, final LayerNorm, LM head, argmax) can be captured
+ * once as a CUDA graph and replayed. All sequences of the batch sit at one position
+ * `*pos` (device int32), which mtrtq_decode_advance increments. fp32 throughout.
+ * They return MTRTQ_ERR_INVALID_ARG or MTRTQ_ERR_CUDA (launch failure). */
+
+/* x[b, :] = wte[tok, :] + wpe[*pos, :] (tools/run_gpt2.cpp:138-140), tok =
+ * prompt[b * prompt_len + *pos] while *pos < prompt_len, else next_tok[b]. wte
+ * [V, D], wpe [n_pos, D]; a position past n_pos gives zeros. */
+int mtrtq_decode_embed(const int32_t* prompt, int64_t prompt_len, const int32_t* next_tok,
+                       const int32_t* pos, const float* wte, const float* wpe, int64_t n_pos, float* x,
+                       int64_t B, int64_t D, int64_t V, void* stream);
+
+/* Row-wise LayerNorm, biased variance (tools/run_gpt2.cpp:113-122,
+ * src/ops/kernels_transformer.cpp:19-54): y = (x - mean) / sqrt(var + eps) * gamma + beta. */
+int mtrtq_layernorm(const float* x, const float* gamma, const float* beta, float* y, int64_t rows,
+                    int64_t D, float eps, void* stream);
+
+/* Attention of each sequence's new query over its cached keys (tools/run_gpt2.cpp:
+ * 143-172): qkv [B, 3*H*head_dim] rows (q | k | v); appends k and v at *pos into
+ * kcache / vcache [B, max_ctx, H*head_dim]; out [B, H*head_dim] =
+ * softmax(q . K^T / sqrt(head_dim)) V over positions 0..*pos per head. */
+int mtrtq_decode_attention(const float* qkv, float* kcache, float* vcache, const int32_t* pos,
+                           float* out, int64_t B, int64_t H, int64_t head_dim, int64_t max_ctx,
+                           void* stream);
+
+/* GPT-2 gelu_new (tools/run_gpt2.cpp:178-181, src/ops/kernels_gpt.cpp:44-61):
+ * y = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))). y may alias x. */
+int mtrtq_gelu_tanh(const float* x, float* y, int64_t n, void* stream);
+
+/* y += a (the residual adds, tools/run_gpt2.cpp:174, :183). */
+int mtrtq_add_inplace(float* y, const float* a, int64_t n, void* stream);
+
+/* Greedy next token (tools/run_gpt2.cpp:42-47): tok[r] = the first index of the
+ * maximum of logits[r, 0..V) (row stride ldl); also history[*pos * rows + r] when
+ * *pos < history_len. */
+int mtrtq_argmax_rows(const float* logits, int64_t rows, int64_t V, int64_t ldl, int32_t* tok,
+                      int32_t* history, const int32_t* pos, int64_t history_len, void* stream);
+
+/* *pos += 1 (one thread). */
+int mtrtq_decode_advance(int32_t* pos, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -52,6 +52,13 @@ SIGNATURES = {
     "mtrtq_read_status": (_int, [_vp]),
     "mtrtq_matmul_gemv_noalloc": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                          _int, _vp]),
+    "mtrtq_decode_embed": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp]),
+    "mtrtq_layernorm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "mtrtq_decode_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "mtrtq_gelu_tanh": (_int, [_vp, _vp, _i64, _vp]),
+    "mtrtq_add_inplace": (_int, [_vp, _vp, _i64, _vp]),
+    "mtrtq_argmax_rows": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
+    "mtrtq_decode_advance": (_int, [_vp, _vp]),
 }
 NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
 

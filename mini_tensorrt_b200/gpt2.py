@@ -1,0 +1,226 @@
+"""GPT-2 KV-cache greedy decoding on the device, every Linear an int8 MatMulQ.
+
+The reference decodes one token at a time on the CPU (KVDecoder,
+tools/run_gpt2.cpp:88-191, with fp32 `cpu::gemm_auto` for every Linear and the LM
+head). Here one decode step runs on the GPU as one CUDA graph: the embedding,
+per layer LayerNorm -> QKV MatMulQ (+bias) -> attention over the KV cache ->
+out-proj MatMulQ (+bias) -> residual -> LayerNorm -> FFN-up MatMulQ (+bias) ->
+gelu_new -> FFN-down MatMulQ (+bias) -> residual, the final LayerNorm, the LM head
+MatMulQ (weights tied to the token embedding) and the greedy argmax, all through
+libmtrtq's C ABI. Q, K and V use one 768x2304 weight: per-column quantization makes
+that identical to three separate 768x768 weights.
+
+A batch of B sequences is B rows of every MatMulQ (M = B). The prompt is consumed
+token by token, as the reference's prefill does (tools/run_gpt2.cpp:205).
+
+Weights here are random (the architecture of GPT-2 small, N(0, 0.02) for every
+matrix, embedding and bias, LayerNorm gamma 1 and beta 0), seeded per tensor.
+"""
+from __future__ import annotations
+
+import zlib
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .matmulq import MODES, PackedWeight, Workspace, quantize_per_channel, workspace_bytes
+
+
+@dataclass(frozen=True)
+class GPT2Config:
+    n_layer: int = 12
+    d_model: int = 768
+    n_head: int = 12
+    d_ff: int = 3072
+    vocab: int = 50257
+    n_pos: int = 1024
+    eps: float = 1e-5
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.n_head
+
+
+def _seed(base: int, name: str) -> int:
+    return (base * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFF
+
+
+def _normal(base: int, name: str, shape) -> np.ndarray:
+    g = np.random.default_rng(_seed(base, name))
+    return g.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+
+
+@dataclass
+class GPT2Weights:
+    """Host weights: fp32 embeddings, LayerNorm and biases; int8 + per-column scale
+    for every Linear (W [K, N], the reference's layout), lm_head = wte^T."""
+    cfg: GPT2Config
+    wte: np.ndarray
+    wpe: np.ndarray
+    layers: list = field(default_factory=list)
+    ln_f: tuple = None
+    lm_head: tuple = None  # (q int8 [D, V], s [V])
+
+
+def random_weights(cfg: GPT2Config = GPT2Config(), seed: int = 0) -> GPT2Weights:
+    D, F = cfg.d_model, cfg.d_ff
+    wte = _normal(seed, "wte", (cfg.vocab, D))
+    w = GPT2Weights(cfg, wte, _normal(seed, "wpe", (cfg.n_pos, D)))
+    ones, zeros = np.ones(D, np.float32), np.zeros(D, np.float32)
+    for l in range(cfg.n_layer):
+        p = f"l{l}_"
+        w.layers.append({
+            "ln1": (ones, zeros),
+            "qkv": quantize_per_channel(_normal(seed, p + "Wqkv", (D, 3 * D))),
+            "bqkv": _normal(seed, p + "bqkv", (3 * D,)),
+            "o": quantize_per_channel(_normal(seed, p + "Wo", (D, D))),
+            "bo": _normal(seed, p + "bo", (D,)),
+            "ln2": (ones, zeros),
+            "fc": quantize_per_channel(_normal(seed, p + "Wfc", (D, F))),
+            "bfc": _normal(seed, p + "bfc", (F,)),
+            "proj": quantize_per_channel(_normal(seed, p + "Wproj", (F, D))),
+            "bproj": _normal(seed, p + "bproj", (D,)),
+        })
+    w.ln_f = (ones, zeros)
+    w.lm_head = quantize_per_channel(np.ascontiguousarray(wte.T))
+    return w
+
+
+class DeviceDecoder:
+    """Greedy KV-cache decoding of `batch` sequences on one GPU.
+
+    mode: MatMulQ mode for every Linear ("fp32" keeps the activations in fp32;
+    "bf16" rounds them to bf16 before each product)."""
+
+    def __init__(self, w: GPT2Weights, batch: int, max_ctx: int, mode: str = "fp32",
+                 device="cuda", max_steps: int | None = None):
+        cfg = w.cfg
+        self.cfg, self.B, self.max_ctx, self.mode = cfg, batch, max_ctx, mode
+        if max_ctx > cfg.n_pos:
+            raise ValueError("max_ctx exceeds the position table")
+        self.dev = torch.device(device)
+        dev = self.dev
+        f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        pk = lambda qs: PackedWeight.from_int8(torch.from_numpy(qs[0]), torch.from_numpy(qs[1]), dev)
+        self.wte, self.wpe = f32(w.wte), f32(w.wpe)
+        self.layers = []
+        for L in w.layers:
+            self.layers.append({
+                "ln1": (f32(L["ln1"][0]), f32(L["ln1"][1])), "qkv": pk(L["qkv"]), "bqkv": f32(L["bqkv"]),
+                "o": pk(L["o"]), "bo": f32(L["bo"]), "ln2": (f32(L["ln2"][0]), f32(L["ln2"][1])),
+                "fc": pk(L["fc"]), "bfc": f32(L["bfc"]), "proj": pk(L["proj"]), "bproj": f32(L["bproj"]),
+            })
+        self.ln_f = (f32(w.ln_f[0]), f32(w.ln_f[1]))
+        self.lm_head = pk(w.lm_head)
+        B, D, F, V = batch, cfg.d_model, cfg.d_ff, cfg.vocab
+        z = lambda *s: torch.zeros(s, dtype=torch.float32, device=dev)
+        self.x, self.h, self.attn, self.ao = z(B, D), z(B, D), z(B, D), z(B, D)
+        self.qkv, self.mh, self.logits = z(B, 3 * D), z(B, F), z(B, V)
+        self.kc = [z(B, max_ctx, D) for _ in range(cfg.n_layer)]
+        self.vc = [z(B, max_ctx, D) for _ in range(cfg.n_layer)]
+        self.next_tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.max_steps = max_steps or max_ctx
+        self.history = torch.zeros((self.max_steps, B), dtype=torch.int32, device=dev)
+        self.prompt = torch.zeros((B, 1), dtype=torch.int32, device=dev)
+        xd = torch.float32
+        need = max(workspace_bytes(B, K, N, xd, mode)
+                   for K, N in [(D, 3 * D), (D, D), (D, F), (F, D), (D, V)])
+        self.ws = Workspace(dev)
+        self.ws_buf = self.ws.get(need)
+        self.graph = None
+        self.stream = torch.cuda.Stream(dev)
+
+    # -- one decode step, as launches on self.stream ------------------------------
+    def _mm(self, x, w: PackedWeight, bias, y):
+        ws = self.ws_buf
+        check(lib().mtrtq_matmul(x.data_ptr(), _lib.DTYPE_F32, x.stride(0), w.packed.data_ptr(),
+                                 w.scale.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                 y.data_ptr(), y.stride(0), x.shape[0], w.K, w.N, MODES[self.mode],
+                                 ws.data_ptr() if ws is not None else None,
+                                 ws.numel() if ws is not None else 0, self._sp), "mtrtq_matmul")
+
+    def _launch_step(self):
+        cfg, B, D, sp, L = self.cfg, self.B, self.cfg.d_model, self._sp, lib()
+        P = self.prompt.shape[1]
+        check(L.mtrtq_decode_embed(self.prompt.data_ptr(), P, self.next_tok.data_ptr(),
+                                   self.pos.data_ptr(), self.wte.data_ptr(), self.wpe.data_ptr(),
+                                   cfg.n_pos, self.x.data_ptr(), B, D, cfg.vocab, sp), "embed")
+        for i, ly in enumerate(self.layers):
+            check(L.mtrtq_layernorm(self.x.data_ptr(), ly["ln1"][0].data_ptr(), ly["ln1"][1].data_ptr(),
+                                    self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
+            self._mm(self.h, ly["qkv"], ly["bqkv"], self.qkv)
+            check(L.mtrtq_decode_attention(self.qkv.data_ptr(), self.kc[i].data_ptr(),
+                                           self.vc[i].data_ptr(), self.pos.data_ptr(),
+                                           self.attn.data_ptr(), B, cfg.n_head, cfg.head_dim,
+                                           self.max_ctx, sp), "attention")
+            self._mm(self.attn, ly["o"], ly["bo"], self.ao)
+            check(L.mtrtq_add_inplace(self.x.data_ptr(), self.ao.data_ptr(), B * D, sp), "add")
+            check(L.mtrtq_layernorm(self.x.data_ptr(), ly["ln2"][0].data_ptr(), ly["ln2"][1].data_ptr(),
+                                    self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
+            self._mm(self.h, ly["fc"], ly["bfc"], self.mh)
+            check(L.mtrtq_gelu_tanh(self.mh.data_ptr(), self.mh.data_ptr(), self.mh.numel(), sp), "gelu")
+            self._mm(self.mh, ly["proj"], ly["bproj"], self.ao)
+            check(L.mtrtq_add_inplace(self.x.data_ptr(), self.ao.data_ptr(), B * D, sp), "add")
+        check(L.mtrtq_layernorm(self.x.data_ptr(), self.ln_f[0].data_ptr(), self.ln_f[1].data_ptr(),
+                                self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
+        self._mm(self.h, self.lm_head, None, self.logits)
+        check(L.mtrtq_argmax_rows(self.logits.data_ptr(), B, cfg.vocab, cfg.vocab,
+                                  self.next_tok.data_ptr(), self.history.data_ptr(),
+                                  self.pos.data_ptr(), self.max_steps, sp), "argmax")
+        check(L.mtrtq_decode_advance(self.pos.data_ptr(), sp), "advance")
+
+    @property
+    def _sp(self) -> int:
+        return self.stream.cuda_stream
+
+    def _reset(self, prompt: torch.Tensor):
+        with torch.cuda.stream(self.stream):
+            if self.prompt.shape != prompt.shape:
+                self.prompt = torch.empty_like(prompt, device=self.dev)
+                self.graph = None  # the graph holds the prompt's address and length
+            self.prompt.copy_(prompt)
+            self.pos.zero_()
+            self.next_tok.zero_()
+            self.history.zero_()
+
+    def generate(self, prompt, max_new: int, use_graph: bool = True) -> dict:
+        """prompt: int [B, P] token ids. Runs P + max_new - 1 steps (the P prompt
+        positions, then one per generated token after the first) and returns
+        {"tokens": int32 [B, max_new], "prefill_s", "decode_s"} with the step times
+        measured by CUDA events."""
+        prompt = torch.as_tensor(np.asarray(prompt), dtype=torch.int32)
+        B, P = prompt.shape
+        if B != self.B:
+            raise ValueError(f"batch {B} != {self.B}")
+        steps = P + max_new - 1
+        if steps > self.max_ctx or steps > self.max_steps:
+            raise ValueError("prompt + max_new exceeds max_ctx")
+        self._reset(prompt)
+        if use_graph and self.graph is None:
+            # one eager step (per-device setup), then capture one step and reset
+            with torch.cuda.stream(self.stream):
+                self._launch_step()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self._launch_step()
+            self.graph = g
+            self._reset(prompt)
+        run = (lambda: self.graph.replay()) if use_graph else self._launch_step
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        with torch.cuda.stream(self.stream):
+            ev[0].record(self.stream)
+            for _ in range(P):
+                run()
+            ev[1].record(self.stream)
+            for _ in range(max_new - 1):
+                run()
+            ev[2].record(self.stream)
+        torch.cuda.synchronize()
+        hist = self.history[P - 1:P - 1 + max_new].t().contiguous().cpu().numpy()
+        return {"tokens": hist, "prefill_s": ev[0].elapsed_time(ev[1]) / 1e3,
+                "decode_s": ev[1].elapsed_time(ev[2]) / 1e3, "steps": steps}
