@@ -128,6 +128,24 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
                  const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N,
                  int mode, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Epilogues of mtrtq_matmul_ex: what happens to t = scale[j] * sum + bias[j]. */
+enum {
+  MTRTQ_EPILOGUE_NONE = 0,        /* Y = t (mtrtq_matmul) */
+  MTRTQ_EPILOGUE_GELU_TANH = 1,   /* Y = gelu_new(t): the int8 form of the reference's
+                                     FusedMatMulBiasGeluTanh (src/ops/kernels_fused.cpp:19-59) */
+  MTRTQ_EPILOGUE_ADD_RESIDUAL = 2 /* Y = residual[i*ldr + j] + t: MatMulQ + Add + the
+                                     residual Add of the decoder (tools/run_gpt2.cpp:174);
+                                     residual may be Y itself (in place) */
+};
+
+/* mtrtq_matmul with an epilogue fused into the kernel's store. residual (device
+ * f32, row stride ldr >= N, 4-byte aligned) is read only by
+ * MTRTQ_EPILOGUE_ADD_RESIDUAL. */
+int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                    const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
+                    void* workspace, size_t workspace_bytes, int epilogue, const float* residual,
+                    int64_t ldr, void* stream);
+
 /* Y = X x dequant(W) (+ bias) through the decode GEMV (CUDA cores, split-K), with
  * the same arguments and results as mtrtq_matmul on its GEMV path, but without a
  * caller workspace and without allocating anything.
@@ -230,14 +248,16 @@ int mtrtq_gelu_tanh(const float* x, float* y, int64_t n, void* stream);
 /* y += a (the residual adds, tools/run_gpt2.cpp:174, :183). */
 int mtrtq_add_inplace(float* y, const float* a, int64_t n, void* stream);
 
-/* Greedy next token (tools/run_gpt2.cpp:42-47): tok[r] = the first index of the
- * maximum of logits[r, 0..V) (row stride ldl); also history[*pos * rows + r] when
- * *pos < history_len. */
-int mtrtq_argmax_rows(const float* logits, int64_t rows, int64_t V, int64_t ldl, int32_t* tok,
-                      int32_t* history, const int32_t* pos, int64_t history_len, void* stream);
-
-/* *pos += 1 (one thread). */
-int mtrtq_decode_advance(int32_t* pos, void* stream);
+/* Greedy next token (tools/run_gpt2.cpp:42-47), in two launches.
+ * mtrtq_argmax_rows folds the maximum of logits[r, 0..V) (row stride ldl) into
+ * best[r], a 64-bit key holding the value and, among equal values, the first
+ * index; best[] (device, rows entries) must be zero before the first fold.
+ * mtrtq_decode_next then sets tok[r] to that index and history[*pos * rows + r]
+ * too (when *pos < history_len), zeroes best[] and advances *pos by one. */
+int mtrtq_argmax_rows(const float* logits, int64_t rows, int64_t V, int64_t ldl,
+                      unsigned long long* best, void* stream);
+int mtrtq_decode_next(unsigned long long* best, int64_t rows, int32_t* tok, int32_t* history,
+                      int64_t history_len, int32_t* pos, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -30,6 +30,7 @@ ZERO_COLUMN_ZERO = 1
 OPT_GEMM_A_SOURCE = 1
 OPT_FORCE_PATH = 2
 OPT_OVERLAP_LAUNCH = 3
+EPILOGUE_NONE, EPILOGUE_GELU_TANH, EPILOGUE_ADD_RESIDUAL = 0, 1, 2
 
 # Every function the header declares, with its ctypes signature.
 _vp = ctypes.c_void_p
@@ -47,6 +48,8 @@ SIGNATURES = {
     "mtrtq_workspace_bytes": (_i64, [_i64, _i64, _i64, _int, _int]),
     "mtrtq_matmul": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int,
                             _vp, _sz, _vp]),
+    "mtrtq_matmul_ex": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int,
+                               _vp, _sz, _int, _vp, _i64, _vp]),
     "mtrtq_set_option": (_int, [_int, _i64]),
     "mtrtq_plan_info": (_int, [_i64, _i64, _i64, _int, _int, _vp, _int]),
     "mtrtq_read_status": (_int, [_vp]),
@@ -57,8 +60,8 @@ SIGNATURES = {
     "mtrtq_decode_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "mtrtq_gelu_tanh": (_int, [_vp, _vp, _i64, _vp]),
     "mtrtq_add_inplace": (_int, [_vp, _vp, _i64, _vp]),
-    "mtrtq_argmax_rows": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
-    "mtrtq_decode_advance": (_int, [_vp, _vp]),
+    "mtrtq_argmax_rows": (_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "mtrtq_decode_next": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp]),
 }
 NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
 

@@ -429,7 +429,27 @@ int64_t mtrtq_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int 
 int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                  const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
                  void* workspace, size_t workspace_bytes, void* stream) {
+  return mtrtq_matmul_ex(X, x_dtype, ldx, packed, scale, bias, Y, ldy, M, K, N, mode, workspace,
+                         workspace_bytes, MTRTQ_EPILOGUE_NONE, nullptr, 0, stream);
+}
+
+int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                    const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
+                    void* workspace, size_t workspace_bytes, int epilogue, const float* residual,
+                    int64_t ldr, void* stream) {
   if (!X || !packed || !scale || !Y) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  if (epilogue != MTRTQ_EPILOGUE_NONE && epilogue != MTRTQ_EPILOGUE_GELU_TANH &&
+      epilogue != MTRTQ_EPILOGUE_ADD_RESIDUAL)
+    return fail(MTRTQ_ERR_INVALID_ARG, "unknown epilogue %d", epilogue);
+  Epilogue epi;
+  epi.kind = epilogue;
+  if (epilogue == MTRTQ_EPILOGUE_ADD_RESIDUAL) {
+    if (!residual) return fail(MTRTQ_ERR_INVALID_ARG, "the residual epilogue needs a residual");
+    if (ldr < N) return fail(MTRTQ_ERR_INVALID_ARG, "ldr (%lld) < N (%lld)", (long long)ldr, (long long)N);
+    if (!aligned(residual, 4)) return fail(MTRTQ_ERR_ALIGNMENT, "residual must be 4-byte aligned");
+    epi.residual = residual;
+    epi.ldr = ldr;
+  }
   if (ldx < K) return fail(MTRTQ_ERR_INVALID_ARG, "ldx (%lld) < K (%lld)", (long long)ldx, (long long)K);
   if (ldy < N) return fail(MTRTQ_ERR_INVALID_ARG, "ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
   DeviceInfo d;
@@ -448,7 +468,7 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (p.kind == Plan::kGemv) {
-    e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, workspace, st);
+    e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, workspace, epi, st);
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     return MTRTQ_OK;
   }
@@ -457,7 +477,7 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   if (e != cudaSuccess) return cuda_fail(e, "device status address");
   if (p.kind == Plan::kGemvCluster) {
     e = launch_gemv_cluster(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, status,
-                            g_opt_overlap != 0, st);
+                            g_opt_overlap != 0, epi, st);
     if (e != cudaSuccess) return cuda_fail(e, "cluster GEMV launch");
     return MTRTQ_OK;
   }
@@ -465,7 +485,7 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
     CUtensorMap unused;
     std::memset(&unused, 0, sizeof(unused));
     e = launch_skinny_tc(p, scale, bias, Y, ldy, packed, workspace, unused, true, X, ldx, x_dtype,
-                         status, st);
+                         status, epi, st);
     if (e != cudaSuccess) return cuda_fail(e, "stream-K kernel launch");
     return MTRTQ_OK;
   }
@@ -488,7 +508,7 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
     const int rc = make_x_tensor_map(&xmap, xsrc, M, K, ldxs, p.tile_m, x_f32);
     if (rc != 0) return fail(MTRTQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", rc);
     e = launch_skinny_tc(p, scale, bias, Y, ldy, packed, workspace, xmap, x_f32, xsrc, ldxs,
-                         x_f32 ? MTRTQ_DTYPE_F32 : MTRTQ_DTYPE_BF16, status, st);
+                         x_f32 ? MTRTQ_DTYPE_F32 : MTRTQ_DTYPE_BF16, status, epi, st);
     if (e != cudaSuccess) return cuda_fail(e, "stream-K kernel launch");
     return MTRTQ_OK;
   }
@@ -507,7 +527,7 @@ int mtrtq_matmul(const void* X, int x_dtype, int64_t ldx, const void* packed, co
   const int rc = make_x_tensor_map(&xmap, xb, M, K, ldxb, p.tile_m);
   if (rc != 0) return fail(MTRTQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", rc);
   e = launch_gemm_tc(p, xb, ldxb, packed, scale, bias, Y, ldy, workspace, xmap,
-                     g_opt_gemm_a_source == 0 ? 1 : 0, status, st);
+                     g_opt_gemm_a_source == 0 ? 1 : 0, status, epi, st);
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return MTRTQ_OK;
 }
@@ -569,7 +589,7 @@ int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const voi
   // gave up on a timeout may not, so clear them (memset: no allocation).
   cudaError_t e = cudaMemsetAsync(static_cast<char*>(scratch) + p.off_counters, 0, kCounterBytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "clear no-allocation counters");
-  e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, scratch, st);
+  e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, scratch, Epilogue(), st);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return MTRTQ_OK;
 }

@@ -5,14 +5,16 @@
 // (:138-140), LayerNorm with biased variance and eps 1e-5 (:113-122), attention
 // of the new query over the cached keys and values (:146-172), gelu_new
 // (:178-181), the residual adds (:174, :183) and the greedy argmax
-// (:42-47, first index of the maximum). All sequences of a batch sit at the same
+// (:42-47, first index of the maximum; the residual adds and gelu_new are also
+// available fused into MatMulQ, mtrtq_matmul_ex). All sequences of a batch sit at the same
 // position, which lives in device memory so that one CUDA graph replays every
 // step; the embedding reads the prompt while the position is inside it, and the
 // previous step's argmax after it.
 //
-// The arithmetic is fp32 in the reference's order where it has one (mean, then
-// the biased variance of the centred values; scores, max, exp and sum in key
-// order; weights times values in key order); block reductions add in a tree.
+// The arithmetic is fp32 with the reference's formulas (mean, then the biased
+// variance of the centred values; max-subtracted exponentials; weights times
+// values); sums over a row or over keys are split across threads and added in a
+// fixed tree order, so results do not depend on timing.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -57,42 +59,82 @@ __global__ void embed_kernel(const int32_t* prompt, int64_t prompt_len, const in
     x[b * D + i] = wte[tok * D + i] + wpe[(int64_t)pos * D + i];
 }
 
-// One block per row: y = (x - mean) / sqrt(var + eps) * gamma + beta.
+// One block per row: y = (x - mean) / sqrt(var + eps) * gamma + beta. Rows of up
+// to kLnRegs * blockDim.x elements stay in registers (one read of x); longer rows
+// are read again for each pass.
+constexpr int kLnRegs = 8;
+
 __global__ void layernorm_kernel(const float* x, const float* g, const float* bta, float* y,
                                  int64_t D, float eps) {
   __shared__ float red[32];
   const float* xr = x + blockIdx.x * D;
   float* yr = y + blockIdx.x * D;
+  const bool in_regs = D <= (int64_t)kLnRegs * blockDim.x;
+  float v[kLnRegs];
   float s = 0.0f;
-  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) s += xr[i];
-  const float mean = block_sum(s, red) / (float)D;
-  float v = 0.0f;
-  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
-    const float c = xr[i] - mean;
-    v += c * c;
+  if (in_regs) {
+#pragma unroll
+    for (int c = 0; c < kLnRegs; ++c) {
+      const int64_t i = threadIdx.x + (int64_t)c * blockDim.x;
+      v[c] = i < D ? xr[i] : 0.0f;
+    }
+#pragma unroll
+    for (int c = 0; c < kLnRegs; ++c) s += v[c];
+  } else {
+    for (int64_t i = threadIdx.x; i < D; i += blockDim.x) s += xr[i];
   }
-  const float var = block_sum(v, red) / (float)D;
+  const float mean = block_sum(s, red) / (float)D;
+  float q = 0.0f;
+  if (in_regs) {
+#pragma unroll
+    for (int c = 0; c < kLnRegs; ++c) {
+      const int64_t i = threadIdx.x + (int64_t)c * blockDim.x;
+      const float cv = v[c] - mean;
+      if (i < D) q += cv * cv;
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
+      const float c = xr[i] - mean;
+      q += c * c;
+    }
+  }
+  const float var = block_sum(q, red) / (float)D;
   const float inv = 1.0f / sqrtf(var + eps);
-  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) yr[i] = (xr[i] - mean) * inv * g[i] + bta[i];
+  if (in_regs) {
+#pragma unroll
+    for (int c = 0; c < kLnRegs; ++c) {
+      const int64_t i = threadIdx.x + (int64_t)c * blockDim.x;
+      if (i < D) yr[i] = (v[c] - mean) * inv * g[i] + bta[i];
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < D; i += blockDim.x) yr[i] = (xr[i] - mean) * inv * g[i] + bta[i];
+  }
 }
 
-// One block per (head, sequence). qkv: [B, 3D] rows (q | k | v). Appends this
-// position's k and v (its head slice) to the caches [B, max_ctx, D], then
+// One block (8 warps) per (head, sequence). qkv: [B, 3D] rows (q | k | v). Appends
+// this position's k and v (its head slice) to the caches [B, max_ctx, D], then
 // out[b, head slice] = softmax(q . K / sqrt(d)) V over cached positions 0..pos.
-// Dynamic shared memory: max_ctx + head_dim floats.
+// Scores: a warp per key. Softmax: the max and the sum of exponentials over the
+// keys in key order by one warp (lane j reduces keys j, j+32, ... then the lanes
+// in order). Weighted sum: warp w takes keys w, w+8, ... for all head_dim
+// columns (lane -> columns), and the 8 warps' sums are added in warp order.
+// Dynamic shared memory: head_dim + max_ctx + 8 * head_dim floats.
+constexpr int kAttnWarps = 8;
+
 __global__ void attention_kernel(const float* qkv, float* kc, float* vc, const int32_t* pos_p,
                                  float* out, int64_t H, int64_t hd, int64_t max_ctx) {
   extern __shared__ float sm[];
-  __shared__ float red[32];
+  __shared__ float stat[2];
   const int64_t h = blockIdx.x, b = blockIdx.y;
   const int64_t D = H * hd;
   const int pos = *pos_p;
   if (pos < 0 || pos >= max_ctx) {  // past the cache: zeros, no access out of bounds
-    for (int64_t t = threadIdx.x; t < hd; t += blockDim.x) out[b * H * hd + h * hd + t] = 0.0f;
+    for (int64_t t = threadIdx.x; t < hd; t += blockDim.x) out[b * D + h * hd + t] = 0.0f;
     return;
   }
-  float* qs = sm;            // [hd]
-  float* sc = sm + hd;       // [max_ctx]
+  float* qs = sm;                 // [hd]
+  float* sc = sm + hd;            // [max_ctx]
+  float* part = sc + max_ctx;     // [kAttnWarps][hd]
   const float* row = qkv + b * 3 * D;
   float* kb = kc + b * max_ctx * D;
   float* vb = vc + b * max_ctx * D;
@@ -103,9 +145,8 @@ __global__ void attention_kernel(const float* qkv, float* kc, float* vc, const i
   }
   __syncthreads();
   const float scale = 1.0f / sqrtf((float)hd);
-  // scores: one warp per key, lanes over the head dimension
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int j = warp; j <= pos; j += nw) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int j = warp; j <= pos; j += kAttnWarps) {
     const float* kj = kb + (int64_t)j * D + h * hd;
     float s = 0.0f;
     for (int64_t t = lane; t < hd; t += 32) s += qs[t] * kj[t];
@@ -113,22 +154,45 @@ __global__ void attention_kernel(const float* qkv, float* kc, float* vc, const i
     if (lane == 0) sc[j] = s * scale;
   }
   __syncthreads();
-  // max, then exp and sum in key order (one thread: at most max_ctx terms)
-  if (threadIdx.x == 0) {
+  if (warp == 0) {
     float mx = -1e30f;
-    for (int j = 0; j <= pos; ++j) mx = sc[j] > mx ? sc[j] : mx;
+    for (int j = lane; j <= pos; j += 32) mx = fmaxf(mx, sc[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.0f;
-    for (int j = 0; j <= pos; ++j) {
-      sc[j] = expf(sc[j] - mx);
-      sum += sc[j];
+    for (int j = lane; j <= pos; j += 32) {
+      const float e = expf(sc[j] - mx);
+      sc[j] = e;
+      sum += e;
     }
-    red[0] = 1.0f / sum;
+    sum = warp_sum(sum);
+    if (lane == 0) stat[0] = 1.0f / sum;
   }
   __syncthreads();
-  const float inv = red[0];
+  const float inv = stat[0];
+  for (int64_t t0 = 0; t0 < hd; t0 += 32) {
+    const int64_t t = t0 + lane;
+    float a = 0.0f;
+    if (t < hd) {
+      int j = warp;
+      for (; j + 3 * kAttnWarps <= pos; j += 4 * kAttnWarps) {  // four keys' loads in flight
+        const float v0 = vb[(int64_t)j * D + h * hd + t];
+        const float v1 = vb[(int64_t)(j + kAttnWarps) * D + h * hd + t];
+        const float v2 = vb[(int64_t)(j + 2 * kAttnWarps) * D + h * hd + t];
+        const float v3 = vb[(int64_t)(j + 3 * kAttnWarps) * D + h * hd + t];
+        a += (sc[j] * inv) * v0;
+        a += (sc[j + kAttnWarps] * inv) * v1;
+        a += (sc[j + 2 * kAttnWarps] * inv) * v2;
+        a += (sc[j + 3 * kAttnWarps] * inv) * v3;
+      }
+      for (; j <= pos; j += kAttnWarps) a += (sc[j] * inv) * vb[(int64_t)j * D + h * hd + t];
+      part[warp * hd + t] = a;
+    }
+  }
+  __syncthreads();
   for (int64_t t = threadIdx.x; t < hd; t += blockDim.x) {
     float a = 0.0f;
-    for (int j = 0; j <= pos; ++j) a += (sc[j] * inv) * vb[(int64_t)j * D + h * hd + t];
+    for (int w = 0; w < kAttnWarps; ++w) a += part[w * hd + t];
     out[b * D + h * hd + t] = a;
   }
 }
@@ -147,52 +211,62 @@ __global__ void add_kernel(float* y, const float* a, int64_t n) {
     y[i] += a[i];
 }
 
-// One block per row: the first index of the row's maximum -> tok[row] and
-// history[pos * rows + row].
-__global__ void argmax_kernel(const float* logits, int64_t V, int64_t ldl, int32_t* tok,
-                              int32_t* history, const int32_t* pos_p, int64_t history_len) {
-  __shared__ float bv[32];
-  __shared__ int bi[32];
-  const float* r = logits + blockIdx.x * ldl;
-  float best = -INFINITY;
-  int idx = 0x7fffffff;
-  for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
+// Greedy argmax in two launches. A 64-bit key orders (value, index) so that the
+// larger key is the larger value and, between equal values, the lower index:
+// high word = the float's bits made monotonic as an unsigned integer, low word =
+// ~index. argmax_fold_kernel: one block per (chunk of 4096 logits, row) folds its
+// chunk's best key into best[row] with atomicMax (order-free, so deterministic).
+// NaN logits are skipped.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t hi = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)hi << 32) | (uint32_t)(~(uint32_t)idx);
+}
+
+constexpr int kArgmaxChunk = 4096;
+
+__global__ void argmax_fold_kernel(const float* logits, int64_t V, int64_t ldl, unsigned long long* best) {
+  __shared__ unsigned long long bk[32];
+  const float* r = logits + blockIdx.y * ldl;
+  const int64_t j0 = (int64_t)blockIdx.x * kArgmaxChunk;
+  const int64_t j1 = j0 + kArgmaxChunk < V ? j0 + kArgmaxChunk : V;
+  unsigned long long k = 0;
+  for (int64_t j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
     const float v = r[j];
-    if (v > best) {  // strictly greater: the first (lowest) index of this thread's max
-      best = v;
-      idx = (int)j;
+    if (v == v) {
+      const unsigned long long c = argmax_key(v, (int)j);
+      k = c > k ? c : k;
     }
   }
-  // ties between threads go to the lower index
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ov > best || (ov == best && oi < idx)) {
-      best = ov;
-      idx = oi;
-    }
+    const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+    k = ok > k ? ok : k;
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  if (lane == 0) {
-    bv[warp] = best;
-    bi[warp] = idx;
-  }
+  if (lane == 0) bk[warp] = k;
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < nw; ++w)
-      if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
-        best = bv[w];
-        idx = bi[w];
-      }
-    if (idx == 0x7fffffff) idx = 0;  // an all-NaN row
-    tok[blockIdx.x] = idx;
-    const int pos = *pos_p;
-    if (history && pos < history_len) history[(int64_t)pos * gridDim.x + blockIdx.x] = idx;
+    for (int w = 1; w < nw; ++w) k = bk[w] > k ? bk[w] : k;
+    if (k) atomicMax(best + blockIdx.y, k);
   }
 }
 
-__global__ void advance_kernel(int32_t* pos) { *pos += 1; }
+// tok[r] = the index in best[r] (0 for a row with no finite logit), history[*pos *
+// rows + r] too, best[r] = 0 for the next step; then *pos += 1.
+__global__ void decode_next_kernel(unsigned long long* best, int64_t rows, int32_t* tok, int32_t* history,
+                                   int64_t history_len, int32_t* pos) {
+  const int p = *pos;
+  for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
+    const unsigned long long k = best[r];
+    const int idx = k ? (int)(~(uint32_t)(k & 0xffffffffu)) : 0;
+    tok[r] = idx;
+    if (history && p >= 0 && p < history_len) history[(int64_t)p * rows + r] = idx;
+    best[r] = 0ull;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *pos = p + 1;
+}
 
 int launch_status(cudaError_t e) { return e == cudaSuccess ? MTRTQ_OK : MTRTQ_ERR_CUDA; }
 
@@ -227,9 +301,10 @@ int mtrtq_decode_attention(const float* qkv, float* kcache, float* vcache, const
   if (!qkv || !kcache || !vcache || !pos || !out || B <= 0 || H <= 0 || head_dim <= 0 ||
       max_ctx <= 0 || B > 65535 || H > 2147483647)
     return MTRTQ_ERR_INVALID_ARG;
-  const size_t smem = (size_t)(max_ctx + head_dim) * sizeof(float);
-  if (smem > 48 * 1024) return MTRTQ_ERR_INVALID_ARG;  // contexts up to ~12k positions
-  attention_kernel<<<dim3((unsigned)H, (unsigned)B), 128, smem, static_cast<cudaStream_t>(stream)>>>(
+  const size_t smem = (size_t)(max_ctx + (1 + kAttnWarps) * head_dim) * sizeof(float);
+  if (smem > 48 * 1024) return MTRTQ_ERR_INVALID_ARG;  // contexts up to ~11k positions at d = 64
+  attention_kernel<<<dim3((unsigned)H, (unsigned)B), 32 * kAttnWarps, smem,
+                     static_cast<cudaStream_t>(stream)>>>(
       qkv, kcache, vcache, pos, out, H, head_dim, max_ctx);
   return launch_status(cudaGetLastError());
 }
@@ -248,19 +323,21 @@ int mtrtq_add_inplace(float* y, const float* a, int64_t n, void* stream) {
   return launch_status(cudaGetLastError());
 }
 
-int mtrtq_argmax_rows(const float* logits, int64_t rows, int64_t V, int64_t ldl, int32_t* tok,
-                      int32_t* history, const int32_t* pos, int64_t history_len, void* stream) {
-  if (!logits || !tok || !pos || rows <= 0 || V <= 0 || ldl < V || rows > 65535 ||
-      V > 2147483647 || (history_len > 0 && !history))
+int mtrtq_argmax_rows(const float* logits, int64_t rows, int64_t V, int64_t ldl,
+                      unsigned long long* best, void* stream) {
+  if (!logits || !best || rows <= 0 || V <= 0 || ldl < V || rows > 65535 || V > 2147483647)
     return MTRTQ_ERR_INVALID_ARG;
-  argmax_kernel<<<(unsigned)rows, 512, 0, static_cast<cudaStream_t>(stream)>>>(logits, V, ldl, tok, history,
-                                                                              pos, history_len);
+  const int64_t chunks = (V + kArgmaxChunk - 1) / kArgmaxChunk;
+  argmax_fold_kernel<<<dim3((unsigned)chunks, (unsigned)rows), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      logits, V, ldl, best);
   return launch_status(cudaGetLastError());
 }
 
-int mtrtq_decode_advance(int32_t* pos, void* stream) {
-  if (!pos) return MTRTQ_ERR_INVALID_ARG;
-  advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(pos);
+int mtrtq_decode_next(unsigned long long* best, int64_t rows, int32_t* tok, int32_t* history,
+                      int64_t history_len, int32_t* pos, void* stream) {
+  if (!best || !tok || !pos || rows <= 0 || (history_len > 0 && !history)) return MTRTQ_ERR_INVALID_ARG;
+  decode_next_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(best, rows, tok, history,
+                                                                    history_len, pos);
   return launch_status(cudaGetLastError());
 }
 

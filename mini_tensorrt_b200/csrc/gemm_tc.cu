@@ -34,6 +34,7 @@ struct GemmParams {
   const float* bias;
   float* Y;
   int64_t ldy;
+  Epilogue epi;
   int M, N, n_pad;
   int KB;                 // k blocks of 64 in K_pad
   int kb_per_split;
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(192, 1)
             if (n_ok && m < p.M) {
               float y = __fmul_rn(__uint_as_float(v[j]), sc);
               if (p.bias) y = __fadd_rn(y, b);
-              p.Y[(int64_t)m * p.ldy + n] = y;
+              p.Y[(int64_t)m * p.ldy + n] = epi_apply(p.epi, y, m, n);
             }
           }
         } else {
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(192, 1)
               if (m < p.M) {
                 float y = __fmul_rn(sum[j], sc);
                 if (p.bias) y = __fadd_rn(y, b);
-                p.Y[(int64_t)m * p.ldy + n] = y;
+                p.Y[(int64_t)m * p.ldy + n] = epi_apply(p.epi, y, m, n);
               }
             }
           }
@@ -340,10 +341,11 @@ bool gemm_tile_supported(int tile_m) {
 cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const void* packed,
                            const float* scale, const float* bias, float* Y, int64_t ldy,
                            void* workspace, const CUtensorMap& xmap, int a_from_tmem,
-                           unsigned* status, cudaStream_t st) {
+                           unsigned* status, const Epilogue& epi, cudaStream_t st) {
   (void)Xb;
   (void)ldxb;
   GemmParams gp;
+  gp.epi = epi;
   gp.W = static_cast<const uint8_t*>(packed);
   gp.scale = scale;
   gp.bias = bias;

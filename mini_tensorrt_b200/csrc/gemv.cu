@@ -32,6 +32,7 @@ struct GemvParams {
   const float* bias;
   float* Y;
   int64_t ldy;
+  Epilogue epi;
   int M, K, N;
   int n_pad;
   int KS;               // slabs of 16 in K_pad
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(128) gemv_q8_kernel(const GemvParams p) {
         if (m < mrem) {
           float y = __fmul_rn(r[m], sc);
           if (p.bias) y = __fadd_rn(y, b);
-          p.Y[(int64_t)(m0 + m) * p.ldy + n] = y;
+          p.Y[(int64_t)(m0 + m) * p.ldy + n] = epi_apply(p.epi, y, m0 + m, n);
         }
       }
     }
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(128) gemv_q8_kernel(const GemvParams p) {
       if (m < mrem) {
         float y = __fmul_rn(sum[m], sc);
         if (p.bias) y = __fadd_rn(y, b);
-        p.Y[(int64_t)(m0 + m) * p.ldy + n] = y;
+        p.Y[(int64_t)(m0 + m) * p.ldy + n] = epi_apply(p.epi, y, m0 + m, n);
       }
     }
   }
@@ -215,8 +216,9 @@ static cudaError_t launch_by_mt(int mt, const GemvParams& gp, dim3 grid, cudaStr
 
 cudaError_t launch_gemv(const Plan& p, const void* X, int x_dtype, int64_t ldx, const void* packed,
                         const float* scale, const float* bias, float* Y, int64_t ldy,
-                        void* workspace, cudaStream_t st) {
+                        void* workspace, const Epilogue& epi, cudaStream_t st) {
   GemvParams gp;
+  gp.epi = epi;
   gp.X = X;
   gp.ldx = ldx;
   gp.W = static_cast<const uint4*>(packed);

@@ -62,6 +62,7 @@ struct GemvClParams {
   const float* bias;
   float* Y;
   int64_t ldy;
+  Epilogue epi;
   int M, K, N;
   int KB;          // 64-k units per tile
   int stages;      // shared memory ring stages (2..kGemvClMaxStages)
@@ -520,7 +521,7 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
     if (n < p.N) {
       float y = __fmul_rn(sum, s_sb[0][r]);
       if (p.bias) y = __fadd_rn(y, s_sb[1][r]);
-      p.Y[(int64_t)m * p.ldy + n] = y;
+      p.Y[(int64_t)m * p.ldy + n] = epi_apply(p.epi, y, m, n);
     }
   }
   // No CTA leaves while another rank may still read its shared memory. Those
@@ -565,8 +566,10 @@ size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages) {
 
 cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,
                                 const void* packed, const float* scale, const float* bias, float* Y,
-                                int64_t ldy, unsigned* status, bool pdl, cudaStream_t st) {
+                                int64_t ldy, unsigned* status, bool pdl, const Epilogue& epi,
+                                cudaStream_t st) {
   GemvClParams gp;
+  gp.epi = epi;
   gp.X = X;
   gp.ldx = ldx;
   gp.W = static_cast<const char*>(packed);

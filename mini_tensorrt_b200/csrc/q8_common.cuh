@@ -14,6 +14,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "q8_internal.h"
+
 namespace mtrtq {
 
 // About one second of SM clock at B200 clocks: the cap on any spin-wait.
@@ -64,6 +66,19 @@ __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
+}
+
+// ---- epilogue ----------------------------------------------------------------
+
+// The epilogue (Epilogue, q8_internal.h) applied to t = (acc * scale) + bias
+// before the store.
+__device__ __forceinline__ float epi_apply(const Epilogue& e, float t, int64_t m, int64_t n) {
+  if (e.kind == 1) {
+    const float inner = 0.7978845608028654f * (t + 0.044715f * t * t * t);
+    return 0.5f * t * (1.0f + tanhf(inner));
+  }
+  if (e.kind == 2) return __fadd_rn(e.residual[m * e.ldr + n], t);
+  return t;
 }
 
 // ---- shared-memory addressing, mbarriers -------------------------------------

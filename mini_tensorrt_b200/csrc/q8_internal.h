@@ -8,6 +8,18 @@
 
 namespace mtrtq {
 
+// What a MatMulQ call does with t = (acc * scale) + bias before it stores it:
+//  kind 0: y = t;
+//  kind 1: y = gelu_new(t), the reference's FusedMatMulBiasGeluTanh activation
+//          (src/ops/kernels_fused.cpp:46-57);
+//  kind 2: y = residual[m, n] + t, the decoder's residual add (tools/run_gpt2.cpp:174).
+// residual may be Y itself: each element is read and written by the same thread.
+struct Epilogue {
+  int kind = 0;
+  const float* residual = nullptr;
+  int64_t ldr = 0;
+};
+
 // How one mtrtq_matmul call is carried out; computed by plan_matmul() from the
 // problem alone (and the device's SM count), so the workspace query and the
 // launch always agree.
@@ -57,7 +69,8 @@ constexpr int kGemvClMaxStages = 8;
 size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages);
 cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,
                                 const void* packed, const float* scale, const float* bias, float* Y,
-                                int64_t ldy, unsigned* status, bool pdl, cudaStream_t st);
+                                int64_t ldy, unsigned* status, bool pdl, const Epilogue& epi,
+                                cudaStream_t st);
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_prepack(const int8_t* q, int64_t K, int64_t N, void* packed, cudaStream_t st);
@@ -65,16 +78,16 @@ cudaError_t launch_x_to_bf16(const void* X, int x_dtype, int64_t ldx, int64_t M,
                              void* Xb, int64_t ldxb, cudaStream_t st);
 cudaError_t launch_gemv(const Plan& p, const void* X, int x_dtype, int64_t ldx, const void* packed,
                         const float* scale, const float* bias, float* Y, int64_t ldy,
-                        void* workspace, cudaStream_t st);
+                        void* workspace, const Epilogue& epi, cudaStream_t st);
 cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const void* packed,
                            const float* scale, const float* bias, float* Y, int64_t ldy,
                            void* workspace, const CUtensorMap& xmap, int a_from_tmem,
-                           unsigned* status, cudaStream_t st);
+                           unsigned* status, const Epilogue& epi, cudaStream_t st);
 
 cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bias, float* Y,
                              int64_t ldy, const void* packed, void* workspace,
                              const CUtensorMap& xmap, bool x_f32, const void* X, int64_t ldx,
-                             int x_dtype, unsigned* status, cudaStream_t st);
+                             int x_dtype, unsigned* status, const Epilogue& epi, cudaStream_t st);
 // True when the stream-K kernel keeps the whole bf16 activation matrix in shared
 // memory (it then reads X directly, at any stride, and needs no tensor map).
 bool skinny_x_resident(int tile_m, int64_t k_pad);

@@ -53,6 +53,7 @@ struct SkinnyParams {
   const float* bias;
   float* Y;
   int64_t ldy;
+  Epilogue epi;
   const void* X;          // activations (X_RES staging), row stride ldx elements
   int64_t ldx;
   int x_bf16;             // X element type for X_RES staging
@@ -441,7 +442,7 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
             if (j < p.M) {
               float y = __fmul_rn(v[j], sc);
               if (p.bias) y = __fadd_rn(y, bi);
-              p.Y[(int64_t)j * p.ldy + n] = y;
+              p.Y[(int64_t)j * p.ldy + n] = epi_apply(p.epi, y, j, n);
             }
           }
         }
@@ -495,7 +496,7 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
                 if (j0 + j < p.M) {
                   float y = __fmul_rn(sum[j], sc);
                   if (p.bias) y = __fadd_rn(y, bi);
-                  p.Y[(int64_t)(j0 + j) * p.ldy + n] = y;
+                  p.Y[(int64_t)(j0 + j) * p.ldy + n] = epi_apply(p.epi, y, j0 + j, n);
                 }
               }
             }
@@ -532,8 +533,9 @@ bool skinny_x_resident(int tile_m, int64_t k_pad) {
 cudaError_t launch_skinny_tc(const Plan& p, const float* scale, const float* bias, float* Y,
                              int64_t ldy, const void* packed, void* workspace,
                              const CUtensorMap& xmap, bool x_f32, const void* X, int64_t ldx,
-                             int x_dtype, unsigned* status, cudaStream_t st) {
+                             int x_dtype, unsigned* status, const Epilogue& epi, cudaStream_t st) {
   SkinnyParams sp;
+  sp.epi = epi;
   sp.W = static_cast<const uint8_t*>(packed);
   sp.scale = scale;
   sp.bias = bias;

@@ -4,8 +4,9 @@ The reference decodes one token at a time on the CPU (KVDecoder,
 tools/run_gpt2.cpp:88-191, with fp32 `cpu::gemm_auto` for every Linear and the LM
 head). Here one decode step runs on the GPU as one CUDA graph: the embedding,
 per layer LayerNorm -> QKV MatMulQ (+bias) -> attention over the KV cache ->
-out-proj MatMulQ (+bias) -> residual -> LayerNorm -> FFN-up MatMulQ (+bias) ->
-gelu_new -> FFN-down MatMulQ (+bias) -> residual, the final LayerNorm, the LM head
+out-proj MatMulQ (+bias, + residual fused into its store) -> LayerNorm -> FFN-up
+MatMulQ (+bias, gelu_new fused) -> FFN-down MatMulQ (+bias, + residual fused), the
+final LayerNorm, the LM head
 MatMulQ (weights tied to the token embedding) and the greedy argmax, all through
 libmtrtq's C ABI. Q, K and V use one 768x2304 weight: per-column quantization makes
 that identical to three separate 768x768 weights.
@@ -122,6 +123,7 @@ class DeviceDecoder:
         self.kc = [z(B, max_ctx, D) for _ in range(cfg.n_layer)]
         self.vc = [z(B, max_ctx, D) for _ in range(cfg.n_layer)]
         self.next_tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.best = torch.zeros(B, dtype=torch.int64, device=dev)  # argmax keys, zeroed per step
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.max_steps = max_steps or max_ctx
         self.history = torch.zeros((self.max_steps, B), dtype=torch.int32, device=dev)
@@ -135,13 +137,16 @@ class DeviceDecoder:
         self.stream = torch.cuda.Stream(dev)
 
     # -- one decode step, as launches on self.stream ------------------------------
-    def _mm(self, x, w: PackedWeight, bias, y):
+    def _mm(self, x, w: PackedWeight, bias, y, epilogue=_lib.EPILOGUE_NONE, residual=None):
         ws = self.ws_buf
-        check(lib().mtrtq_matmul(x.data_ptr(), _lib.DTYPE_F32, x.stride(0), w.packed.data_ptr(),
-                                 w.scale.data_ptr(), bias.data_ptr() if bias is not None else None,
-                                 y.data_ptr(), y.stride(0), x.shape[0], w.K, w.N, MODES[self.mode],
-                                 ws.data_ptr() if ws is not None else None,
-                                 ws.numel() if ws is not None else 0, self._sp), "mtrtq_matmul")
+        check(lib().mtrtq_matmul_ex(x.data_ptr(), _lib.DTYPE_F32, x.stride(0), w.packed.data_ptr(),
+                                    w.scale.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                    y.data_ptr(), y.stride(0), x.shape[0], w.K, w.N, MODES[self.mode],
+                                    ws.data_ptr() if ws is not None else None,
+                                    ws.numel() if ws is not None else 0, epilogue,
+                                    residual.data_ptr() if residual is not None else None,
+                                    residual.stride(0) if residual is not None else 0, self._sp),
+              "mtrtq_matmul_ex")
 
     def _launch_step(self):
         cfg, B, D, sp, L = self.cfg, self.B, self.cfg.d_model, self._sp, lib()
@@ -157,21 +162,20 @@ class DeviceDecoder:
                                            self.vc[i].data_ptr(), self.pos.data_ptr(),
                                            self.attn.data_ptr(), B, cfg.n_head, cfg.head_dim,
                                            self.max_ctx, sp), "attention")
-            self._mm(self.attn, ly["o"], ly["bo"], self.ao)
-            check(L.mtrtq_add_inplace(self.x.data_ptr(), self.ao.data_ptr(), B * D, sp), "add")
+            # x += attn @ Wo + bo, fused into the MatMulQ store
+            self._mm(self.attn, ly["o"], ly["bo"], self.x, _lib.EPILOGUE_ADD_RESIDUAL, self.x)
             check(L.mtrtq_layernorm(self.x.data_ptr(), ly["ln2"][0].data_ptr(), ly["ln2"][1].data_ptr(),
                                     self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
-            self._mm(self.h, ly["fc"], ly["bfc"], self.mh)
-            check(L.mtrtq_gelu_tanh(self.mh.data_ptr(), self.mh.data_ptr(), self.mh.numel(), sp), "gelu")
-            self._mm(self.mh, ly["proj"], ly["bproj"], self.ao)
-            check(L.mtrtq_add_inplace(self.x.data_ptr(), self.ao.data_ptr(), B * D, sp), "add")
+            self._mm(self.h, ly["fc"], ly["bfc"], self.mh, _lib.EPILOGUE_GELU_TANH)
+            self._mm(self.mh, ly["proj"], ly["bproj"], self.x, _lib.EPILOGUE_ADD_RESIDUAL, self.x)
         check(L.mtrtq_layernorm(self.x.data_ptr(), self.ln_f[0].data_ptr(), self.ln_f[1].data_ptr(),
                                 self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
         self._mm(self.h, self.lm_head, None, self.logits)
         check(L.mtrtq_argmax_rows(self.logits.data_ptr(), B, cfg.vocab, cfg.vocab,
-                                  self.next_tok.data_ptr(), self.history.data_ptr(),
-                                  self.pos.data_ptr(), self.max_steps, sp), "argmax")
-        check(L.mtrtq_decode_advance(self.pos.data_ptr(), sp), "advance")
+                                  self.best.data_ptr(), sp), "argmax")
+        check(L.mtrtq_decode_next(self.best.data_ptr(), B, self.next_tok.data_ptr(),
+                                  self.history.data_ptr(), self.max_steps, self.pos.data_ptr(), sp),
+              "decode_next")
 
     @property
     def _sp(self) -> int:
@@ -184,6 +188,7 @@ class DeviceDecoder:
                 self.graph = None  # the graph holds the prompt's address and length
             self.prompt.copy_(prompt)
             self.pos.zero_()
+            self.best.zero_()
             self.next_tok.zero_()
             self.history.zero_()
 

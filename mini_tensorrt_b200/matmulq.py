@@ -154,13 +154,20 @@ def plan_info(M: int, K: int, N: int, x_dtype=torch.float32, mode: str = "bf16")
     return out
 
 
+EPILOGUES = {"none": _lib.EPILOGUE_NONE, "gelu": _lib.EPILOGUE_GELU_TANH,
+             "residual": _lib.EPILOGUE_ADD_RESIDUAL}
+
+
 def matmul_q8(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None = None,
               out: torch.Tensor | None = None, mode: str = "bf16",
-              workspace: Workspace | torch.Tensor | None = None, stream=None) -> torch.Tensor:
+              workspace: Workspace | torch.Tensor | None = None, stream=None,
+              epilogue: str = "none", residual: torch.Tensor | None = None) -> torch.Tensor:
     """out[M,N] = x[M,K] @ dequant(w) (+ bias): the reference MatMulQ (+ Add) on the GPU.
 
     x: float32 or bfloat16 CUDA tensor [M, K] (row stride may exceed K).
-    mode: "bf16" (x rounded to bf16, tensor cores for M > 8) or "fp32" (CUDA cores).
+    mode: "bf16" (x rounded to bf16 before the product) or "fp32".
+    epilogue: "none"; "gelu" (gelu_new after the bias, the reference's fused
+    MatMul+Bias+GeluTanh); "residual" (out = residual + result; residual may be out).
     """
     if x.dim() != 2 or x.shape[1] != w.K:
         raise ValueError(f"x must be [M, {w.K}], got {tuple(x.shape)}")
@@ -183,11 +190,19 @@ def matmul_q8(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None = None
         ws = (workspace or default_workspace(x.device)).get(need)
     ws_ptr = ws.data_ptr() if ws is not None else None
     ws_bytes = ws.numel() * ws.element_size() if ws is not None else 0
+    epi = EPILOGUES[epilogue]
+    if epi == _lib.EPILOGUE_ADD_RESIDUAL:
+        if residual is None or residual.dtype != torch.float32 or residual.shape != (M, w.N) \
+                or residual.stride(1) != 1:
+            raise ValueError("the residual epilogue needs residual float32 [M, N], unit stride")
     with torch.cuda.device(x.device):
-        check(lib().mtrtq_matmul(x.data_ptr(), xd, x.stride(0), w.packed.data_ptr(),
-                                 w.scale.data_ptr(), _ptr(bias), out.data_ptr(), out.stride(0),
-                                 M, w.K, w.N, MODES[mode], ws_ptr, ws_bytes, _stream_ptr(stream)),
-              "mtrtq_matmul")
+        check(lib().mtrtq_matmul_ex(x.data_ptr(), xd, x.stride(0), w.packed.data_ptr(),
+                                    w.scale.data_ptr(), _ptr(bias), out.data_ptr(), out.stride(0),
+                                    M, w.K, w.N, MODES[mode], ws_ptr, ws_bytes, epi,
+                                    _ptr(residual) if epi == _lib.EPILOGUE_ADD_RESIDUAL else None,
+                                    residual.stride(0) if epi == _lib.EPILOGUE_ADD_RESIDUAL else 0,
+                                    _stream_ptr(stream)),
+              "mtrtq_matmul_ex")
     return out
 
 

@@ -403,3 +403,43 @@ def test_overlapped_launches_wait_for_their_inputs(cuda_device, graph):
         err = normwise_rel_err(out, oracle.matmul_q8(inp, q, s))
         assert err <= FP32_TOL, f"fp32 mode rel err {err:.3e}"
         inp = out
+
+
+EPI_PATHS = {1: "gemv", 2: "gemm_tc", 3: "stream_k_tc", 4: "cluster_gemv"}
+EPI_CASES = [(1, 768, 3072), (8, 3072, 768), (24, 768, 1000), (64, 768, 3072)]
+
+
+def _gelu_new(u):
+    u = u.astype(np.float64)
+    return (0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))).astype(np.float32)
+
+
+@pytest.mark.parametrize("M,K,N", EPI_CASES, ids=[f"{M}x{K}x{N}" for M, K, N in EPI_CASES])
+@pytest.mark.parametrize("path", sorted(EPI_PATHS), ids=list(EPI_PATHS.values()))
+@pytest.mark.parametrize("epilogue", ["gelu", "residual"])
+def test_fused_epilogues(cuda_device, M, K, N, path, epilogue):
+    """gelu_new after the bias (the reference's FusedMatMulBiasGeluTanh) and the
+    residual add (in place: out is the residual), on every kernel that takes the shape."""
+    mode = "fp32" if path == 1 else "bf16"
+    if (path == 3 and M > 32) or (path == 4 and M > 8):
+        pytest.skip("the kernel does not take this M")
+    W = wl.weights(K, N, 601)
+    q, s = matmulq.quantize_per_channel(W)
+    X = oracle.round_bf16(wl.activations(M, K, 602)) if mode == "bf16" else wl.activations(M, K, 602)
+    b = wl.bias(N, 603)
+    R = wl.activations(M, N, 604)
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+    x = torch.from_numpy(X).to(cuda_device)
+    bt = torch.from_numpy(b).to(cuda_device)
+    y = torch.from_numpy(R).to(cuda_device).clone()
+    with forced(path):
+        if epilogue == "gelu":
+            matmul_q8(x, pw, bias=bt, out=y, mode=mode, epilogue="gelu")
+        else:
+            matmul_q8(x, pw, bias=bt, out=y, mode=mode, epilogue="residual", residual=y)
+    torch.cuda.synchronize()
+    assert matmulq.read_device_status() == 0
+    t = oracle.matmul_q8(X, q, s, b)
+    want = _gelu_new(t) if epilogue == "gelu" else (R + t).astype(np.float32)
+    err = normwise_rel_err(y.cpu().numpy(), want)
+    assert err <= (1e-4 if path in (1, 4) else 1e-3), f"rel err {err:.3e}"
