@@ -88,6 +88,8 @@ size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 constexpr int64_t kMaxDim = int64_t(1) << 30;
 constexpr size_t kCounterBytes = 4096;                       // fixed ticket region
 constexpr int64_t kMaxSplitTiles = kCounterBytes / sizeof(unsigned);
+// Weight bytes up to which bf16 calls with 8 < M <= 32 take the cluster GEMV.
+constexpr int64_t kClusterWideMaxBytes = 8ll << 20;
 
 int check_dims(int64_t M, int64_t K, int64_t N) {
   if (M <= 0 || K <= 0 || N <= 0)
@@ -103,23 +105,25 @@ int check_dims(int64_t M, int64_t K, int64_t N) {
 
 // Cluster GEMV geometry: one cluster of CS CTAs (CS <= 8) per 128-channel tile,
 // each CTA streaming ceil(KB / CS) 64-k units through a ring of shared memory stages.
-// All clusters should be resident at once (kGemvClCtasPerSm CTAs per SM): CS is the
-// largest split that keeps n_tiles * CS within that, at most KB; it grows, if
-// needed, until a CTA's staged activations leave room for two stages; the ring
-// then takes what the shared memory cap leaves (2 to 8 stages).
+// All clusters should be resident at once (3 CTAs per SM for M <= 8, 2 above):
+// CS is the largest split that keeps n_tiles * CS within that, at most KB; it
+// grows, if needed, until a CTA's activation digits leave room for two stages;
+// the ring then takes what the shared memory cap leaves (2 to 8 stages).
 static bool gemv_cluster_plan(int64_t M, int sm_count, Plan* p) {
   if (M > kGemvClMaxM || p->n_tiles > 65535) return false;
+  const bool wide = M > 8;
+  const size_t cap = wide ? kGemvClSmemCapWide : kGemvClSmemCap;
   const int64_t KB = p->k_pad / kBlockK;
-  const int64_t capacity = (int64_t)sm_count * kGemvClCtasPerSm;
+  const int64_t capacity = (int64_t)sm_count * (wide ? kGemvClCtasPerSmWide : kGemvClCtasPerSm);
   int64_t cs = capacity / p->n_tiles;
   if (cs > KB) cs = KB;
   if (cs > 8) cs = 8;
   if (cs < 1) cs = 1;
-  while (cs < 8 && cs < KB && gemv_cluster_smem_bytes((int)M, KB, (int)cs, 2) > kGemvClSmemCap) ++cs;
-  if (gemv_cluster_smem_bytes((int)M, KB, (int)cs, 2) > kGemvClSmemCap) return false;
+  while (cs < 8 && cs < KB && gemv_cluster_smem_bytes((int)M, KB, (int)cs, 2) > cap) ++cs;
+  if (gemv_cluster_smem_bytes((int)M, KB, (int)cs, 2) > cap) return false;
   int stages = 2;
   while (stages < kGemvClMaxStages && stages < ceil_div64(KB, cs) &&
-         gemv_cluster_smem_bytes((int)M, KB, (int)cs, stages + 1) <= kGemvClSmemCap)
+         gemv_cluster_smem_bytes((int)M, KB, (int)cs, stages + 1) <= cap)
     ++stages;
   p->kind = Plan::kGemvCluster;
   p->tile_m = (int)M;
@@ -151,15 +155,20 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   p.k_pad = round_up64(K, kBlockK);
   p.n_tiles = (int)(p.n_pad / kTileN);
 
-  // Path: M <= 8 -> the cluster GEMV (either mode) when its shared memory allows;
+  // Path: M <= 32 -> the cluster GEMV when its shared memory allows (bf16 mode with
+  // M > 8: small weights only);
   // otherwise bf16 mode -> stream-K tcgen05 kernel for M <= 32 (and at most
   // kMaxSplitTiles channel tiles), tile tcgen05 GEMM above; fp32 mode -> the
   // CUDA-core split-K GEMV.
   int path = 1;
   if (mode == MTRTQ_MODE_BF16) path = (M <= 32 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
   {
+    // For 8 < M <= 32 in bf16 mode the stream-K tcgen05 kernel is faster on large
+    // weights (its MMAs do the 32 tokens in one pass); the cluster GEMV stays
+    // ahead on small ones, where a call is latency-bound.
     Plan q = p;
-    if (gemv_cluster_plan(M, sm_count, &q)) path = 4;
+    const bool small_w = K * N <= kClusterWideMaxBytes;
+    if ((M <= 8 || mode == MTRTQ_MODE_FP32 || small_w) && gemv_cluster_plan(M, sm_count, &q)) path = 4;
   }
   if (force_path != 0) {
     if ((force_path == 2 || force_path == 3) && mode != MTRTQ_MODE_BF16)
@@ -170,7 +179,8 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
       Plan q = p;
       if (!gemv_cluster_plan(M, sm_count, &q))
         return fail(MTRTQ_ERR_INVALID_ARG,
-                    "the cluster GEMV takes M <= 8 and at most 74 KiB of shared memory per CTA");
+                    "the cluster GEMV takes M <= 32 and at most 72 KiB (M <= 8) or 110 KiB of "
+                    "shared memory per CTA");
     }
     path = force_path;
   }

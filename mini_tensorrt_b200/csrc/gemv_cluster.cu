@@ -287,27 +287,71 @@ template <bool X_BF16, bool ROUND, int RES>
 struct ClStager {
   static constexpr int kRes = RES;  // groups per lane held in registers
   static constexpr int kBatch = 6;  // groups per lane per batch otherwise
-  int m, gbeg, gend, kbase;
+  int m, gbeg, gend, kbase, warp_, nu_;
   bool vec, resident;
   uint4 raw[kRes];
 
   __device__ __forceinline__ void begin(const GemvClParams& p, int u0, int nu, int warp, int lane) {
     const int mt = p.M;
+    warp_ = warp;
+    nu_ = nu;
+    kbase = u0 * 64;
+    vec = (p.ldx & 3) == 0;
+    if (mt > kClWarps) {  // more tokens than warps: finish() stages them whole
+      resident = false;
+      return;
+    }
     m = warp % mt;
     const int share_warps = (kClWarps - 1 - m) / mt + 1;  // warps staging token m
     const int j = warp / mt;
     const int n4 = nu * 16;  // 4-element groups of the range
     gbeg = (int)((int64_t)j * n4 / share_warps);
     gend = (int)((int64_t)(j + 1) * n4 / share_warps);
-    kbase = u0 * 64;
-    vec = (p.ldx & 3) == 0;
     resident = gend - gbeg <= 32 * kRes;
     if (resident) cl_issue_groups<kRes, X_BF16>(p, raw, m, kbase, gbeg + lane, gend, vec);
+  }
+
+  // More tokens than warps: warp w stages tokens w, w + 8, ... over the whole range.
+  __device__ __forceinline__ void finish_many(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
+                                              int* s_bad, int lane) {
+    const int mt = p.M, n4 = nu_ * 16;
+    for (int t = warp_; t < mt; t += kClWarps) {
+      float mx = 0.0f;
+      bool bad = false;
+      for (int g0 = lane; g0 < n4; g0 += 32 * kBatch) {
+        float4 w[kBatch];
+        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec);
+        cl_max_groups<kBatch>(w, mx, bad);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        bad |= __shfl_xor_sync(0xffffffffu, (int)bad, o) != 0;
+      }
+      if (lane == 0) {
+        atomicMax(&s_max[t], __float_as_int(mx));
+        if (bad) atomicOr(&s_bad[t], 1);
+      }
+    }
+    named_bar_sync(1, kClThreads);
+    for (int t = warp_; t < mt; t += kClWarps) {
+      const float smax = __int_as_float(s_max[t]);
+      const float inv = (smax > 0.0f && !s_bad[t]) ? 127.0f / smax : 0.0f;
+      for (int g0 = lane; g0 < n4; g0 += 32 * kBatch) {
+        float4 w[kBatch];
+        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec);
+        cl_store_digits<kBatch>(w, inv, xd, plane, mt, t, g0, n4);
+      }
+    }
   }
 
   __device__ __forceinline__ void finish(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
                                          int* s_bad, int lane) {
     const int mt = p.M;
+    if (mt > kClWarps) {
+      finish_many(p, xd, plane, s_max, s_bad, lane);
+      return;
+    }
     float mx = 0.0f;
     bool bad = false;
     float4 v[kRes];
@@ -345,14 +389,17 @@ struct ClStager {
   }
 };
 
-template <bool X_BF16, bool ROUND, int RES>
-__global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kernel(const GemvClParams p) {
-  // Shared memory: ring [stages][8 KiB] (the exchange buffer part[8][128] fp32
+// NB: blocks of 8 tokens (M <= 8 * NB); more blocks need more registers, so fewer
+// CTAs fit an SM.
+template <bool X_BF16, bool ROUND, int RES, int NB>
+__global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvClCtasPerSmWide)
+    gemv_cluster_kernel(const GemvClParams p) {
+  // Shared memory: ring [stages][8 KiB] (the exchange buffer part[8 * NB][128] fp32
   // reuses it at the end) | full[8], empty[8], xready (+ pad) barriers |
   // digits [3][nu][M][64] s8.
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_abort;
-  __shared__ int s_max[8], s_bad[8];  // per token: max |x| (fp32 bits), non-finite flag
+  __shared__ int s_max[32], s_bad[32];  // per token: max |x| (fp32 bits), non-finite flag
   __shared__ float s_sb[2][128];      // scale and bias of the rows this CTA finishes
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
@@ -365,7 +412,7 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
   const int u0 = (int)((int64_t)rank * p.KB / CS), u1 = (int)((int64_t)(rank + 1) * p.KB / CS);
   const int nu = u1 - u0;
   unsigned char* ring = smem;
-  const size_t ring_bytes = max((size_t)nst * kUnitBytes, (size_t)8 * 128 * sizeof(float));
+  const size_t ring_bytes = max((size_t)nst * kUnitBytes, (size_t)8 * NB * 128 * sizeof(float));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_bytes);
   uint64_t* empty = full + kGemvClMaxStages;
   uint64_t* xready = empty + kGemvClMaxStages;
@@ -393,7 +440,7 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
       }
       mbar_init(xready, 1);
       s_abort = 0;
-      for (int i = 0; i < 8; ++i) s_max[i] = s_bad[i] = 0;
+      for (int i = 0; i < 32; ++i) s_max[i] = s_bad[i] = 0;
       fence_barrier_init();
       for (; issued < prefill; ++issued) {
         mbar_arrive_expect_tx(&full[st_p], kUnitBytes);
@@ -408,11 +455,13 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
   }
   __syncthreads();
 
-  int acc[kDigits][4];
+  int acc[NB][kDigits][4];
 #pragma unroll
-  for (int d = 0; d < kDigits; ++d)
+  for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[d][j] = 0;
+    for (int d = 0; d < kDigits; ++d)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[nb][d][j] = 0;
 
   if (warp == kClWarps) {
     // Producer: one thread keeps up to nst units in flight. The activations are
@@ -451,8 +500,7 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
     // lane's 16-byte slab rows: k = 16c + 8i + 0..7.
     const int g = lane >> 2, c = lane & 3;
     const int ra = warp * 16 + g;
-    const bool has_x = g < mt;
-    const int8_t* xg = xd + g * 64 + c * 16;
+    const int8_t* xg = xd + g * 64 + c * 16;  // token g of block 0; block nb adds 8 * nb tokens
     int st = 0;
     uint32_t ph = 0;
     for (int u = 0; u < nu; ++u) {
@@ -460,18 +508,25 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
       const uint4* w = reinterpret_cast<const uint4*>(ring + (size_t)st * kUnitBytes);
       const uint4 wa = w[c * 128 + ra];
       const uint4 wb = w[c * 128 + ra + 8];
-      uint4 xv[kDigits];
 #pragma unroll
-      for (int d = 0; d < kDigits; ++d)
-        xv[d] = has_x ? *reinterpret_cast<const uint4*>(xg + d * plane + u * mt * 64)
-                      : make_uint4(0u, 0u, 0u, 0u);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);  // the weights are in registers
+      for (int nb = 0; nb < NB; ++nb) {
+        uint4 xv[kDigits];
+        const bool has_x = 8 * nb + g < mt;
 #pragma unroll
-      for (int d = 0; d < kDigits; ++d) {
-        mma_s8(acc[d], wa.x, wb.x, wa.y, wb.y, xv[d].x, xv[d].y);
-        mma_s8(acc[d], wa.z, wb.z, wa.w, wb.w, xv[d].z, xv[d].w);
+        for (int d = 0; d < kDigits; ++d)
+          xv[d] = has_x ? *reinterpret_cast<const uint4*>(xg + d * plane + (u * mt + 8 * nb) * 64)
+                        : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int d = 0; d < kDigits; ++d) {
+          mma_s8(acc[nb][d], wa.x, wb.x, wa.y, wb.y, xv[d].x, xv[d].y);
+          mma_s8(acc[nb][d], wa.z, wb.z, wa.w, wb.w, xv[d].z, xv[d].w);
+        }
       }
+      // The stage goes back to the producer only after the MMAs have consumed the
+      // weights read from it: a shared memory read is not finished when issued, and
+      // the next bulk copy into the stage must not overtake it.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
       if (++st == nst) { st = 0; ph ^= 1u; }
     }
   }
@@ -479,20 +534,24 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
 
   // Accumulators -> fp32 partials part[token][row] in this CTA's shared memory.
   // Element j of a warp's C fragment: row ra (j < 2) or ra + 8, token 2c + (j & 1).
-  float* part = reinterpret_cast<float*>(smem);  // [8][128], read by the other ranks
+  float* part = reinterpret_cast<float*>(smem);  // [8 * NB][128], read by the other ranks
   if (warp < kClWarps) {
     const int g = lane >> 2, c = lane & 3;
     const int ra = warp * 16 + g;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int m = 2 * c + (j & 1), row = ra + (j >> 1) * 8;
-      float v = 0.0f;
-      if (m < mt) {
-        const float sm = s_bad[m] ? __int_as_float(0x7fc00000) : __int_as_float(s_max[m]) * (1.0f / 127.0f);
-        v = sm * ((float)acc[0][j] + (float)acc[1][j] * (1.0f / 128.0f) +
-                  (float)acc[2][j] * (1.0f / 16384.0f));
+    for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = 8 * nb + 2 * c + (j & 1), row = ra + (j >> 1) * 8;
+        float v = 0.0f;
+        if (m < mt) {
+          const float sm =
+              s_bad[m] ? __int_as_float(0x7fc00000) : __int_as_float(s_max[m]) * (1.0f / 127.0f);
+          v = sm * ((float)acc[nb][0][j] + (float)acc[nb][1][j] * (1.0f / 128.0f) +
+                    (float)acc[nb][2][j] * (1.0f / 16384.0f));
+        }
+        part[m * 128 + row] = v;
       }
-      part[m * 128 + row] = v;
     }
   }
 
@@ -530,11 +589,12 @@ __global__ void __launch_bounds__(kClBlock, kGemvClCtasPerSm) gemv_cluster_kerne
   if (CS > 1) cluster_sync_relaxed();
 }
 
-template <bool X_BF16, bool ROUND, int RES>
+template <bool X_BF16, bool ROUND, int RES, int NB>
 cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, bool pdl, cudaStream_t st) {
-  auto kern = gemv_cluster_kernel<X_BF16, ROUND, RES>;
+  auto kern = gemv_cluster_kernel<X_BF16, ROUND, RES, NB>;
   if (smem > 48 * 1024) {
-    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), (int)kGemvClSmemCap))
+    if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern),
+                                          (int)(NB == 1 ? kGemvClSmemCap : kGemvClSmemCapWide)))
       return e;
   }
   cudaLaunchConfig_t cfg = {};
@@ -559,7 +619,7 @@ cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, 
 size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages) {
   const int64_t nu = (units + cs - 1) / cs;  // the largest CTA range
   const size_t ring = (size_t)stages * kUnitBytes;
-  const size_t exch = (size_t)8 * 128 * sizeof(float);  // reuses the ring
+  const size_t exch = (size_t)((m + 7) / 8) * 8 * 128 * sizeof(float);  // reuses the ring
   return (ring > exch ? ring : exch) + (2 * kGemvClMaxStages + 2) * sizeof(uint64_t) +
          (size_t)kDigits * (size_t)nu * (size_t)m * 64;
 }
@@ -586,18 +646,24 @@ cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64
   gp.status = status;
   const size_t smem = gemv_cluster_smem_bytes((int)p.M, p.kunits, p.splits, p.stages);
   // Activation groups a staging lane holds: 6 unless some warp's share needs
-  // more to be staged in one pass (a token has floor(8 / M) warps).
-  const int64_t nu_max = (p.kunits + p.splits - 1) / p.splits;
-  const int64_t share = (nu_max * 16 + kClWarps / p.M - 1) / (kClWarps / p.M);
-  const bool wide = share > 32 * 6;
-  if (x_dtype == 1)
-    return wide ? cl_launch<true, false, 12>(gp, p.splits, p.n_tiles, smem, pdl, st)
-                : cl_launch<true, false, 6>(gp, p.splits, p.n_tiles, smem, pdl, st);
-  if (p.round_x)
-    return wide ? cl_launch<false, true, 12>(gp, p.splits, p.n_tiles, smem, pdl, st)
-                : cl_launch<false, true, 6>(gp, p.splits, p.n_tiles, smem, pdl, st);
-  return wide ? cl_launch<false, false, 12>(gp, p.splits, p.n_tiles, smem, pdl, st)
-              : cl_launch<false, false, 6>(gp, p.splits, p.n_tiles, smem, pdl, st);
+  // more to be staged in one pass (a token has floor(8 / M) warps; M > 8 stages
+  // whole tokens per warp in batches).
+  const int nb = p.M <= 8 ? 1 : (p.M <= 16 ? 2 : 4);
+  bool wide = false;
+  if (p.M <= 8) {
+    const int64_t nu_max = (p.kunits + p.splits - 1) / p.splits;
+    const int64_t share = (nu_max * 16 + kClWarps / p.M - 1) / (kClWarps / p.M);
+    wide = share > 32 * 6;
+  }
+#define MTRTQ_CL_LAUNCH(XB, RD)                                                                     \
+  (nb == 1 ? (wide ? cl_launch<XB, RD, 12, 1>(gp, p.splits, p.n_tiles, smem, pdl, st)               \
+                   : cl_launch<XB, RD, 6, 1>(gp, p.splits, p.n_tiles, smem, pdl, st))               \
+           : nb == 2 ? cl_launch<XB, RD, 6, 2>(gp, p.splits, p.n_tiles, smem, pdl, st)              \
+                     : cl_launch<XB, RD, 6, 4>(gp, p.splits, p.n_tiles, smem, pdl, st))
+  if (x_dtype == 1) return MTRTQ_CL_LAUNCH(true, false);
+  if (p.round_x) return MTRTQ_CL_LAUNCH(false, true);
+  return MTRTQ_CL_LAUNCH(false, false);
+#undef MTRTQ_CL_LAUNCH
 }
 
 }  // namespace mtrtq

@@ -48,7 +48,7 @@ struct Plan {
 constexpr int kGemvUnroll = 8;
 
 // Cluster GEMV: the most activation rows (tokens) it takes.
-constexpr int kGemvClMaxM = 8;
+constexpr int kGemvClMaxM = 32;
 
 struct DeviceInfo {
   int device = -1;
@@ -61,10 +61,13 @@ struct DeviceInfo {
 // once per (device, kernel); later calls only look the pair up.
 cudaError_t ensure_smem_limit(const void* kernel, int bytes);
 
-// Cluster GEMV: CTAs resident per SM (registers are capped to allow it), the
-// shared memory a CTA may use so that they fit, and the most ring stages.
+// Cluster GEMV: CTAs resident per SM (registers are capped to allow it) and the
+// shared memory a CTA may use so that they fit, for M <= 8 and for larger M (more
+// accumulators: fewer, larger CTAs); the most ring stages.
 constexpr int kGemvClCtasPerSm = 3;
-constexpr size_t kGemvClSmemCap = 74 * 1024;
+constexpr size_t kGemvClSmemCap = 72 * 1024;  // 3 x (72 + static + 1 reserved) KiB <= 228 KiB
+constexpr int kGemvClCtasPerSmWide = 2;
+constexpr size_t kGemvClSmemCapWide = 110 * 1024;
 constexpr int kGemvClMaxStages = 8;
 size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages);
 cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,

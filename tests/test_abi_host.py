@@ -125,12 +125,14 @@ def test_launch_without_device_fails_loudly():
 
 @pytest.mark.parametrize("M,K,N,mode,path", [
     (1, 768, 50257, "bf16", "cluster_gemv"), (8, 768, 768, "fp32", "cluster_gemv"),
-    (8, 3072, 768, "bf16", "cluster_gemv"), (9, 768, 768, "bf16", "stream_k_tc"),
-    (32, 768, 3072, "bf16", "stream_k_tc"), (33, 768, 3072, "bf16", "gemm_tc"),
+    (8, 3072, 768, "bf16", "cluster_gemv"), (9, 768, 768, "bf16", "cluster_gemv"),
+    (32, 768, 3072, "bf16", "cluster_gemv"), (33, 768, 3072, "bf16", "gemm_tc"),
+    (16, 768, 50257, "bf16", "stream_k_tc"), (16, 768, 50257, "fp32", "cluster_gemv"),
     (64, 768, 3072, "bf16", "gemm_tc"),
     (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv"),
-    (1, 768, 200000, "bf16", "cluster_gemv"), (9, 768, 200000, "bf16", "gemm_tc"),
-    (8, 24576, 128, "bf16", "stream_k_tc"), (8, 24576, 128, "fp32", "gemv"),
+    (1, 768, 200000, "bf16", "cluster_gemv"), (33, 768, 200000, "bf16", "gemm_tc"),
+    (8, 24576, 128, "bf16", "stream_k_tc"), (32, 65536, 128, "bf16", "stream_k_tc"),
+    (32, 65536, 128, "fp32", "gemv"),
 ])
 def test_planner(M, K, N, mode, path):
     info = matmulq.plan_info(M, K, N, torch.float32, mode)
@@ -175,7 +177,7 @@ def test_forced_paths_change_the_plan():
         assert matmulq.plan_info(8, 768, 768, mode="fp32")["path"] == "cluster_gemv"
         assert matmulq.workspace_bytes(8, 768, 768, torch.float32, "fp32") == 0
         with pytest.raises(_lib.MtrtqError):
-            matmulq.plan_info(9, 768, 768)
+            matmulq.plan_info(33, 768, 768)
         with pytest.raises(_lib.MtrtqError):
             matmulq.set_option(_lib.OPT_FORCE_PATH, 5)
     finally:
@@ -185,12 +187,14 @@ def test_forced_paths_change_the_plan():
 @pytest.mark.parametrize("M,K,N,cs", [(1, 768, 768, 8), (1, 768, 50257, 1), (1, 4096, 14336, 3),
                                       (8, 14336, 4096, 8), (1, 64, 128, 1), (3, 768, 2304, 8),
                                       (8, 3072, 768, 8), (1, 768, 200000, 1), (8, 4096, 14336, 3),
-                                      (8, 16384, 128, 8), (8, 24576, 128, None)])
+                                      (8, 16384, 128, 8), (8, 24576, 128, None),
+                                      (16, 768, 50257, 1), (32, 4096, 14336, 5), (32, 768, 768, 8),
+                                      (32, 14336, 4096, None), (33, 768, 768, None)])
 def test_cluster_gemv_plan(M, K, N, cs):
     """One cluster per 128-channel tile, 1 to 8 CTAs splitting K into 64-k units,
-    all clusters resident at three CTAs per SM where the tiles allow; refused when
-    a CTA's activation digits (3 bytes per activation) and two 8 KiB ring stages
-    exceed 74 KiB."""
+    all clusters resident (3 CTAs per SM for M <= 8, 2 above) where the tiles
+    allow; refused when a CTA's activation digits (3 bytes per activation) and two
+    8 KiB ring stages exceed 72 KiB (M <= 8) or 110 KiB, or when M > 32."""
     matmulq.set_option(_lib.OPT_FORCE_PATH, 4)
     try:
         if cs is None:
@@ -202,7 +206,8 @@ def test_cluster_gemv_plan(M, K, N, cs):
         assert info["n_tiles"] == -(-N // 128)
         kb = -(-K // 64)
         assert info["k_per_split"] == -(-kb // cs) * 64
-        assert 3 * M * -(-kb // cs) * 64 + 2 * 8192 <= 74 * 1024
+        cap = (72 if M <= 8 else 110) * 1024
+        assert 3 * M * -(-kb // cs) * 64 + 2 * 8192 <= cap
         assert matmulq.workspace_bytes(M, K, N, torch.float32, "bf16") == 0
     finally:
         matmulq.set_option(_lib.OPT_FORCE_PATH, 0)

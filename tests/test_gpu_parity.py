@@ -157,7 +157,7 @@ def test_every_path_agrees(cuda_device, M):
     q, s = oracle.quantize_per_channel(W)
     X = wl.activations(M, K, 6)
     outs = []
-    for path in ((1, 2, 3, 4) if M <= 8 else (1, 2, 3) if M <= 32 else (1, 2)):
+    for path in ((1, 2, 3, 4) if M <= 32 else (1, 2)):
         matmulq.set_option(_lib.OPT_FORCE_PATH, path)
         try:
             outs.append(run(X, q, s, "bf16"))
@@ -303,7 +303,9 @@ def test_stream_k_partitions(cuda_device, M, K, N):
     check(Y, X, q, s, "bf16", bias=b, tc=True)
 
 
-GSK_CASES = [(1, 64, 128), (3, 64, 50257), (8, 12288, 256), (2, 4096, 14336), (1, 768, 50257),
+GSK_CASES = [(12, 768, 3072), (16, 768, 50257), (24, 4096, 1000), (32, 3072, 768), (9, 100, 300),
+             (31, 77, 129),
+             (1, 64, 128), (3, 64, 50257), (8, 12288, 256), (2, 4096, 14336), (1, 768, 50257),
              (5, 64 * 23, 128 * 7), (7, 12000, 100), (8, 4096, 1000), (4, 100, 300), (6, 77, 129)]
 
 
@@ -421,7 +423,7 @@ def test_fused_epilogues(cuda_device, M, K, N, path, epilogue):
     """gelu_new after the bias (the reference's FusedMatMulBiasGeluTanh) and the
     residual add (in place: out is the residual), on every kernel that takes the shape."""
     mode = "fp32" if path == 1 else "bf16"
-    if (path == 3 and M > 32) or (path == 4 and M > 8):
+    if (path == 3 and M > 32) or (path == 4 and M > 32):
         pytest.skip("the kernel does not take this M")
     W = wl.weights(K, N, 601)
     q, s = matmulq.quantize_per_channel(W)
