@@ -146,6 +146,26 @@ int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed,
                     void* workspace, size_t workspace_bytes, int epilogue, const float* residual,
                     int64_t ldr, void* stream);
 
+/* The reference's op on host tensors: X [M, K] and Y [M, N] are fp32 in HOST memory
+ * (contiguous), the packed weights, scale and bias are resident on the device
+ * (as for mtrtq_matmul). Enqueues on `stream` the copy of X into the workspace,
+ * the product (mtrtq_matmul's plan for fp32 X) into the workspace, and the copy of
+ * Y back to the host. With blocking != 0 it returns after Y has arrived, as the
+ * reference's CPU kernel does (src/ops/kernels_matmul.cpp:42-74); with 0 it
+ * returns at once and the caller synchronizes the stream before reading Y.
+ * Pinned (page-locked) X and Y let the copies run asynchronously; pageable ones
+ * work but copy synchronously.
+ *   workspace  device, >= mtrtq_host_workspace_bytes(M,K,N,mode) bytes, 256-byte
+ *              aligned, zero-filled once after allocation. Its first part is the
+ *              kernel scratch of mtrtq_matmul (at least the 4 KiB counter region,
+ *              so the workspace may also serve mtrtq_matmul calls); the X and Y
+ *              staging follow.
+ * Calls that share a workspace must be ordered on one stream. */
+int64_t mtrtq_host_workspace_bytes(int64_t M, int64_t K, int64_t N, int mode);
+int mtrtq_matmul_host(const float* X, const void* packed, const float* scale, const float* bias,
+                      float* Y, int64_t M, int64_t K, int64_t N, int mode, void* workspace,
+                      size_t workspace_bytes, int blocking, void* stream);
+
 /* Y = X x dequant(W) (+ bias) through the decode GEMV (CUDA cores, split-K), with
  * the same arguments and results as mtrtq_matmul on its GEMV path, but without a
  * caller workspace and without allocating anything.

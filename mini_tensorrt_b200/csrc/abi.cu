@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -69,6 +70,11 @@ int current_device(DeviceInfo* out) {
     d.major = prop.major;
     d.minor = prop.minor;
     d.smem_optin = prop.sharedMemPerBlockOptin;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status), g_device_status);
+    if (e != cudaSuccess) {
+      d.device = -1;
+      return cuda_fail(e, "device status address");
+    }
   }
   *out = d;
   return MTRTQ_OK;
@@ -482,9 +488,7 @@ int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed,
     if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     return MTRTQ_OK;
   }
-  unsigned* status = nullptr;
-  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
-  if (e != cudaSuccess) return cuda_fail(e, "device status address");
+  unsigned* status = d.status;
   if (p.kind == Plan::kGemvCluster) {
     e = launch_gemv_cluster(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, status,
                             g_opt_overlap != 0, epi, st);
@@ -539,6 +543,54 @@ int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed,
   e = launch_gemm_tc(p, xb, ldxb, packed, scale, bias, Y, ldy, workspace, xmap,
                      g_opt_gemm_a_source == 0 ? 1 : 0, status, epi, st);
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  return MTRTQ_OK;
+}
+
+// Host staging sits after the kernel scratch: X [M, K] then Y [M, N], fp32, each
+// 256-byte aligned. It never starts inside the ticket-counter region, even for a
+// plan without scratch: a workspace shared with other calls keeps its counters
+// there, and they must stay zero.
+static int host_layout(int64_t M, int64_t K, int64_t N, int mode, size_t* scratch, size_t* xbytes,
+                       size_t* total) {
+  Plan p;
+  if (int rc = plan_matmul(M, K, N, MTRTQ_DTYPE_F32, mode, sm_count_or_default(), &p, g_opt_force_path))
+    return rc;
+  *scratch = std::max(round256(p.total), kCounterBytes);
+  *xbytes = round256((size_t)(M * K) * sizeof(float));
+  *total = *scratch + *xbytes + round256((size_t)(M * N) * sizeof(float));
+  return MTRTQ_OK;
+}
+
+int64_t mtrtq_host_workspace_bytes(int64_t M, int64_t K, int64_t N, int mode) {
+  size_t scratch, xbytes, total;
+  if (host_layout(M, K, N, mode, &scratch, &xbytes, &total) != MTRTQ_OK) return -1;
+  return (int64_t)total;
+}
+
+int mtrtq_matmul_host(const float* X, const void* packed, const float* scale, const float* bias,
+                      float* Y, int64_t M, int64_t K, int64_t N, int mode, void* workspace,
+                      size_t workspace_bytes, int blocking, void* stream) {
+  if (!X || !Y || !workspace) return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  size_t scratch, xbytes, total;
+  if (int rc = host_layout(M, K, N, mode, &scratch, &xbytes, &total)) return rc;
+  if (workspace_bytes < total)
+    return fail(MTRTQ_ERR_WORKSPACE, "workspace %zu bytes < %zu", workspace_bytes, total);
+  if (!aligned(workspace, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  float* xd = reinterpret_cast<float*>(ws + scratch);
+  float* yd = reinterpret_cast<float*>(ws + scratch + xbytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(xd, X, (size_t)(M * K) * sizeof(float), cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "copy of X to the device");
+  if (int rc = mtrtq_matmul_ex(xd, MTRTQ_DTYPE_F32, K, packed, scale, bias, yd, N, M, K, N, mode,
+                               workspace, scratch, MTRTQ_EPILOGUE_NONE, nullptr, 0, stream))
+    return rc;
+  e = cudaMemcpyAsync(Y, yd, (size_t)(M * N) * sizeof(float), cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return cuda_fail(e, "copy of Y to the host");
+  if (blocking) {
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+  }
   return MTRTQ_OK;
 }
 

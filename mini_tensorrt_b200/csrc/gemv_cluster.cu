@@ -50,12 +50,13 @@ constexpr int kClBlock = kClThreads + 32;  // + the producer warp
 constexpr uint32_t kUnitBytes = 8192;      // 64 k x 128 channels of int8
 constexpr int kDigits = 3;
 // Weight units issued before the activations land (at most the ring's stages).
-// The activation loads are already in flight by then, so three units cover the
-// wait; under programmatic dependent launch they are fetched while the grid
-// ahead finishes. Measured on B200: 3 beats 1 and 2 on the LM head
-// (768 x 50257: 11.0 vs 12.0 us with overlap) and ties 8 elsewhere.
-constexpr int kClEarlyUnits = 3;
-constexpr int kClEarlyUnitsPdl = 3;
+// After them the weight stream waits until every consumer warp has read its
+// activations, so that those loads do not queue behind weight traffic; under
+// programmatic dependent launch the early units are fetched while the grid
+// ahead finishes. Measured on B200 (768 x 50257, M = 1, overlapped launches):
+// 4 units 10.7 us, 3 units 11.0 us, 1 unit 12.0 us.
+constexpr int kClEarlyUnits = 4;
+constexpr int kClEarlyUnitsPdl = 4;
 
 struct GemvClParams {
   const void* X;
@@ -316,7 +317,7 @@ struct ClStager {
 
   // More tokens than warps: warp w stages tokens w, w + 8, ... over the whole range.
   __device__ __forceinline__ void finish_many(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
-                                              int* s_bad, int lane) {
+                                              int* s_bad, uint64_t* xready, int lane) {
     const int mt = p.M, n4 = nu_ * 16;
     for (int t = warp_; t < mt; t += kClWarps) {
       float mx = 0.0f;
@@ -336,6 +337,7 @@ struct ClStager {
         if (bad) atomicOr(&s_bad[t], 1);
       }
     }
+    if (lane == 0) mbar_arrive(xready);  // this warp's activations have been read
     named_bar_sync(1, kClThreads);
     for (int t = warp_; t < mt; t += kClWarps) {
       const float smax = __int_as_float(s_max[t]);
@@ -349,10 +351,10 @@ struct ClStager {
   }
 
   __device__ __forceinline__ void finish(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
-                                         int* s_bad, int lane) {
+                                         int* s_bad, uint64_t* xready, int lane) {
     const int mt = p.M;
     if (mt > kClWarps) {
-      finish_many(p, xd, plane, s_max, s_bad, lane);
+      finish_many(p, xd, plane, s_max, s_bad, xready, lane);
       return;
     }
     float mx = 0.0f;
@@ -368,6 +370,10 @@ struct ClStager {
         cl_max_groups<kBatch>(w, mx, bad);
       }
     }
+    // This warp's activations have been read: the weight stream may resume while
+    // the maxima and digits are computed.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xready);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -441,7 +447,7 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
         mbar_init(&full[i], 1);
         mbar_init(&empty[i], kClWarps);
       }
-      mbar_init(xready, 1);
+      mbar_init(xready, kClWarps);
       s_abort = 0;
       for (int i = 0; i < 32; ++i) s_max[i] = s_bad[i] = 0;
       fence_barrier_init();
@@ -495,9 +501,8 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
     __syncwarp();
   } else {
     // Consumers: activation digits first (the weights are already in flight).
-    stager.finish(p, xd, plane, s_max, s_bad, lane);
+    stager.finish(p, xd, plane, s_max, s_bad, xready, lane);
     named_bar_sync(1, kClThreads);
-    if (tid == 0) mbar_arrive(xready);
     // Warp w: channel rows w*16 + g and w*16 + g + 8 (g = lane / 4); lane's slab c
     // (= lane % 4) of each unit. Step i of a unit takes words 2i, 2i+1 of the
     // lane's 16-byte slab rows: k = 16c + 8i + 0..7.

@@ -55,6 +55,7 @@ struct DeviceInfo {
   int sm_count = 148;
   int major = 0, minor = 0;
   size_t smem_optin = 0;
+  unsigned* status = nullptr;  // this device's g_device_status (bounded-wait errors)
 };
 
 // Raises a kernel's dynamic shared memory limit to `bytes` on the current device,

@@ -206,6 +206,43 @@ def matmul_q8(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None = None
     return out
 
 
+def host_workspace_bytes(M: int, K: int, N: int, mode: str = "bf16") -> int:
+    n = lib().mtrtq_host_workspace_bytes(M, K, N, MODES[mode])
+    if n < 0:
+        raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_host_workspace_bytes", _lib.last_error())
+    return n
+
+
+def matmul_q8_host(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None, mode: str = "bf16",
+                   workspace: Workspace | torch.Tensor | None = None, stream=None,
+                   blocking: bool = True) -> torch.Tensor:
+    """The reference's MatMulQ (+ Add) on host tensors: x float32 [M, K] and the
+    result in host memory, weights resident on w's device (mtrtq_matmul_host).
+    Pinned x and out make the copies asynchronous; with blocking=False the caller
+    synchronizes `stream` before reading out."""
+    if x.device.type != "cpu" or x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != w.K:
+        raise ValueError(f"x must be a float32 host tensor [M, {w.K}]")
+    x = x.contiguous()
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, w.N), dtype=torch.float32, pin_memory=x.is_pinned())
+    if out.device.type != "cpu" or out.dtype != torch.float32 or out.shape != (M, w.N) \
+            or not out.is_contiguous():
+        raise ValueError("out must be a contiguous float32 host tensor [M, N]")
+    dev = w.packed.device
+    need = host_workspace_bytes(M, w.K, w.N, mode)
+    ws = workspace if isinstance(workspace, torch.Tensor) else \
+        (workspace or default_workspace(dev)).get(need)
+    with torch.cuda.device(dev):
+        check(lib().mtrtq_matmul_host(x.data_ptr(), w.packed.data_ptr(), w.scale.data_ptr(),
+                                      _ptr(bias), out.data_ptr(), M, w.K, w.N, MODES[mode],
+                                      ws.data_ptr(), ws.numel() * ws.element_size(),
+                                      1 if blocking else 0, _stream_ptr(stream)),
+              "mtrtq_matmul_host")
+    return out
+
+
 def set_option(option: int, value: int) -> None:
     check(lib().mtrtq_set_option(option, value), "mtrtq_set_option")
 

@@ -7,8 +7,10 @@ include/mtrt/op_context.h:13-20, src/ops/registry.cpp:7-24); MatMulQ is keyed
 output (src/ops/kernels_matmul.cpp:42-81). This module keeps those names, argument
 meanings and the setup-time lookup, so a caller (an executor's plan loop,
 src/runtime/executor.cpp:105-142) finds the device kernel the same way it finds
-the CPU one. Tensors are torch CUDA tensors; W may be a PackedWeight (pre-packed
-at load time, as an executor would) or a raw int8 [K,N] tensor (packed per call).
+the CPU one. A and C are torch CUDA tensors, or host tensors (copied in and out
+around the device product, as the reference's CPU kernel is called); W may be a
+PackedWeight (pre-packed at load time, as an executor would) or a raw int8 [K,N]
+tensor (packed per call).
 """
 from __future__ import annotations
 
@@ -17,7 +19,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from .matmulq import PackedWeight, matmul_q8
+from .matmulq import PackedWeight, matmul_q8, matmul_q8_host
 
 
 class DType(enum.Enum):
@@ -85,17 +87,27 @@ def matmul_q8_f32_cuda(ctx: OpContext) -> None:
         pw = W
         _require(scale is None or scale.numel() == pw.N, "MatMulQ scale must be per-column [N]")
         if scale is not None and scale.data_ptr() != pw.scale.data_ptr():
-            pw = PackedWeight(pw.packed, scale.to(torch.float32).contiguous(), pw.K, pw.N)
+            pw = PackedWeight(pw.packed, scale.to(device=pw.packed.device, dtype=torch.float32)
+                              .contiguous(), pw.K, pw.N)
     else:
         _require(W.dtype == torch.int8, "MatMulQ: W must be i8")
         _require(W.dim() == 2 and W.is_contiguous(), "MatMulQ: W must be contiguous [K, N]")
         _require(scale.numel() == W.shape[1], "MatMulQ scale must be per-column [N]")
-        pw = PackedWeight.from_int8(W, scale, device=A.device)
+        pw = PackedWeight.from_int8(W, scale, device=A.device if A.is_cuda else "cuda")
     M, K = A.shape
     _require(pw.K == K, "MatMulQ inner dimensions disagree")
     _require(tuple(C.shape) == (M, pw.N), "MatMulQ output shape wrong")
     _require(C.dtype == torch.float32, "MatMulQ output must be f32")
     bias = ctx.node.attrs.get("bias") if ctx.node is not None else None
+    if bias is not None:
+        bias = bias.to(device=pw.packed.device, dtype=torch.float32)
+    if A.device.type == "cpu":
+        # Host tensors, as the reference's executor hands its CPU kernel: copies in
+        # and out around the device product (mtrtq_matmul_host), blocking.
+        _require(C.device.type == "cpu", "MatMulQ: a host A needs a host output")
+        _require(A.dtype == torch.float32, "MatMulQ: a host A must be f32")
+        matmul_q8_host(A, pw, bias=bias, out=C, mode=mode)
+        return
     matmul_q8(A, pw, bias=bias, out=C, mode=mode)
 
 

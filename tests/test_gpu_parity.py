@@ -223,6 +223,13 @@ def test_registry_device_kernel_matches_golden(cuda_device):
         assert np.allclose(got, g["out"], rtol=0.05, atol=0.05)
     with pytest.raises(registry.GraphError):
         registry.run_kernel(reg, "MatMulQ", [A, W], torch.empty((2, 5), device=cuda_device))
+    # host tensors, as the reference's executor passes them: copied in and out
+    for mode in ("fp32", "bf16"):
+        out = torch.full((2, 5), float("nan"))
+        registry.run_kernel(reg, "MatMulQ", [A.cpu(), W.cpu(), s.cpu()], out, {"mode": mode})
+        if mode == "fp32":
+            assert normwise_rel_err(out.numpy(), g["c_ref"]) <= FP32_TOL
+        assert np.allclose(out.numpy(), g["out"], rtol=0.05, atol=0.05)
 
 
 def test_argument_errors_on_device(cuda_device):
@@ -445,3 +452,64 @@ def test_fused_epilogues(cuda_device, M, K, N, path, epilogue):
     want = _gelu_new(t) if epilogue == "gelu" else (R + t).astype(np.float32)
     err = normwise_rel_err(y.cpu().numpy(), want)
     assert err <= (1e-4 if path in (1, 4) else 1e-3), f"rel err {err:.3e}"
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 768, 2304), (8, 768, 50257), (64, 768, 3072), (300, 1000, 520)])
+@pytest.mark.parametrize("pinned", [True, False], ids=["pinned", "pageable"])
+def test_host_buffers(cuda_device, M, K, N, pinned):
+    """mtrtq_matmul_host: X and Y in host memory, copies and product on one stream."""
+    W = wl.weights(K, N, 90 + M)
+    q, s = oracle.quantize_per_channel(W)
+    bias = wl.activations(1, N, 91)[0]
+    X = wl.activations(M, K, 92 + M)
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+    bt = torch.from_numpy(bias).to(cuda_device)
+    xh = torch.from_numpy(X)
+    if pinned:
+        xh = xh.pin_memory()
+    for mode in ("bf16", "fp32"):
+        Y = matmulq.matmul_q8_host(xh, pw, bias=bt, mode=mode)
+        assert Y.device.type == "cpu"
+        assert matmulq.read_device_status() == 0
+        check(Y.numpy(), X, q, s, mode, bias=bias, tc=(mode == "bf16"))
+    # non-blocking: results appear after the stream is synchronized
+    st = torch.cuda.Stream(cuda_device)
+    out = torch.full((M, N), float("nan"), pin_memory=pinned)
+    matmulq.matmul_q8_host(xh, pw, bias=bt, out=out, mode="fp32", stream=st, blocking=False)
+    st.synchronize()
+    check(out.numpy(), X, q, s, "fp32", bias=bias)
+
+
+def test_host_buffers_argument_errors(cuda_device):
+    q, s = oracle.quantize_per_channel(wl.weights(64, 128, 93))
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+    lib = _lib.lib()
+    x = torch.zeros(2, 64)
+    y = torch.zeros(2, 128)
+    need = matmulq.host_workspace_bytes(2, 64, 128)
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda_device)
+    args = lambda wsb: (x.data_ptr(), pw.packed.data_ptr(), pw.scale.data_ptr(), None, y.data_ptr(),
+                        2, 64, 128, _lib.MODE_BF16, ws.data_ptr(), wsb, 1, None)
+    assert lib.mtrtq_matmul_host(*args(need - 1)) == _lib.ERR_WORKSPACE
+    assert lib.mtrtq_matmul_host(*args(need)) == 0
+    bad = list(args(need))
+    bad[0] = None
+    assert lib.mtrtq_matmul_host(*bad) == _lib.ERR_INVALID_ARG
+
+
+def test_host_call_leaves_shared_workspace_counters(cuda_device):
+    """A host-buffer call whose plan needs no scratch still stages X and Y past the
+    counter region, so a split-K call on the same workspace stays correct."""
+    K, N = 768, 2304
+    q, s = oracle.quantize_per_channel(wl.weights(K, N, 94))
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+    ws = torch.zeros(max(matmulq.host_workspace_bytes(1, K, N),
+                         matmulq.workspace_bytes(3, K, N, torch.float32, "fp32") + (1 << 20)),
+                     dtype=torch.uint8, device=cuda_device)
+    X = wl.activations(3, K, 95)
+    matmulq.matmul_q8_host(torch.from_numpy(X[:1]), pw, mode="bf16", workspace=ws)
+    with forced(1):
+        y = torch.full((3, N), float("nan"), device=cuda_device)
+        matmul_q8(torch.from_numpy(X).to(cuda_device), pw, out=y, mode="fp32", workspace=ws)
+        torch.cuda.synchronize()
+    check(y.cpu().numpy(), X, q, s, "fp32")
