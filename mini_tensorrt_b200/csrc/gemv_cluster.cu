@@ -123,6 +123,24 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Weight fragments of one m16n8k32 step from a unit in shared memory ([slab][128
+// rows][16 B]): slabs s and s + 1 of rows ra0 .. ra0 + 15. Each of the four 8 x 16 B
+// matrices is eight consecutive rows of one slab, 128 contiguous bytes, so the
+// load has no bank conflict (16-byte loads of one row from four slabs 2 KiB
+// apart, by the four lanes of an MMA group, would meet in the same banks); lane
+// l addresses row l & 7 of matrix l >> 3, and lane (g, t) receives bytes
+// 4t .. 4t + 3 of row g of each matrix: the A fragment (rows g and g + 8,
+// k = 16 s + 4t .. and 16 (s + 1) + 4t ..).
+__device__ __forceinline__ void ld_weight_frag(const unsigned char* unit_base, int ra0, int s, int lane,
+                                               uint32_t (&a)[4]) {
+  const int mat = lane >> 3;
+  const uint32_t addr = smem_u32(unit_base + (size_t)(s + (mat >> 1)) * 2048 +
+                                 (size_t)(ra0 + (lane & 7) + (mat & 1) * 8) * 16);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+               : "r"(addr));
+}
+
 // Four consecutive activations of row m from k (zeros past K) as fp32; a vector
 // load when the row stride allows it and all four lie inside the row.
 template <bool X_BF16>
@@ -266,8 +284,11 @@ __device__ __forceinline__ void cl_store_digits(const float4 (&v)[kB], float inv
       cl_digits(__fmul_rn(v[b].y, inv), b0, b1, b2);
       cl_digits(__fmul_rn(v[b].z, inv), c0, c1, c2);
       cl_digits(__fmul_rn(v[b].w, inv), e0, e1, e2);
-      const int u = g >> 4, k = (g & 15) * 4;
-      const int off = (u * mt + m) * 64 + k;
+      // Group q = g & 15 of the unit (k = 4q .. 4q + 3) sits at byte (q & 3) * 16 +
+      // (q >> 2) * 4 of the token's 64-byte row: lane t of an MMA group then finds
+      // its four B-fragment words (k = 4t + 16j, j = 0..3) in one 16-byte load.
+      const int u = g >> 4, q = g & 15;
+      const int off = (u * mt + m) * 64 + (q & 3) * 16 + (q >> 2) * 4;
       *reinterpret_cast<uint32_t*>(xd + off) = cl_pack_low_bytes(a0, b0, c0, e0);
       *reinterpret_cast<uint32_t*>(xd + plane + off) = cl_pack_low_bytes(a1, b1, c1, e1);
       *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) = cl_pack_low_bytes(a2, b2, c2, e2);
@@ -503,9 +524,10 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
     // Consumers: activation digits first (the weights are already in flight).
     stager.finish(p, xd, plane, s_max, s_bad, xready, lane);
     named_bar_sync(1, kClThreads);
-    // Warp w: channel rows w*16 + g and w*16 + g + 8 (g = lane / 4); lane's slab c
-    // (= lane % 4) of each unit. Step i of a unit takes words 2i, 2i+1 of the
-    // lane's 16-byte slab rows: k = 16c + 8i + 0..7.
+    // Warp w: channel rows w*16 + g and w*16 + g + 8 (g = lane / 4). MMA step i
+    // of a unit covers k = 32i .. 32i + 31 (slabs 2i, 2i + 1); lane (g, c) holds
+    // the activation words of token g at k = 4c + 16j (j = 0..3) as one 16-byte
+    // load, words 2i and 2i + 1 feeding step i.
     const int g = lane >> 2, c = lane & 3;
     const int ra = warp * 16 + g;
     const int8_t* xg = xd + g * 64 + c * 16;  // token g of block 0; block nb adds 8 * nb tokens
@@ -513,9 +535,9 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
     uint32_t ph = 0;
     for (int u = 0; u < nu; ++u) {
       if (!mbar_wait_bounded(&full[st], ph, &s_abort, p.status)) break;
-      const uint4* w = reinterpret_cast<const uint4*>(ring + (size_t)st * kUnitBytes);
-      const uint4 wa = w[c * 128 + ra];
-      const uint4 wb = w[c * 128 + ra + 8];
+      uint32_t a1[4], a2[4];
+      ld_weight_frag(ring + (size_t)st * kUnitBytes, warp * 16, 0, lane, a1);
+      ld_weight_frag(ring + (size_t)st * kUnitBytes, warp * 16, 2, lane, a2);
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
         uint4 xv[kDigits];
@@ -526,8 +548,8 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
                         : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int d = 0; d < kDigits; ++d) {
-          mma_s8(acc[nb][d], wa.x, wb.x, wa.y, wb.y, xv[d].x, xv[d].y);
-          mma_s8(acc[nb][d], wa.z, wb.z, wa.w, wb.w, xv[d].z, xv[d].w);
+          mma_s8(acc[nb][d], a1[0], a1[1], a1[2], a1[3], xv[d].x, xv[d].y);
+          mma_s8(acc[nb][d], a2[0], a2[1], a2[2], a2[3], xv[d].z, xv[d].w);
         }
       }
       // The stage goes back to the producer only after the MMAs have consumed the
