@@ -216,7 +216,11 @@ enum {
                                   reads X or writes Y: set it only where the kernel
                                   ahead never writes the weights, scales or biases
                                   (for example, not right after mtrtq_prepack on the
-                                  same stream). */
+                                  same stream). The decode-loop helpers below
+                                  (embedding, LayerNorm, attention, gelu, add,
+                                  argmax, next token) are then launched the same
+                                  way; each waits for the kernel ahead before it
+                                  touches global memory. */
 };
 int mtrtq_set_option(int option, int64_t value);
 

@@ -308,6 +308,8 @@ int check_device_sm100(DeviceInfo* d) {
 static std::mutex g_smem_mu;
 static std::set<std::pair<int, const void*>> g_smem_done;
 
+bool overlap_launch_enabled() { return g_opt_overlap != 0; }
+
 cudaError_t ensure_smem_limit(const void* kernel, int bytes) {
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return e;

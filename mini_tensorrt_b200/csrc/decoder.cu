@@ -22,7 +22,20 @@
 #include "../../include/mtrtq.h"
 
 namespace mtrtq {
+// MTRTQ_OPT_OVERLAP_LAUNCH (abi.cu).
+bool overlap_launch_enabled();
+
 namespace {
+
+// Programmatic dependent launch. Every kernel here starts with pdl_begin(): it
+// waits until the grid ahead of it in the stream has completed and its writes are
+// visible (a no-op when the launch did not ask for programmatic serialization),
+// and only then touches global memory; it then lets the grid behind it start
+// launching, so that grid's set-up overlaps this one.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -47,6 +60,7 @@ __device__ float block_sum(float v, float* red) {
 __global__ void embed_kernel(const int32_t* prompt, int64_t prompt_len, const int32_t* next_tok,
                              const int32_t* pos_p, const float* wte, const float* wpe, float* x,
                              int64_t D, int64_t V, int64_t n_pos) {
+  pdl_begin();
   const int64_t b = blockIdx.x;
   const int pos = *pos_p;
   if (pos < 0 || pos >= n_pos) {  // past the position table: zeros, no read out of bounds
@@ -67,6 +81,7 @@ constexpr int kLnRegs = 8;
 __global__ void layernorm_kernel(const float* x, const float* g, const float* bta, float* y,
                                  int64_t D, float eps) {
   __shared__ float red[32];
+  pdl_begin();
   const float* xr = x + blockIdx.x * D;
   float* yr = y + blockIdx.x * D;
   const bool in_regs = D <= (int64_t)kLnRegs * blockDim.x;
@@ -111,93 +126,152 @@ __global__ void layernorm_kernel(const float* x, const float* g, const float* bt
   }
 }
 
-// One block (8 warps) per (head, sequence). qkv: [B, 3D] rows (q | k | v). Appends
-// this position's k and v (its head slice) to the caches [B, max_ctx, D], then
-// out[b, head slice] = softmax(q . K / sqrt(d)) V over cached positions 0..pos.
-// Scores: a warp per key. Softmax: the max and the sum of exponentials over the
-// keys in key order by one warp (lane j reduces keys j, j+32, ... then the lanes
-// in order). Weighted sum: warp w takes keys w, w+8, ... for all head_dim
-// columns (lane -> columns), and the 8 warps' sums are added in warp order.
-// Dynamic shared memory: head_dim + max_ctx + 8 * head_dim floats.
-constexpr int kAttnWarps = 8;
+// One block of kAttnThreads per (head, sequence). qkv: [B, 3D] rows (q | k | v).
+// Appends this position's k and v (its head slice) to the caches [B, max_ctx, D],
+// then out[b, head slice] = softmax(q . K / sqrt(d)) V over cached positions
+// 0..pos. Decode attention is a chain of dependent memory reads, so every step
+// keeps many reads in flight instead of walking keys one after another:
+// * scores: a thread per key, its dot product over head_dim in k order (16-byte
+//   loads when the rows allow them, all issued before they are used);
+// * softmax: the max and the sum of exponentials as block reductions (fixed tree
+//   order);
+// * weighted sum: thread (g, c) adds keys g, g + G, ... for column chunk c (4
+//   columns, or 1), and the G groups' partial sums are added in group order.
+// Every sum has a fixed order, so results do not depend on timing.
+// Dynamic shared memory: head_dim + max_ctx (rounded up to a multiple of 4) +
+// max(head_dim, kAttnThreads * 4) floats.
+constexpr int kAttnThreads = 256;
 
-__global__ void attention_kernel(const float* qkv, float* kc, float* vc, const int32_t* pos_p,
-                                 float* out, int64_t H, int64_t hd, int64_t max_ctx) {
+__device__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+  return t;
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* qkv, float* kc, float* vc,
+                                                                 const int32_t* pos_p, float* out,
+                                                                 int64_t H, int64_t hd, int64_t max_ctx) {
   extern __shared__ float sm[];
-  __shared__ float stat[2];
+  __shared__ float red[32];
+  pdl_begin();
   const int64_t h = blockIdx.x, b = blockIdx.y;
   const int64_t D = H * hd;
   const int pos = *pos_p;
+  const int tid = threadIdx.x;
   if (pos < 0 || pos >= max_ctx) {  // past the cache: zeros, no access out of bounds
-    for (int64_t t = threadIdx.x; t < hd; t += blockDim.x) out[b * D + h * hd + t] = 0.0f;
+    for (int64_t t = tid; t < hd; t += blockDim.x) out[b * D + h * hd + t] = 0.0f;
     return;
   }
   float* qs = sm;                 // [hd]
   float* sc = sm + hd;            // [max_ctx]
-  float* part = sc + max_ctx;     // [kAttnWarps][hd]
+  float* part = sm + ((hd + max_ctx + 3) & ~(int64_t)3);  // [G][hd], 16-byte aligned
   const float* row = qkv + b * 3 * D;
-  float* kb = kc + b * max_ctx * D;
-  float* vb = vc + b * max_ctx * D;
-  for (int64_t t = threadIdx.x; t < hd; t += blockDim.x) {
+  float* kb = kc + b * max_ctx * D + h * hd;
+  float* vb = vc + b * max_ctx * D + h * hd;
+  for (int64_t t = tid; t < hd; t += blockDim.x) {
     qs[t] = row[h * hd + t];
-    kb[(int64_t)pos * D + h * hd + t] = row[D + h * hd + t];
-    vb[(int64_t)pos * D + h * hd + t] = row[2 * D + h * hd + t];
+    kb[(int64_t)pos * D + t] = row[D + h * hd + t];
+    vb[(int64_t)pos * D + t] = row[2 * D + h * hd + t];
   }
   __syncthreads();
+  // 16-byte loads of cache rows when every row start is 16-byte aligned.
+  const bool vec = (hd % 4 == 0) && (D % 4 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) % 16 == 0);
   const float scale = 1.0f / sqrtf((float)hd);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int j = warp; j <= pos; j += kAttnWarps) {
-    const float* kj = kb + (int64_t)j * D + h * hd;
+  for (int j = tid; j <= pos; j += blockDim.x) {
+    const float* kj = kb + (int64_t)j * D;
     float s = 0.0f;
-    for (int64_t t = lane; t < hd; t += 32) s += qs[t] * kj[t];
-    s = warp_sum(s);
-    if (lane == 0) sc[j] = s * scale;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    float mx = -1e30f;
-    for (int j = lane; j <= pos; j += 32) mx = fmaxf(mx, sc[j]);
+    if (vec) {
+      for (int64_t t = 0; t < hd; t += 16) {
+        float4 k4[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.0f;
-    for (int j = lane; j <= pos; j += 32) {
-      const float e = expf(sc[j] - mx);
-      sc[j] = e;
-      sum += e;
-    }
-    sum = warp_sum(sum);
-    if (lane == 0) stat[0] = 1.0f / sum;
-  }
-  __syncthreads();
-  const float inv = stat[0];
-  for (int64_t t0 = 0; t0 < hd; t0 += 32) {
-    const int64_t t = t0 + lane;
-    float a = 0.0f;
-    if (t < hd) {
-      int j = warp;
-      for (; j + 3 * kAttnWarps <= pos; j += 4 * kAttnWarps) {  // four keys' loads in flight
-        const float v0 = vb[(int64_t)j * D + h * hd + t];
-        const float v1 = vb[(int64_t)(j + kAttnWarps) * D + h * hd + t];
-        const float v2 = vb[(int64_t)(j + 2 * kAttnWarps) * D + h * hd + t];
-        const float v3 = vb[(int64_t)(j + 3 * kAttnWarps) * D + h * hd + t];
-        a += (sc[j] * inv) * v0;
-        a += (sc[j + kAttnWarps] * inv) * v1;
-        a += (sc[j + 2 * kAttnWarps] * inv) * v2;
-        a += (sc[j + 3 * kAttnWarps] * inv) * v3;
+        for (int i = 0; i < 4; ++i)
+          k4[i] = t + 4 * i < hd ? *reinterpret_cast<const float4*>(kj + t + 4 * i)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (t + 4 * i < hd) {
+            const float* qq = qs + t + 4 * i;
+            s += qq[0] * k4[i].x;
+            s += qq[1] * k4[i].y;
+            s += qq[2] * k4[i].z;
+            s += qq[3] * k4[i].w;
+          }
+        }
       }
-      for (; j <= pos; j += kAttnWarps) a += (sc[j] * inv) * vb[(int64_t)j * D + h * hd + t];
-      part[warp * hd + t] = a;
+    } else {
+      for (int64_t t = 0; t < hd; ++t) s += qs[t] * kj[t];
+    }
+    sc[j] = s * scale;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int j = tid; j <= pos; j += blockDim.x) mx = fmaxf(mx, sc[j]);
+  mx = block_max(mx, red);
+  float sum = 0.0f;
+  for (int j = tid; j <= pos; j += blockDim.x) {
+    const float e = expf(sc[j] - mx);
+    sc[j] = e;
+    sum += e;
+  }
+  sum = block_sum(sum, red);  // ends with the exponentials visible block-wide
+  const float inv = 1.0f / sum;
+  // Weighted sum over (key group, column chunk) threads.
+  const int w = vec ? 4 : 1;
+  const int nc = (int)((hd + w - 1) / w);            // column chunks
+  const int G = nc >= blockDim.x ? 1 : blockDim.x / nc;  // key groups
+  const int g = tid / nc;
+  if (g < G) {
+    for (int c = tid % nc; c < nc; c += (nc >= blockDim.x ? blockDim.x : nc)) {
+      if (vec) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        int j = g;
+        for (; j + 3 * G <= pos; j += 4 * G) {  // four keys' loads in flight
+          float4 v4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v4[i] = *reinterpret_cast<const float4*>(vb + (int64_t)(j + i * G) * D + 4 * c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float p = sc[j + i * G] * inv;
+            a.x += p * v4[i].x;
+            a.y += p * v4[i].y;
+            a.z += p * v4[i].z;
+            a.w += p * v4[i].w;
+          }
+        }
+        for (; j <= pos; j += G) {
+          const float4 v4 = *reinterpret_cast<const float4*>(vb + (int64_t)j * D + 4 * c);
+          const float p = sc[j] * inv;
+          a.x += p * v4.x;
+          a.y += p * v4.y;
+          a.z += p * v4.z;
+          a.w += p * v4.w;
+        }
+        *reinterpret_cast<float4*>(part + (int64_t)g * hd + 4 * c) = a;
+      } else {
+        float a = 0.0f;
+        for (int j = g; j <= pos; j += G) a += (sc[j] * inv) * vb[(int64_t)j * D + c];
+        part[(int64_t)g * hd + c] = a;
+      }
     }
   }
   __syncthreads();
-  for (int64_t t = threadIdx.x; t < hd; t += blockDim.x) {
+  for (int64_t t = tid; t < hd; t += blockDim.x) {
     float a = 0.0f;
-    for (int w = 0; w < kAttnWarps; ++w) a += part[w * hd + t];
+    for (int q = 0; q < G; ++q) a += part[(int64_t)q * hd + t];
     out[b * D + h * hd + t] = a;
   }
 }
 
 __global__ void gelu_tanh_kernel(const float* x, float* y, int64_t n) {
+  pdl_begin();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float u = x[i];
@@ -206,6 +280,7 @@ __global__ void gelu_tanh_kernel(const float* x, float* y, int64_t n) {
 }
 
 __global__ void add_kernel(float* y, const float* a, int64_t n) {
+  pdl_begin();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     y[i] += a[i];
@@ -227,6 +302,7 @@ constexpr int kArgmaxChunk = 4096;
 
 __global__ void argmax_fold_kernel(const float* logits, int64_t V, int64_t ldl, unsigned long long* best) {
   __shared__ unsigned long long bk[32];
+  pdl_begin();
   const float* r = logits + blockIdx.y * ldl;
   const int64_t j0 = (int64_t)blockIdx.x * kArgmaxChunk;
   const int64_t j1 = j0 + kArgmaxChunk < V ? j0 + kArgmaxChunk : V;
@@ -256,6 +332,7 @@ __global__ void argmax_fold_kernel(const float* logits, int64_t V, int64_t ldl, 
 // rows + r] too, best[r] = 0 for the next step; then *pos += 1.
 __global__ void decode_next_kernel(unsigned long long* best, int64_t rows, int32_t* tok, int32_t* history,
                                    int64_t history_len, int32_t* pos) {
+  pdl_begin();
   const int p = *pos;
   for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
     const unsigned long long k = best[r];
@@ -270,6 +347,25 @@ __global__ void decode_next_kernel(unsigned long long* best, int64_t rows, int32
 
 int launch_status(cudaError_t e) { return e == cudaSuccess ? MTRTQ_OK : MTRTQ_ERR_CUDA; }
 
+// Launches kern on `stream`, with programmatic stream serialization when
+// MTRTQ_OPT_OVERLAP_LAUNCH is set (every kernel here waits for the grid ahead
+// before it reads or writes global memory, so the attribute is safe for them).
+template <typename... Params, typename... Args>
+int launch_helper(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, void* stream,
+                  Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap_launch_enabled() ? 1 : 0;
+  return launch_status(cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...));
+}
+
 }  // namespace
 }  // namespace mtrtq
 
@@ -283,16 +379,15 @@ int mtrtq_decode_embed(const int32_t* prompt, int64_t prompt_len, const int32_t*
   if (!pos || !wte || !wpe || !x || !next_tok || B <= 0 || D <= 0 || V <= 0 || n_pos <= 0 ||
       (prompt_len > 0 && !prompt) || B > 65535)
     return MTRTQ_ERR_INVALID_ARG;
-  embed_kernel<<<(unsigned)B, 256, 0, static_cast<cudaStream_t>(stream)>>>(prompt, prompt_len, next_tok,
-                                                                         pos, wte, wpe, x, D, V, n_pos);
-  return launch_status(cudaGetLastError());
+  return launch_helper(embed_kernel, dim3((unsigned)B), dim3(256), 0, stream, prompt, prompt_len,
+                       next_tok, pos, wte, wpe, x, D, V, n_pos);
 }
 
 int mtrtq_layernorm(const float* x, const float* gamma, const float* beta, float* y, int64_t rows,
                     int64_t D, float eps, void* stream) {
   if (!x || !gamma || !beta || !y || rows <= 0 || D <= 0 || rows > 2147483647) return MTRTQ_ERR_INVALID_ARG;
-  layernorm_kernel<<<(unsigned)rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, gamma, beta, y, D, eps);
-  return launch_status(cudaGetLastError());
+  return launch_helper(layernorm_kernel, dim3((unsigned)rows), dim3(256), 0, stream, x, gamma, beta, y,
+                       D, eps);
 }
 
 int mtrtq_decode_attention(const float* qkv, float* kcache, float* vcache, const int32_t* pos,
@@ -301,26 +396,25 @@ int mtrtq_decode_attention(const float* qkv, float* kcache, float* vcache, const
   if (!qkv || !kcache || !vcache || !pos || !out || B <= 0 || H <= 0 || head_dim <= 0 ||
       max_ctx <= 0 || B > 65535 || H > 2147483647)
     return MTRTQ_ERR_INVALID_ARG;
-  const size_t smem = (size_t)(max_ctx + (1 + kAttnWarps) * head_dim) * sizeof(float);
+  // q, the scores and the key groups' partial sums (at most kAttnThreads chunks of
+  // up to 4 columns each, or one group of head_dim columns).
+  const int64_t parts = head_dim > 4 * kAttnThreads ? head_dim : 4 * kAttnThreads;
+  const size_t smem = (size_t)(((head_dim + max_ctx + 3) & ~(int64_t)3) + parts) * sizeof(float);
   if (smem > 48 * 1024) return MTRTQ_ERR_INVALID_ARG;  // contexts up to ~11k positions at d = 64
-  attention_kernel<<<dim3((unsigned)H, (unsigned)B), 32 * kAttnWarps, smem,
-                     static_cast<cudaStream_t>(stream)>>>(
-      qkv, kcache, vcache, pos, out, H, head_dim, max_ctx);
-  return launch_status(cudaGetLastError());
+  return launch_helper(attention_kernel, dim3((unsigned)H, (unsigned)B), dim3(kAttnThreads), smem,
+                       stream, qkv, kcache, vcache, pos, out, H, head_dim, max_ctx);
 }
 
 int mtrtq_gelu_tanh(const float* x, float* y, int64_t n, void* stream) {
   if (!x || !y || n <= 0) return MTRTQ_ERR_INVALID_ARG;
   const int64_t blocks = n / 256 + 1 < 4096 ? n / 256 + 1 : 4096;
-  gelu_tanh_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
-  return launch_status(cudaGetLastError());
+  return launch_helper(gelu_tanh_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, x, y, n);
 }
 
 int mtrtq_add_inplace(float* y, const float* a, int64_t n, void* stream) {
   if (!y || !a || n <= 0) return MTRTQ_ERR_INVALID_ARG;
   const int64_t blocks = n / 256 + 1 < 4096 ? n / 256 + 1 : 4096;
-  add_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, a, n);
-  return launch_status(cudaGetLastError());
+  return launch_helper(add_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, y, a, n);
 }
 
 int mtrtq_argmax_rows(const float* logits, int64_t rows, int64_t V, int64_t ldl,
@@ -328,17 +422,15 @@ int mtrtq_argmax_rows(const float* logits, int64_t rows, int64_t V, int64_t ldl,
   if (!logits || !best || rows <= 0 || V <= 0 || ldl < V || rows > 65535 || V > 2147483647)
     return MTRTQ_ERR_INVALID_ARG;
   const int64_t chunks = (V + kArgmaxChunk - 1) / kArgmaxChunk;
-  argmax_fold_kernel<<<dim3((unsigned)chunks, (unsigned)rows), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      logits, V, ldl, best);
-  return launch_status(cudaGetLastError());
+  return launch_helper(argmax_fold_kernel, dim3((unsigned)chunks, (unsigned)rows), dim3(256), 0, stream,
+                       logits, V, ldl, best);
 }
 
 int mtrtq_decode_next(unsigned long long* best, int64_t rows, int32_t* tok, int32_t* history,
                       int64_t history_len, int32_t* pos, void* stream) {
   if (!best || !tok || !pos || rows <= 0 || (history_len > 0 && !history)) return MTRTQ_ERR_INVALID_ARG;
-  decode_next_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(best, rows, tok, history,
-                                                                    history_len, pos);
-  return launch_status(cudaGetLastError());
+  return launch_helper(decode_next_kernel, dim3(1), dim3(256), 0, stream, best, rows, tok, history,
+                       history_len, pos);
 }
 
 }  // extern "C"

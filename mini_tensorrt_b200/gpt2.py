@@ -25,7 +25,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, matmulq
 from ._lib import check, lib
 from .matmulq import MODES, PackedWeight, Workspace, quantize_per_channel, workspace_bytes
 
@@ -94,12 +94,17 @@ class DeviceDecoder:
     """Greedy KV-cache decoding of `batch` sequences on one GPU.
 
     mode: MatMulQ mode for every Linear ("fp32" keeps the activations in fp32;
-    "bf16" rounds them to bf16 before each product)."""
+    "bf16" rounds them to bf16 before each product).
+    overlap: launch the step's kernels with programmatic dependent launch
+    (MTRTQ_OPT_OVERLAP_LAUNCH while the step is recorded or launched), so each one
+    starts while the one ahead finishes; the weights are never written during
+    decoding, which is the option's condition."""
 
     def __init__(self, w: GPT2Weights, batch: int, max_ctx: int, mode: str = "fp32",
-                 device="cuda", max_steps: int | None = None):
+                 device="cuda", max_steps: int | None = None, overlap: bool = True):
         cfg = w.cfg
         self.cfg, self.B, self.max_ctx, self.mode = cfg, batch, max_ctx, mode
+        self.overlap = overlap
         if max_ctx > cfg.n_pos:
             raise ValueError("max_ctx exceeds the position table")
         self.dev = torch.device(device)
@@ -149,6 +154,10 @@ class DeviceDecoder:
               "mtrtq_matmul_ex")
 
     def _launch_step(self):
+        with matmulq.option(_lib.OPT_OVERLAP_LAUNCH, 1 if self.overlap else 0):
+            self._launch_step_kernels()
+
+    def _launch_step_kernels(self):
         cfg, B, D, sp, L = self.cfg, self.B, self.cfg.d_model, self._sp, lib()
         P = self.prompt.shape[1]
         check(L.mtrtq_decode_embed(self.prompt.data_ptr(), P, self.next_tok.data_ptr(),

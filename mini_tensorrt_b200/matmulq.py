@@ -6,6 +6,8 @@ except the host quantizer, which is the library's own C function.
 """
 from __future__ import annotations
 
+import contextlib
+
 import ctypes
 from dataclasses import dataclass
 
@@ -243,8 +245,28 @@ def matmul_q8_host(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None =
     return out
 
 
+_options: dict = {}  # values set through set_option (the library starts with all at 0)
+
+
 def set_option(option: int, value: int) -> None:
     check(lib().mtrtq_set_option(option, value), "mtrtq_set_option")
+    _options[option] = value
+
+
+def get_option(option: int) -> int:
+    """The value last given to set_option in this process (0 if never set)."""
+    return _options.get(option, 0)
+
+
+@contextlib.contextmanager
+def option(opt: int, value: int):
+    """Runs the block with a process-wide option set, then restores its value."""
+    old = get_option(opt)
+    set_option(opt, value)
+    try:
+        yield
+    finally:
+        set_option(opt, old)
 
 
 def read_device_status() -> int:

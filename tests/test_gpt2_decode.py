@@ -25,16 +25,40 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 SMALL = gpt2.GPT2Config(n_layer=2, d_model=128, n_head=4, d_ff=512, vocab=1000, n_pos=64)
 
 
+@pytest.mark.parametrize("overlap", [True, False], ids=["overlapped", "serial"])
 @pytest.mark.parametrize("batch", [1, 3])
-def test_small_model_matches_oracle(cuda_device, batch):
+def test_small_model_matches_oracle(cuda_device, batch, overlap):
+    """Also with every kernel of the step launched with programmatic dependent
+    launch (each may start while the one ahead finishes), the default."""
     w = gpt2.random_weights(SMALL, seed=5)
     prompt = np.random.default_rng(6).integers(0, SMALL.vocab, (batch, 5), dtype=np.int32)
-    dec = gpt2.DeviceDecoder(w, batch, max_ctx=32, mode="fp32", device=cuda_device)
+    dec = gpt2.DeviceDecoder(w, batch, max_ctx=32, mode="fp32", device=cuda_device, overlap=overlap)
     got = dec.generate(prompt, max_new=12)
     want = OracleDecoder(w, batch, 32).generate(prompt, 12)
     np.testing.assert_array_equal(got["tokens"], want)
     # logits of the last step run on the device (position 5 + 12 - 2)
     ref = OracleDecoder(w, batch, 32)
+    toks = np.concatenate([prompt, want[:, :-1]], axis=1)
+    for pos in range(toks.shape[1]):
+        _, logits = ref.step(toks[:, pos], pos)
+    err = normwise_rel_err(dec.logits.cpu().numpy(), logits)
+    assert err <= 1e-4, f"logits rel err {err:.3e}"
+
+
+# head_dim 30 (no 16-byte rows: scalar attention reads), odd cache length, d_model
+# not a multiple of 4
+ODD = gpt2.GPT2Config(n_layer=2, d_model=90, n_head=3, d_ff=200, vocab=500, n_pos=64)
+
+
+@pytest.mark.parametrize("cfg,max_ctx", [(ODD, 37), (SMALL, 37)], ids=["hd30_ctx37", "hd32_ctx37"])
+def test_odd_shapes_match_oracle(cuda_device, cfg, max_ctx):
+    w = gpt2.random_weights(cfg, seed=7)
+    prompt = np.random.default_rng(8).integers(0, cfg.vocab, (2, 9), dtype=np.int32)
+    dec = gpt2.DeviceDecoder(w, 2, max_ctx=max_ctx, mode="fp32", device=cuda_device)
+    got = dec.generate(prompt, 20)
+    want = OracleDecoder(w, 2, max_ctx).generate(prompt, 20)
+    np.testing.assert_array_equal(got["tokens"], want)
+    ref = OracleDecoder(w, 2, max_ctx)
     toks = np.concatenate([prompt, want[:, :-1]], axis=1)
     for pos in range(toks.shape[1]):
         _, logits = ref.step(toks[:, pos], pos)
