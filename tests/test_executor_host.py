@@ -1,0 +1,159 @@
+"""Model plumbing on the host (mini_tensorrt_b200.executor): the int8-safe JSON
+loader, the MatMul -> MatMulQ rewrite, the MatMulQ epilogue fusion and the arena
+planner. No GPU needed."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from mini_tensorrt_b200 import executor as ex
+from mini_tensorrt_b200.registry import GraphError, Node
+
+
+def mlp_model(M=3, D=64, F=96, seed=0, residual=True):
+    """x -> LayerNorm -> MatMul W1 -> Add b1 -> GeluTanh -> MatMul W2 -> Add b2 (-> Add x)."""
+    rng = np.random.default_rng(seed)
+    g = ex.Graph()
+    T = lambda name, dt, shape, kind: g.add_tensor(ex.TensorInfo(name, dt, tuple(shape), kind))
+    x = T("x", "f32", (M, D), "input")
+    lg, lb = T("ln.g", "f32", (D,), "weight"), T("ln.b", "f32", (D,), "weight")
+    w1, b1 = T("fc.w", "f32", (D, F), "weight"), T("fc.b", "f32", (F,), "weight")
+    w2, b2 = T("proj.w", "f32", (F, D), "weight"), T("proj.b", "f32", (D,), "weight")
+    h, t0, t1, t2, t3, t4 = (T(n, "f32", s, "intermediate") for n, s in
+                             [("h", (M, D)), ("t0", (M, F)), ("t1", (M, F)), ("t2", (M, F)), ("t3", (M, D)),
+                              ("t4", (M, D))])
+    y = T("y", "f32", (M, D), "output")
+    g.nodes = [Node("LayerNorm", [x, lg, lb], [h], {"eps": 1e-5}),
+               Node("MatMul", [h, w1], [t0]), Node("Add", [t0, b1], [t1]), Node("GeluTanh", [t1], [t2]),
+               Node("MatMul", [t2, w2], [t3])]
+    if residual:
+        g.nodes += [Node("Add", [t3, b2], [t4]), Node("Add", [x, t4], [y])]
+    else:
+        g.tensors[t4] = ex.TensorInfo("t4", "f32", (M, D), "intermediate")
+        g.nodes += [Node("Add", [t3, b2], [y])]
+    g.inputs, g.outputs = [x], [y]
+    f32 = lambda *s, sc=1.0: (rng.standard_normal(s) * sc).astype(np.float32)
+    weights = {lg: 1.0 + f32(D, sc=0.1), lb: f32(D, sc=0.1), w1: f32(D, F, sc=0.02), b1: f32(F, sc=0.02),
+               w2: f32(F, D, sc=0.02), b2: f32(D, sc=0.02)}
+    return ex.LoadedModel(g, weights)
+
+
+def test_json_round_trip_keeps_every_dtype(tmp_path):
+    m = mlp_model()
+    g = m.graph
+    q = g.add_tensor(ex.TensorInfo("q", "i8", (4, 5), "weight"))
+    ids = g.add_tensor(ex.TensorInfo("ids", "i32", (3,), "weight"))
+    m.weights[q] = np.arange(-10, 10, dtype=np.int8).reshape(4, 5)
+    m.weights[ids] = np.array([7, -1, 2 ** 30], dtype=np.int32)
+    path = str(tmp_path / "model.json")
+    ex.save_json_model(m, path)
+    back = ex.load_json_model(path)
+    assert [t for t in back.graph.tensors] == [t for t in g.tensors]
+    assert [(n.op_type, n.inputs, n.outputs, n.attrs) for n in back.graph.nodes] == \
+        [(n.op_type, n.inputs, n.outputs, n.attrs) for n in g.nodes]
+    for tid, w in m.weights.items():
+        assert back.weights[tid].dtype == w.dtype and np.array_equal(back.weights[tid], w)
+
+
+@pytest.mark.parametrize("edit,msg", [
+    (lambda j: j["tensors"][0].update(dtype="f16"), "unsupported dtype"),
+    (lambda j: j["tensors"][0].update(kind="scratch"), "unknown tensor kind"),
+    (lambda j: j["tensors"].append(dict(j["tensors"][0])), "duplicate tensor name"),
+    (lambda j: j["tensors"][1].update(offset=10 ** 9), "exceeds weights blob"),
+    (lambda j: j["tensors"][1].update(nbytes=4), "byte size mismatch"),
+    (lambda j: j["nodes"][0]["inputs"].__setitem__(0, "nope"), "unknown tensor"),
+])
+def test_loader_errors(tmp_path, edit, msg):
+    """The reference loader's errors (src/frontend/json/json_loader.cpp:17-31, 78-127)."""
+    path = str(tmp_path / "model.json")
+    ex.save_json_model(mlp_model(), path)
+    with open(path) as f:
+        j = json.load(f)
+    edit(j)
+    with open(path, "w") as f:
+        json.dump(j, f)
+    with pytest.raises(GraphError, match=msg):
+        ex.load_json_model(path)
+
+
+def test_topo_order_rules():
+    g = mlp_model().graph
+    order = g.topo_order()
+    pos = {ni: i for i, ni in enumerate(order)}
+    prod = {t: ni for ni, n in enumerate(g.nodes) for t in n.outputs}
+    for ni, n in enumerate(g.nodes):
+        for t in n.inputs:
+            if t in prod:
+                assert pos[prod[t]] < pos[ni]
+    g2 = mlp_model().graph
+    g2.nodes.append(Node("GeluTanh", [g2.nodes[0].inputs[0]], [g2.nodes[0].outputs[0]]))
+    with pytest.raises(GraphError, match="more than one producer"):
+        g2.topo_order()
+    g3 = mlp_model().graph
+    g3.nodes[0].inputs[0] = g3.nodes[-1].outputs[0]  # LayerNorm reads y: a cycle
+    g3.tensors[g3.nodes[-1].outputs[0]] = ex.TensorInfo("y", "f32", (3, 64), "intermediate")
+    with pytest.raises(GraphError, match="cycle"):
+        g3.topo_order()
+
+
+def test_quantize_rewrites_matmul_with_the_reference_packer():
+    m = mlp_model()
+    q = ex.quantize_matmuls(m)
+    ops = [n.op_type for n in q.graph.nodes]
+    assert ops.count("MatMulQ") == 2 and "MatMul" not in ops
+    for n in q.graph.nodes:
+        if n.op_type != "MatMulQ":
+            continue
+        x, wq, sc = n.inputs
+        src = next(t for t in range(len(m.graph.tensors)) if m.graph.tensors[t].name + ".q8" ==
+                   q.graph.tensors[wq].name)
+        qo, so = oracle.quantize_per_channel(m.weights[src])  # the reference packer, restated
+        assert q.graph.tensors[wq].dtype == "i8" and np.array_equal(q.weights[wq], qo)
+        assert np.array_equal(q.weights[sc].view(np.uint32), so.view(np.uint32))
+        assert src not in q.weights  # the fp32 weight is no longer needed
+
+
+def test_fusion_patterns():
+    q = ex.quantize_matmuls(mlp_model(residual=True))
+    f = ex.fuse_matmulq_epilogues(q)
+    ops = [(n.op_type, n.attrs.get("epilogue"), "bias" in n.attrs) for n in f.graph.nodes]
+    # LN, MatMulQ{bias, gelu}, MatMulQ{bias}, Add(x, t4)
+    assert ops == [("LayerNorm", None, False), ("MatMulQ", "gelu", True), ("MatMulQ", None, True),
+                   ("Add", None, False)]
+    # without the bias Add the residual folds into the second MatMulQ
+    g = q.graph
+    mm2 = next(n for n in g.nodes if n.op_type == "MatMulQ" and n.inputs[0] != g.nodes[0].outputs[0])
+    t3 = mm2.outputs[0]
+    add_b = next(n for n in g.nodes if n.op_type == "Add" and n.inputs[0] == t3)
+    g.nodes.remove(add_b)
+    last = next(n for n in g.nodes if n.op_type == "Add" and n.inputs[0] == g.inputs[0])
+    last.inputs[1] = t3
+    f2 = ex.fuse_matmulq_epilogues(q)
+    assert [(n.op_type, n.attrs.get("epilogue")) for n in f2.graph.nodes][-1] == ("MatMulQ", "residual")
+    # a MatMulQ output read twice is not fused
+    q3 = ex.quantize_matmuls(mlp_model())
+    g3 = q3.graph
+    t0 = g3.nodes[1].outputs[0]
+    g3.outputs.append(t0)
+    f3 = ex.fuse_matmulq_epilogues(q3)
+    assert not any(n.attrs.get("epilogue") == "gelu" for n in f3.graph.nodes)
+
+
+def test_plan_memory_aligns_and_never_overlaps_live_tensors():
+    for seed in range(4):
+        m = ex.fuse_matmulq_epilogues(ex.quantize_matmuls(mlp_model(M=1 + seed, seed=seed)))
+        g = m.graph
+        plan = ex.plan_memory(g)
+        ivs = {t: (a, b, nb) for t, a, b, nb in plan.intervals}
+        for t, off in plan.offset.items():
+            assert off % ex.ARENA_ALIGNMENT == 0
+            assert off + g.tensors[t].nbytes <= plan.total_bytes
+        for t, (a, b, nb) in ivs.items():
+            for u, (c, d, nu) in ivs.items():
+                if t < u and a <= d and c <= b:  # live at the same time
+                    o1, o2 = plan.offset[t], plan.offset[u]
+                    assert o1 + nb <= o2 or o2 + nu <= o1
+        assert plan.total_bytes % ex.ARENA_ALIGNMENT == 0
+        assert plan.total_bytes <= sum(-(-nb // 256) * 256 for _, _, nb in ivs.values())
