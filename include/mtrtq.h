@@ -146,6 +146,22 @@ int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed,
                     void* workspace, size_t workspace_bytes, int epilogue, const float* residual,
                     int64_t ldr, void* stream);
 
+/* LayerNorm then MatMulQ in one kernel: Y = epilogue(LN(X) x dequant(W) (+ bias)),
+ * LN(X)[i,k] = (X[i,k] - mean_i) * inv_i * ln_gamma[k] + ln_beta[k] with the mean and
+ * the biased variance of row i over its K values and inv_i = 1 / sqrt(var_i + ln_eps)
+ * (the reference's LayerNorm, src/ops/kernels_transformer.cpp:19-54, followed by its
+ * MatMulQ, as the decoder runs them: tools/run_gpt2.cpp:142-143, :176-177, :188-189).
+ * X is fp32; ln_gamma and ln_beta are device f32 [K]; the rest as mtrtq_matmul_ex.
+ * Runs on the cluster GEMV, which computes each row's statistics in every CTA that
+ * reads the row; a call that plans another kernel (mtrtq_plan_info path != 3) fails
+ * with MTRTQ_ERR_INVALID_ARG, and the caller runs mtrtq_layernorm and mtrtq_matmul_ex
+ * instead. The workspace arguments are accepted for symmetry and not used. */
+int mtrtq_matmul_ln_ex(const float* X, int64_t ldx, const float* ln_gamma, const float* ln_beta,
+                       float ln_eps, const void* packed, const float* scale, const float* bias, float* Y,
+                       int64_t ldy, int64_t M, int64_t K, int64_t N, int mode, void* workspace,
+                       size_t workspace_bytes, int epilogue, const float* residual, int64_t ldr,
+                       void* stream);
+
 /* The reference's op on host tensors: X [M, K] and Y [M, N] are fp32 in HOST memory
  * (contiguous), the packed weights, scale and bias are resident on the device
  * (as for mtrtq_matmul). Enqueues on `stream` the copy of X into the workspace,

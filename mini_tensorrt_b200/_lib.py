@@ -50,6 +50,8 @@ SIGNATURES = {
                             _vp, _sz, _vp]),
     "mtrtq_matmul_ex": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int,
                                _vp, _sz, _int, _vp, _i64, _vp]),
+    "mtrtq_matmul_ln_ex": (_int, [_vp, _i64, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                  _i64, _int, _vp, _sz, _int, _vp, _i64, _vp]),
     "mtrtq_host_workspace_bytes": (_i64, [_i64, _i64, _i64, _int]),
     "mtrtq_matmul_host": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp]),
     "mtrtq_set_option": (_int, [_int, _i64]),

@@ -548,6 +548,50 @@ int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed,
   return MTRTQ_OK;
 }
 
+int mtrtq_matmul_ln_ex(const float* X, int64_t ldx, const float* ln_gamma, const float* ln_beta,
+                       float ln_eps, const void* packed, const float* scale, const float* bias, float* Y,
+                       int64_t ldy, int64_t M, int64_t K, int64_t N, int mode, void* workspace,
+                       size_t workspace_bytes, int epilogue, const float* residual, int64_t ldr,
+                       void* stream) {
+  if (!X || !ln_gamma || !ln_beta || !packed || !scale || !Y)
+    return fail(MTRTQ_ERR_INVALID_ARG, "null pointer");
+  if (epilogue != MTRTQ_EPILOGUE_NONE && epilogue != MTRTQ_EPILOGUE_GELU_TANH &&
+      epilogue != MTRTQ_EPILOGUE_ADD_RESIDUAL)
+    return fail(MTRTQ_ERR_INVALID_ARG, "unknown epilogue %d", epilogue);
+  Epilogue epi;
+  epi.kind = epilogue;
+  if (epilogue == MTRTQ_EPILOGUE_ADD_RESIDUAL) {
+    if (!residual) return fail(MTRTQ_ERR_INVALID_ARG, "the residual epilogue needs a residual");
+    if (ldr < N) return fail(MTRTQ_ERR_INVALID_ARG, "ldr (%lld) < N (%lld)", (long long)ldr, (long long)N);
+    if (!aligned(residual, 4)) return fail(MTRTQ_ERR_ALIGNMENT, "residual must be 4-byte aligned");
+    epi.residual = residual;
+    epi.ldr = ldr;
+  }
+  if (ldx < K) return fail(MTRTQ_ERR_INVALID_ARG, "ldx (%lld) < K (%lld)", (long long)ldx, (long long)K);
+  if (ldy < N) return fail(MTRTQ_ERR_INVALID_ARG, "ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
+  DeviceInfo d;
+  if (int rc = check_device_sm100(&d)) return rc;
+  Plan p;
+  if (int rc = plan_matmul(M, K, N, MTRTQ_DTYPE_F32, mode, d.sm_count, &p, g_opt_force_path)) return rc;
+  if (p.kind != Plan::kGemvCluster)
+    return fail(MTRTQ_ERR_INVALID_ARG,
+                "the LayerNorm prologue runs on the cluster GEMV only; this call plans another kernel "
+                "(M=%lld K=%lld N=%lld): run mtrtq_layernorm, then mtrtq_matmul_ex",
+                (long long)M, (long long)K, (long long)N);
+  if (!aligned(packed, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "packed weights must be 256-byte aligned");
+  if (!aligned(scale, 4) || (bias && !aligned(bias, 4)) || !aligned(Y, 4) || !aligned(ln_gamma, 4) ||
+      !aligned(ln_beta, 4))
+    return fail(MTRTQ_ERR_ALIGNMENT, "scale, bias, Y, gamma and beta must be 4-byte aligned");
+  if (!aligned(X, 16)) return fail(MTRTQ_ERR_ALIGNMENT, "X must be 16-byte aligned");
+  (void)workspace;
+  (void)workspace_bytes;
+  cudaError_t e = launch_gemv_cluster(p, X, MTRTQ_DTYPE_F32, ldx, packed, scale, bias, Y, ldy, d.status,
+                                      g_opt_overlap != 0, epi, static_cast<cudaStream_t>(stream), ln_gamma,
+                                      ln_beta, ln_eps);
+  if (e != cudaSuccess) return cuda_fail(e, "cluster GEMV launch");
+  return MTRTQ_OK;
+}
+
 // Host staging sits after the kernel scratch: X [M, K] then Y [M, N], fp32, each
 // 256-byte aligned. It never starts inside the ticket-counter region, even for a
 // plan without scratch: a workspace shared with other calls keeps its counters

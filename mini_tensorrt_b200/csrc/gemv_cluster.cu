@@ -72,6 +72,10 @@ struct GemvClParams {
   int stages;      // shared memory ring stages (2..kGemvClMaxStages)
   int early_units; // weight units issued before the activations have arrived
   unsigned* status;
+  // LayerNorm of each activation row before the product (null: none); fp32 X only.
+  const float* ln_gamma;
+  const float* ln_beta;
+  float ln_eps;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -204,15 +208,30 @@ __device__ __forceinline__ uint32_t cl_pack_low_bytes(uint32_t a, uint32_t b, ui
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, e, 0x0040), 0x5410);
 }
 
+// LayerNorm of four consecutive activations of token m at k, with the token's
+// mean and 1 / sqrt(var + eps) in ln[m] and ln[32 + m] (the reference's
+// (x - mean) * inv * gamma + beta, src/ops/kernels_transformer.cpp:50-51); those
+// past K stay zero. No-op when ln is null.
+__device__ __forceinline__ float4 cl_ln4(const GemvClParams& p, float4 v, int m, int k, const float* ln) {
+  if (!ln) return v;
+  const float mean = ln[m], inv = ln[32 + m];
+  float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    a[i] = k + i < p.K ? (a[i] - mean) * inv * __ldg(p.ln_gamma + k + i) + __ldg(p.ln_beta + k + i) : 0.0f;
+  return make_float4(a[0], a[1], a[2], a[3]);
+}
+
 // Loads groups g0, g0 + 32, ... (kB of them, those below gend) of token m's range
-// as fp32 (rounded to bf16 when ROUND); zeros elsewhere.
+// as fp32 (layer-normalized when ln is set, then rounded to bf16 when ROUND);
+// zeros elsewhere.
 template <int kB, bool X_BF16, bool ROUND>
 __device__ __forceinline__ void cl_load_groups(const GemvClParams& p, float4 (&v)[kB], int m, int kbase,
-                                               int g0, int gend, bool vec) {
+                                               int g0, int gend, bool vec, const float* ln) {
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
-    const int g = g0 + b * 32;
-    v[b] = g < gend ? cl_round<ROUND>(cl_load_x4<X_BF16>(p, m, kbase + g * 4, vec))
+    const int g = g0 + b * 32, k = kbase + g * 4;
+    v[b] = g < gend ? cl_round<ROUND>(cl_ln4(p, cl_load_x4<X_BF16>(p, m, k, vec), m, k, ln))
                     : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
@@ -239,10 +258,12 @@ __device__ __forceinline__ void cl_issue_groups(const GemvClParams& p, uint4 (&r
 
 // The values of the groups cl_issue_groups covered, from their raw bits; the
 // others (past the row's end or at a stride that rules out vector loads) are
-// read here element by element. Rounded to bf16 when ROUND.
+// read here element by element. Layer-normalized when ln is set, then rounded to
+// bf16 when ROUND.
 template <int kB, bool X_BF16, bool ROUND>
 __device__ __forceinline__ void cl_decode_groups(const GemvClParams& p, const uint4 (&raw)[kB], float4 (&v)[kB],
-                                                 int m, int kbase, int g0, int gend, bool vec) {
+                                                 int m, int kbase, int g0, int gend, bool vec,
+                                                 const float* ln) {
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
     const int g = g0 + b * 32, k = kbase + g * 4;
@@ -257,6 +278,7 @@ __device__ __forceinline__ void cl_decode_groups(const GemvClParams& p, const ui
     } else {
       v[b] = cl_load_x4<X_BF16>(p, m, k, vec);
     }
+    if (g < gend) v[b] = cl_ln4(p, v[b], m, k, ln);
     v[b] = cl_round<ROUND>(v[b]);
   }
 }
@@ -314,6 +336,7 @@ struct ClStager {
   static constexpr int kBatch = 6;  // groups per lane per batch otherwise
   int m, gbeg, gend, kbase, warp_, nu_;
   bool vec, resident;
+  const float* ln = nullptr;  // per-token LayerNorm statistics in shared memory, if any
   uint4 raw[kRes];
 
   __device__ __forceinline__ void begin(const GemvClParams& p, int u0, int nu, int warp, int lane) {
@@ -345,7 +368,7 @@ struct ClStager {
       bool bad = false;
       for (int g0 = lane; g0 < n4; g0 += 32 * kBatch) {
         float4 w[kBatch];
-        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec);
+        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec, ln);
         cl_max_groups<kBatch>(w, mx, bad);
       }
 #pragma unroll
@@ -365,7 +388,7 @@ struct ClStager {
       const float inv = (smax > 0.0f && !s_bad[t]) ? 127.0f / smax : 0.0f;
       for (int g0 = lane; g0 < n4; g0 += 32 * kBatch) {
         float4 w[kBatch];
-        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec);
+        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec, ln);
         cl_store_digits<kBatch>(w, inv, xd, plane, mt, t, g0, n4);
       }
     }
@@ -382,12 +405,12 @@ struct ClStager {
     bool bad = false;
     float4 v[kRes];
     if (resident) {
-      cl_decode_groups<kRes, X_BF16, ROUND>(p, raw, v, m, kbase, gbeg + lane, gend, vec);
+      cl_decode_groups<kRes, X_BF16, ROUND>(p, raw, v, m, kbase, gbeg + lane, gend, vec, ln);
       cl_max_groups<kRes>(v, mx, bad);
     } else {
       for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
         float4 w[kBatch];
-        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, m, kbase, g0, gend, vec);
+        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, m, kbase, g0, gend, vec, ln);
         cl_max_groups<kBatch>(w, mx, bad);
       }
     }
@@ -413,15 +436,45 @@ struct ClStager {
     }
     for (int g0 = gbeg + lane; g0 < gend; g0 += 32 * kBatch) {
       float4 w[kBatch];
-      cl_load_groups<kBatch, X_BF16, ROUND>(p, w, m, kbase, g0, gend, vec);
+      cl_load_groups<kBatch, X_BF16, ROUND>(p, w, m, kbase, g0, gend, vec, ln);
       cl_store_digits<kBatch>(w, inv, xd, plane, mt, m, g0, gend);
     }
   }
 };
 
+// Per-token LayerNorm statistics over the whole row, with the reference's formula
+// (src/ops/kernels_transformer.cpp:38-49): the mean, then the biased variance of
+// the centred values, inv = 1 / sqrt(var + eps); ln[t] = mean, ln[32 + t] = inv.
+// Warp w takes tokens w, w + 8, ...; each lane adds its elements in k order and
+// the lanes are added in a fixed tree order. Every CTA of a split computes the
+// same statistics from the same row.
+__device__ void cl_ln_stats(const GemvClParams& p, float* ln, int warp, int lane) {
+  const float* X = static_cast<const float*>(p.X);
+  for (int t = warp; t < p.M; t += kClWarps) {
+    const float* row = X + (int64_t)t * p.ldx;
+    float s = 0.0f;
+    for (int k = lane; k < p.K; k += 32) s += __ldg(row + k);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / (float)p.K;
+    float q = 0.0f;
+    for (int k = lane; k < p.K; k += 32) {  // the row again, from L1
+      const float c = __ldg(row + k) - mean;
+      q += c * c;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if (lane == 0) {
+      ln[t] = mean;
+      ln[32 + t] = 1.0f / sqrtf(q / (float)p.K + p.ln_eps);
+    }
+  }
+}
+
 // NB: blocks of 8 tokens (M <= 8 * NB); more blocks need more registers, so fewer
 // CTAs fit an SM.
-template <bool X_BF16, bool ROUND, int RES, int NB>
+// LN: the LayerNorm prologue (p.ln_gamma) is compiled in (fp32 X only).
+template <bool X_BF16, bool ROUND, int RES, int NB, bool LN>
 __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvClCtasPerSmWide)
     gemv_cluster_kernel(const GemvClParams p) {
   // Shared memory: ring [stages][8 KiB] (the exchange buffer part[8 * NB][128] fp32
@@ -431,6 +484,7 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
   __shared__ int s_abort;
   __shared__ int s_max[32], s_bad[32];  // per token: max |x| (fp32 bits), non-finite flag
   __shared__ float s_sb[2][128];      // scale and bias of the rows this CTA finishes
+  __shared__ float s_ln[64];          // LayerNorm mean [32] and 1 / std [32] per token
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
   const int CS = (int)gridDim.x;  // the cluster spans x
@@ -521,7 +575,13 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
     }
     __syncwarp();
   } else {
-    // Consumers: activation digits first (the weights are already in flight).
+    // Consumers: activation digits first (the weights are already in flight),
+    // after the LayerNorm statistics when the call asks for them.
+    if (LN && !X_BF16) {
+      cl_ln_stats(p, s_ln, warp, lane);
+      named_bar_sync(1, kClThreads);
+      stager.ln = s_ln;
+    }
     stager.finish(p, xd, plane, s_max, s_bad, xready, lane);
     named_bar_sync(1, kClThreads);
     // Warp w: channel rows w*16 + g and w*16 + g + 8 (g = lane / 4). MMA step i
@@ -619,9 +679,9 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
   if (CS > 1) cluster_sync_relaxed();
 }
 
-template <bool X_BF16, bool ROUND, int RES, int NB>
+template <bool X_BF16, bool ROUND, int RES, int NB, bool LN = false>
 cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, bool pdl, cudaStream_t st) {
-  auto kern = gemv_cluster_kernel<X_BF16, ROUND, RES, NB>;
+  auto kern = gemv_cluster_kernel<X_BF16, ROUND, RES, NB, LN>;
   if (smem > 48 * 1024) {
     if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern),
                                           (int)(NB == 1 ? kGemvClSmemCap : kGemvClSmemCapWide)))
@@ -657,8 +717,12 @@ size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages) {
 cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,
                                 const void* packed, const float* scale, const float* bias, float* Y,
                                 int64_t ldy, unsigned* status, bool pdl, const Epilogue& epi,
-                                cudaStream_t st) {
+                                cudaStream_t st, const float* ln_gamma, const float* ln_beta,
+                                float ln_eps) {
   GemvClParams gp;
+  gp.ln_gamma = ln_gamma;
+  gp.ln_beta = ln_beta;
+  gp.ln_eps = ln_eps;
   gp.epi = epi;
   gp.X = X;
   gp.ldx = ldx;
@@ -690,6 +754,16 @@ cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64
                    : cl_launch<XB, RD, 6, 1>(gp, p.splits, p.n_tiles, smem, pdl, st))               \
            : nb == 2 ? cl_launch<XB, RD, 6, 2>(gp, p.splits, p.n_tiles, smem, pdl, st)              \
                      : cl_launch<XB, RD, 6, 4>(gp, p.splits, p.n_tiles, smem, pdl, st))
+  if (ln_gamma) {
+    // The LayerNorm prologue: fp32 X, six-group staging (longer shares are read twice).
+    if (x_dtype == 1) return cudaErrorInvalidValue;
+#define MTRTQ_CL_LAUNCH_LN(RD)                                                               \
+  (nb == 1 ? cl_launch<false, RD, 6, 1, true>(gp, p.splits, p.n_tiles, smem, pdl, st)        \
+           : nb == 2 ? cl_launch<false, RD, 6, 2, true>(gp, p.splits, p.n_tiles, smem, pdl, st) \
+                     : cl_launch<false, RD, 6, 4, true>(gp, p.splits, p.n_tiles, smem, pdl, st))
+    return p.round_x ? MTRTQ_CL_LAUNCH_LN(true) : MTRTQ_CL_LAUNCH_LN(false);
+#undef MTRTQ_CL_LAUNCH_LN
+  }
   if (x_dtype == 1) return MTRTQ_CL_LAUNCH(true, false);
   if (p.round_x) return MTRTQ_CL_LAUNCH(false, true);
   return MTRTQ_CL_LAUNCH(false, false);

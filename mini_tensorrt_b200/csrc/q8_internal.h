@@ -71,10 +71,13 @@ constexpr int kGemvClCtasPerSmWide = 2;
 constexpr size_t kGemvClSmemCapWide = 110 * 1024;
 constexpr int kGemvClMaxStages = 8;
 size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages);
+// ln_gamma non-null: each row of X (fp32) is layer-normalized (ln_gamma,
+// ln_beta, ln_eps) before the product.
 cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64_t ldx,
                                 const void* packed, const float* scale, const float* bias, float* Y,
                                 int64_t ldy, unsigned* status, bool pdl, const Epilogue& epi,
-                                cudaStream_t st);
+                                cudaStream_t st, const float* ln_gamma = nullptr,
+                                const float* ln_beta = nullptr, float ln_eps = 0.0f);
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_prepack(const int8_t* q, int64_t K, int64_t N, void* packed, cudaStream_t st);

@@ -98,10 +98,12 @@ class DeviceDecoder:
     overlap: launch the step's kernels with programmatic dependent launch
     (MTRTQ_OPT_OVERLAP_LAUNCH while the step is recorded or launched), so each one
     starts while the one ahead finishes; the weights are never written during
-    decoding, which is the option's condition."""
+    decoding, which is the option's condition.
+    fold_ln: fold each LayerNorm into the MatMulQ that reads it where the shape
+    runs on the cluster GEMV (one launch instead of two)."""
 
     def __init__(self, w: GPT2Weights, batch: int, max_ctx: int, mode: str = "fp32",
-                 device="cuda", max_steps: int | None = None, overlap: bool = True):
+                 device="cuda", max_steps: int | None = None, overlap: bool = True, fold_ln: bool = True):
         cfg = w.cfg
         self.cfg, self.B, self.max_ctx, self.mode = cfg, batch, max_ctx, mode
         self.overlap = overlap
@@ -140,6 +142,13 @@ class DeviceDecoder:
         self.ws_buf = self.ws.get(need)
         self.graph = None
         self.stream = torch.cuda.Stream(dev)
+        # LayerNorm folded into the MatMulQ that reads it (mtrtq_matmul_ln_ex) up to 8
+        # rows, where the shape runs on the cluster GEMV; otherwise a LayerNorm
+        # launch first. Every CTA of the GEMV computes the rows' statistics, which
+        # costs more than the separate launch saves at 16 rows (B200: batch 16
+        # decode 0.65 ms/step folded against 0.61 ms).
+        self.fold_ln = {name: fold_ln and B <= 8 and matmulq.supports_ln(B, K, N, mode)
+                        for name, (K, N) in {"qkv": (D, 3 * D), "fc": (D, F), "lm": (D, V)}.items()}
 
     # -- one decode step, as launches on self.stream ------------------------------
     def _mm(self, x, w: PackedWeight, bias, y, epilogue=_lib.EPILOGUE_NONE, residual=None):
@@ -153,6 +162,24 @@ class DeviceDecoder:
                                     residual.stride(0) if residual is not None else 0, self._sp),
               "mtrtq_matmul_ex")
 
+    def _mm_ln(self, x, ln, w: PackedWeight, bias, y, epilogue=_lib.EPILOGUE_NONE):
+        """y = epilogue(LayerNorm(x; ln) @ w + bias) in one kernel."""
+        check(lib().mtrtq_matmul_ln_ex(x.data_ptr(), x.stride(0), ln[0].data_ptr(), ln[1].data_ptr(),
+                                       self.cfg.eps, w.packed.data_ptr(), w.scale.data_ptr(),
+                                       bias.data_ptr() if bias is not None else None, y.data_ptr(),
+                                       y.stride(0), x.shape[0], w.K, w.N, MODES[self.mode], None, 0, epilogue,
+                                       None, 0, self._sp), "mtrtq_matmul_ln_ex")
+
+    def _ln_then(self, name, ln, w, bias, y, epilogue=_lib.EPILOGUE_NONE):
+        """LayerNorm of x feeding one Linear: folded into it when the shape allows."""
+        if self.fold_ln[name]:
+            self._mm_ln(self.x, ln, w, bias, y, epilogue)
+            return
+        cfg = self.cfg
+        check(lib().mtrtq_layernorm(self.x.data_ptr(), ln[0].data_ptr(), ln[1].data_ptr(), self.h.data_ptr(),
+                                    self.B, cfg.d_model, cfg.eps, self._sp), "layernorm")
+        self._mm(self.h, w, bias, y, epilogue)
+
     def _launch_step(self):
         with matmulq.option(_lib.OPT_OVERLAP_LAUNCH, 1 if self.overlap else 0):
             self._launch_step_kernels()
@@ -164,22 +191,16 @@ class DeviceDecoder:
                                    self.pos.data_ptr(), self.wte.data_ptr(), self.wpe.data_ptr(),
                                    cfg.n_pos, self.x.data_ptr(), B, D, cfg.vocab, sp), "embed")
         for i, ly in enumerate(self.layers):
-            check(L.mtrtq_layernorm(self.x.data_ptr(), ly["ln1"][0].data_ptr(), ly["ln1"][1].data_ptr(),
-                                    self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
-            self._mm(self.h, ly["qkv"], ly["bqkv"], self.qkv)
+            self._ln_then("qkv", ly["ln1"], ly["qkv"], ly["bqkv"], self.qkv)
             check(L.mtrtq_decode_attention(self.qkv.data_ptr(), self.kc[i].data_ptr(),
                                            self.vc[i].data_ptr(), self.pos.data_ptr(),
                                            self.attn.data_ptr(), B, cfg.n_head, cfg.head_dim,
                                            self.max_ctx, sp), "attention")
             # x += attn @ Wo + bo, fused into the MatMulQ store
             self._mm(self.attn, ly["o"], ly["bo"], self.x, _lib.EPILOGUE_ADD_RESIDUAL, self.x)
-            check(L.mtrtq_layernorm(self.x.data_ptr(), ly["ln2"][0].data_ptr(), ly["ln2"][1].data_ptr(),
-                                    self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
-            self._mm(self.h, ly["fc"], ly["bfc"], self.mh, _lib.EPILOGUE_GELU_TANH)
+            self._ln_then("fc", ly["ln2"], ly["fc"], ly["bfc"], self.mh, _lib.EPILOGUE_GELU_TANH)
             self._mm(self.mh, ly["proj"], ly["bproj"], self.x, _lib.EPILOGUE_ADD_RESIDUAL, self.x)
-        check(L.mtrtq_layernorm(self.x.data_ptr(), self.ln_f[0].data_ptr(), self.ln_f[1].data_ptr(),
-                                self.h.data_ptr(), B, D, cfg.eps, sp), "layernorm")
-        self._mm(self.h, self.lm_head, None, self.logits)
+        self._ln_then("lm", self.ln_f, self.lm_head, None, self.logits)
         check(L.mtrtq_argmax_rows(self.logits.data_ptr(), B, cfg.vocab, cfg.vocab,
                                   self.best.data_ptr(), sp), "argmax")
         check(L.mtrtq_decode_next(self.best.data_ptr(), B, self.next_tok.data_ptr(),

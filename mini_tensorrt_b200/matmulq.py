@@ -208,6 +208,36 @@ def matmul_q8(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None = None
     return out
 
 
+def matmul_q8_ln(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float, w: PackedWeight,
+                 bias: torch.Tensor | None = None, out: torch.Tensor | None = None, mode: str = "bf16",
+                 stream=None, epilogue: str = "none", residual: torch.Tensor | None = None) -> torch.Tensor:
+    """out = epilogue(LayerNorm(x; gamma, beta, eps) @ dequant(w) (+ bias)) in one
+    kernel (mtrtq_matmul_ln_ex). x: float32 CUDA [M, K]; raises MtrtqError when the
+    shape plans a kernel other than the cluster GEMV (check supports_ln first)."""
+    if x.dim() != 2 or x.shape[1] != w.K or x.dtype != torch.float32 or x.stride(1) != 1:
+        raise ValueError(f"x must be float32 [M, {w.K}] with unit stride along K")
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, w.N), dtype=torch.float32, device=x.device)
+    epi = EPILOGUES[epilogue]
+    if epi == _lib.EPILOGUE_ADD_RESIDUAL and (residual is None or residual.shape != (M, w.N)):
+        raise ValueError("the residual epilogue needs residual float32 [M, N]")
+    with torch.cuda.device(x.device):
+        check(lib().mtrtq_matmul_ln_ex(x.data_ptr(), x.stride(0), gamma.data_ptr(), beta.data_ptr(), float(eps),
+                                       w.packed.data_ptr(), w.scale.data_ptr(), _ptr(bias), out.data_ptr(),
+                                       out.stride(0), M, w.K, w.N, MODES[mode], None, 0, epi,
+                                       _ptr(residual) if epi == _lib.EPILOGUE_ADD_RESIDUAL else None,
+                                       residual.stride(0) if epi == _lib.EPILOGUE_ADD_RESIDUAL else 0,
+                                       _stream_ptr(stream)),
+              "mtrtq_matmul_ln_ex")
+    return out
+
+
+def supports_ln(M: int, K: int, N: int, mode: str = "bf16") -> bool:
+    """Whether mtrtq_matmul_ln_ex takes this shape (it plans the cluster GEMV)."""
+    return plan_info(M, K, N, torch.float32, mode)["path"] == "cluster_gemv"
+
+
 def host_workspace_bytes(M: int, K: int, N: int, mode: str = "bf16") -> int:
     n = lib().mtrtq_host_workspace_bytes(M, K, N, MODES[mode])
     if n < 0:

@@ -25,14 +25,18 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 SMALL = gpt2.GPT2Config(n_layer=2, d_model=128, n_head=4, d_ff=512, vocab=1000, n_pos=64)
 
 
-@pytest.mark.parametrize("overlap", [True, False], ids=["overlapped", "serial"])
+@pytest.mark.parametrize("overlap,fold_ln", [(True, True), (False, True), (True, False)],
+                         ids=["overlapped", "serial", "separate_layernorm"])
 @pytest.mark.parametrize("batch", [1, 3])
-def test_small_model_matches_oracle(cuda_device, batch, overlap):
+def test_small_model_matches_oracle(cuda_device, batch, overlap, fold_ln):
     """Also with every kernel of the step launched with programmatic dependent
-    launch (each may start while the one ahead finishes), the default."""
+    launch (each may start while the one ahead finishes) and each LayerNorm folded
+    into the MatMulQ after it, the defaults."""
     w = gpt2.random_weights(SMALL, seed=5)
     prompt = np.random.default_rng(6).integers(0, SMALL.vocab, (batch, 5), dtype=np.int32)
-    dec = gpt2.DeviceDecoder(w, batch, max_ctx=32, mode="fp32", device=cuda_device, overlap=overlap)
+    dec = gpt2.DeviceDecoder(w, batch, max_ctx=32, mode="fp32", device=cuda_device, overlap=overlap,
+                             fold_ln=fold_ln)
+    assert all(dec.fold_ln.values()) == fold_ln
     got = dec.generate(prompt, max_new=12)
     want = OracleDecoder(w, batch, 32).generate(prompt, 12)
     np.testing.assert_array_equal(got["tokens"], want)

@@ -513,3 +513,73 @@ def test_host_call_leaves_shared_workspace_counters(cuda_device):
         matmul_q8(torch.from_numpy(X).to(cuda_device), pw, out=y, mode="fp32", workspace=ws)
         torch.cuda.synchronize()
     check(y.cpu().numpy(), X, q, s, "fp32")
+
+
+def _layernorm(x, g, b, eps):
+    """The reference's LayerNorm (src/ops/kernels_transformer.cpp:38-52) in fp32."""
+    mean = x.mean(axis=1, keepdims=True, dtype=np.float32)
+    c = (x - mean).astype(np.float32)
+    var = (c * c).mean(axis=1, keepdims=True, dtype=np.float32)
+    return (c * (np.float32(1.0) / np.sqrt(var + np.float32(eps))) * g + b).astype(np.float32)
+
+
+LN_CASES = [(1, 768, 2304), (8, 768, 3072), (3, 100, 300), (16, 768, 768), (32, 768, 3072), (8, 4096, 1000),
+            (5, 1000, 520), (8, 768, 50257)]
+
+
+@pytest.mark.parametrize("M,K,N", LN_CASES, ids=[f"{M}x{K}x{N}" for M, K, N in LN_CASES])
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("epilogue", ["none", "gelu", "residual"])
+def test_layernorm_prologue(cuda_device, M, K, N, mode, epilogue):
+    """mtrtq_matmul_ln_ex: LayerNorm of each row, then MatMulQ (+ bias, epilogue), in
+    one cluster GEMV; against the reference's LayerNorm and MatMulQ on the CPU."""
+    if not matmulq.supports_ln(M, K, N, mode):
+        pytest.skip("shape plans another kernel")
+    W = wl.weights(K, N, 700 + M)
+    q, s = matmulq.quantize_per_channel(W)
+    rng = np.random.default_rng(701 + M)
+    X = (rng.standard_normal((M, K)) * 3 + 0.5).astype(np.float32)
+    g = (1.0 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+    be = (0.1 * rng.standard_normal(K)).astype(np.float32)
+    b = wl.bias(N, 702)
+    R = wl.activations(M, N, 703)
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+    T = lambda a: torch.from_numpy(a).to(cuda_device)
+    # contiguous rows (16-byte loads) for even M, a padded stride (element loads) for odd M
+    ldx = K + 13 if M % 2 else K
+    xb = torch.zeros((M, ldx), device=cuda_device)
+    xb[:, :K] = T(X)
+    y = T(R).clone() if epilogue == "residual" else torch.full((M, N), float("nan"), device=cuda_device)
+    matmulq.matmul_q8_ln(xb[:, :K], T(g), T(be), 1e-5, pw, bias=T(b), out=y, mode=mode, epilogue=epilogue,
+                         residual=y if epilogue == "residual" else None)
+    torch.cuda.synchronize()
+    assert matmulq.read_device_status() == 0
+    H = _layernorm(X, g, be, 1e-5)
+
+    def finish(t):
+        if epilogue == "gelu":
+            u = t.astype(np.float64)
+            return (0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))).astype(np.float32)
+        return (R + t).astype(np.float32) if epilogue == "residual" else t
+
+    got = y.cpu().numpy()
+    assert np.all(np.isfinite(got))
+    err = normwise_rel_err(got, finish(oracle.matmul_q8(H, q, s, b)))
+    if mode == "fp32":
+        assert err <= FP32_TOL, f"fp32 rel err {err:.3e}"
+    else:
+        assert err <= BF16_SPEC_TOL, f"bf16 rel err {err:.3e}"
+        errb = normwise_rel_err(got, finish(oracle.matmul_q8(oracle.round_bf16(H), q, s, b)))
+        assert errb <= 2e-3, f"bf16 rel err vs rounded LayerNorm output {errb:.3e}"
+
+
+def test_layernorm_prologue_refuses_other_kernels(cuda_device):
+    q, s = matmulq.quantize_per_channel(wl.weights(768, 768, 710))
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+    x = torch.zeros((64, 768), device=cuda_device)
+    g = torch.ones(768, device=cuda_device)
+    with pytest.raises(_lib.MtrtqError, match="cluster GEMV"):
+        matmulq.matmul_q8_ln(x, g, g, 1e-5, pw)  # M = 64: the tile GEMM
+    with forced(1):
+        with pytest.raises(_lib.MtrtqError, match="cluster GEMV"):
+            matmulq.matmul_q8_ln(x[:4], g, g, 1e-5, pw)
