@@ -1,5 +1,6 @@
-// Decode GEMV for the INT8 weight-only MatMul, M <= 8: split-K inside a thread-block
-// cluster, reduced through distributed shared memory.
+// Decode GEMV for the INT8 weight-only MatMul, M <= 32 (blocks of 8 tokens):
+// split-K inside a thread-block cluster, reduced through distributed shared
+// memory; optionally with each activation row layer-normalized first.
 //
 // Replaces, for the decode sites, the reference's scalar MatMulQ loop
 // (src/ops/kernels_matmul.cpp:66-73) and the KV-cache decoder's fp32 GEMV
@@ -23,9 +24,10 @@
 // In MTRTQ_MODE_BF16, fp32 activations are first rounded to bf16. Non-finite
 // activations make the token's outputs NaN.
 //
-// K order: an MMA sums over k in any order, so each lane loads the 16 bytes of
-// one 16-k slab row and feeds them to two k32 steps; the activation digits are
-// laid out with the same permutation.
+// Operand loads: the weight fragments of a unit's two k32 steps come from two
+// ldmatrix.x4 (each 8 x 16 B matrix is eight consecutive rows of one 16-k slab,
+// 128 contiguous bytes: no bank conflict), and the activation digits are stored
+// in fragment order, so a lane's four B-fragment words are one 16-byte load.
 //
 // Partial sums never leave the SM cluster: each warp owns 16 channel rows, the CS
 // ranks' partials are exchanged through distributed shared memory after a cluster
