@@ -46,6 +46,8 @@ sys.path.insert(0, ROOT)
 METRIC = "int8-W GEMM TFLOP/s & GEMV HBM GB/s vs peak; GPT-2 decode tok/s @1/2/4/8 GPU"
 UNIT = "GB/s"
 WEIGHT_COPIES = 6
+DECODE_SET_WORKLOAD = ("decode GEMV set, GPT-2-small shapes (QKV 768x2304, attn-out 768x768, FFN-up 768x3072, "
+                       "FFN-down 3072x768, LM head 768x50257) x M in {1,8}")
 E2E_STREAMS = 3  # host-buffer calls of a step spread over this many streams
 LAUNCHES_PER_GRAPH = 4 * WEIGHT_COPIES  # dominant-kernel timing: launches per graph
 FALLBACK_HBM_GBS = 6650.0
@@ -282,8 +284,7 @@ def run_ours(args, torch, rank, world, dev, dist):
         "scaling": "weak", "vs_baseline": None,
         "dtype": PATH_DTYPES[per_kernel[dom_m]["plan"]["path"]],
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantized per channel)",
-        "config": {"workload": "decode GEMV set, GPT-2-small shapes (QKV 768x2304, attn-out 768x768, "
-                               "FFN-up 768x3072, FFN-down 3072x768, LM head 768x50257) x M in {1,8}",
+        "config": {"workload": DECODE_SET_WORKLOAD,
                    "calls_per_step": len(calls), "algorithmic_bytes_per_step": step_bytes,
                    "mode": args.mode, "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": f"weights rotated over {WEIGHT_COPIES} copies "
@@ -659,7 +660,9 @@ def run_reference_arm(args):
             "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
             "ms_per_step": round(secs / n * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "i8w-f32acc", "data": "synthetic",
-            "config": {"workload": "decode GEMV set, GPT-2-small shapes x M in {1,8}", "mode": "fp32"},
+            "config": {"workload": DECODE_SET_WORKLOAD, "calls_per_step": 10,
+                       "algorithmic_bytes_per_step": step_bytes, "mode": "fp32 (the reference's arithmetic)",
+                       "parallelism": "single"},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
                              "kind": "reference", "sample": sample},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
