@@ -591,7 +591,6 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
     // the activation words of token g at k = 4c + 16j (j = 0..3) as one 16-byte
     // load, words 2i and 2i + 1 feeding step i.
     const int g = lane >> 2, c = lane & 3;
-    const int ra = warp * 16 + g;
     const int8_t* xg = xd + g * 64 + c * 16;  // token g of block 0; block nb adds 8 * nb tokens
     int st = 0;
     uint32_t ph = 0;
