@@ -350,12 +350,16 @@ class DeviceExecutor:
     device memory.
 
     mode: MatMulQ mode ("bf16" rounds activations to bf16; "fp32" keeps them).
+    use_graph: record the node launches of the first run() as a CUDA graph and
+    replay it in later runs (the inputs, arena and outputs keep their addresses, so
+    one recording serves every run); the copies in and out stay outside the graph.
     """
 
     SUPPORTED = ("MatMulQ", "Add", "LayerNorm", "GeluTanh")
 
-    def __init__(self, model: LoadedModel, device="cuda", mode: str = "bf16"):
+    def __init__(self, model: LoadedModel, device="cuda", mode: str = "bf16", use_graph: bool = False):
         self.model, self.g, self.mode = model, model.graph, mode
+        self.use_graph, self.graph = use_graph, None
         self.dev = torch.device(device)
         self.order = self.g.topo_order()
         self.stream = torch.cuda.Stream(self.dev)
@@ -489,9 +493,21 @@ class DeviceExecutor:
                 h = self.host[tid]
                 h.numpy()[...] = np.asarray(arr).reshape(h.shape)
                 self.buf[tid].copy_(h, non_blocking=True)
-            for ni in self.order:
-                self._launch(g.nodes[ni])
+            if self.graph is not None:
+                self.graph.replay()
+            else:
+                for ni in self.order:
+                    self._launch(g.nodes[ni])
             for tid in g.outputs:
                 self.host[tid].copy_(self.buf[tid], non_blocking=True)
         self.stream.synchronize()
-        return [self.host[tid].numpy().copy() for tid in g.outputs]
+        out = [self.host[tid].numpy().copy() for tid in g.outputs]
+        if self.use_graph and self.graph is None:
+            # record after one eager run (first launches do per-device set-up)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=self.stream):
+                for ni in self.order:
+                    self._launch(g.nodes[ni])
+            self.stream.synchronize()
+            self.graph = graph
+        return out

@@ -88,3 +88,17 @@ def test_unsupported_ops_fail_at_setup(cuda_device):
     m2 = ex.quantize_matmuls(mlp_model(M=2, D=64, F=96))
     with pytest.raises(GraphError, match="broadcast Add"):
         ex.DeviceExecutor(m2, cuda_device)
+
+
+def test_graph_replay_matches_eager(cuda_device):
+    """use_graph: the first run records the node launches, later runs replay them."""
+    m = ex.fuse_matmulq_epilogues(ex.quantize_matmuls(mlp_model(M=8, D=768, F=3072)))
+    eager = ex.DeviceExecutor(m, cuda_device, mode="fp32")
+    graphed = ex.DeviceExecutor(m, cuda_device, mode="fp32", use_graph=True)
+    rng = np.random.default_rng(3)
+    for i in range(3):
+        x = rng.standard_normal((8, 768)).astype(np.float32)
+        want = eager.run(x)[0]
+        got = graphed.run(x)[0]
+        assert np.array_equal(got, want), f"run {i}"
+    assert graphed.graph is not None
