@@ -215,14 +215,17 @@ def _consumers(g: Graph) -> dict:
 def quantize_matmuls(model: LoadedModel) -> LoadedModel:
     """MatMul(x, W) with W an fp32 weight [K, N] -> MatMulQ(x, Wq, scale): Wq int8
     [K, N] and scale f32 [N] by the reference packer (tests/golden_kernel_test.cpp:
-    163-170; an all-zero column is rejected). Other nodes are kept; the fp32 weight
-    is dropped when nothing else reads it."""
+    163-170; an all-zero column is rejected). A FusedMatMulBiasGeluTanh(x, W, bias)
+    left by the reference's own fusion pass (src/optimizer/fusion.cpp:91-93) becomes
+    MatMulQ {bias, epilogue "gelu"}. Other nodes are kept; the fp32 weight is dropped
+    when nothing else reads it."""
     g = model.graph
     out = Graph(list(g.tensors), [], list(g.inputs), list(g.outputs))
     weights = dict(model.weights)
     cons = _consumers(g)
     for nd in g.nodes:
-        if nd.op_type == "MatMul" and len(nd.inputs) == 2:
+        fused_gelu = nd.op_type == "FusedMatMulBiasGeluTanh" and len(nd.inputs) == 3
+        if (nd.op_type == "MatMul" and len(nd.inputs) == 2) or fused_gelu:
             w_id = nd.inputs[1]
             info = g.tensors[w_id]
             if info.kind == "weight" and info.dtype == "f32" and len(info.shape) == 2:
@@ -230,7 +233,10 @@ def quantize_matmuls(model: LoadedModel) -> LoadedModel:
                 qi = out.add_tensor(TensorInfo(info.name + ".q8", "i8", info.shape, "weight"))
                 si = out.add_tensor(TensorInfo(info.name + ".scale", "f32", (info.shape[1],), "weight"))
                 weights[qi], weights[si] = q, s
-                out.nodes.append(Node("MatMulQ", [nd.inputs[0], qi, si], list(nd.outputs), dict(nd.attrs)))
+                attrs = dict(nd.attrs)
+                if fused_gelu:
+                    attrs.update(bias=nd.inputs[2], epilogue="gelu")
+                out.nodes.append(Node("MatMulQ", [nd.inputs[0], qi, si], list(nd.outputs), attrs))
                 if len(cons.get(w_id, [])) == 1:
                     weights.pop(w_id, None)
                 continue

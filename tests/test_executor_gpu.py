@@ -102,3 +102,18 @@ def test_graph_replay_matches_eager(cuda_device):
         got = graphed.run(x)[0]
         assert np.array_equal(got, want), f"run {i}"
     assert graphed.graph is not None
+
+
+def test_reference_fused_graph_runs(cuda_device):
+    """FusedMatMulBiasGeluTanh from the reference's fusion pass runs as one MatMulQ."""
+    m = mlp_model(M=4, D=768, F=3072, seed=9)
+    g = m.graph
+    mm, add, gelu = g.nodes[1], g.nodes[2], g.nodes[3]
+    ref_model = ex.LoadedModel(ex.Graph(list(g.tensors), list(g.nodes), list(g.inputs), list(g.outputs)),
+                               dict(m.weights))
+    g.nodes[1:4] = [Node("FusedMatMulBiasGeluTanh", [mm.inputs[0], mm.inputs[1], add.inputs[1]],
+                         list(gelu.outputs))]
+    run_model = ex.fuse_matmulq_epilogues(ex.quantize_matmuls(m))
+    x = np.random.default_rng(9).standard_normal((4, 768)).astype(np.float32)
+    y = ex.DeviceExecutor(run_model, cuda_device, mode="fp32").run(x)[0]
+    assert normwise_rel_err(y, reference_forward(ref_model, x)) <= 1e-4

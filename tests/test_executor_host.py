@@ -157,3 +157,18 @@ def test_plan_memory_aligns_and_never_overlaps_live_tensors():
                     assert o1 + nb <= o2 or o2 + nu <= o1
         assert plan.total_bytes % ex.ARENA_ALIGNMENT == 0
         assert plan.total_bytes <= sum(-(-nb // 256) * 256 for _, _, nb in ivs.values())
+
+
+def test_reference_fused_node_becomes_matmulq_with_epilogue():
+    """A graph the reference's fuse_matmul_bias_gelu already rewrote."""
+    m = mlp_model()
+    g = m.graph
+    mm, add, gelu = g.nodes[1], g.nodes[2], g.nodes[3]
+    g.nodes[1:4] = [Node("FusedMatMulBiasGeluTanh", [mm.inputs[0], mm.inputs[1], add.inputs[1]],
+                         list(gelu.outputs))]
+    q = ex.quantize_matmuls(m)
+    n = q.graph.nodes[1]
+    assert n.op_type == "MatMulQ" and n.attrs == {"bias": add.inputs[1], "epilogue": "gelu"}
+    assert n.outputs == gelu.outputs
+    # the executor's node checks accept it (no device needed for the planner)
+    assert ex.plan_memory(q.graph).total_bytes > 0
