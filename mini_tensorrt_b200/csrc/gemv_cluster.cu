@@ -55,10 +55,12 @@ constexpr int kDigits = 3;
 // After them the weight stream waits until every consumer warp has read its
 // activations, so that those loads do not queue behind weight traffic; under
 // programmatic dependent launch the early units are fetched while the grid
-// ahead finishes. Measured on B200 (768 x 50257, M = 1, overlapped launches):
-// 4 units 10.7 us, 3 units 11.0 us, 1 unit 12.0 us.
-constexpr int kClEarlyUnits = 4;
-constexpr int kClEarlyUnitsPdl = 4;
+// ahead finishes. Measured on B200 with overlapped launches (conflict-free
+// operand loads): 6 units against 4 gives 768 x 50257 M = 1 9.41 / 9.83 us,
+// 3072 x 768 M = 8 5.05 / 5.48 us, 4096 x 14336 M = 1 14.18 / 14.5 us, and the
+// same at M = 8 on the large shapes; 8 units is no better than 6.
+constexpr int kClEarlyUnits = 6;
+constexpr int kClEarlyUnitsPdl = 6;
 
 struct GemvClParams {
   const void* X;
