@@ -61,6 +61,22 @@ class TensorInfo:
         return int(np.prod(self.shape, dtype=np.int64)) * np.dtype(DTYPES[self.dtype]).itemsize
 
 
+# Attributes of a fused MatMulQ that name tensors it reads in its epilogue.
+EPILOGUE_OPERANDS = ("bias", "residual")
+
+
+def node_reads(nd) -> list:
+    """Every tensor a node reads: its inputs, then the epilogue operands a fused
+    MatMulQ names in its attributes (bias, residual). Ordering, consumer counts
+    and arena lifetimes all go through this, so a tensor read only by an
+    epilogue is ordered before its reader and stays live until it has run."""
+    reads = list(nd.inputs)
+    for k in EPILOGUE_OPERANDS:
+        if k in nd.attrs:
+            reads.append(int(nd.attrs[k]))
+    return reads
+
+
 @dataclass
 class Graph:
     tensors: list = field(default_factory=list)   # TensorInfo, indexed by tensor id
@@ -88,7 +104,7 @@ class Graph:
         indeg = [0] * n
         consumers = [[] for _ in range(n)]
         for ni, nd in enumerate(self.nodes):
-            for t in nd.inputs:
+            for t in node_reads(nd):
                 if not 0 <= t < len(self.tensors):
                     raise GraphError("node reads out-of-range tensor id")
                 p = producer[t]
@@ -207,7 +223,7 @@ def save_json_model(model: LoadedModel, path: str, weights_file: str | None = No
 def _consumers(g: Graph) -> dict:
     out = {}
     for ni, nd in enumerate(g.nodes):
-        for t in nd.inputs:
+        for t in node_reads(nd):
             out.setdefault(t, []).append(ni)
     return out
 
@@ -324,7 +340,7 @@ def plan_memory(g: Graph, alignment: int = ARENA_ALIGNMENT) -> MemoryPlan:
         for t in nd.outputs:
             if g.tensors[t].kind == "intermediate" and t not in live:
                 live[t] = [step, step]
-        for t in nd.inputs:
+        for t in node_reads(nd):
             if t in live:
                 live[t][1] = step
     ivs = sorted(((t, a, b, g.tensors[t].nbytes) for t, (a, b) in live.items()), key=lambda x: (-x[3], x[0]))

@@ -8,8 +8,8 @@ import torch
 import oracle
 from mini_tensorrt_b200 import executor as ex
 from mini_tensorrt_b200.registry import GraphError, Node
-from tests.conftest import normwise_rel_err
-from tests.test_executor_host import mlp_model
+from tests.conftest import rel_err
+from tests.test_executor_host import block_chain, mlp_model
 
 pytestmark = pytest.mark.gpu
 
@@ -61,7 +61,7 @@ def test_mlp_block_from_json_matches_reference(cuda_device, tmp_path, M, mode):
     x = np.random.default_rng(M).standard_normal((M, 768)).astype(np.float32)
     y = exe.run(x)[0]
     want = reference_forward(m, x)
-    err = normwise_rel_err(y, want)
+    err = rel_err(y, want)
     assert err <= (1e-4 if mode == "fp32" else 2e-2), f"rel err {err:.3e}"
 
 
@@ -116,4 +116,17 @@ def test_reference_fused_graph_runs(cuda_device):
     run_model = ex.fuse_matmulq_epilogues(ex.quantize_matmuls(m))
     x = np.random.default_rng(9).standard_normal((4, 768)).astype(np.float32)
     y = ex.DeviceExecutor(run_model, cuda_device, mode="fp32").run(x)[0]
-    assert normwise_rel_err(y, reference_forward(ref_model, x)) <= 1e-4
+    assert rel_err(y, reference_forward(ref_model, x)) <= 1e-4
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+def test_block_chain_with_arena_residual(cuda_device, mode):
+    """Three chained blocks: from the second on, the residual a fused MatMulQ adds is
+    an intermediate in the arena, so its bytes must survive until that MatMulQ."""
+    m = block_chain(n_blocks=3, M=8, D=768, F=3072, seed=5)
+    run_model = ex.fuse_matmulq_epilogues(ex.quantize_matmuls(m))
+    assert sum(n.attrs.get("epilogue") == "residual" for n in run_model.graph.nodes) == 3
+    x = np.random.default_rng(5).standard_normal((8, 768)).astype(np.float32)
+    y = ex.DeviceExecutor(run_model, cuda_device, mode=mode).run(x)[0]
+    err = rel_err(y, reference_forward(m, x))
+    assert err <= (1e-4 if mode == "fp32" else 2e-2), f"rel err {err:.3e}"

@@ -40,6 +40,57 @@ def mlp_model(M=3, D=64, F=96, seed=0, residual=True):
     return ex.LoadedModel(g, weights)
 
 
+def block_chain(n_blocks=2, M=3, D=64, F=96, seed=0):
+    """n pre-LN MLP blocks whose output projection has no bias, so each block's
+    residual Add folds into its second MatMulQ:
+      x_{i+1} = x_i + MatMul(GeluTanh(MatMul(LayerNorm(x_i), W1) + b1), W2).
+    From the second block on, the residual x_i is an intermediate in the arena,
+    read by the fused MatMulQ's epilogue only."""
+    rng = np.random.default_rng(seed)
+    g = ex.Graph()
+    T = lambda name, dt, shape, kind: g.add_tensor(ex.TensorInfo(name, dt, tuple(shape), kind))
+    f32 = lambda *s, sc=1.0: (rng.standard_normal(s) * sc).astype(np.float32)
+    x = T("x", "f32", (M, D), "input")
+    g.inputs = [x]
+    weights = {}
+    cur = x
+    for i in range(n_blocks):
+        lg, lb = T(f"b{i}.ln.g", "f32", (D,), "weight"), T(f"b{i}.ln.b", "f32", (D,), "weight")
+        w1, b1 = T(f"b{i}.fc.w", "f32", (D, F), "weight"), T(f"b{i}.fc.b", "f32", (F,), "weight")
+        w2 = T(f"b{i}.proj.w", "f32", (F, D), "weight")
+        weights.update({lg: 1.0 + f32(D, sc=0.1), lb: f32(D, sc=0.1), w1: f32(D, F, sc=0.02),
+                        b1: f32(F, sc=0.02), w2: f32(F, D, sc=0.02)})
+        h, t0, t1, t2, t3 = (T(f"b{i}.{n}", "f32", s, "intermediate") for n, s in
+                             [("h", (M, D)), ("t0", (M, F)), ("t1", (M, F)), ("t2", (M, F)), ("t3", (M, D))])
+        last = i == n_blocks - 1
+        nxt = T("y" if last else f"x{i + 1}", "f32", (M, D), "output" if last else "intermediate")
+        g.nodes += [Node("LayerNorm", [cur, lg, lb], [h], {"eps": 1e-5}),
+                    Node("MatMul", [h, w1], [t0]), Node("Add", [t0, b1], [t1]), Node("GeluTanh", [t1], [t2]),
+                    Node("MatMul", [t2, w2], [t3]), Node("Add", [cur, t3], [nxt])]
+        cur = nxt
+    g.outputs = [cur]
+    return ex.LoadedModel(g, weights)
+
+
+def _independent_intervals(g):
+    """Live intervals computed here from first principles (not by the planner):
+    an intermediate is live from its producer's step to the step of its last
+    reader, where a fused MatMulQ also reads the tensors its bias and residual
+    attributes name."""
+    order = g.topo_order()
+    live = {}
+    for step, ni in enumerate(order):
+        nd = g.nodes[ni]
+        for t in nd.outputs:
+            if g.tensors[t].kind == "intermediate":
+                live.setdefault(t, [step, step])
+        reads = list(nd.inputs) + [nd.attrs[k] for k in ("bias", "residual") if k in nd.attrs]
+        for t in reads:
+            if t in live:
+                live[t][1] = step
+    return live
+
+
 def test_json_round_trip_keeps_every_dtype(tmp_path):
     m = mlp_model()
     g = m.graph
@@ -172,3 +223,39 @@ def test_reference_fused_node_becomes_matmulq_with_epilogue():
     assert n.outputs == gelu.outputs
     # the executor's node checks accept it (no device needed for the planner)
     assert ex.plan_memory(q.graph).total_bytes > 0
+
+
+def test_epilogue_operands_stay_live_until_their_reader():
+    """A residual that is an intermediate and read only by a fused MatMulQ's
+    epilogue must not share arena bytes with anything written before that MatMulQ
+    runs (here: the first MatMulQ's output of the same block)."""
+    m = ex.fuse_matmulq_epilogues(ex.quantize_matmuls(block_chain(n_blocks=3, M=2)))
+    g = m.graph
+    fused = [n for n in g.nodes if n.op_type == "MatMulQ" and n.attrs.get("epilogue") == "residual"]
+    assert len(fused) == 3
+    assert any(g.tensors[n.attrs["residual"]].kind == "intermediate" for n in fused)
+    plan = ex.plan_memory(g)
+    live = _independent_intervals(g)
+    assert set(live) == set(plan.offset)
+    for t, (a, b) in live.items():
+        for u, (c, d) in live.items():
+            if t < u and a <= d and c <= b:
+                o1, o2 = plan.offset[t], plan.offset[u]
+                assert o1 + g.tensors[t].nbytes <= o2 or o2 + g.tensors[u].nbytes <= o1, \
+                    (g.tensors[t].name, g.tensors[u].name)
+
+
+def test_epilogue_operand_orders_its_producer_first():
+    """A node whose bias or residual is produced by a node listed later is ordered
+    after that producer, and the producer's output counts as read (not single-use
+    when something else reads it too)."""
+    g = ex.Graph()
+    T = lambda name, shape, kind: g.add_tensor(ex.TensorInfo(name, "f32", tuple(shape), kind))
+    x, wq, sc = T("x", (2, 4), "input"), T("wq", (4, 4), "weight"), T("sc", (4,), "weight")
+    r, y = T("r", (2, 4), "intermediate"), T("y", (2, 4), "output")
+    g.tensors[wq] = ex.TensorInfo("wq", "i8", (4, 4), "weight")
+    g.nodes = [Node("MatMulQ", [x, wq, sc], [y], {"epilogue": "residual", "residual": r}),
+               Node("GeluTanh", [x], [r])]
+    g.inputs, g.outputs = [x], [y]
+    assert g.topo_order() == [1, 0]
+    assert ex.node_reads(g.nodes[0]) == [x, wq, sc, r]
