@@ -5,7 +5,8 @@
 Workload (one step): the decode GEMV set at GPT-2-small shapes -- QKV 768x2304,
 attn-out 768x768, FFN-up 768x3072, FFN-down 3072x768, LM head 768x50257 (tied),
 each at M = 1 and M = 8 token rows (10 MatMulQ calls), fp32 activations ~ N(0,1),
-int8 per-channel weights from N(0, 0.02), MTRTQ_MODE_BF16. Every call has 6
+int8 per-channel weights from N(0, 0.02), MTRTQ_MODE_FP32 (activations keep the
+reference's fp32 values; --mode bf16 rounds them once). Every call has 6
 device copies of its weights and consecutive steps rotate through them (548 MB
 of int8 weights in all, > 4x the 126 MB L2), so weights stream from HBM. The
 calls are launched with MTRTQ_OPT_OVERLAP_LAUNCH (each may start while the one
@@ -24,8 +25,10 @@ GEMV set (data-parallel replicas of the path, no collective on the data path);
 value = all ranks' bytes / the max over ranks of the timed region.
 
 --impl reference: the reference's own CPU MatMulQ (oracle/_ref, compiled from
-its sources) on the same workload, every call split into single-row calls
-(rows are independent in its loop) spread over all host threads; rank 0 only.
+its sources) on the same workload, every call split into row x column-chunk
+pieces (rows and columns are independent in its loop), each prepared once and
+timed as the kernel call alone, spread over all host threads; rank 0 only. It
+imports nothing of the package (inputs come from workloads.py loaded by path).
 """
 from __future__ import annotations
 
@@ -48,6 +51,7 @@ UNIT = "GB/s"
 WEIGHT_COPIES = 6
 DECODE_SET_WORKLOAD = ("decode GEMV set, GPT-2-small shapes (QKV 768x2304, attn-out 768x768, FFN-up 768x3072, "
                        "FFN-down 3072x768, LM head 768x50257) x M in {1,8}")
+DECODE_SET_WEIGHT_BYTES = 2 * (768 * 2304 + 768 * 768 + 768 * 3072 + 3072 * 768 + 768 * 50257)  # M = 1 and 8
 E2E_STREAMS = 3  # host-buffer calls of a step spread over this many streams
 LAUNCHES_PER_GRAPH = 4 * WEIGHT_COPIES  # dominant-kernel timing: launches per graph
 FALLBACK_HBM_GBS = 6650.0
@@ -60,7 +64,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--mode", choices=["bf16", "fp32"], default="fp32",
+                    help="fp32 (default): activations keep the reference's fp32 values; bf16: rounded once")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--workload", default="decode_set",
@@ -284,12 +289,8 @@ def run_ours(args, torch, rank, world, dev, dist):
         "scaling": "weak", "vs_baseline": None,
         "dtype": PATH_DTYPES[per_kernel[dom_m]["plan"]["path"]],
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantized per channel)",
-        "config": {"workload": DECODE_SET_WORKLOAD,
-                   "calls_per_step": len(calls), "algorithmic_bytes_per_step": step_bytes,
-                   "mode": args.mode, "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": f"weights rotated over {WEIGHT_COPIES} copies "
-                         f"({WEIGHT_COPIES * sum(c['K'] * c['N'] for c in calls) / 1e6:.0f} MB > 2x L2)",
-                   "timing": "CUDA graphs of one step, CUDA events on the launching stream",
+        "config": decode_set_config(args, world, step_bytes),
+        "method": {"timing": "CUDA graphs of one step, CUDA events on the launching stream",
                    "overlap_launch": not args.no_overlap},
         "roofline": roofline,
         "e2e": e2e,
@@ -562,39 +563,74 @@ def run_sharded(args, torch, rank, world, dev, dist):
 # ---------------------------------------------------------------------- CPU legs
 
 
-def cpu_tasks():
-    """The decode GEMV set as single-row reference calls: (K, N, q, s, x_row)."""
-    from mini_tensorrt_b200 import matmulq, workloads as wl
-    tasks, step_bytes = [], 0
+def _workloads():
+    """mini_tensorrt_b200/workloads.py (seeded numpy inputs) loaded by file path,
+    so the CPU legs import nothing else of the package: no libmtrtq.so, no torch."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "_mtrtq_workloads", os.path.join(ROOT, "mini_tensorrt_b200", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def decode_set_calls():
+    """The decode GEMV set's calls as the CPU legs see them: (name, X f32 [M,K],
+    q int8 [K,N], scale f32 [N]); packed by the oracle's restatement of the
+    reference packer (bit-exact with it)."""
+    import oracle
+    wl = _workloads()
+    calls, step_bytes = [], 0
+    packed = {}
     for M in wl.DECODE_M:
         for name, K, N in wl.DECODE_SHAPES:
-            q, s = matmulq.quantize_per_channel(wl.decode_weight(name, K, N))
+            if name not in packed:
+                packed[name] = oracle.quantize_per_channel(wl.decode_weight(name, K, N))
+            q, s = packed[name]
             X = wl.activations(M, K, wl.shape_seed("x:" + name, M, K))
-            for r in range(M):
-                tasks.append((K, N, q, s, np.ascontiguousarray(X[r:r + 1])))
+            calls.append((name, X, q, s))
             step_bytes += wl.algorithmic_bytes(M, K, N, 4)
-    return tasks, step_bytes
+    return calls, step_bytes
 
 
-def run_cpu_reference(tasks, threads, min_seconds=None, steps=None):
-    """Runs whole steps of `tasks` through the reference MatMulQ (oracle/_ref) on
-    `threads` host threads; returns (steps run, seconds)."""
+def decode_set_config(args, world, step_bytes):
+    """The workload as both arms name it (identical dicts, so the two lines compare)."""
+    return {"workload": DECODE_SET_WORKLOAD, "calls_per_step": 10, "algorithmic_bytes_per_step": step_bytes,
+            "mode": args.mode, "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": f"inputs larger than L2: the GPU arm rotates every call over {WEIGHT_COPIES} device copies "
+                  f"of its weights ({WEIGHT_COPIES * DECODE_SET_WEIGHT_BYTES / 1e6:.0f} MB > 2x the 126 MB L2); "
+                  f"the CPU arm reads one host copy"}
+
+
+def cpu_row_tasks(calls, chunk_cols=1000):
+    """Independent pieces of the step for a pool of host threads: every call split
+    by rows and by column chunks of <= chunk_cols. Rows and columns are
+    independent in the reference loop (src/ops/kernels_matmul.cpp:66-73), and each
+    piece runs the unmodified reference kernel on its own slice. The chunk width
+    is the best measured for that kernel: its inner loop strides W by N bytes, and
+    a power-of-two stride (4096) maps every k to the same cache sets; on one x86
+    core an LM head row took 134 ms whole, 218 ms in 4096-column chunks and 51 ms
+    in 1000-column chunks."""
     import oracle
-    ref = oracle.ref()
+    tasks = []
+    for _, X, q, s in calls:
+        N = q.shape[1]
+        for r in range(X.shape[0]):
+            for j0 in range(0, N, chunk_cols):
+                j1 = min(N, j0 + chunk_cols)
+                tasks.append(oracle.RefMatmulqCall(X[r:r + 1], np.ascontiguousarray(q[:, j0:j1]), s[j0:j1]))
+    return tasks
 
-    def one(t):
-        K, N, q, s, x = t
-        C = np.empty((1, N), np.float32)
-        ref.ref_matmulq(x.ctypes.data_as(oracle._f32p), q.ctypes.data_as(oracle._i8p),
-                        s.ctypes.data_as(oracle._f32p), C.ctypes.data_as(oracle._f32p), 1, K, N)
 
-    # Longest calls first so the pool finishes together.
-    order = sorted(tasks, key=lambda t: -t[0] * t[1])
+def run_pool(tasks, threads, min_seconds=None, steps=None):
+    """Runs whole steps of `tasks` (objects with run(), called from host threads;
+    the C calls release the GIL) on `threads` threads; returns (steps, seconds)."""
+    order = sorted(tasks, key=lambda t: -(t.M * t.N))  # longest first
 
     def run_step():
         if threads == 1:
             for t in order:
-                one(t)
+                t.run()
             return
         idx = [0]
         lock = threading.Lock()
@@ -606,7 +642,7 @@ def run_cpu_reference(tasks, threads, min_seconds=None, steps=None):
                     idx[0] += 1
                 if i >= len(order):
                     return
-                one(order[i])
+                order[i].run()
         ws = [threading.Thread(target=worker) for _ in range(threads)]
         for w in ws:
             w.start()
@@ -625,19 +661,62 @@ def run_cpu_reference(tasks, threads, min_seconds=None, steps=None):
     return n, time.perf_counter() - t0
 
 
-def cpu_baseline_line():
+class _GemmAutoCall:
+    """One call of the reference's fp32 gemm_auto (backends/cpu/gemm.cpp:288-302) on
+    the dequantized weights q * scale: its own thread rule (the ThreadPool's
+    hardware_concurrency() threads when M >= 32 and 2MNK >= 2^21, one otherwise)."""
+
+    def __init__(self, X, q, s):
+        import oracle
+        self.X = np.ascontiguousarray(X, np.float32)
+        self.W = np.ascontiguousarray(q.astype(np.float32) * s[None, :])
+        self.M, self.N = X.shape[0], q.shape[1]
+        self.C = np.zeros((self.M, self.N), np.float32)
+        self._fn = oracle.ref().ref_gemm_auto
+        self._args = (oracle._ptr(self.X, oracle._f32p), oracle._ptr(self.W, oracle._f32p),
+                      oracle._ptr(self.C, oracle._f32p), self.M, self.N, self.X.shape[1])
+
+    def run(self):
+        self._fn(*self._args)
+
+
+def cpu_baseline_line(calls, step_bytes, seconds=8.0):
+    """The reference's CPU paths on this host, timed beside the GPU: (1) its MatMulQ
+    kernel, single-threaded as it runs, each call prepared once and timed as the
+    kernel call alone; (2) its fp32 'NEON / multithreaded' gemm_auto on dequantized
+    weights with its own thread rule (on x86-64 its NEON step is the scalar packed
+    fallback, gemm.cpp:251-254; at M < 32 it runs on one thread)."""
     import oracle
-    tasks, step_bytes = cpu_tasks()
-    kind = "reference" if oracle.ref_available() else "port"
-    if kind == "port":
+    if not oracle.ref_available():
         return {"value": None, "unit": UNIT, "cores": 1, "kind": "port",
                 "sample": "oracle/_ref missing on this host"}
-    n, secs = run_cpu_reference(tasks, 1, min_seconds=10.0)
-    return {"value": round(step_bytes * n / secs / 1e9, 4), "unit": UNIT, "cores": 1,
-            "kind": "reference",
+    mq = [oracle.RefMatmulqCall(X, q, s) for _, X, q, s in calls]
+    n, secs = run_pool(mq, 1, min_seconds=seconds)
+    mq_val = step_bytes * n / secs / 1e9
+    ga = [_GemmAutoCall(X, q, s) for _, X, q, s in calls]
+    n2, secs2 = run_pool(ga, 1, min_seconds=seconds)
+    ga_val = step_bytes * n2 / secs2 / 1e9
+    hw = int(oracle.ref().ref_hardware_threads())
+    ga_threads = max(1 if X.shape[0] < 32 else hw for _, X, _, _ in calls)
+    return {"value": round(mq_val, 4), "unit": UNIT, "cores": 1, "kind": "reference",
             "sample": f"{n} full decode GEMV set steps (10 calls) through the reference MatMulQ "
-                      f"(oracle/_ref, registry lookup), single thread as the reference runs it, "
-                      f"{secs:.1f} s"}
+                      f"(oracle/_ref, registry lookup once, kernel call timed), one thread as the "
+                      f"reference runs it, {secs:.1f} s",
+            "columns": [
+                {"path": "MatMulQ (src/ops/kernels_matmul.cpp:42-74)", "value": round(mq_val, 4),
+                 "unit": UNIT, "cores": 1, "steps": n, "seconds": round(secs, 2)},
+                {"path": "fp32 gemm_auto on dequantized weights (backends/cpu/gemm.cpp:288-302)",
+                 "value": round(ga_val, 4), "unit": UNIT, "cores": ga_threads, "steps": n2,
+                 "seconds": round(secs2, 2),
+                 "note": "its thread rule gives one thread at M < 32; its NEON kernel is the scalar "
+                         "packed fallback on x86-64"}],
+            "host_threads": hw}
+
+
+def _assert_product_not_loaded():
+    with open("/proc/self/maps") as f:
+        if "libmtrtq" in f.read():
+            raise RuntimeError("the reference arm loaded libmtrtq.so")
 
 
 def run_reference_arm(args):
@@ -648,21 +727,23 @@ def run_reference_arm(args):
     if not oracle.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built"}))
         return
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    calls, step_bytes = decode_set_calls()
+    tasks = cpu_row_tasks(calls)
     threads = max(1, os.cpu_count() or 1)
-    tasks, step_bytes = cpu_tasks()
-    threads = min(threads, len(tasks))
-    run_cpu_reference(tasks, threads, steps=max(1, args.warmup))
-    n, secs = run_cpu_reference(tasks, threads, steps=args.steps)
+    run_pool(tasks, threads, steps=max(1, args.warmup))
+    n, secs = run_pool(tasks, threads, steps=args.steps)
+    _assert_product_not_loaded()
     value = step_bytes * n / secs / 1e9
-    sample = (f"each step: the full decode GEMV set as {len(tasks)} single-row MatMulQ calls "
-              f"through the reference kernel (oracle/_ref) on {threads} host threads")
+    sample = (f"each step: the full decode GEMV set as {len(tasks)} row x column-chunk pieces, each the "
+              f"reference MatMulQ kernel (oracle/_ref, prepared once, registry lookup) on its slice, "
+              f"on {threads} host threads")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
             "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
             "ms_per_step": round(secs / n * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "i8w-f32acc", "data": "synthetic",
-            "config": {"workload": DECODE_SET_WORKLOAD, "calls_per_step": 10,
-                       "algorithmic_bytes_per_step": step_bytes, "mode": "fp32 (the reference's arithmetic)",
-                       "parallelism": "single"},
+            "vs_baseline": None, "dtype": "int8 W -> fp32, fp32 multiply-add (the reference's MatMulQ)",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantized per channel)",
+            "config": decode_set_config(args, world, step_bytes),
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
                              "kind": "reference", "sample": sample},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -711,7 +792,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_extras:
         line["extras"] = run_extras(torch, dev, args, stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_line()
+        cpu_calls, cpu_bytes = decode_set_calls()
+        line["cpu_baseline"] = cpu_baseline_line(cpu_calls, cpu_bytes)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -57,13 +57,23 @@ enum {
 /* Activation element types accepted for A. */
 enum { MTRTQ_DTYPE_F32 = 0, MTRTQ_DTYPE_BF16 = 1 };
 
-/* Arithmetic modes.
- *  MTRTQ_MODE_BF16: A is rounded to bf16 (round-to-nearest-even) once; the int8
- *    weights are exact in bf16; products accumulate in fp32 on tcgen05 tensor cores
- *    (TMEM accumulators): a stream-K kernel for M <= 64 (decode and small prefill),
- *    a tiled GEMM above.
- *  MTRTQ_MODE_FP32: A stays fp32 and every product and sum is fp32 on CUDA cores,
- *    the reference's arithmetic up to summation order. */
+/* Arithmetic modes. The mode fixes what A is before the product; the kernel then
+ * depends on the shape (mtrtq_plan_info reports it).
+ *  MTRTQ_MODE_BF16: fp32 A is rounded to bf16 (round-to-nearest-even) once.
+ *  MTRTQ_MODE_FP32: A keeps its fp32 value (result within 1e-4 of the reference).
+ * Kernels:
+ *  - decode, M <= 8 in either mode, and fp32 mode up to M = 32 (bf16 mode too when
+ *    the weights are at most 8 MiB): the cluster GEMV. The int8 weights are never
+ *    converted; each activation is written as three int8 digits over its CTA's k
+ *    range, x = (s/127)(d0 + d1/2^7 + d2/2^14) with s the range's max |x|, which
+ *    represents it to within 2^-15 s/127 (about 2^-22 of that max); int8 x int8
+ *    warp MMAs accumulate exactly in int32, and the digits are combined in fp32.
+ *  - bf16 mode, M <= 32 otherwise: a stream-K tcgen05 kernel; above, a tiled
+ *    tcgen05 GEMM. Weights are dequantized to bf16 exactly, products accumulate in
+ *    fp32 in TMEM.
+ *  - fp32 mode above M = 32: a CUDA-core split-K GEMV, every product and sum fp32.
+ * In every kernel the per-channel scale multiplies the finished sum, then the bias
+ * is added, as in the reference (src/ops/kernels_matmul.cpp:66-73). */
 enum { MTRTQ_MODE_BF16 = 0, MTRTQ_MODE_FP32 = 1 };
 
 /* Quantize-time policy for an all-zero weight column (the reference packer divides
@@ -199,9 +209,10 @@ int mtrtq_matmul_host(const float* X, const void* packed, const float* scale, co
  * (mtrtq_workspace_bytes with MTRTQ_OPT_FORCE_PATH = 1) exceeds it are rejected
  * with MTRTQ_ERR_WORKSPACE. The first call on a device looks up that device's
  * array address (cudaGetSymbolAddress, with the device current); make that first
- * call before any stream capture. Every call resets the array's split counters on
- * `stream` before its kernel. All calls share the one array, so calls that overlap
- * on the GPU (different streams, or other host threads) race: keep them ordered. */
+ * call before any stream capture. A call whose plan splits K resets the array's
+ * split counters on `stream` before its kernel. All calls share the one array, so
+ * calls that overlap on the GPU (different streams, or other host threads) race:
+ * keep them ordered. */
 #define MTRTQ_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const void* packed,
                               const float* scale, const float* bias, float* Y, int64_t ldy,

@@ -49,7 +49,7 @@ int g_opt_force_path = 0;     // 0 auto, else the kernel (MTRTQ_OPT_FORCE_PATH)
 int g_opt_overlap = 0;        // 1: programmatic dependent launch (MTRTQ_OPT_OVERLAP_LAUNCH)
 
 std::mutex g_dev_mu;
-DeviceInfo g_dev_cache[64];
+DeviceInfo g_dev_cache[64];  // indexed by device ordinal; current_device() rejects >= 64
 
 // Current device's properties; sm_count 148 when there is no device.
 int current_device(DeviceInfo* out) {
@@ -650,12 +650,15 @@ namespace {
 // address comes from cudaGetSymbolAddress, once per device.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[MTRTQ_NOALLOC_SCRATCH_BYTES];
 
+constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {nullptr};
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
 
 // This device's address of g_noalloc_scratch (looked up on its first use here,
 // with the device current).
 int noalloc_scratch(int dev, void** out) {
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(MTRTQ_ERR_NO_DEVICE, "device ordinal %d is outside 0..%d", dev, kMaxDevices - 1);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* ptr = nullptr;
@@ -693,10 +696,14 @@ int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const voi
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(d.device, &scratch)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Counters must start at zero; a previous call leaves them at zero, but one that
-  // gave up on a timeout may not, so clear them (memset: no allocation).
-  cudaError_t e = cudaMemsetAsync(static_cast<char*>(scratch) + p.off_counters, 0, kCounterBytes, st);
-  if (e != cudaSuccess) return cuda_fail(e, "clear no-allocation counters");
+  // Split counters must start at zero; a previous call leaves them at zero, but one
+  // that gave up on a timeout may not, so clear them (memset: no allocation). A plan
+  // with one split touches neither counters nor partials.
+  cudaError_t e = cudaSuccess;
+  if (p.splits > 1) {
+    e = cudaMemsetAsync(static_cast<char*>(scratch) + p.off_counters, 0, kCounterBytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "clear no-allocation counters");
+  }
   e = launch_gemv(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, scratch, Epilogue(), st);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return MTRTQ_OK;

@@ -65,6 +65,44 @@ def ref_available() -> bool:
     return os.path.exists(_REF_PATH)
 
 
+_PIN_PATH = os.path.join(_HERE, "_ref", "ref_packer_pin")
+
+
+def ref_packer_available() -> bool:
+    return os.path.exists(_PIN_PATH)
+
+
+def ref_packer(W: np.ndarray, A: np.ndarray | None = None, expected: np.ndarray | None = None):
+    """Packs W f32 [K,N] with the reference's own packer lines: the body of its
+    TEST(Golden, MatMulQ) (tests/golden_kernel_test.cpp:155-175, packer at
+    :163-170) compiled unmodified into oracle/_ref/ref_packer_pin. Returns
+    (q int8 [K,N], scale f32 [N], C or None, checks_failed): C is the reference
+    kernel's output on A when the test's fixed [2,5] output fits it, and
+    checks_failed counts the test's own failed assertions (its 0.05 bar against
+    `expected`, zeros when not given)."""
+    import subprocess
+    import tempfile
+    if not ref_packer_available():
+        raise RuntimeError(f"reference packer missing: {_PIN_PATH} (run oracle/build_ref.sh)")
+    W = _f32(W)
+    K, N = W.shape
+    A = np.zeros((2, K), np.float32) if A is None else _f32(A)
+    expected = np.zeros((2, 5), np.float32) if expected is None else _f32(expected)
+    with tempfile.TemporaryDirectory() as d:
+        np.save(os.path.join(d, "op_matmul_a.npy"), A)
+        np.save(os.path.join(d, "op_matmul_b.npy"), W)
+        np.save(os.path.join(d, "op_matmul_out.npy"), expected)
+        out = os.path.join(d, "pin")
+        r = subprocess.run([_PIN_PATH, d, out], capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"ref_packer_pin failed ({r.returncode}): {r.stderr}")
+        failed = int(r.stdout.strip().split("=")[1])
+        q = np.fromfile(out + ".q", np.int8).reshape(K, N)
+        s = np.fromfile(out + ".s", np.float32)
+        C = np.fromfile(out + ".c", np.float32).reshape(A.shape[0], N) if os.path.exists(out + ".c") else None
+    return q, s, C, failed
+
+
 def ref():
     """The reference's own MatMulQ path (oracle/_ref). Raises if absent."""
     global _ref
@@ -80,6 +118,14 @@ def ref():
         r.ref_gemm_auto.restype = None
         r.ref_hardware_threads.argtypes = []
         r.ref_hardware_threads.restype = ctypes.c_int
+        r.ref_matmulq_prepare.argtypes = [_f32p, _i8p, _f32p, _i64, _i64, _i64]
+        r.ref_matmulq_prepare.restype = ctypes.c_void_p
+        r.ref_matmulq_run.argtypes = [ctypes.c_void_p]
+        r.ref_matmulq_run.restype = None
+        r.ref_matmulq_output.argtypes = [ctypes.c_void_p, _f32p]
+        r.ref_matmulq_output.restype = None
+        r.ref_matmulq_free.argtypes = [ctypes.c_void_p]
+        r.ref_matmulq_free.restype = None
         _ref = r
     return _ref
 
@@ -154,6 +200,35 @@ def ref_matmul_q8(A, q, s, bias=None):
         if ref().ref_add_bias(_ptr(C, _f32p), _ptr(b, _f32p), M, N) != 0:
             raise RuntimeError("reference registry has no Add kernel")
     return C
+
+
+class RefMatmulqCall:
+    """One reference MatMulQ call prepared once (Tensors built, kernel looked up);
+    run() is the kernel call alone, as the reference executor's run loop makes it."""
+
+    def __init__(self, A, q, s):
+        A = _f32(A)
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        s = _f32(s)
+        self.M, K = A.shape
+        self.N = q.shape[1]
+        self._h = ref().ref_matmulq_prepare(_ptr(A, _f32p), _ptr(q, _i8p), _ptr(s, _f32p), self.M, K, self.N)
+        if not self._h:
+            raise RuntimeError("reference registry has no MatMulQ kernel")
+        self._run = ref().ref_matmulq_run
+
+    def run(self):
+        self._run(self._h)
+
+    def output(self):
+        C = np.empty((self.M, self.N), np.float32)
+        ref().ref_matmulq_output(self._h, _ptr(C, _f32p))
+        return C
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            ref().ref_matmulq_free(self._h)
+            self._h = None
 
 
 def ref_gemm_auto(A, B):

@@ -1,9 +1,11 @@
 #!/usr/bin/env bash
-# Builds the oracle's two shared libraries. Test infrastructure only.
+# Builds the oracle's libraries. Test infrastructure only.
 #
 #   oracle/liboracle.so        the C restatement (matmulq_oracle.c), always built
 #   oracle/_ref/libmtrt_ref.so the reference's own MatMulQ path, compiled from its
 #                              unmodified sources where they lie, plus ref_shim.cpp
+#   oracle/_ref/ref_packer_pin the reference's Golden.MatMulQ test body (its int8
+#                              packer) compiled unmodified, plus ref_packer_pin.cpp
 #
 # The reference's CMake build needs network (FetchContent of gtest/nlohmann), so the
 # few sources on the MatMulQ path are compiled directly with g++. The JSON/ONNX
@@ -11,10 +13,12 @@
 # Release flags (-DNDEBUG) as the reference's own benchmarks use; -ffp-contract=off
 # keeps multiply and add separate in both libraries so they agree bit for bit.
 #
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+# REFERENCE_ROOT: the argument, else $MTRTQ_REFERENCE_ROOT, else a checkout named
+# "reference" beside this repository.
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF="${1:-/root/reference}"
+REF="${1:-${MTRTQ_REFERENCE_ROOT:-${HERE}/../../reference}}"
 CFLAGS="-O3 -fPIC -ffp-contract=off -fno-fast-math"
 
 gcc ${CFLAGS} -std=c11 -shared -o "${HERE}/liboracle.so" "${HERE}/matmulq_oracle.c" -lm
@@ -44,4 +48,16 @@ for s in "${SRCS[@]}"; do ABS+=("${REF}/${s}"); done
 g++ -std=c++17 ${CFLAGS} -DNDEBUG -shared -pthread \
   -I "${REF}/include" -I "${REF}" -I "${REF}/src" -I "${REF}/src/ops" \
   -o "${HERE}/_ref/libmtrt_ref.so" "${HERE}/ref_shim.cpp" "${ABS[@]}"
-echo "build_ref: built ${HERE}/liboracle.so and ${HERE}/_ref/libmtrt_ref.so"
+
+# The reference's own packer, run as written: its tests/golden_kernel_test.cpp,
+# unmodified, against the local gtest stand-in, with the registry call and the
+# goldens directory redirected (see ref_packer_pin.cpp).
+g++ -std=c++17 ${CFLAGS} -DNDEBUG -pthread -c \
+  -I "${HERE}/gtest_shim" -I "${REF}/include" -I "${REF}" -I "${REF}/src" -I "${REF}/src/ops" \
+  -include "${HERE}/pin_prelude.h" -Dregister_builtin_kernels=pin_register_builtin_kernels \
+  "-DMTRT_GOLDENS_DIR=pin_goldens_dir()" \
+  -o "${HERE}/_ref/golden_kernel_test.o" "${REF}/tests/golden_kernel_test.cpp"
+g++ -std=c++17 ${CFLAGS} -DNDEBUG -pthread \
+  -I "${HERE}/gtest_shim" -I "${REF}/include" -I "${REF}" -I "${REF}/src" -I "${REF}/src/ops" \
+  -o "${HERE}/_ref/ref_packer_pin" "${HERE}/ref_packer_pin.cpp" "${HERE}/_ref/golden_kernel_test.o" "${ABS[@]}"
+echo "build_ref: built ${HERE}/liboracle.so, ${HERE}/_ref/libmtrt_ref.so and ${HERE}/_ref/ref_packer_pin"

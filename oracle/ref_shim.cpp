@@ -70,6 +70,42 @@ int ref_matmulq(const float* A, const int8_t* W, const float* scale, float* C, i
   return 0;
 }
 
+// A MatMulQ call prepared once -- its reference Tensors built and the kernel looked
+// up, as the reference executor does at construction (src/runtime/executor.cpp:
+// 51-123) -- so that timing ref_matmulq_run measures the kernel call alone, as the
+// executor's run loop makes it (:139-142).
+struct RefMatmulq {
+  mtrt::KernelFn fn;
+  mtrt::Tensor A, W, S, C;
+  mtrt::Node node;
+};
+
+void* ref_matmulq_prepare(const float* A, const int8_t* W, const float* scale, int64_t M, int64_t K,
+                          int64_t N) {
+  mtrt::KernelFn fn = registry().lookup("MatMulQ", mtrt::DType::kF32);
+  if (!fn) return nullptr;
+  RefMatmulq* h = new RefMatmulq{fn, make_tensor(mtrt::DType::kF32, {M, K}, A),
+                                 make_tensor(mtrt::DType::kI8, {K, N}, W),
+                                 make_tensor(mtrt::DType::kF32, {N}, scale),
+                                 mtrt::Tensor::owning(mtrt::DType::kF32, {M, N}), mtrt::Node{}};
+  h->node.op_type = "MatMulQ";
+  return h;
+}
+
+void ref_matmulq_run(void* handle) {
+  RefMatmulq* h = static_cast<RefMatmulq*>(handle);
+  std::vector<const mtrt::Tensor*> ins{&h->A, &h->W, &h->S};
+  std::vector<mtrt::Tensor*> outs{&h->C};
+  h->fn(mtrt::OpContext{ins, outs, h->node});
+}
+
+void ref_matmulq_output(void* handle, float* C) {
+  RefMatmulq* h = static_cast<RefMatmulq*>(handle);
+  std::memcpy(C, h->C.data<float>(), static_cast<size_t>(h->C.numel()) * sizeof(float));
+}
+
+void ref_matmulq_free(void* handle) { delete static_cast<RefMatmulq*>(handle); }
+
 // Y[M,N] = Y + b[N] through the registry's "Add" kernel (bias broadcast form).
 int ref_add_bias(float* Y, const float* b, int64_t M, int64_t N) {
   mtrt::KernelFn fn = registry().lookup("Add", mtrt::DType::kF32);

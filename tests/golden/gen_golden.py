@@ -3,17 +3,22 @@
 Run in a checkout where the reference sources are available and the oracle
 libraries are built (oracle/build_ref.sh):
 
-    python tests/golden/gen_golden.py [REFERENCE_ROOT]     # default /root/reference
+    python tests/golden/gen_golden.py [REFERENCE_ROOT]
+
+REFERENCE_ROOT: the argument, else $MTRTQ_REFERENCE_ROOT, else a checkout named
+"reference" beside this repository.
 
 Writes into tests/golden/:
   * matmulq_op.npz -- the reference's own Golden.MatMulQ case
     (tests/golden_kernel_test.cpp:155-175): its fixtures op_matmul_a [2,3],
     op_matmul_b [3,5], op_matmul_out [2,5] (PyTorch seed 123,
-    python/gen_goldens.py:54-59), the per-column int8 packing of B and its scales,
-    and MatMulQ's output computed by the reference's own kernel (oracle/_ref).
+    python/gen_goldens.py:54-59), the per-column int8 packing of B and its scales
+    as the reference's own test body packs them (oracle/_ref/ref_packer_pin), and
+    MatMulQ's output computed by the reference's own kernel on them.
   * seeded.json -- for seeded inputs at the GPT-2 / large-model shapes
-    (mini_tensorrt_b200/workloads.py): SHA-256 of the packed int8 weights, the
-    scales and the reference kernel's fp32 output bytes, plus a few output values.
+    (mini_tensorrt_b200/workloads.py): SHA-256 of the packed int8 weights and the
+    scales (packed by the reference's own packer lines, oracle/_ref/ref_packer_pin)
+    and of the reference kernel's fp32 output bytes, plus a few output values.
     The reference library computes the outputs, so a match of the oracle's bytes
     pins the oracle to the reference bit for bit without shipping megabytes.
 """
@@ -60,7 +65,8 @@ def sha(a: np.ndarray) -> str:
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get(
+        "MTRTQ_REFERENCE_ROOT", os.path.join(ROOT, "..", "reference"))
     if not oracle.ref_available():
         raise SystemExit("oracle/_ref/libmtrt_ref.so missing: run oracle/build_ref.sh first")
 
@@ -68,15 +74,19 @@ def main():
     A = np.load(os.path.join(g, "op_matmul_a.npy")).astype(np.float32)
     B = np.load(os.path.join(g, "op_matmul_b.npy")).astype(np.float32)
     out = np.load(os.path.join(g, "op_matmul_out.npy")).astype(np.float32)
-    q, s = oracle.quantize_per_channel(B)
-    C = oracle.ref_matmul_q8(A, q, s)
+    if not oracle.ref_packer_available():
+        raise SystemExit("oracle/_ref/ref_packer_pin missing: run oracle/build_ref.sh first")
+    # Packing comes from the reference's own packer lines (its Golden.MatMulQ test
+    # body, run by oracle/_ref/ref_packer_pin), not from the oracle's restatement.
+    q, s, C, failed = oracle.ref_packer(B, A, out)
+    assert failed == 0, "the reference's Golden.MatMulQ checks failed"
     np.savez(os.path.join(HERE, "matmulq_op.npz"), a=A, b=B, out=out, q=q, s=s, c_ref=C)
 
     cases = {}
     for case in SEEDED_CASES:
         cid, M, K, N, with_bias, _ = case
         X, W, b = case_inputs(case)
-        q, s = oracle.quantize_per_channel(W)
+        q, s, _, _ = oracle.ref_packer(W)
         C = oracle.ref_matmul_q8(X, q, s, b)
         idx = np.linspace(0, C.size - 1, 8).astype(np.int64)
         cases[cid] = {
@@ -86,7 +96,10 @@ def main():
         }
         print(cid, cases[cid]["c_sha256"][:16])
     with open(os.path.join(HERE, "seeded.json"), "w") as f:
-        json.dump({"generator": "tests/golden/gen_golden.py", "cases": cases}, f, indent=1)
+        json.dump({"generator": "tests/golden/gen_golden.py",
+                   "packing": "the reference's Golden.MatMulQ packer (oracle/_ref/ref_packer_pin)",
+                   "outputs": "the reference's registry MatMulQ + Add (oracle/_ref/libmtrt_ref.so)",
+                   "cases": cases}, f, indent=1)
 
 
 if __name__ == "__main__":

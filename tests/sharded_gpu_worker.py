@@ -13,7 +13,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 import oracle  # noqa: E402
 from mini_tensorrt_b200 import matmulq, sharded, workloads as wl  # noqa: E402
-from tests.conftest import normwise_rel_err  # noqa: E402
+from tests.conftest import rel_err  # noqa: E402
 
 CASES = [("N", 8, 768, 50257), ("K", 8, 768, 50257), ("N", 1, 4096, 14336), ("K", 2, 4096, 4096),
          ("N", 64, 768, 3072), ("K", 64, 3072, 768), ("N", 3, 200, 300)]
@@ -35,7 +35,7 @@ def main():
             y = op(torch.from_numpy(X).cuda()).cpu().numpy()
             rows = np.unique(np.linspace(0, M - 1, min(M, 8)).astype(np.int64))
             ref = oracle.matmul_q8_rows(X, q, s, rows, b)
-            err = normwise_rel_err(y[rows], ref)
+            err = rel_err(y[rows], ref)
             assert np.isfinite(y).all(), f"case {i}: non-finite output"
             assert err <= 1e-4, f"rank {rank} case {i} ({split}, {M}x{K}x{N}): rel err {err:.3e}"
         torch.cuda.synchronize()

@@ -17,7 +17,7 @@ import torch
 
 from mini_tensorrt_b200 import gpt2
 from oracle.gpt2_decode import OracleDecoder
-from tests.conftest import normwise_rel_err
+from tests.conftest import rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -45,7 +45,7 @@ def test_small_model_matches_oracle(cuda_device, batch, overlap, fold_ln):
     toks = np.concatenate([prompt, want[:, :-1]], axis=1)
     for pos in range(toks.shape[1]):
         _, logits = ref.step(toks[:, pos], pos)
-    err = normwise_rel_err(dec.logits.cpu().numpy(), logits)
+    err = rel_err(dec.logits.cpu().numpy(), logits)
     assert err <= 1e-4, f"logits rel err {err:.3e}"
 
 
@@ -66,7 +66,7 @@ def test_odd_shapes_match_oracle(cuda_device, cfg, max_ctx):
     toks = np.concatenate([prompt, want[:, :-1]], axis=1)
     for pos in range(toks.shape[1]):
         _, logits = ref.step(toks[:, pos], pos)
-    err = normwise_rel_err(dec.logits.cpu().numpy(), logits)
+    err = rel_err(dec.logits.cpu().numpy(), logits)
     assert err <= 1e-4, f"logits rel err {err:.3e}"
 
 

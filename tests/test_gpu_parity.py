@@ -18,7 +18,7 @@ import torch
 import oracle
 from mini_tensorrt_b200 import _lib, matmulq, registry, workloads as wl
 from mini_tensorrt_b200.matmulq import PackedWeight, matmul_q8
-from tests.conftest import normwise_rel_err
+from tests.conftest import rel_err
 from tests.golden.gen_golden import SEEDED_CASES, case_inputs
 
 pytestmark = pytest.mark.gpu
@@ -60,12 +60,12 @@ def check(Y, X, q, s, mode, bias=None, rows=None, tc=False):
         refb = oracle.matmul_q8(oracle.round_bf16(X), q, s, bias)
     assert np.all(np.isfinite(Y))
     if mode == "fp32":
-        err = normwise_rel_err(Y, ref)
+        err = rel_err(Y, ref)
         assert err <= FP32_TOL, f"fp32 mode rel err {err:.3e}"
     else:
-        err = normwise_rel_err(Y, ref)
+        err = rel_err(Y, ref)
         assert err <= BF16_SPEC_TOL, f"bf16 mode rel err vs fp32 inputs {err:.3e}"
-        errb = normwise_rel_err(Y, refb)
+        errb = rel_err(Y, refb)
         tol = BF16_SAME_INPUT_TOL_TC if tc else BF16_SAME_INPUT_TOL_CORES
         assert errb <= tol, f"bf16 mode rel err vs rounded inputs {errb:.3e}"
 
@@ -219,7 +219,7 @@ def test_registry_device_kernel_matches_golden(cuda_device):
         registry.run_kernel(reg, "MatMulQ", [A, W, s], out, {"mode": mode})
         got = out.cpu().numpy()
         if mode == "fp32":
-            assert normwise_rel_err(got, g["c_ref"]) <= FP32_TOL
+            assert rel_err(got, g["c_ref"]) <= FP32_TOL
         assert np.allclose(got, g["out"], rtol=0.05, atol=0.05)
     with pytest.raises(registry.GraphError):
         registry.run_kernel(reg, "MatMulQ", [A, W], torch.empty((2, 5), device=cuda_device))
@@ -228,7 +228,7 @@ def test_registry_device_kernel_matches_golden(cuda_device):
         out = torch.full((2, 5), float("nan"))
         registry.run_kernel(reg, "MatMulQ", [A.cpu(), W.cpu(), s.cpu()], out, {"mode": mode})
         if mode == "fp32":
-            assert normwise_rel_err(out.numpy(), g["c_ref"]) <= FP32_TOL
+            assert rel_err(out.numpy(), g["c_ref"]) <= FP32_TOL
         assert np.allclose(out.numpy(), g["out"], rtol=0.05, atol=0.05)
 
 
@@ -409,7 +409,7 @@ def test_overlapped_launches_wait_for_their_inputs(cuda_device, graph):
     for (q, s, _), y in zip(qs, ys):
         out = y.cpu().numpy()
         assert np.all(np.isfinite(out)), "a call read its input before it was written"
-        err = normwise_rel_err(out, oracle.matmul_q8(inp, q, s))
+        err = rel_err(out, oracle.matmul_q8(inp, q, s))
         assert err <= FP32_TOL, f"fp32 mode rel err {err:.3e}"
         inp = out
 
@@ -450,7 +450,7 @@ def test_fused_epilogues(cuda_device, M, K, N, path, epilogue):
     assert matmulq.read_device_status() == 0
     t = oracle.matmul_q8(X, q, s, b)
     want = _gelu_new(t) if epilogue == "gelu" else (R + t).astype(np.float32)
-    err = normwise_rel_err(y.cpu().numpy(), want)
+    err = rel_err(y.cpu().numpy(), want)
     assert err <= (1e-4 if path in (1, 4) else 1e-3), f"rel err {err:.3e}"
 
 
@@ -564,12 +564,12 @@ def test_layernorm_prologue(cuda_device, M, K, N, mode, epilogue):
 
     got = y.cpu().numpy()
     assert np.all(np.isfinite(got))
-    err = normwise_rel_err(got, finish(oracle.matmul_q8(H, q, s, b)))
+    err = rel_err(got, finish(oracle.matmul_q8(H, q, s, b)))
     if mode == "fp32":
         assert err <= FP32_TOL, f"fp32 rel err {err:.3e}"
     else:
         assert err <= BF16_SPEC_TOL, f"bf16 rel err {err:.3e}"
-        errb = normwise_rel_err(got, finish(oracle.matmul_q8(oracle.round_bf16(H), q, s, b)))
+        errb = rel_err(got, finish(oracle.matmul_q8(oracle.round_bf16(H), q, s, b)))
         assert errb <= 2e-3, f"bf16 rel err vs rounded LayerNorm output {errb:.3e}"
 
 

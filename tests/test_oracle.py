@@ -4,7 +4,9 @@
 * against the reference library's outputs for seeded inputs at every GPT-2 and
   large-model shape (hashes in tests/golden/seeded.json, made by gen_golden.py);
 * live against oracle/_ref on ragged shapes when that library is present;
-* the packer's rounding rule (lround: ties away from zero) and zero columns.
+* the packer's rounding rule (lround: ties away from zero) and zero columns;
+* the packing itself against the reference's own packer lines, run unmodified
+  (its Golden.MatMulQ test body, oracle/_ref/ref_packer_pin), when built here.
 """
 import hashlib
 import json
@@ -106,3 +108,56 @@ def test_round_bf16_matches_torch():
     a = oracle.round_bf16(x)
     t = torch.from_numpy(x).to(torch.bfloat16).to(torch.float32).numpy()
     assert np.array_equal(a.view(np.uint32), t.view(np.uint32))
+
+
+_needs_pin = pytest.mark.skipif(not oracle.ref_packer_available(),
+                                reason="oracle/_ref/ref_packer_pin not built here")
+
+
+@_needs_pin
+def test_reference_packer_runs_golden_matmulq():
+    """The reference's TEST(Golden, MatMulQ), run as written on its own fixtures:
+    its checks pass, and the packed bytes, scales and kernel output it produces are
+    the committed ones (which the oracle matches above)."""
+    g = np.load(os.path.join(GOLDEN, "matmulq_op.npz"))
+    q, s, C, failed = oracle.ref_packer(g["b"], g["a"], g["out"])
+    assert failed == 0
+    assert np.array_equal(q, g["q"]) and np.array_equal(s.view(np.uint32), g["s"].view(np.uint32))
+    assert np.array_equal(C.view(np.uint32), g["c_ref"].view(np.uint32))
+
+
+def _unique_weight_cases():
+    seen, out = set(), []
+    for case in SEEDED_CASES:
+        key = (case[2], case[3], case[5])
+        if key not in seen:
+            seen.add(key)
+            out.append(case)
+    return out
+
+
+@_needs_pin
+@pytest.mark.parametrize("case", _unique_weight_cases(), ids=lambda c: f"{c[5]}_{c[2]}x{c[3]}")
+def test_reference_packer_pins_seeded_packing(case):
+    """The reference's packer lines pack every seeded weight matrix into the bytes
+    whose hashes are committed, and the oracle's restatement packs the same."""
+    exp = _SEEDED[case[0]]
+    _, W, _ = case_inputs(case)
+    q, s, _, _ = oracle.ref_packer(W)
+    assert _sha(q) == exp["q_sha256"] and _sha(s) == exp["scale_sha256"]
+    qo, so = oracle.quantize_per_channel(W)
+    assert np.array_equal(q, qo) and np.array_equal(s.view(np.uint32), so.view(np.uint32))
+
+
+@_needs_pin
+def test_reference_packer_ties_and_zero_column():
+    """Exact .5 ties and an all-zero column through the reference's own lines: ties
+    round away from zero (lround), and the zero column stores s = 0 with q = 0
+    (0/0 through lround and the int8 cast on x86-64), as the oracle does."""
+    W = np.array([[127.0, 2.5, 0.0], [2.5, -2.5, 0.0], [-3.5, 127.0, 0.0], [0.5, -0.5, 0.0]],
+                 dtype=np.float32)
+    q, s, _, _ = oracle.ref_packer(W)
+    qo, so = oracle.quantize_per_channel(W)
+    assert s.tolist() == [1.0, 1.0, 0.0] and np.array_equal(s.view(np.uint32), so.view(np.uint32))
+    assert np.array_equal(q, qo)
+    assert q[:, 0].tolist() == [127, 3, -4, 1] and q[:, 2].tolist() == [0, 0, 0, 0]

@@ -20,7 +20,7 @@ import torch.multiprocessing as mp
 
 import oracle
 from mini_tensorrt_b200 import sharded, workloads as wl
-from tests.conftest import normwise_rel_err
+from tests.conftest import rel_err
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -67,7 +67,7 @@ def _cpu_worker(rank, world, port, split, M, K, N, q):
                                     local_matmul=local, pack=pack)
         y = op(torch.from_numpy(X)).numpy()
         ref = oracle.matmul_q8(X, qm, s, b)
-        err = normwise_rel_err(y, ref)
+        err = rel_err(y, ref)
         q.put((rank, float(err), bool(np.isfinite(y).all())))
     finally:
         dist.destroy_process_group()

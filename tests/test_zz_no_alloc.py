@@ -18,7 +18,7 @@ import torch
 
 from mini_tensorrt_b200 import _lib, matmulq, workloads as wl
 from mini_tensorrt_b200.matmulq import MODES, PackedWeight
-from tests.conftest import normwise_rel_err
+from tests.conftest import rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -51,7 +51,7 @@ def test_no_alloc_entry_point_matches_matmul_twice_in_a_row(cuda_device, mode):
             torch.cuda.synchronize()
             got, want = y.cpu().numpy(), ref.cpu().numpy()
             assert np.all(np.isfinite(got))
-            err = normwise_rel_err(got, want)
+            err = rel_err(got, want)
             assert err <= TOL[mode], f"rep {rep} case {i}: rel err {err:.3e}"
     assert matmulq.read_device_status() == 0
 
