@@ -94,7 +94,7 @@ size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 constexpr int64_t kMaxDim = int64_t(1) << 30;
 constexpr size_t kCounterBytes = 4096;                       // fixed ticket region
 constexpr int64_t kMaxSplitTiles = kCounterBytes / sizeof(unsigned);
-// Weight bytes up to which bf16 calls with 8 < M <= 32 take the cluster GEMV.
+// Weight bytes up to which bf16 calls with 8 < M <= 64 take the cluster GEMV.
 constexpr int64_t kClusterWideMaxBytes = 8ll << 20;
 
 int check_dims(int64_t M, int64_t K, int64_t N) {
@@ -111,16 +111,19 @@ int check_dims(int64_t M, int64_t K, int64_t N) {
 
 // Cluster GEMV geometry: one cluster of CS CTAs (CS <= 8) per 128-channel tile,
 // each CTA streaming ceil(KB / CS) 64-k units through a ring of shared memory stages.
-// All clusters should be resident at once (3 CTAs per SM for M <= 8, 2 above):
+// All clusters should be resident at once (3 CTAs per SM for M <= 8, 2 up to 32, 1
+// up to 64):
 // CS is the largest split that keeps n_tiles * CS within that, at most KB; it
 // grows, if needed, until a CTA's activation digits leave room for two stages;
 // the ring then takes what the shared memory cap leaves (2 to 8 stages).
 static bool gemv_cluster_plan(int64_t M, int sm_count, Plan* p) {
   if (M > kGemvClMaxM || p->n_tiles > 65535) return false;
-  const bool wide = M > 8;
-  const size_t cap = wide ? kGemvClSmemCapWide : kGemvClSmemCap;
+  // One block of 8 tokens: 3 CTAs per SM; up to four: 2; up to eight: 1.
+  const int tier = M <= 8 ? 0 : M <= 32 ? 1 : 2;
+  const size_t cap = tier == 0 ? kGemvClSmemCap : tier == 1 ? kGemvClSmemCapWide : kGemvClSmemCapWide8;
   const int64_t KB = p->k_pad / kBlockK;
-  const int64_t capacity = (int64_t)sm_count * (wide ? kGemvClCtasPerSmWide : kGemvClCtasPerSm);
+  const int64_t capacity =
+      (int64_t)sm_count * (tier == 0 ? kGemvClCtasPerSm : tier == 1 ? kGemvClCtasPerSmWide : kGemvClCtasPerSmWide8);
   int64_t cs = capacity / p->n_tiles;
   if (cs > KB) cs = KB;
   if (cs > 8) cs = 8;
@@ -161,7 +164,7 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   p.k_pad = round_up64(K, kBlockK);
   p.n_tiles = (int)(p.n_pad / kTileN);
 
-  // Path: M <= 32 -> the cluster GEMV when its shared memory allows (bf16 mode with
+  // Path: M <= 64 -> the cluster GEMV when its shared memory allows (bf16 mode with
   // M > 8: small weights only);
   // otherwise bf16 mode -> stream-K tcgen05 kernel for M <= 32 (and at most
   // kMaxSplitTiles channel tiles), tile tcgen05 GEMM above; fp32 mode -> the
@@ -170,8 +173,8 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   if (mode == MTRTQ_MODE_BF16) path = (M <= 32 && p.n_tiles <= kMaxSplitTiles) ? 3 : 2;
   {
     // For 8 < M <= 32 in bf16 mode the stream-K tcgen05 kernel is faster on large
-    // weights (its MMAs do the 32 tokens in one pass); the cluster GEMV stays
-    // ahead on small ones, where a call is latency-bound.
+    // weights (its MMAs do the 32 tokens in one pass), and the tile GEMM above; the
+    // cluster GEMV stays ahead on small ones, where a call is latency-bound.
     Plan q = p;
     const bool small_w = K * N <= kClusterWideMaxBytes;
     if ((M <= 8 || mode == MTRTQ_MODE_FP32 || small_w) && gemv_cluster_plan(M, sm_count, &q)) path = 4;
@@ -185,8 +188,8 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
       Plan q = p;
       if (!gemv_cluster_plan(M, sm_count, &q))
         return fail(MTRTQ_ERR_INVALID_ARG,
-                    "the cluster GEMV takes M <= 32 and at most 72 KiB (M <= 8) or 110 KiB of "
-                    "shared memory per CTA");
+                    "the cluster GEMV takes M <= 64 and at most 72 KiB (M <= 8), 110 KiB (M <= 32) "
+                    "or 200 KiB (M <= 64) of shared memory per CTA");
     }
     path = force_path;
   }

@@ -1,4 +1,4 @@
-// Decode GEMV for the INT8 weight-only MatMul, M <= 32 (blocks of 8 tokens):
+// Decode GEMV for the INT8 weight-only MatMul, M <= 64 (blocks of 8 tokens):
 // split-K inside a thread-block cluster, reduced through distributed shared
 // memory; optionally with each activation row layer-normalized first.
 //
@@ -51,6 +51,7 @@ constexpr int kClThreads = kClWarps * 32;  // consumer threads
 constexpr int kClBlock = kClThreads + 32;  // + the producer warp
 constexpr uint32_t kUnitBytes = 8192;      // 64 k x 128 channels of int8
 constexpr int kDigits = 3;
+constexpr int kClMaxTokens = kGemvClMaxM;  // 8 blocks of 8 tokens
 // Weight units issued before the activations land (at most the ring's stages).
 // After them the weight stream waits until every consumer warp has read its
 // activations, so that those loads do not queue behind weight traffic; under
@@ -213,12 +214,12 @@ __device__ __forceinline__ uint32_t cl_pack_low_bytes(uint32_t a, uint32_t b, ui
 }
 
 // LayerNorm of four consecutive activations of token m at k, with the token's
-// mean and 1 / sqrt(var + eps) in ln[m] and ln[32 + m] (the reference's
+// mean and 1 / sqrt(var + eps) in ln[m] and ln[kClMaxTokens + m] (the reference's
 // (x - mean) * inv * gamma + beta, src/ops/kernels_transformer.cpp:50-51); those
 // past K stay zero. No-op when ln is null.
 __device__ __forceinline__ float4 cl_ln4(const GemvClParams& p, float4 v, int m, int k, const float* ln) {
   if (!ln) return v;
-  const float mean = ln[m], inv = ln[32 + m];
+  const float mean = ln[m], inv = ln[kClMaxTokens + m];
   float a[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -448,7 +449,7 @@ struct ClStager {
 
 // Per-token LayerNorm statistics over the whole row, with the reference's formula
 // (src/ops/kernels_transformer.cpp:38-49): the mean, then the biased variance of
-// the centred values, inv = 1 / sqrt(var + eps); ln[t] = mean, ln[32 + t] = inv.
+// the centred values, inv = 1 / sqrt(var + eps); ln[t] = mean, ln[kClMaxTokens + t] = inv.
 // Warp w takes tokens w, w + 8, ...; each lane adds its elements in k order and
 // the lanes are added in a fixed tree order. Every CTA of a split computes the
 // same statistics from the same row.
@@ -470,25 +471,26 @@ __device__ void cl_ln_stats(const GemvClParams& p, float* ln, int warp, int lane
     for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
     if (lane == 0) {
       ln[t] = mean;
-      ln[32 + t] = 1.0f / sqrtf(q / (float)p.K + p.ln_eps);
+      ln[kClMaxTokens + t] = 1.0f / sqrtf(q / (float)p.K + p.ln_eps);
     }
   }
 }
 
 // NB: blocks of 8 tokens (M <= 8 * NB); more blocks need more registers, so fewer
-// CTAs fit an SM.
+// CTAs fit an SM (3 for one block, 2 for up to four, 1 for eight).
 // LN: the LayerNorm prologue (p.ln_gamma) is compiled in (fp32 X only).
 template <bool X_BF16, bool ROUND, int RES, int NB, bool LN>
-__global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvClCtasPerSmWide)
+__global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm
+                                             : NB <= 4 ? kGemvClCtasPerSmWide : kGemvClCtasPerSmWide8)
     gemv_cluster_kernel(const GemvClParams p) {
   // Shared memory: ring [stages][8 KiB] (the exchange buffer part[8 * NB][128] fp32
   // reuses it at the end) | full[8], empty[8], xready (+ pad) barriers |
   // digits [3][nu][M][64] s8.
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_abort;
-  __shared__ int s_max[32], s_bad[32];  // per token: max |x| (fp32 bits), non-finite flag
+  __shared__ int s_max[kClMaxTokens], s_bad[kClMaxTokens];  // per token: max |x| (fp32 bits), non-finite flag
   __shared__ float s_sb[2][128];      // scale and bias of the rows this CTA finishes
-  __shared__ float s_ln[64];          // LayerNorm mean [32] and 1 / std [32] per token
+  __shared__ float s_ln[2 * kClMaxTokens];  // LayerNorm mean and 1 / std per token
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
   const int CS = (int)gridDim.x;  // the cluster spans x
@@ -528,7 +530,7 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm : kGemvCl
       }
       mbar_init(xready, kClWarps);
       s_abort = 0;
-      for (int i = 0; i < 32; ++i) s_max[i] = s_bad[i] = 0;
+      for (int i = 0; i < kClMaxTokens; ++i) s_max[i] = s_bad[i] = 0;
       fence_barrier_init();
       for (; issued < prefill; ++issued) {
         mbar_arrive_expect_tx(&full[st_p], kUnitBytes);
@@ -687,7 +689,8 @@ cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, 
   auto kern = gemv_cluster_kernel<X_BF16, ROUND, RES, NB, LN>;
   if (smem > 48 * 1024) {
     if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern),
-                                          (int)(NB == 1 ? kGemvClSmemCap : kGemvClSmemCapWide)))
+                                          (int)(NB == 1 ? kGemvClSmemCap
+                                                : NB <= 4 ? kGemvClSmemCapWide : kGemvClSmemCapWide8)))
       return e;
   }
   cudaLaunchConfig_t cfg = {};
@@ -745,7 +748,7 @@ cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64
   // Activation groups a staging lane holds: 6 unless some warp's share needs
   // more to be staged in one pass (a token has floor(8 / M) warps; M > 8 stages
   // whole tokens per warp in batches).
-  const int nb = p.M <= 8 ? 1 : (p.M <= 16 ? 2 : 4);
+  const int nb = p.M <= 8 ? 1 : p.M <= 16 ? 2 : p.M <= 32 ? 4 : 8;
   bool wide = false;
   if (p.M <= 8) {
     const int64_t nu_max = (p.kunits + p.splits - 1) / p.splits;
@@ -755,15 +758,17 @@ cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64
 #define MTRTQ_CL_LAUNCH(XB, RD)                                                                     \
   (nb == 1 ? (wide ? cl_launch<XB, RD, 12, 1>(gp, p.splits, p.n_tiles, smem, pdl, st)               \
                    : cl_launch<XB, RD, 6, 1>(gp, p.splits, p.n_tiles, smem, pdl, st))               \
-           : nb == 2 ? cl_launch<XB, RD, 6, 2>(gp, p.splits, p.n_tiles, smem, pdl, st)              \
-                     : cl_launch<XB, RD, 6, 4>(gp, p.splits, p.n_tiles, smem, pdl, st))
+   : nb == 2 ? cl_launch<XB, RD, 6, 2>(gp, p.splits, p.n_tiles, smem, pdl, st)                      \
+   : nb == 4 ? cl_launch<XB, RD, 6, 4>(gp, p.splits, p.n_tiles, smem, pdl, st)                      \
+             : cl_launch<XB, RD, 6, 8>(gp, p.splits, p.n_tiles, smem, pdl, st))
   if (ln_gamma) {
     // The LayerNorm prologue: fp32 X, six-group staging (longer shares are read twice).
     if (x_dtype == 1) return cudaErrorInvalidValue;
 #define MTRTQ_CL_LAUNCH_LN(RD)                                                               \
   (nb == 1 ? cl_launch<false, RD, 6, 1, true>(gp, p.splits, p.n_tiles, smem, pdl, st)        \
-           : nb == 2 ? cl_launch<false, RD, 6, 2, true>(gp, p.splits, p.n_tiles, smem, pdl, st) \
-                     : cl_launch<false, RD, 6, 4, true>(gp, p.splits, p.n_tiles, smem, pdl, st))
+   : nb == 2 ? cl_launch<false, RD, 6, 2, true>(gp, p.splits, p.n_tiles, smem, pdl, st)      \
+   : nb == 4 ? cl_launch<false, RD, 6, 4, true>(gp, p.splits, p.n_tiles, smem, pdl, st)      \
+             : cl_launch<false, RD, 6, 8, true>(gp, p.splits, p.n_tiles, smem, pdl, st))
     return p.round_x ? MTRTQ_CL_LAUNCH_LN(true) : MTRTQ_CL_LAUNCH_LN(false);
 #undef MTRTQ_CL_LAUNCH_LN
   }

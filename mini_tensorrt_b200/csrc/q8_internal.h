@@ -48,7 +48,7 @@ struct Plan {
 constexpr int kGemvUnroll = 8;
 
 // Cluster GEMV: the most activation rows (tokens) it takes.
-constexpr int kGemvClMaxM = 32;
+constexpr int kGemvClMaxM = 64;
 
 struct DeviceInfo {
   int device = -1;
@@ -67,8 +67,10 @@ cudaError_t ensure_smem_limit(const void* kernel, int bytes);
 // accumulators: fewer, larger CTAs); the most ring stages.
 constexpr int kGemvClCtasPerSm = 3;
 constexpr size_t kGemvClSmemCap = 72 * 1024;  // 3 x (72 + static + 1 reserved) KiB <= 228 KiB
-constexpr int kGemvClCtasPerSmWide = 2;
+constexpr int kGemvClCtasPerSmWide = 2;     // 8 < M <= 32
 constexpr size_t kGemvClSmemCapWide = 110 * 1024;
+constexpr int kGemvClCtasPerSmWide8 = 1;    // 32 < M <= 64: 96 accumulator registers a thread
+constexpr size_t kGemvClSmemCapWide8 = 200 * 1024;
 constexpr int kGemvClMaxStages = 8;
 size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages);
 // ln_gamma non-null: each row of X (fp32) is layer-normalized (ln_gamma,

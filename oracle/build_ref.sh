@@ -60,4 +60,19 @@ g++ -std=c++17 ${CFLAGS} -DNDEBUG -pthread -c \
 g++ -std=c++17 ${CFLAGS} -DNDEBUG -pthread \
   -I "${HERE}/gtest_shim" -I "${REF}/include" -I "${REF}" -I "${REF}/src" -I "${REF}/src/ops" \
   -o "${HERE}/_ref/ref_packer_pin" "${HERE}/ref_packer_pin.cpp" "${HERE}/_ref/golden_kernel_test.o" "${ABS[@]}"
-echo "build_ref: built ${HERE}/liboracle.so, ${HERE}/_ref/libmtrt_ref.so and ${HERE}/_ref/ref_packer_pin"
+
+# The drop-in as the reference sees it (tests/cpp/registry_drop_in.cpp): the device
+# MatMulQ registered into the reference's own KernelRegistry, the reference's
+# Golden.MatMulQ run through it. Needs libmtrtq.so (built first) and the CUDA runtime.
+LIBDIR="${HERE}/../mini_tensorrt_b200"
+CUDA_ROOT="${CUDA_HOME:-$(dirname "$(dirname "$(command -v nvcc || echo /usr/local/cuda/bin/nvcc)")")}"
+if [[ -f "${LIBDIR}/libmtrtq.so" ]]; then
+  g++ -std=c++17 -O2 -DNDEBUG -pthread \
+    -I "${HERE}/gtest_shim" -I "${REF}/include" -I "${REF}" -I "${REF}/src" -I "${REF}/src/ops" \
+    -I "${HERE}/../include" -I "${CUDA_ROOT}/include" \
+    -o "${HERE}/_ref/registry_drop_in" "${HERE}/../tests/cpp/registry_drop_in.cpp" \
+    "${HERE}/_ref/golden_kernel_test.o" "${ABS[@]}" \
+    -L "${LIBDIR}" -lmtrtq -Wl,-rpath,'$ORIGIN/../../mini_tensorrt_b200' \
+    -L "${CUDA_ROOT}/lib64" -lcudart_static -ldl -lrt
+fi
+echo "build_ref: built ${HERE}/liboracle.so, ${HERE}/_ref/libmtrt_ref.so, ${HERE}/_ref/ref_packer_pin and ${HERE}/_ref/registry_drop_in"

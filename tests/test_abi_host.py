@@ -126,10 +126,12 @@ def test_launch_without_device_fails_loudly():
 @pytest.mark.parametrize("M,K,N,mode,path", [
     (1, 768, 50257, "bf16", "cluster_gemv"), (8, 768, 768, "fp32", "cluster_gemv"),
     (8, 3072, 768, "bf16", "cluster_gemv"), (9, 768, 768, "bf16", "cluster_gemv"),
-    (32, 768, 3072, "bf16", "cluster_gemv"), (33, 768, 3072, "bf16", "gemm_tc"),
+    (32, 768, 3072, "bf16", "cluster_gemv"), (33, 768, 3072, "bf16", "cluster_gemv"),
     (16, 768, 50257, "bf16", "stream_k_tc"), (16, 768, 50257, "fp32", "cluster_gemv"),
-    (64, 768, 3072, "bf16", "gemm_tc"),
-    (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv"),
+    (64, 768, 3072, "bf16", "cluster_gemv"), (65, 768, 3072, "bf16", "gemm_tc"),
+    (64, 4096, 4096, "bf16", "gemm_tc"), (64, 4096, 14336, "fp32", "cluster_gemv"),
+    (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "cluster_gemv"),
+    (65, 768, 3072, "fp32", "gemv"),
     (1, 768, 200000, "bf16", "cluster_gemv"), (33, 768, 200000, "bf16", "gemm_tc"),
     (8, 24576, 128, "bf16", "stream_k_tc"), (32, 65536, 128, "bf16", "stream_k_tc"),
     (32, 65536, 128, "fp32", "gemv"),
@@ -177,7 +179,7 @@ def test_forced_paths_change_the_plan():
         assert matmulq.plan_info(8, 768, 768, mode="fp32")["path"] == "cluster_gemv"
         assert matmulq.workspace_bytes(8, 768, 768, torch.float32, "fp32") == 0
         with pytest.raises(_lib.MtrtqError):
-            matmulq.plan_info(33, 768, 768)
+            matmulq.plan_info(65, 768, 768)
         with pytest.raises(_lib.MtrtqError):
             matmulq.set_option(_lib.OPT_FORCE_PATH, 5)
     finally:
@@ -189,12 +191,14 @@ def test_forced_paths_change_the_plan():
                                       (8, 3072, 768, 8), (1, 768, 200000, 1), (8, 4096, 14336, 3),
                                       (8, 16384, 128, 8), (8, 24576, 128, None),
                                       (16, 768, 50257, 1), (32, 4096, 14336, 5), (32, 768, 768, 8),
-                                      (32, 14336, 4096, None), (33, 768, 768, None)])
+                                      (32, 14336, 4096, None), (33, 768, 768, 8), (64, 768, 3072, 6),
+                                      (64, 4096, 14336, 5), (65, 768, 768, None)])
 def test_cluster_gemv_plan(M, K, N, cs):
     """One cluster per 128-channel tile, 1 to 8 CTAs splitting K into 64-k units,
-    all clusters resident (3 CTAs per SM for M <= 8, 2 above) where the tiles
-    allow; refused when a CTA's activation digits (3 bytes per activation) and two
-    8 KiB ring stages exceed 72 KiB (M <= 8) or 110 KiB, or when M > 32."""
+    all clusters resident (3 CTAs per SM for M <= 8, 2 up to 32, 1 up to 64) where
+    the tiles allow; refused when a CTA's activation digits (3 bytes per activation)
+    and two 8 KiB ring stages exceed 72 KiB (M <= 8), 110 KiB (M <= 32) or 200 KiB,
+    or when M > 64."""
     matmulq.set_option(_lib.OPT_FORCE_PATH, 4)
     try:
         if cs is None:
@@ -206,7 +210,7 @@ def test_cluster_gemv_plan(M, K, N, cs):
         assert info["n_tiles"] == -(-N // 128)
         kb = -(-K // 64)
         assert info["k_per_split"] == -(-kb // cs) * 64
-        cap = (72 if M <= 8 else 110) * 1024
+        cap = (72 if M <= 8 else 110 if M <= 32 else 200) * 1024
         assert 3 * M * -(-kb // cs) * 64 + 2 * 8192 <= cap
         assert matmulq.workspace_bytes(M, K, N, torch.float32, "bf16") == 0
     finally:

@@ -157,7 +157,7 @@ def test_every_path_agrees(cuda_device, M):
     q, s = oracle.quantize_per_channel(W)
     X = wl.activations(M, K, 6)
     outs = []
-    for path in ((1, 2, 3, 4) if M <= 32 else (1, 2)):
+    for path in ((1, 2, 3, 4) if M <= 32 else (1, 2, 4) if M <= 64 else (1, 2)):
         matmulq.set_option(_lib.OPT_FORCE_PATH, path)
         try:
             outs.append(run(X, q, s, "bf16"))
@@ -311,7 +311,8 @@ def test_stream_k_partitions(cuda_device, M, K, N):
 
 
 GSK_CASES = [(12, 768, 3072), (16, 768, 50257), (24, 4096, 1000), (32, 3072, 768), (9, 100, 300),
-             (31, 77, 129),
+             (31, 77, 129), (64, 768, 3072), (40, 100, 300), (33, 4096, 1000), (64, 4096, 14336),
+             (57, 77, 129),
              (1, 64, 128), (3, 64, 50257), (8, 12288, 256), (2, 4096, 14336), (1, 768, 50257),
              (5, 64 * 23, 128 * 7), (7, 12000, 100), (8, 4096, 1000), (4, 100, 300), (6, 77, 129)]
 
@@ -430,7 +431,7 @@ def test_fused_epilogues(cuda_device, M, K, N, path, epilogue):
     """gelu_new after the bias (the reference's FusedMatMulBiasGeluTanh) and the
     residual add (in place: out is the residual), on every kernel that takes the shape."""
     mode = "fp32" if path == 1 else "bf16"
-    if (path == 3 and M > 32) or (path == 4 and M > 32):
+    if (path == 3 and M > 32) or (path == 4 and M > 64):
         pytest.skip("the kernel does not take this M")
     W = wl.weights(K, N, 601)
     q, s = matmulq.quantize_per_channel(W)
@@ -524,7 +525,7 @@ def _layernorm(x, g, b, eps):
 
 
 LN_CASES = [(1, 768, 2304), (8, 768, 3072), (3, 100, 300), (16, 768, 768), (32, 768, 3072), (8, 4096, 1000),
-            (5, 1000, 520), (8, 768, 50257)]
+            (5, 1000, 520), (8, 768, 50257), (64, 768, 3072), (41, 768, 768)]
 
 
 @pytest.mark.parametrize("M,K,N", LN_CASES, ids=[f"{M}x{K}x{N}" for M, K, N in LN_CASES])
@@ -576,10 +577,10 @@ def test_layernorm_prologue(cuda_device, M, K, N, mode, epilogue):
 def test_layernorm_prologue_refuses_other_kernels(cuda_device):
     q, s = matmulq.quantize_per_channel(wl.weights(768, 768, 710))
     pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
-    x = torch.zeros((64, 768), device=cuda_device)
+    x = torch.zeros((65, 768), device=cuda_device)
     g = torch.ones(768, device=cuda_device)
     with pytest.raises(_lib.MtrtqError, match="cluster GEMV"):
-        matmulq.matmul_q8_ln(x, g, g, 1e-5, pw)  # M = 64: the tile GEMM
+        matmulq.matmul_q8_ln(x, g, g, 1e-5, pw)  # M = 65: the tile GEMM
     with forced(1):
         with pytest.raises(_lib.MtrtqError, match="cluster GEMV"):
             matmulq.matmul_q8_ln(x[:4], g, g, 1e-5, pw)
