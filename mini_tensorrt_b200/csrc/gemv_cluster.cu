@@ -288,14 +288,39 @@ __device__ __forceinline__ void cl_decode_groups(const GemvClParams& p, const ui
   }
 }
 
+// max |v| over a group, and whether any of its values is NaN or infinite: fmaxf
+// drops a NaN, so the sum of the four values (NaN if any of them is) is tested
+// too; an infinity shows in the maximum.
+__device__ __forceinline__ float cl_group_max(const float4 v, bool& bad) {
+  const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  const float sum = (v.x + v.y) + (v.z + v.w);
+  bad |= !(a <= 3.402823466e38f) || sum != sum;
+  return a;
+}
+
 template <int kB>
 __device__ __forceinline__ void cl_max_groups(const float4 (&v)[kB], float& mx, bool& bad) {
 #pragma unroll
-  for (int b = 0; b < kB; ++b) {
-    const float a = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
-    bad |= !(a <= 3.402823466e38f);  // NaN or infinity
-    mx = fmaxf(mx, a);
-  }
+  for (int b = 0; b < kB; ++b) mx = fmaxf(mx, cl_group_max(v[b], bad));
+}
+
+// Writes the three digit planes of group g (k = 4g .. 4g + 3 of the CTA's range)
+// of token m.
+__device__ __forceinline__ void cl_store_digit_group(const float4 v, float inv, int8_t* xd, int plane, int mt,
+                                                     int m, int g) {
+  uint32_t a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
+  cl_digits(__fmul_rn(v.x, inv), a0, a1, a2);
+  cl_digits(__fmul_rn(v.y, inv), b0, b1, b2);
+  cl_digits(__fmul_rn(v.z, inv), c0, c1, c2);
+  cl_digits(__fmul_rn(v.w, inv), e0, e1, e2);
+  // Group q = g & 15 of the unit (k = 4q .. 4q + 3) sits at byte (q & 3) * 16 +
+  // (q >> 2) * 4 of the token's 64-byte row: lane t of an MMA group then finds
+  // its four B-fragment words (k = 4t + 16j, j = 0..3) in one 16-byte load.
+  const int u = g >> 4, q = g & 15;
+  const int off = (u * mt + m) * 64 + (q & 3) * 16 + (q >> 2) * 4;
+  *reinterpret_cast<uint32_t*>(xd + off) = cl_pack_low_bytes(a0, b0, c0, e0);
+  *reinterpret_cast<uint32_t*>(xd + plane + off) = cl_pack_low_bytes(a1, b1, c1, e1);
+  *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) = cl_pack_low_bytes(a2, b2, c2, e2);
 }
 
 // Writes the three digit planes of groups g0, g0 + 32, ... (those below gend).
@@ -305,21 +330,7 @@ __device__ __forceinline__ void cl_store_digits(const float4 (&v)[kB], float inv
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
     const int g = g0 + b * 32;
-    if (g < gend) {
-      uint32_t a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
-      cl_digits(__fmul_rn(v[b].x, inv), a0, a1, a2);
-      cl_digits(__fmul_rn(v[b].y, inv), b0, b1, b2);
-      cl_digits(__fmul_rn(v[b].z, inv), c0, c1, c2);
-      cl_digits(__fmul_rn(v[b].w, inv), e0, e1, e2);
-      // Group q = g & 15 of the unit (k = 4q .. 4q + 3) sits at byte (q & 3) * 16 +
-      // (q >> 2) * 4 of the token's 64-byte row: lane t of an MMA group then finds
-      // its four B-fragment words (k = 4t + 16j, j = 0..3) in one 16-byte load.
-      const int u = g >> 4, q = g & 15;
-      const int off = (u * mt + m) * 64 + (q & 3) * 16 + (q >> 2) * 4;
-      *reinterpret_cast<uint32_t*>(xd + off) = cl_pack_low_bytes(a0, b0, c0, e0);
-      *reinterpret_cast<uint32_t*>(xd + plane + off) = cl_pack_low_bytes(a1, b1, c1, e1);
-      *reinterpret_cast<uint32_t*>(xd + 2 * plane + off) = cl_pack_low_bytes(a2, b2, c2, e2);
-    }
+    if (g < gend) cl_store_digit_group(v[b], inv, xd, plane, mt, m, g);
   }
 }
 
@@ -335,7 +346,9 @@ __device__ __forceinline__ void cl_store_digits(const float4 (&v)[kB], float inv
 // setup); finish() decodes them, completes the maxima across warps (one named
 // barrier) and writes the digits. A longer share is read twice, in batches, in finish():
 // the second time from the caches the first pass filled.
-template <bool X_BF16, bool ROUND, int RES>
+// MANY: the kernel instance takes more tokens than it has consumer warps (NB > 1);
+// without it the many-token staging is not compiled in.
+template <bool X_BF16, bool ROUND, int RES, bool MANY>
 struct ClStager {
   static constexpr int kRes = RES;  // groups per lane held in registers
   static constexpr int kBatch = 6;  // groups per lane per batch otherwise
@@ -364,37 +377,63 @@ struct ClStager {
     if (resident) cl_issue_groups<kRes, X_BF16>(p, raw, m, kbase, gbeg + lane, gend, vec);
   }
 
-  // More tokens than warps: warp w stages tokens w, w + 8, ... over the whole range.
-  __device__ __forceinline__ void finish_many(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
-                                              int* s_bad, uint64_t* xready, int lane) {
-    const int mt = p.M, n4 = nu_ * 16;
-    for (int t = warp_; t < mt; t += kClWarps) {
-      float mx = 0.0f;
-      bool bad = false;
-      for (int g0 = lane; g0 < n4; g0 += 32 * kBatch) {
-        float4 w[kBatch];
-        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec, ln);
-        cl_max_groups<kBatch>(w, mx, bad);
-      }
+  // More tokens than warps: the consumer threads take the 4-element groups of all
+  // tokens together (group e of the M x n4: token e / n4, group e % n4), kMany per
+  // thread per pass with all of a pass's loads in flight at once (one warp per token
+  // in turn would wait for one round trip per token). The maxima go to shared
+  // memory atomically. A range that fits one pass keeps its values in registers
+  // for the digits; a longer one is read again, from the caches the first read
+  // filled.
+  static constexpr int kMany = 8;
+  __device__ __forceinline__ void many_load(const GemvClParams& p, float4 (&v)[kMany], int base, int ct, int n4,
+                                            int total) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        bad |= __shfl_xor_sync(0xffffffffu, (int)bad, o) != 0;
-      }
-      if (lane == 0) {
-        atomicMax(&s_max[t], __float_as_int(mx));
-        if (bad) atomicOr(&s_bad[t], 1);
+    for (int i = 0; i < kMany; ++i) {
+      const int e = base + i * kClThreads + ct;
+      if (e < total) {
+        const int t = e / n4, g = e - t * n4, k = kbase + g * 4;
+        v[i] = cl_round<ROUND>(cl_ln4(p, cl_load_x4<X_BF16>(p, t, k, vec), t, k, ln));
+      } else {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
+  }
+
+  __device__ __forceinline__ void finish_many(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
+                                              int* s_bad, uint64_t* xready, int lane) {
+    const int mt = p.M, n4 = nu_ * 16, total = mt * n4;
+    const int ct = warp_ * 32 + lane;
+    constexpr int kPass = kClThreads * kMany;
+    const bool one_pass = total <= kPass;
+    float4 v[kMany];
+    for (int base = 0; base < total; base += kPass) {
+      many_load(p, v, base, ct, n4, total);
+#pragma unroll
+      for (int i = 0; i < kMany; ++i) {
+        const int e = base + i * kClThreads + ct;
+        if (e < total) {
+          bool bad = false;
+          const float a = cl_group_max(v[i], bad);
+          const int t = e / n4;
+          atomicMax(&s_max[t], __float_as_int(a));  // a >= 0: bit order is value order
+          if (bad) atomicOr(&s_bad[t], 1);
+        }
+      }
+    }
+    __syncwarp();
     if (lane == 0) mbar_arrive(xready);  // this warp's activations have been read
     named_bar_sync(1, kClThreads);
-    for (int t = warp_; t < mt; t += kClWarps) {
-      const float smax = __int_as_float(s_max[t]);
-      const float inv = (smax > 0.0f && !s_bad[t]) ? 127.0f / smax : 0.0f;
-      for (int g0 = lane; g0 < n4; g0 += 32 * kBatch) {
-        float4 w[kBatch];
-        cl_load_groups<kBatch, X_BF16, ROUND>(p, w, t, kbase, g0, n4, vec, ln);
-        cl_store_digits<kBatch>(w, inv, xd, plane, mt, t, g0, n4);
+    for (int base = 0; base < total; base += kPass) {
+      if (!one_pass) many_load(p, v, base, ct, n4, total);
+#pragma unroll
+      for (int i = 0; i < kMany; ++i) {
+        const int e = base + i * kClThreads + ct;
+        if (e < total) {
+          const int t = e / n4, g = e - t * n4;
+          const float smax = __int_as_float(s_max[t]);
+          const float inv = (smax > 0.0f && !s_bad[t]) ? 127.0f / smax : 0.0f;
+          cl_store_digit_group(v[i], inv, xd, plane, mt, t, g);
+        }
       }
     }
   }
@@ -402,7 +441,7 @@ struct ClStager {
   __device__ __forceinline__ void finish(const GemvClParams& p, int8_t* xd, int plane, int* s_max,
                                          int* s_bad, uint64_t* xready, int lane) {
     const int mt = p.M;
-    if (mt > kClWarps) {
+    if (MANY && mt > kClWarps) {
       finish_many(p, xd, plane, s_max, s_bad, xready, lane);
       return;
     }
@@ -516,7 +555,7 @@ __global__ void __launch_bounds__(kClBlock, NB == 1 ? kGemvClCtasPerSm
   //  * consumers: wait for the grid this launch depends on (a no-op unless it was
   //    launched with programmatic stream serialization), then issue the
   //    activation loads, whose latency overlaps the rest of the setup.
-  ClStager<X_BF16, ROUND, RES> stager;
+  ClStager<X_BF16, ROUND, RES, (NB > 1)> stager;
   const char* src = p.W + ((int64_t)t * p.KB + u0) * kUnitBytes;
   int issued = 0, st_p = 0;
   uint32_t ph_p = 0;
@@ -712,10 +751,15 @@ cudaError_t cl_launch(const GemvClParams& gp, int cs, int n_tiles, size_t smem, 
 
 }  // namespace
 
+// Blocks of 8 tokens of the kernel instance that serves m tokens (its NB).
+static int cl_token_blocks(int m) { return m <= 8 ? 1 : m <= 16 ? 2 : m <= 32 ? 4 : 8; }
+
 size_t gemv_cluster_smem_bytes(int m, int64_t units, int cs, int stages) {
   const int64_t nu = (units + cs - 1) / cs;  // the largest CTA range
   const size_t ring = (size_t)stages * kUnitBytes;
-  const size_t exch = (size_t)((m + 7) / 8) * 8 * 128 * sizeof(float);  // reuses the ring
+  // The exchange buffer part[8 * NB][128] (it reuses the ring): the kernel writes
+  // all 8 * NB token rows, so it is sized by NB, not by m.
+  const size_t exch = (size_t)cl_token_blocks(m) * 8 * 128 * sizeof(float);
   return (ring > exch ? ring : exch) + (2 * kGemvClMaxStages + 2) * sizeof(uint64_t) +
          (size_t)kDigits * (size_t)nu * (size_t)m * 64;
 }
@@ -748,7 +792,7 @@ cudaError_t launch_gemv_cluster(const Plan& p, const void* X, int x_dtype, int64
   // Activation groups a staging lane holds: 6 unless some warp's share needs
   // more to be staged in one pass (a token has floor(8 / M) warps; M > 8 stages
   // whole tokens per warp in batches).
-  const int nb = p.M <= 8 ? 1 : p.M <= 16 ? 2 : p.M <= 32 ? 4 : 8;
+  const int nb = cl_token_blocks((int)p.M);
   bool wide = false;
   if (p.M <= 8) {
     const int64_t nu_max = (p.kunits + p.splits - 1) / p.splits;

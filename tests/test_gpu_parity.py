@@ -167,6 +167,22 @@ def test_every_path_agrees(cuda_device, M):
         check(Y, X, q, s, "bf16", tc=True)
 
 
+@pytest.mark.parametrize("M", [3, 8, 20, 64])
+@pytest.mark.parametrize("mode,path", [("fp32", 0), ("bf16", 0), ("fp32", 1), ("fp32", 4), ("bf16", 4)])
+def test_nan_activation_poisons_its_row_only(cuda_device, M, mode, path):
+    """A NaN activation makes its row's outputs NaN, as in the reference loop (every
+    output of the row adds a NaN product), and leaves the other rows exact."""
+    K, N = 300, 700
+    q, s = oracle.quantize_per_channel(wl.weights(K, N, 81))
+    X = wl.activations(M, K, 82)
+    X[1, 5] = np.nan
+    with forced(path):
+        Y = run(X, q, s, mode)
+    assert np.all(np.isnan(Y[1]))
+    keep = np.arange(M) != 1
+    check(Y[keep], X[keep], q, s, mode, tc=(mode == "bf16" and path != 4))
+
+
 def test_strided_input_and_output(cuda_device):
     M, K, N = 24, 200, 300
     W = wl.weights(K, N, 11)
