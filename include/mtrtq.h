@@ -218,6 +218,46 @@ int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const voi
                               const float* scale, const float* bias, float* Y, int64_t ldy,
                               int64_t M, int64_t K, int64_t N, int mode, void* stream);
 
+/* ---- a group of independent decode products in one launch ------------------------ */
+
+/* One problem of a group: Y = X x dequant(W) (+ bias), then the epilogue, with the
+ * arguments of mtrtq_matmul_ex (M <= 8). */
+typedef struct mtrtq_gemv_problem {
+  const void* X;          /* [M, ldx], 16-byte aligned, the group's x_dtype */
+  int64_t ldx;
+  const void* packed;     /* mtrtq_prepack layout, 256-byte aligned */
+  const float* scale;     /* [N] */
+  const float* bias;      /* [N] or NULL */
+  float* Y;               /* [M, ldy] */
+  int64_t ldy;
+  int64_t M, K, N;        /* 1 <= M <= 8 */
+  int epilogue;           /* MTRTQ_EPILOGUE_* */
+  const float* residual;  /* MTRTQ_EPILOGUE_ADD_RESIDUAL: [M, ldr] (may be Y) */
+  int64_t ldr;
+} mtrtq_gemv_problem;
+
+#define MTRTQ_GROUP_MAX 16
+
+/* Computes `count` (1..MTRTQ_GROUP_MAX) independent decode products in one launch
+ * of the persistent grouped GEMV: the problems' 64-k weight units are split into
+ * equal contiguous ranges over three CTAs per SM, so every SM streams the same
+ * bytes whatever the shapes and the launch's fixed cost is paid once. Results are
+ * those of mtrtq_matmul_ex on each problem within its tolerance (the cluster GEMV's
+ * arithmetic: int8 weights times three int8 digits of each activation, exact int32
+ * sums), deterministic (cut tiles are summed in a fixed order).
+ *
+ * Replaces a run of independent MatMulQ calls of the reference
+ * (src/ops/kernels_matmul.cpp:42-74), such as the Q, K and V projections its KV
+ * decoder issues one after another (tools/run_gpt2.cpp:142-150).
+ *
+ * No Y may overlap another problem's X, Y or residual. At most 1024 channel tiles
+ * of 128 in all. workspace: >= mtrtq_gemv_group_workspace_bytes, 256-byte aligned,
+ * zero-filled once after allocation (calls leave its tickets at zero); calls
+ * sharing it must be stream-ordered. Honours MTRTQ_OPT_OVERLAP_LAUNCH. */
+int64_t mtrtq_gemv_group_workspace_bytes(const mtrtq_gemv_problem* problems, int count);
+int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype, int mode, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 /* ---- options and diagnostics ----------------------------------------------------- */
 
 /* Process-wide options. Both change how a call is carried out, never its result

@@ -68,6 +68,18 @@ SIGNATURES = {
     "mtrtq_decode_next": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _vp]),
 }
 NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
+GROUP_MAX = 16
+
+
+class GemvProblem(ctypes.Structure):
+    """mtrtq_gemv_problem (include/mtrtq.h)."""
+    _fields_ = [("X", _vp), ("ldx", _i64), ("packed", _vp), ("scale", _vp), ("bias", _vp), ("Y", _vp),
+                ("ldy", _i64), ("M", _i64), ("K", _i64), ("N", _i64), ("epilogue", _int), ("residual", _vp),
+                ("ldr", _i64)]
+
+
+SIGNATURES["mtrtq_gemv_group_workspace_bytes"] = (_i64, [_vp, _int])
+SIGNATURES["mtrtq_gemv_group"] = (_int, [_vp, _int, _int, _int, _vp, _sz, _vp])
 
 
 class MtrtqError(RuntimeError):

@@ -712,6 +712,110 @@ int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const voi
   return MTRTQ_OK;
 }
 
+}  // extern "C"
+
+namespace mtrtq {
+namespace {
+
+// Validates a group and lays its problems out in one unit list; *units and *tiles
+// receive the totals. Device pointers are checked only when check_ptrs is set.
+int group_layout(const mtrtq_gemv_problem* probs, int count, bool check_ptrs, GroupProblem* out,
+                 int64_t* units, int* tiles) {
+  if (!probs) return fail(MTRTQ_ERR_INVALID_ARG, "null problem list");
+  if (count < 1 || count > kGroupMax)
+    return fail(MTRTQ_ERR_INVALID_ARG, "a group holds 1 to %d problems (got %d)", kGroupMax, count);
+  int64_t u = 0;
+  int t = 0;
+  for (int i = 0; i < count; ++i) {
+    const mtrtq_gemv_problem& q = probs[i];
+    if (int rc = check_dims(q.M, q.K, q.N)) return rc;
+    if (q.M > 8) return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: a group takes M <= 8 (M=%lld)", i, (long long)q.M);
+    if (q.epilogue != MTRTQ_EPILOGUE_NONE && q.epilogue != MTRTQ_EPILOGUE_GELU_TANH &&
+        q.epilogue != MTRTQ_EPILOGUE_ADD_RESIDUAL)
+      return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: unknown epilogue %d", i, q.epilogue);
+    if (check_ptrs) {
+      if (!q.X || !q.packed || !q.scale || !q.Y) return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: null pointer", i);
+      if (q.ldx < q.K || q.ldy < q.N)
+        return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: ldx < K or ldy < N", i);
+      if (!aligned(q.packed, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "problem %d: packed weights must be 256-byte aligned", i);
+      if (!aligned(q.X, 16)) return fail(MTRTQ_ERR_ALIGNMENT, "problem %d: X must be 16-byte aligned", i);
+      if (!aligned(q.scale, 4) || (q.bias && !aligned(q.bias, 4)) || !aligned(q.Y, 4))
+        return fail(MTRTQ_ERR_ALIGNMENT, "problem %d: scale, bias and Y must be 4-byte aligned", i);
+      if (q.epilogue == MTRTQ_EPILOGUE_ADD_RESIDUAL && (!q.residual || q.ldr < q.N || !aligned(q.residual, 4)))
+        return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: the residual epilogue needs a residual with ldr >= N", i);
+    }
+    GroupProblem& g = out[i];
+    g.X = q.X;
+    g.ldx = q.ldx;
+    g.W = static_cast<const char*>(q.packed);
+    g.scale = q.scale;
+    g.bias = q.bias;
+    g.Y = q.Y;
+    g.ldy = q.ldy;
+    g.epi.kind = q.epilogue;
+    g.epi.residual = q.epilogue == MTRTQ_EPILOGUE_ADD_RESIDUAL ? q.residual : nullptr;
+    g.epi.ldr = q.ldr;
+    g.M = (int)q.M;
+    g.K = (int)q.K;
+    g.N = (int)q.N;
+    g.KB = (int)(round_up64(q.K, kBlockK) / kBlockK);
+    g.n_tiles = (int)(round_up64(q.N, kTileN) / kTileN);
+    g.tile_begin = t;
+    g.unit_begin = u;
+    t += g.n_tiles;
+    u += (int64_t)g.n_tiles * g.KB;
+    if (t > kStreamMaxTiles)
+      return fail(MTRTQ_ERR_INVALID_ARG, "a group holds at most %d channel tiles of 128", kStreamMaxTiles);
+  }
+  *units = u;
+  *tiles = t;
+  return MTRTQ_OK;
+}
+
+int group_grid(int64_t units, int sm_count) {
+  const int64_t g = (int64_t)sm_count * kSCtasPerSm;
+  return (int)(units < g ? units : g);
+}
+
+}  // namespace
+}  // namespace mtrtq
+
+extern "C" {
+
+int64_t mtrtq_gemv_group_workspace_bytes(const mtrtq_gemv_problem* problems, int count) {
+  GroupProblem gp[kGroupMax];
+  int64_t units = 0;
+  int tiles = 0;
+  if (group_layout(problems, count, false, gp, &units, &tiles) != MTRTQ_OK) return -1;
+  return (int64_t)gemv_stream_workspace_bytes(group_grid(units, sm_count_or_default()));
+}
+
+int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype, int mode, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (x_dtype != MTRTQ_DTYPE_F32 && x_dtype != MTRTQ_DTYPE_BF16)
+    return fail(MTRTQ_ERR_INVALID_ARG, "x_dtype must be MTRTQ_DTYPE_F32 or MTRTQ_DTYPE_BF16");
+  if (mode != MTRTQ_MODE_BF16 && mode != MTRTQ_MODE_FP32)
+    return fail(MTRTQ_ERR_INVALID_ARG, "mode must be MTRTQ_MODE_BF16 or MTRTQ_MODE_FP32");
+  if (mode == MTRTQ_MODE_FP32 && x_dtype == MTRTQ_DTYPE_BF16)
+    return fail(MTRTQ_ERR_INVALID_ARG, "MTRTQ_MODE_FP32 needs fp32 activations");
+  GroupProblem gp[kGroupMax];
+  int64_t units = 0;
+  int tiles = 0;
+  if (int rc = group_layout(problems, count, true, gp, &units, &tiles)) return rc;
+  DeviceInfo d;
+  if (int rc = check_device_sm100(&d)) return rc;
+  const int grid = group_grid(units, d.sm_count);
+  const size_t need = gemv_stream_workspace_bytes(grid);
+  if (!workspace || workspace_bytes < need)
+    return fail(MTRTQ_ERR_WORKSPACE, "workspace %zu bytes < %zu", workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  const bool round_x = mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32;
+  cudaError_t e = launch_gemv_stream(gp, count, units, grid, x_dtype, round_x, workspace, d.status,
+                                     g_opt_overlap != 0, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMV launch");
+  return MTRTQ_OK;
+}
+
 int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info, int n_info) {
   if (!info || n_info < 6) return fail(MTRTQ_ERR_INVALID_ARG, "info needs 6 slots");
   Plan p;

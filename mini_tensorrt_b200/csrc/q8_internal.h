@@ -62,6 +62,40 @@ struct DeviceInfo {
 // once per (device, kernel); later calls only look the pair up.
 cudaError_t ensure_smem_limit(const void* kernel, int bytes);
 
+// Persistent grouped decode GEMV (gemv_stream.cu): up to kGroupMax independent
+// problems of M <= 8 tokens in one launch, their 64-k weight units split evenly
+// over kSCtasPerSm CTAs per SM.
+constexpr int kGroupMax = 16;
+constexpr int kSChunk = 12;       // units whose activation digits are staged together
+constexpr int kSStages = 6;       // ring stages of 8 KiB
+constexpr int kSCtasPerSm = 3;
+constexpr size_t kStreamSmemBytes = (size_t)kSStages * 8192 + 2 * kSStages * 8 + 3 * (size_t)kSChunk * 8 * 64;
+constexpr size_t kStreamCounterBytes = 4096;  // tickets: one per tile of the group
+constexpr int kStreamMaxTiles = (int)(kStreamCounterBytes / 4);
+
+struct GroupProblem {
+  const void* X;
+  int64_t ldx;
+  const char* W;        // packed weights
+  const float* scale;
+  const float* bias;
+  float* Y;
+  int64_t ldy;
+  Epilogue epi;
+  int M, K, N;
+  int KB;               // 64-k units per tile
+  int n_tiles;
+  int tile_begin;       // first ticket of this problem
+  int64_t unit_begin;   // first unit of this problem in the group's unit list
+};
+
+// Workspace of a group launch: tickets, then [grid][2][8][128] fp32 partials.
+inline size_t gemv_stream_workspace_bytes(int grid) {
+  return kStreamCounterBytes + (size_t)grid * 2 * 8 * 128 * sizeof(float);
+}
+cudaError_t launch_gemv_stream(const GroupProblem* probs, int count, int64_t units, int grid, int x_dtype,
+                               bool round_x, void* workspace, unsigned* status, bool pdl, cudaStream_t st);
+
 // Cluster GEMV: CTAs resident per SM (registers are capped to allow it) and the
 // shared memory a CTA may use so that they fit, for M <= 8 and for larger M (more
 // accumulators: fewer, larger CTAs); the most ring stages.

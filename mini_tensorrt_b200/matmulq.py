@@ -208,6 +208,66 @@ def matmul_q8(x: torch.Tensor, w: PackedWeight, bias: torch.Tensor | None = None
     return out
 
 
+def _group_problems(items):
+    arr = (_lib.GemvProblem * len(items))()
+    for i, it in enumerate(items):
+        x, w, out = it["x"], it["w"], it["out"]
+        bias, epi, res = it.get("bias"), EPILOGUES[it.get("epilogue", "none")], it.get("residual")
+        if x.dim() != 2 or x.shape[1] != w.K or x.stride(1) != 1:
+            raise ValueError(f"problem {i}: x must be [M, {w.K}] with unit stride along K")
+        M = x.shape[0]
+        if out.dtype != torch.float32 or out.shape != (M, w.N) or out.stride(1) != 1:
+            raise ValueError(f"problem {i}: out must be float32 [M, N] with unit stride along N")
+        if epi == _lib.EPILOGUE_ADD_RESIDUAL and (res is None or res.shape != (M, w.N) or res.stride(1) != 1):
+            raise ValueError(f"problem {i}: the residual epilogue needs residual float32 [M, N]")
+        arr[i] = _lib.GemvProblem(x.data_ptr(), x.stride(0), w.packed.data_ptr(), w.scale.data_ptr(), _ptr(bias),
+                                  out.data_ptr(), out.stride(0), M, w.K, w.N, epi,
+                                  _ptr(res) if epi == _lib.EPILOGUE_ADD_RESIDUAL else None,
+                                  res.stride(0) if epi == _lib.EPILOGUE_ADD_RESIDUAL else 0)
+    return arr
+
+
+def group_workspace_bytes(items) -> int:
+    """Bytes of workspace mtrtq_gemv_group needs for these problems."""
+    arr = _group_problems(items)
+    n = lib().mtrtq_gemv_group_workspace_bytes(arr, len(items))
+    if n < 0:
+        raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_gemv_group_workspace_bytes", _lib.last_error())
+    return n
+
+
+class GemvGroup:
+    """A fixed group of independent decode products (M <= 8 each) run in one launch
+    by mtrtq_gemv_group. items: dicts with x, w (PackedWeight), out, and optionally
+    bias, epilogue ("none" | "gelu" | "residual") and residual. The tensors are bound
+    once (their addresses are what the launch uses); the workspace is allocated and
+    zero-filled here, at set-up."""
+
+    def __init__(self, items, mode: str = "bf16"):
+        if not items:
+            raise ValueError("a group needs at least one problem")
+        xd = {it["x"].dtype for it in items}
+        if len(xd) != 1 or not xd <= {torch.float32, torch.bfloat16}:
+            raise ValueError("every problem's x must have the same dtype, float32 or bfloat16")
+        self.items = list(items)
+        self.mode = mode
+        self.x_dtype = _lib.DTYPE_BF16 if xd == {torch.bfloat16} else _lib.DTYPE_F32
+        self.problems = _group_problems(self.items)
+        dev = self.items[0]["x"].device
+        n = lib().mtrtq_gemv_group_workspace_bytes(self.problems, len(self.items))
+        if n < 0:
+            raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_gemv_group_workspace_bytes", _lib.last_error())
+        self.workspace = torch.zeros(max(n, 256), dtype=torch.uint8, device=dev)
+        self.device = dev
+
+    def __call__(self, stream=None):
+        with torch.cuda.device(self.device):
+            check(lib().mtrtq_gemv_group(self.problems, len(self.items), self.x_dtype, MODES[self.mode],
+                                         self.workspace.data_ptr(), self.workspace.numel(), _stream_ptr(stream)),
+                  "mtrtq_gemv_group")
+        return [it["out"] for it in self.items]
+
+
 def matmul_q8_ln(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float, w: PackedWeight,
                  bias: torch.Tensor | None = None, out: torch.Tensor | None = None, mode: str = "bf16",
                  stream=None, epilogue: str = "none", residual: torch.Tensor | None = None) -> torch.Tensor:

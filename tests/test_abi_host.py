@@ -215,3 +215,29 @@ def test_cluster_gemv_plan(M, K, N, cs):
         assert matmulq.workspace_bytes(M, K, N, torch.float32, "bf16") == 0
     finally:
         matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
+
+
+def _problem(M, K, N):
+    p = _lib.GemvProblem()
+    p.M, p.K, p.N, p.ldx, p.ldy, p.epilogue = M, K, N, K, N, 0
+    return p
+
+
+def test_group_workspace_and_limits():
+    """mtrtq_gemv_group_workspace_bytes: tickets (4 KiB) + 8 KiB of partials per CTA,
+    three CTAs per SM but never more CTAs than 64-k units; groups of 1..16
+    problems of M <= 8 and at most 1024 channel tiles."""
+    lib = _lib.lib()
+    decode = [(M, K, N) for M in (1, 8) for K, N in ((768, 2304), (768, 768), (768, 3072), (3072, 768),
+                                                       (768, 50257))]
+    arr = (_lib.GemvProblem * 10)(*[_problem(*s) for s in decode])
+    assert lib.mtrtq_gemv_group_workspace_bytes(arr, 10) == 4096 + 148 * 3 * 8192
+    one = (_lib.GemvProblem * 1)(_problem(1, 64, 128))
+    assert lib.mtrtq_gemv_group_workspace_bytes(one, 1) == 4096 + 1 * 8192
+    assert lib.mtrtq_gemv_group_workspace_bytes(arr, 0) == -1
+    many = (_lib.GemvProblem * 17)(*[_problem(1, 64, 128)] * 17)
+    assert lib.mtrtq_gemv_group_workspace_bytes(many, 17) == -1
+    assert lib.mtrtq_gemv_group_workspace_bytes((_lib.GemvProblem * 1)(_problem(9, 64, 128)), 1) == -1
+    wide = (_lib.GemvProblem * 3)(*[_problem(1, 64, 50257)] * 3)  # 3 x 393 tiles > 1024
+    assert lib.mtrtq_gemv_group_workspace_bytes(wide, 3) == -1
+    assert "1024" in _lib.last_error()

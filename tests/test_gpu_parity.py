@@ -327,7 +327,7 @@ def test_stream_k_partitions(cuda_device, M, K, N):
 
 
 GSK_CASES = [(12, 768, 3072), (16, 768, 50257), (24, 4096, 1000), (32, 3072, 768), (9, 100, 300),
-             (31, 77, 129), (64, 768, 3072), (40, 100, 300), (33, 4096, 1000), (64, 4096, 14336),
+             (31, 77, 129), (64, 768, 3072), (40, 768, 3072), (40, 100, 300), (33, 4096, 1000), (64, 4096, 14336),
              (57, 77, 129),
              (1, 64, 128), (3, 64, 50257), (8, 12288, 256), (2, 4096, 14336), (1, 768, 50257),
              (5, 64 * 23, 128 * 7), (7, 12000, 100), (8, 4096, 1000), (4, 100, 300), (6, 77, 129)]
