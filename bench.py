@@ -4,7 +4,8 @@
 
 Workload (one step): the decode GEMV set at GPT-2-small shapes -- QKV 768x2304,
 attn-out 768x768, FFN-up 768x3072, FFN-down 3072x768, LM head 768x50257 (tied),
-each at M = 1 and M = 8 token rows (10 MatMulQ calls), fp32 activations ~ N(0,1),
+each at M = 1 and M = 8 token rows (10 independent MatMulQ problems, run as one
+mtrtq_gemv_group launch; --step-launch calls: one launch each), fp32 activations ~ N(0,1),
 int8 per-channel weights from N(0, 0.02), MTRTQ_MODE_FP32 (activations keep the
 reference's fp32 values; --mode bf16 rounds them once). Every call has 6
 device copies of its weights and consecutive steps rotate through them (548 MB
@@ -77,6 +78,9 @@ def parse():
                          "4 cluster GEMV")
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch every call only after the previous one has finished")
+    ap.add_argument("--step-launch", choices=["group", "hybrid", "calls"], default="group",
+                    help="decode set: one grouped launch per step (default); hybrid: the eight smaller "
+                         "calls grouped and the two LM heads as their own launches; calls: a launch per call")
     ap.add_argument("--branches", type=int, default=1,
                     help="decode set: run the step's independent calls as this many parallel graph branches")
     return ap.parse_args()
@@ -97,6 +101,7 @@ PATH_KERNELS = {"gemv": "gemv_q8_kernel", "gemm_tc": "gemm_q8_tc_kernel",
 
 # Arithmetic of each path: what the product is computed in.
 PATH_DTYPES = {"gemv": "int8 W -> fp32, fp32 FMA",
+               "gemv_stream": "int8 W x int8 activation digits (3 per value), int32 accumulate",
                "gemm_tc": "int8 W -> bf16, bf16 x bf16 tcgen05, fp32 accumulate",
                "stream_k_tc": "int8 W -> bf16, bf16 x bf16 tcgen05, fp32 accumulate",
                "cluster_gemv": "int8 W x int8 activation digits (3 per value), int32 accumulate"}
@@ -258,17 +263,54 @@ def run_ours(args, torch, rank, world, dev, dist):
     branches = branch_plan(calls, args.branches)
     side = [torch.cuda.Stream(dev) for _ in range(len(branches) - 1)]
 
-    # Capture one CUDA graph per weight-copy rotation offset.
-    graphs = []
-    with torch.cuda.stream(stream):
-        launch_step(calls, 0, args.mode, stream, branches, side)  # first launch outside capture
+    def capture_calls():
+        """One graph per weight-copy rotation offset, a MatMulQ launch per call."""
+        out = []
+        with torch.cuda.stream(stream):
+            launch_step(calls, 0, args.mode, stream, branches, side)  # first launch outside capture
+            torch.cuda.synchronize()
+            for g in range(WEIGHT_COPIES):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    launch_step(calls, g, args.mode, stream, branches, side)
+                out.append(graph)
         torch.cuda.synchronize()
-        for g in range(WEIGHT_COPIES):
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                launch_step(calls, g, args.mode, stream, branches, side)
-            graphs.append(graph)
-    torch.cuda.synchronize()
+        return out
+
+    # hybrid: the calls the grouped launch takes (all, or all but the LM heads, which
+    # then run as their own cluster GEMV launches on the same stream).
+    in_group = [i for i, c in enumerate(calls) if args.step_launch == "group" or c["name"] != "lm_head"]
+    alone = [i for i in range(len(calls)) if i not in in_group]
+
+    def capture_group():
+        """One graph per rotation offset: the grouped launch (+ the LM heads alone)."""
+        groups = [matmulq.GemvGroup([{"x": calls[i]["x"], "w": calls[i]["w"][(g + i) % WEIGHT_COPIES],
+                                      "out": calls[i]["y"]} for i in in_group], mode=args.mode)
+                  for g in range(WEIGHT_COPIES)]
+
+        def one(g):
+            groups[g](stream)
+            for i in alone:
+                c = calls[i]
+                matmulq.matmul_q8(c["x"], c["w"][(g + i) % WEIGHT_COPIES], out=c["y"], mode=args.mode,
+                                  workspace=c["ws"], stream=stream)
+        out = []
+        with torch.cuda.stream(stream):
+            one(0)
+            torch.cuda.synchronize()
+            for g in range(WEIGHT_COPIES):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    one(g)
+                out.append(graph)
+        torch.cuda.synchronize()
+        return out, groups
+
+    groups = None
+    if args.step_launch in ("group", "hybrid"):
+        graphs, groups = capture_group()
+    else:
+        graphs = capture_calls()
 
     if world > 1:
         dist.barrier()
@@ -286,6 +328,15 @@ def run_ours(args, torch, rank, world, dev, dist):
     secs = float(t.item())
     value = step_bytes * args.steps * world / secs / 1e9
     assert matmulq.read_device_status() == 0, "a device wait timed out"
+    step_us = secs / args.steps * 1e6
+    other = None
+    if args.step_launch != "calls":
+        # The same step as ten MatMulQ launches (the cluster GEMV), for comparison.
+        call_graphs = capture_calls()
+        s2 = time_graphs(torch, call_graphs, args.steps, args.warmup, stream)
+        other = {"step_launch": "calls", "value": round(step_bytes * args.steps / s2 / 1e9, 1),
+                 "ms_per_step": round(s2 / args.steps * 1e3, 4)}
+        del call_graphs
 
     # Dominant kernel: the LM head GEMVs (most of the bytes). Each is timed as it
     # runs in the step, back to back on the launching stream: one graph of
@@ -306,40 +357,132 @@ def run_ours(args, torch, rank, world, dev, dist):
         per_kernel[c["M"]] = {"us": s / (reps * LAUNCHES_PER_GRAPH) * 1e6, "bytes": c["bytes"],
                               "plan": matmulq.plan_info(c["M"], c["K"], c["N"], mode=args.mode)}
         del graph
-    # the LM head launch with the larger time is the dominant kernel
+    # the LM head launch with the larger time is the dominant kernel of the per-call step
     dom_m = max(per_kernel, key=lambda m: per_kernel[m]["us"])
     dom = per_kernel[dom_m]
-    achieved = dom["bytes"] / (dom["us"] * 1e-6) / 1e9
-    traffic = committed_traffic(f"gemv_lm_head_m{dom_m}_{args.mode}")
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "kernel": f"{PATH_KERNELS[dom['plan']['path']]} (LM head 768x50257, M={dom_m})",
-                "peak_kind": f"{peak_kind} hbm_gbs",
-                "per_launch_us": round(dom["us"], 3),
-                "per_launch_timing": f"mean over graphs of {LAUNCHES_PER_GRAPH} back-to-back "
-                                     f"launches, weights rotated over {WEIGHT_COPIES} copies",
-                "algorithmic_bytes_per_launch": dom["bytes"]}
+    lm_achieved = dom["bytes"] / (dom["us"] * 1e-6) / 1e9
+    lm_head = {"kernel": f"{PATH_KERNELS[dom['plan']['path']]} (LM head 768x50257, M={dom_m})",
+               "achieved": round(lm_achieved, 1), "frac": round(lm_achieved / hbm_peak, 4),
+               "per_launch_us": round(dom["us"], 3), "algorithmic_bytes_per_launch": dom["bytes"],
+               "traffic": committed_traffic(f"gemv_lm_head_m{dom_m}_{args.mode}"),
+               "other_m": {str(m): round(v["us"], 3) for m, v in per_kernel.items()}}
+    if args.step_launch == "group":
+        # One launch per step: the grouped GEMV is the step's only kernel, and its
+        # average launch duration is the step time measured above.
+        achieved = step_bytes / (step_us * 1e-6) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(achieved / hbm_peak, 4),
+                    "traffic": committed_traffic(f"gemv_stream_decode_set_{args.mode}"),
+                    "kernel": "gemv_stream_kernel (the whole decode GEMV set, one launch)",
+                    "peak_kind": f"{peak_kind} hbm_gbs", "per_launch_us": round(step_us, 3),
+                    "per_launch_timing": "CUDA events around graph replays of the one-launch step, weights "
+                                         f"rotated over {WEIGHT_COPIES} copies",
+                    "algorithmic_bytes_per_launch": step_bytes,
+                    "lm_head_per_call": lm_head}
+    else:
+        roofline = {"bound": "hbm", "achieved": lm_head["achieved"], "peak": hbm_peak, "unit": "GB/s",
+                    "frac": lm_head["frac"], "traffic": lm_head["traffic"], "kernel": lm_head["kernel"],
+                    "peak_kind": f"{peak_kind} hbm_gbs", "per_launch_us": lm_head["per_launch_us"],
+                    "per_launch_timing": f"mean over graphs of {LAUNCHES_PER_GRAPH} back-to-back "
+                                         f"launches, weights rotated over {WEIGHT_COPIES} copies",
+                    "algorithmic_bytes_per_launch": dom["bytes"]}
 
     # End to end through the C ABI from the host (pinned buffers, copies timed).
     e2e = run_e2e(torch, calls, args, dev, stream, dist, world)
+    if args.step_launch == "group":
+        per_call = e2e
+        e2e = run_e2e_group(torch, calls, args, dev, stream, dist, world)
+        e2e["per_call_c_abi"] = per_call
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": PATH_DTYPES[per_kernel[dom_m]["plan"]["path"]],
+        "dtype": PATH_DTYPES["cluster_gemv"],
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantized per channel)",
         "config": decode_set_config(args, world, step_bytes),
         "method": {"timing": "CUDA graphs of one step, CUDA events on the launching stream",
                    "overlap_launch": not args.no_overlap,
-                   "graph_branches": [[calls[i]["name"] + f"/M{calls[i]['M']}" for i in b] for b in branches]},
+                   "step_launch": {"group": "one mtrtq_gemv_group launch for the ten calls",
+                                   "hybrid": "one mtrtq_gemv_group launch for the eight smaller calls, then the two "
+                                             "LM heads as cluster GEMV launches",
+                                   "calls": "one MatMulQ launch per call"}[args.step_launch],
+                   "graph_branches": (None if args.step_launch != "calls" else
+                                      [[calls[i]["name"] + f"/M{calls[i]['M']}" for i in b] for b in branches]),
+                   "other_step_launch": other},
         "roofline": roofline,
         "e2e": e2e,
-        "gpu_launches": len(calls) * args.steps,
+        "gpu_launches": {"group": 1, "hybrid": 1 + len(alone), "calls": len(calls)}[args.step_launch] * args.steps,
         "clocks": clk.summary(),
     }
     return line, calls, stream
+
+
+def run_e2e_group(torch, calls, args, dev, stream, dist, world):
+    """End to end through the grouped API with host buffers: per step, one pinned
+    H2D copy of the ten calls' activations (packed in one buffer), one
+    mtrtq_gemv_group launch, one pinned D2H copy of the ten outputs. Steps alternate
+    between two streams, each with its own device buffers, so one step's copies
+    overlap the other's launch; the timed region ends when both streams have
+    delivered their last outputs."""
+    from mini_tensorrt_b200 import matmulq
+    xs = sum(c["M"] * c["K"] for c in calls)
+    ys = sum(c["M"] * c["N"] for c in calls)
+    hx = torch.cat([c["x"].reshape(-1).cpu() for c in calls]).pin_memory()
+    step_bytes = sum(c["bytes"] for c in calls)
+    sets = []
+    for b in range(2):
+        st = stream if b == 0 else torch.cuda.Stream(dev)
+        dx = torch.empty(xs, device=dev)
+        dy = torch.empty(ys, device=dev)
+        hy = torch.empty(ys).pin_memory()
+        views, ox, oy = [], 0, 0
+        for c in calls:
+            views.append((dx[ox:ox + c["M"] * c["K"]].view(c["M"], c["K"]),
+                          dy[oy:oy + c["M"] * c["N"]].view(c["M"], c["N"])))
+            ox += c["M"] * c["K"]
+            oy += c["M"] * c["N"]
+        groups = [matmulq.GemvGroup([{"x": views[i][0], "w": c["w"][(g + i) % WEIGHT_COPIES], "out": views[i][1]}
+                                     for i, c in enumerate(calls)], mode=args.mode) for g in range(WEIGHT_COPIES)]
+        sets.append((st, dx, dy, hy, groups))
+
+    def step(i):
+        st, dx, dy, hy, groups = sets[i % 2]
+        with torch.cuda.stream(st):
+            dx.copy_(hx, non_blocking=True)
+            groups[i % WEIGHT_COPIES](st)
+            hy.copy_(dy, non_blocking=True)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    sets[1][0].wait_event(e0)
+    for i in range(args.steps):
+        step(i)
+    done = torch.cuda.Event()
+    done.record(sets[1][0])
+    stream.wait_event(done)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    # the outputs of the last step delivered to the host are the device's
+    last = sets[(args.steps - 1) % 2]
+    assert torch.equal(last[3], last[2].cpu())
+    secs = e0.elapsed_time(e1) / 1e3
+    t = torch.tensor([secs], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    secs = float(t.item())
+    return {"value": round(step_bytes * args.steps * world / secs / 1e9, 1), "unit": UNIT,
+            "h2d_bytes_per_step": xs * 4, "d2h_bytes_per_step": ys * 4,
+            "ms_per_step": round(secs / args.steps * 1e3, 4),
+            "how": "per step: one pinned H2D of the ten X (packed), one mtrtq_gemv_group launch, one pinned D2H "
+                   "of the ten Y; steps alternate over two streams with their own device buffers; CUDA events "
+                   "around the steps"}
 
 
 def run_e2e(torch, calls, args, dev, stream, dist, world):

@@ -271,7 +271,7 @@ enum {
                                   mtrtq_plan_info). Otherwise one kernel for every
                                   call: 1 CUDA-core split-K GEMV; 2 tile tcgen05 GEMM;
                                   3 stream-K tcgen05 kernel (M <= 32); 4 cluster
-                                  GEMV (M <= 8).
+                                  GEMV (M <= 64).
                                   2 and 3 need MTRTQ_MODE_BF16. A call the forced
                                   kernel cannot take fails with
                                   MTRTQ_ERR_INVALID_ARG. */
@@ -287,7 +287,10 @@ enum {
                                   (embedding, LayerNorm, attention, gelu, add,
                                   argmax, next token) are then launched the same
                                   way; each waits for the kernel ahead before it
-                                  touches global memory. */
+                                  touches global memory. */,
+  MTRTQ_OPT_PRODUCER_LANES = 4 /* 1 (default), 2, 3 or 6: threads of the grouped
+                                  GEMV (mtrtq_gemv_group) that issue its weight
+                                  copies; results do not depend on it. */
 };
 int mtrtq_set_option(int option, int64_t value);
 

@@ -30,6 +30,7 @@ ZERO_COLUMN_ZERO = 1
 OPT_GEMM_A_SOURCE = 1
 OPT_FORCE_PATH = 2
 OPT_OVERLAP_LAUNCH = 3
+OPT_PRODUCER_LANES = 4
 EPILOGUE_NONE, EPILOGUE_GELU_TANH, EPILOGUE_ADD_RESIDUAL = 0, 1, 2
 
 # Every function the header declares, with its ctypes signature.

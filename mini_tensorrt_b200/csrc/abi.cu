@@ -47,6 +47,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 int g_opt_gemm_a_source = 0;  // 0: dequantized weights in TMEM, 1: in shared memory
 int g_opt_force_path = 0;     // 0 auto, else the kernel (MTRTQ_OPT_FORCE_PATH)
 int g_opt_overlap = 0;        // 1: programmatic dependent launch (MTRTQ_OPT_OVERLAP_LAUNCH)
+int g_opt_producers = 1;      // grouped GEMV: bulk-copy issuing lanes (MTRTQ_OPT_PRODUCER_LANES)
 
 std::mutex g_dev_mu;
 DeviceInfo g_dev_cache[64];  // indexed by device ordinal; current_device() rejects >= 64
@@ -360,6 +361,11 @@ int mtrtq_set_option(int option, int64_t value) {
     case MTRTQ_OPT_OVERLAP_LAUNCH:
       if (value != 0 && value != 1) return fail(MTRTQ_ERR_INVALID_ARG, "overlap is 0 or 1");
       g_opt_overlap = (int)value;
+      return MTRTQ_OK;
+    case MTRTQ_OPT_PRODUCER_LANES:
+      if (value != 1 && value != 2 && value != 3 && value != 6)
+        return fail(MTRTQ_ERR_INVALID_ARG, "producer lanes are 1, 2, 3 or 6");
+      g_opt_producers = (int)value;
       return MTRTQ_OK;
     default:
       return fail(MTRTQ_ERR_INVALID_ARG, "unknown option %d", option);
@@ -811,7 +817,7 @@ int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype,
   if (!aligned(workspace, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
   const bool round_x = mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32;
   cudaError_t e = launch_gemv_stream(gp, count, units, grid, x_dtype, round_x, workspace, d.status,
-                                     g_opt_overlap != 0, static_cast<cudaStream_t>(stream));
+                                     g_opt_overlap != 0, g_opt_producers, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "grouped GEMV launch");
   return MTRTQ_OK;
 }

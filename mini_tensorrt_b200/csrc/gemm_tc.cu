@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + c0 + j;
-            if (m < p.M) part[(int64_t)m * p.n_pad] = __uint_as_float(v[j]);
+            if (m < p.M) __stcg(part + (int64_t)m * p.n_pad, __uint_as_float(v[j]));
           }
         }
       }
@@ -261,13 +261,11 @@ __global__ void __launch_bounds__(192, 1)
       // epilogue warps reach both named barriers whatever happened above, and the
       // ticket is always taken, so the counter returns to zero even after a
       // timeout (whose output is then flagged by the device status word).
-      __threadfence();
       named_bar_sync(1, 128);
       unsigned* counter = p.counters + (int64_t)mt * p.n_tiles + nt;
-      if (warp == 2 && lane == 0) *s_ticket = atomicAdd(counter, 1u);
+      if (warp == 2 && lane == 0) *s_ticket = ticket_acq_rel(counter);
       named_bar_sync(1, 128);
       if (*s_ticket == (unsigned)(p.splits - 1)) {
-        __threadfence();
         if (n_ok) {
           // 8 tokens at a time: their loads (rows clamped to M-1, so always in
           // bounds) for one split are independent and issued together; each output

@@ -156,14 +156,12 @@ __global__ void __launch_bounds__(128) gemv_q8_kernel(const GemvParams p) {
   float* part = p.partials + ((int64_t)split * p.M + m0) * p.n_pad + n;
 #pragma unroll
   for (int m = 0; m < MT; ++m)
-    if (m < mrem) part[(int64_t)m * p.n_pad] = r[m];
-  __threadfence();
+    if (m < mrem) __stcg(part + (int64_t)m * p.n_pad, r[m]);
   __syncthreads();
   unsigned* counter = p.counters + (int64_t)mc * p.n_tiles + nt;
-  if (tid == 0) s_ticket = atomicAdd(counter, 1u);
+  if (tid == 0) s_ticket = ticket_acq_rel(counter);
   __syncthreads();
   if (s_ticket != (unsigned)(p.splits - 1)) return;
-  __threadfence();
   if (n < p.N) {
     const float sc = p.scale[n];
     const float b = p.bias ? p.bias[n] : 0.0f;

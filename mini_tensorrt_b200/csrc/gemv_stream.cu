@@ -56,6 +56,7 @@ struct StreamParams {
   unsigned* counters; // one ticket per tile of the group
   float* partials;    // [G][2][8 tokens][128 rows]
   unsigned* status;
+  int producers;      // producer lanes (1, 2, 3 or 6: a divisor of the stage count)
 };
 
 __host__ __device__ __forceinline__ int64_t range_start(int64_t c, int64_t U, int64_t G) { return c * U / G; }
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(kSBlock, kSCtasPerSm) gemv_stream_kernel(const
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_abort;
   __shared__ int s_max[2][8], s_bad[2][8];
-  __shared__ unsigned s_ticket;
+  __shared__ unsigned s_last[1];  // ticket of the cut tile being handed over
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nst = kSStages;
   unsigned char* ring = smem;
@@ -151,24 +152,30 @@ __global__ void __launch_bounds__(kSBlock, kSCtasPerSm) gemv_stream_kernel(const
   if (warp == kSWarps) {
     // Producer: weights only (never written by a kernel this launch may overlap),
     // so no wait for the grid ahead.
-    if (lane == 0) {
+    // Lane l < np issues the CTA's units i = l, l + np, ... (np divides the stage
+    // count, so a lane always refills the same stages): one thread's bulk copies
+    // complete one after another, and several issuing lanes keep more of them in
+    // flight.
+    const int np = p.producers;
+    if (lane < np) {
       int pi = 0;
       while (pi + 1 < p.count && p.prob[pi + 1].unit_begin <= ub) ++pi;
-      int st = 0;
-      uint32_t ph = 0;
-      int64_t issued = 0;
-      for (int64_t u = ub; u < ue; ++u, ++issued) {
-        if (issued >= nst && !mbar_wait_bounded(&empty[st], ph ^ 1u, &s_abort, p.status)) break;
+      const int64_t n = ue - ub;
+      int64_t i = lane;
+      for (; i < n; i += np) {
+        const int st = (int)(i % nst);
+        const uint32_t ph = (uint32_t)(i / nst) & 1u;
+        if (i >= nst && !mbar_wait_bounded(&empty[st], ph ^ 1u, &s_abort, p.status)) break;
+        const int64_t u = ub + i;
         while (pi + 1 < p.count && p.prob[pi + 1].unit_begin <= u) ++pi;
         const char* src = p.prob[pi].W + (u - p.prob[pi].unit_begin) * (int64_t)kSUnit;
         mbar_arrive_expect_tx(&full[st], kSUnit);
         bulk_g2s(ring + (size_t)st * kSUnit, src, kSUnit, &full[st]);
-        if (++st == nst) { st = 0; ph ^= 1u; }
       }
-      // Every issued copy lands before the CTA leaves.
+      // Every copy this lane issued lands before the CTA leaves.
       volatile int no_abort = 0;
-      for (int64_t u = issued > nst ? issued - nst : 0; u < issued; ++u)
-        mbar_wait_bounded(&full[u % nst], (uint32_t)(u / nst) & 1u, &no_abort, p.status);
+      for (int64_t j = i - np; j >= 0 && j >= i - (int64_t)nst; j -= np)
+        mbar_wait_bounded(&full[j % nst], (uint32_t)(j / nst) & 1u, &no_abort, p.status);
     }
     __syncwarp();
   } else {
@@ -239,8 +246,7 @@ __global__ void __launch_bounds__(kSBlock, kSCtasPerSm) gemv_stream_kernel(const
       ++chunk;
       if (ku < P.KB && rem > 0) continue;  // the segment goes on
 
-      // ---- the segment ends: finish the tile or hand its part over ----
-      const int64_t T0 = P.unit_begin + (int64_t)t * P.KB;  // the tile's first unit
+      // ---- the segment ends: finish the tile, or store this CTA's part of it ----
       if (seg_start == 0 && ku == P.KB) {
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
@@ -253,30 +259,31 @@ __global__ void __launch_bounds__(kSBlock, kSCtasPerSm) gemv_stream_kernel(const
           }
         }
       } else {
-        float* slot = p.partials + ((cta * 2 + (seg_first ? 0 : 1)) * 8) * kTileN;
+        const int sl = seg_first ? 0 : 1;
+        float* slot = p.partials + ((cta * 2 + sl) * 8) * kTileN;
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const int m = 2 * c + (jj & 1), row = ra + (jj >> 1) * 8;
           if (m < P.M) __stcg(slot + m * kTileN + row, part[jj]);
         }
-        __threadfence();
-        named_bar_sync(1, kSThreads);
+        named_bar_sync(1, kSThreads);  // every part of this CTA is stored
         unsigned* counter = p.counters + P.tile_begin + t;
-        const int64_t c_lo = cta_of_unit(T0, U, G), c_hi = cta_of_unit(T0 + P.KB - 1, U, G);
-        if (tid == 0) s_ticket = atomicAdd(counter, 1u);
+        if (tid == 0) s_last[0] = ticket_acq_rel(counter);
         named_bar_sync(1, kSThreads);
-        if (s_ticket == (unsigned)(c_hi - c_lo)) {
-          __threadfence();
-          // The first part is the lowest CTA's last segment unless the tile starts
-          // its range; every later CTA's part is its first segment.
+        const int64_t T0 = P.unit_begin + (int64_t)t * P.KB;  // the tile's first unit
+        const int64_t c_lo = cta_of_unit(T0, U, G), c_hi = cta_of_unit(T0 + P.KB - 1, U, G);
+        if (s_last[0] == (unsigned)(c_hi - c_lo)) {
+          // The last CTA to arrive sums the parts in CTA order. The first part is
+          // the lowest CTA's last segment unless the tile starts its range; every
+          // later CTA's part is its first segment.
           const int first_slot = range_start(c_lo, U, G) == T0 ? 0 : 1;
           for (int e = tid; e < kTileN * P.M; e += kSThreads) {
             const int m = e / kTileN, row = e - m * kTileN;
             const int n = t * kTileN + row;
             float sum = 0.0f;
             for (int64_t cc = c_lo; cc <= c_hi; ++cc) {
-              const int sl = cc == c_lo ? first_slot : 0;
-              sum += __ldcg(p.partials + ((cc * 2 + sl) * 8 + m) * kTileN + row);
+              const int csl = cc == c_lo ? first_slot : 0;
+              sum += __ldcg(p.partials + ((cc * 2 + csl) * 8 + m) * kTileN + row);
             }
             if (n < P.N) {
               float y = __fmul_rn(sum, __ldg(P.scale + n));
@@ -299,6 +306,7 @@ __global__ void __launch_bounds__(kSBlock, kSCtasPerSm) gemv_stream_kernel(const
       }
       seg_start = ku;
     }
+
   }
   __syncthreads();  // the ring is idle: every copy has landed and been read
 }
@@ -323,8 +331,10 @@ cudaError_t stream_launch(const StreamParams& sp, bool pdl, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_gemv_stream(const GroupProblem* probs, int count, int64_t units, int grid, int x_dtype,
-                               bool round_x, void* workspace, unsigned* status, bool pdl, cudaStream_t st) {
+                               bool round_x, void* workspace, unsigned* status, bool pdl, int producers,
+                               cudaStream_t st) {
   StreamParams sp;
+  sp.producers = producers;
   for (int i = 0; i < count; ++i) sp.prob[i] = probs[i];
   sp.count = count;
   sp.units = units;

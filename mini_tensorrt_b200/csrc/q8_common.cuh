@@ -158,6 +158,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// ---- split tiles: tickets ---------------------------------------------------------
+
+// Ticket of a split tile, taken by ONE thread after a barrier of the threads that
+// stored this CTA's part: the gpu-scope acq_rel atomic releases every part those
+// threads stored before the barrier (release is cumulative over the barrier) and,
+// for the last arriver, acquires the other CTAs' parts for the reads its threads
+// make after the next barrier. One fence per CTA, where a __threadfence() by every
+// thread is a sequentially consistent fence each (measured as the main stall,
+// membar, of the grouped GEMV). The parts are read with ld.global.cg (L2), never
+// from a stale L1 line.
+__device__ __forceinline__ unsigned ticket_acq_rel(unsigned* counter) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
+
 // ---- TMA (bulk async copies into shared memory) ------------------------------
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,

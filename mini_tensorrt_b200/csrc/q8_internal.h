@@ -94,7 +94,8 @@ inline size_t gemv_stream_workspace_bytes(int grid) {
   return kStreamCounterBytes + (size_t)grid * 2 * 8 * 128 * sizeof(float);
 }
 cudaError_t launch_gemv_stream(const GroupProblem* probs, int count, int64_t units, int grid, int x_dtype,
-                               bool round_x, void* workspace, unsigned* status, bool pdl, cudaStream_t st);
+                               bool round_x, void* workspace, unsigned* status, bool pdl, int producers,
+                               cudaStream_t st);
 
 // Cluster GEMV: CTAs resident per SM (registers are capped to allow it) and the
 // shared memory a CTA may use so that they fit, for M <= 8 and for larger M (more

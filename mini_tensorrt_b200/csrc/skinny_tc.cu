@@ -453,17 +453,15 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         float* part = p.partials + ((int64_t)(c * 2 + slot) * p.M) * kTileN + r;
 #pragma unroll
         for (int j = 0; j < TM; ++j)
-          if (j < p.M) part[(int64_t)j * kTileN] = v[j];
-        __threadfence();
+          if (j < p.M) __stcg(part + (int64_t)j * kTileN, v[j]);
         named_bar_sync(1, 128);
         const int c_first = sk_owner((long long)t * p.KB, U, G);
         const int c_last = sk_owner((long long)(t + 1) * p.KB - 1, U, G);
         const unsigned nslots = (unsigned)(c_last - c_first + 1);
         unsigned* counter = p.counters + t;
-        if (warp == 10 && lane == 0) *s_ticket = atomicAdd(counter, 1u);
+        if (warp == 10 && lane == 0) *s_ticket = ticket_acq_rel(counter);
         named_bar_sync(1, 128);
         if (*s_ticket == nslots - 1) {
-          __threadfence();
           if (n_ok) {
             // Slots are summed in CTA order (= k order), 16 rows at a time; the
             // loads of four slots are issued together.
