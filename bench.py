@@ -642,38 +642,47 @@ def run_shape(args, torch, dev):
             "peak_kind": peak_kind, "weight_copies": n_copies, "plan": plan}
 
 
-def run_gpt2_decode(args, torch, dev):
+def run_gpt2_decode(args, torch, dev, mode=None):
     """Random-init GPT-2 small, every Linear an int8 MatMulQ, greedy KV-cache decoding
     on the device (one CUDA graph per step): prompts of 64 ids, then 64 generated
-    tokens, batch 1 and 16. Reports prefill and decode tokens/s (all sequences) and
-    the decode steps' weight bytes per second (int8 Linears + tied LM head)."""
+    tokens, batch 1 and 16, the prompt prefilled token by token (as the reference
+    does) and in one pass of M = B * 64 products. Reports prefill and decode
+    tokens/s (all sequences) and the decode steps' weight bytes per second (int8
+    Linears + tied LM head). The default mode is fp32, whose tokens are identical to
+    the reference decoder's at both batches (bf16 mode flips a few near-tie
+    argmaxes at batch 16)."""
     from mini_tensorrt_b200 import gpt2
     from mini_tensorrt_b200.matmulq import set_option
     from mini_tensorrt_b200 import _lib
+    mode = mode or args.mode
     set_option(_lib.OPT_OVERLAP_LAUNCH, 0 if args.no_overlap else 1)
     cfg = gpt2.GPT2Config()
     w = gpt2.random_weights(cfg, seed=0)
     P, new = 64, 64
     D, F, V, L = cfg.d_model, cfg.d_ff, cfg.vocab, cfg.n_layer
     step_bytes = L * (D * 3 * D + D * D + D * F + F * D) + D * V
-    out = {"metric": METRIC, "impl": "ours", "workload": "gpt2_decode", "n_gpus": 1,
+    out = {"workload": "gpt2_decode",
            "config": {"model": "GPT-2 small (12L, d 768, 12 heads, d_ff 3072, vocab 50257), random init",
-                      "prompt_len": P, "max_new": new, "mode": args.mode,
+                      "prompt_len": P, "max_new": new, "mode": mode,
                       "weight_bytes_per_step": step_bytes,
-                      "timing": "CUDA events around graph replays of one decode step"},
+                      "timing": "CUDA events around the prefill and around the graph replays of the decode steps"},
            "batches": {}}
     for B in (1, 16):
-        dec = gpt2.DeviceDecoder(w, B, max_ctx=P + new, mode=args.mode, device=dev)
+        dec = gpt2.DeviceDecoder(w, B, max_ctx=P + new, mode=mode, device=dev)
         prompt = np.random.default_rng(1234 + B).integers(0, V, (B, P), dtype=np.int32)
-        dec.generate(prompt, new)  # capture + warm-up
-        runs = [dec.generate(prompt, new) for _ in range(max(3, args.steps // 10))]
-        dsec = min(r["decode_s"] for r in runs)
-        psec = min(r["prefill_s"] for r in runs)
-        nsteps = new - 1
-        out["batches"][str(B)] = {
-            "decode_tok_s": round(B * nsteps / dsec, 1), "decode_ms_per_step": round(dsec / nsteps * 1e3, 4),
-            "prefill_tok_s": round(B * P / psec, 1),
-            "decode_weight_gbs": round(step_bytes * nsteps / dsec / 1e9, 1)}
+        row = {}
+        for pf in ("tokens", "gemm"):
+            dec.generate(prompt, new, prefill=pf)  # capture + warm-up
+            runs = [dec.generate(prompt, new, prefill=pf) for _ in range(3)]
+            dsec = min(r["decode_s"] for r in runs)
+            psec = min(r["prefill_s"] for r in runs)
+            nsteps = new - 1
+            row["decode_tok_s"] = round(B * nsteps / dsec, 1)
+            row["decode_ms_per_step"] = round(dsec / nsteps * 1e3, 4)
+            row["decode_weight_gbs"] = round(step_bytes * nsteps / dsec / 1e9, 1)
+            row[f"prefill_{pf}_tok_s"] = round(B * P / psec, 1)
+            row[f"prefill_{pf}_ms"] = round(psec * 1e3, 3)
+        out["batches"][str(B)] = row
         del dec
         torch.cuda.empty_cache()
     return out
@@ -965,7 +974,7 @@ def main():
         return
     if args.workload == "gpt2_decode":
         if rank == 0:
-            print(json.dumps(run_gpt2_decode(args, torch, dev)))
+            print(json.dumps({"metric": METRIC, "impl": "ours", "n_gpus": 1, **run_gpt2_decode(args, torch, dev)}))
         return
     if args.workload.startswith("sharded:"):
         line = run_sharded(args, torch, rank, world, dev, dist)
@@ -980,6 +989,7 @@ def main():
     torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_extras:
         line["extras"] = run_extras(torch, dev, args, stream)
+        line["extras"]["gpt2_small_decode"] = run_gpt2_decode(args, torch, dev, mode="fp32")
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_calls, cpu_bytes = decode_set_calls()
         line["cpu_baseline"] = cpu_baseline_line(cpu_calls, cpu_bytes)

@@ -326,6 +326,9 @@ int mtrtq_decode_embed(const int32_t* prompt, int64_t prompt_len, const int32_t*
  * src/ops/kernels_transformer.cpp:19-54): y = (x - mean) / sqrt(var + eps) * gamma + beta. */
 int mtrtq_layernorm(const float* x, const float* gamma, const float* beta, float* y, int64_t rows,
                     int64_t D, float eps, void* stream);
+/* The same with rows of x ldx >= D elements apart (y stays [rows, D]). */
+int mtrtq_layernorm_strided(const float* x, int64_t ldx, const float* gamma, const float* beta, float* y,
+                            int64_t rows, int64_t D, float eps, void* stream);
 
 /* Attention of each sequence's new query over its cached keys (tools/run_gpt2.cpp:
  * 143-172): qkv [B, 3*H*head_dim] rows (q | k | v); appends k and v at *pos into
@@ -334,6 +337,20 @@ int mtrtq_layernorm(const float* x, const float* gamma, const float* beta, float
 int mtrtq_decode_attention(const float* qkv, float* kcache, float* vcache, const int32_t* pos,
                            float* out, int64_t B, int64_t H, int64_t head_dim, int64_t max_ctx,
                            void* stream);
+
+/* Prefill of a whole prompt, so that every Linear of the prompt is one MatMulQ of
+ * M = B * P rows (the reference consumes the prompt one position at a time,
+ * tools/run_gpt2.cpp:198-214; rows are independent in its MatMulQ, so the
+ * products are the same).
+ * mtrtq_prefill_embed: x [B*P, D] row b*P + i = wte[ids[b, i]] + wpe[i] (ids [B, P]).
+ * mtrtq_prefill_attention: qkv [B*P, 3*H*head_dim] rows (q | k | v); writes every
+ * position's k and v into kcache / vcache [B, max_ctx, H*head_dim] and out [B*P,
+ * H*head_dim] = causal softmax(q . K^T / sqrt(head_dim)) V, position i over 0..i
+ * (P <= 1536). */
+int mtrtq_prefill_embed(const int32_t* ids, int64_t B, int64_t P, const float* wte, const float* wpe,
+                        int64_t n_pos, float* x, int64_t D, int64_t V, void* stream);
+int mtrtq_prefill_attention(const float* qkv, float* kcache, float* vcache, float* out, int64_t B, int64_t P,
+                            int64_t H, int64_t head_dim, int64_t max_ctx, void* stream);
 
 /* GPT-2 gelu_new (tools/run_gpt2.cpp:178-181, src/ops/kernels_gpt.cpp:44-61):
  * y = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))). y may alias x. */

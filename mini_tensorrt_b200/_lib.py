@@ -62,7 +62,10 @@ SIGNATURES = {
                                          _int, _vp]),
     "mtrtq_decode_embed": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp]),
     "mtrtq_layernorm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "mtrtq_layernorm_strided": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "mtrtq_decode_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "mtrtq_prefill_embed": (_int, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "mtrtq_prefill_attention": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "mtrtq_gelu_tanh": (_int, [_vp, _vp, _i64, _vp]),
     "mtrtq_add_inplace": (_int, [_vp, _vp, _i64, _vp]),
     "mtrtq_argmax_rows": (_int, [_vp, _i64, _i64, _i64, _vp, _vp]),

@@ -78,11 +78,11 @@ __global__ void embed_kernel(const int32_t* prompt, int64_t prompt_len, const in
 // are read again for each pass.
 constexpr int kLnRegs = 8;
 
-__global__ void layernorm_kernel(const float* x, const float* g, const float* bta, float* y,
+__global__ void layernorm_kernel(const float* x, int64_t ldx, const float* g, const float* bta, float* y,
                                  int64_t D, float eps) {
   __shared__ float red[32];
   pdl_begin();
-  const float* xr = x + blockIdx.x * D;
+  const float* xr = x + blockIdx.x * ldx;
   float* yr = y + blockIdx.x * D;
   const bool in_regs = D <= (int64_t)kLnRegs * blockDim.x;
   float v[kLnRegs];
@@ -345,6 +345,77 @@ __global__ void decode_next_kernel(unsigned long long* best, int64_t rows, int32
   if (threadIdx.x == 0) *pos = p + 1;
 }
 
+// ---- prefill of a whole prompt -------------------------------------------------
+
+// x[b * P + i, :] = wte[ids[b, i], :] + wpe[i, :] for every prompt position i: one
+// block per (position, sequence). Ids outside the vocabulary read row 0.
+__global__ void prefill_embed_kernel(const int32_t* ids, int64_t P, const float* wte, const float* wpe,
+                                     float* x, int64_t D, int64_t V) {
+  pdl_begin();
+  const int64_t i = blockIdx.x, b = blockIdx.y;
+  int64_t tok = ids[b * P + i];
+  if (tok < 0 || tok >= V) tok = 0;
+  float* row = x + (b * P + i) * D;
+  for (int64_t c = threadIdx.x; c < D; c += blockDim.x) row[c] = wte[tok * D + c] + wpe[i * D + c];
+}
+
+// Causal attention over a prompt of P positions, one block of kPrefillWarps warps
+// per (head, sequence): the keys and values of positions 0..P-1 (the head's slice
+// of qkv [B*P, 3D] rows q | k | v) go to the caches [B, max_ctx, D], and for every
+// query position i a warp computes, as the reference does one position at a time
+// (tools/run_gpt2.cpp:152-172): scores q_i . k_j * (1 / sqrt(d)) for j <= i (a lane
+// per key, each dot product in k order), the max-subtracted exponentials and their
+// sum (lane tree in fixed order), then out[b * P + i, head slice] = sum over j, in
+// ascending j, of (e_j * (1 / sum)) v_j (a lane per column).
+constexpr int kPrefillWarps = 8;
+__global__ void __launch_bounds__(kPrefillWarps * 32)
+    prefill_attention_kernel(const float* qkv, float* kc, float* vc, float* out, int64_t P, int64_t H,
+                             int64_t d, int64_t max_ctx) {
+  pdl_begin();
+  extern __shared__ float sc[];  // [kPrefillWarps][P] scores
+  const int64_t h = blockIdx.x, b = blockIdx.y, D = H * d;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* base = qkv + b * P * 3 * D;
+  // k and v of every prompt position into the caches (this head's columns).
+  for (int64_t e = threadIdx.x; e < P * d; e += blockDim.x) {
+    const int64_t i = e / d, t = e - i * d;
+    const float* r = base + i * 3 * D + h * d + t;
+    kc[(b * max_ctx + i) * D + h * d + t] = r[D];
+    vc[(b * max_ctx + i) * D + h * d + t] = r[2 * D];
+  }
+  const float scale = 1.0f / sqrtf((float)d);
+  float* s = sc + warp * P;
+  for (int64_t i = warp; i < P; i += kPrefillWarps) {
+    const float* q = base + i * 3 * D + h * d;
+    float mx = -INFINITY;
+    for (int64_t j = lane; j <= i; j += 32) {
+      const float* k = base + j * 3 * D + D + h * d;
+      float acc = 0.0f;
+      for (int64_t t = 0; t < d; ++t) acc += q[t] * k[t];
+      acc *= scale;
+      s[j] = acc;
+      mx = fmaxf(mx, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+    for (int64_t j = lane; j <= i; j += 32) {
+      const float e = expf(s[j] - mx);
+      s[j] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.0f / sum;
+    __syncwarp();
+    for (int64_t t = lane; t < d; t += 32) {
+      float acc = 0.0f;
+      for (int64_t j = 0; j <= i; ++j) acc += (s[j] * inv) * base[j * 3 * D + 2 * D + h * d + t];
+      out[(b * P + i) * D + h * d + t] = acc;
+    }
+    __syncwarp();
+  }
+}
+
 int launch_status(cudaError_t e) { return e == cudaSuccess ? MTRTQ_OK : MTRTQ_ERR_CUDA; }
 
 // Launches kern on `stream`, with programmatic stream serialization when
@@ -386,7 +457,15 @@ int mtrtq_decode_embed(const int32_t* prompt, int64_t prompt_len, const int32_t*
 int mtrtq_layernorm(const float* x, const float* gamma, const float* beta, float* y, int64_t rows,
                     int64_t D, float eps, void* stream) {
   if (!x || !gamma || !beta || !y || rows <= 0 || D <= 0 || rows > 2147483647) return MTRTQ_ERR_INVALID_ARG;
-  return launch_helper(layernorm_kernel, dim3((unsigned)rows), dim3(256), 0, stream, x, gamma, beta, y,
+  return launch_helper(layernorm_kernel, dim3((unsigned)rows), dim3(256), 0, stream, x, D, gamma, beta, y,
+                       D, eps);
+}
+
+int mtrtq_layernorm_strided(const float* x, int64_t ldx, const float* gamma, const float* beta, float* y,
+                            int64_t rows, int64_t D, float eps, void* stream) {
+  if (!x || !gamma || !beta || !y || rows <= 0 || D <= 0 || ldx < D || rows > 2147483647)
+    return MTRTQ_ERR_INVALID_ARG;
+  return launch_helper(layernorm_kernel, dim3((unsigned)rows), dim3(256), 0, stream, x, ldx, gamma, beta, y,
                        D, eps);
 }
 
@@ -403,6 +482,26 @@ int mtrtq_decode_attention(const float* qkv, float* kcache, float* vcache, const
   if (smem > 48 * 1024) return MTRTQ_ERR_INVALID_ARG;  // contexts up to ~11k positions at d = 64
   return launch_helper(attention_kernel, dim3((unsigned)H, (unsigned)B), dim3(kAttnThreads), smem,
                        stream, qkv, kcache, vcache, pos, out, H, head_dim, max_ctx);
+}
+
+int mtrtq_prefill_embed(const int32_t* ids, int64_t B, int64_t P, const float* wte, const float* wpe,
+                        int64_t n_pos, float* x, int64_t D, int64_t V, void* stream) {
+  if (!ids || !wte || !wpe || !x || B <= 0 || P <= 0 || D <= 0 || V <= 0 || P > n_pos || B > 65535 ||
+      P > 2147483647)
+    return MTRTQ_ERR_INVALID_ARG;
+  return launch_helper(prefill_embed_kernel, dim3((unsigned)P, (unsigned)B), dim3(256), 0, stream, ids, P,
+                       wte, wpe, x, D, V);
+}
+
+int mtrtq_prefill_attention(const float* qkv, float* kcache, float* vcache, float* out, int64_t B, int64_t P,
+                            int64_t H, int64_t head_dim, int64_t max_ctx, void* stream) {
+  if (!qkv || !kcache || !vcache || !out || B <= 0 || P <= 0 || H <= 0 || head_dim <= 0 || P > max_ctx ||
+      B > 65535 || H > 65535)
+    return MTRTQ_ERR_INVALID_ARG;
+  const size_t smem = (size_t)kPrefillWarps * (size_t)P * sizeof(float);
+  if (smem > 48 * 1024) return MTRTQ_ERR_INVALID_ARG;  // prompts up to 1536 positions
+  return launch_helper(prefill_attention_kernel, dim3((unsigned)H, (unsigned)B), dim3(kPrefillWarps * 32), smem,
+                       stream, qkv, kcache, vcache, out, P, H, head_dim, max_ctx);
 }
 
 int mtrtq_gelu_tanh(const float* x, float* y, int64_t n, void* stream) {

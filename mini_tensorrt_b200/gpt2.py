@@ -11,8 +11,12 @@ MatMulQ (weights tied to the token embedding) and the greedy argmax, all through
 libmtrtq's C ABI. Q, K and V use one 768x2304 weight: per-column quantization makes
 that identical to three separate 768x768 weights.
 
-A batch of B sequences is B rows of every MatMulQ (M = B). The prompt is consumed
-token by token, as the reference's prefill does (tools/run_gpt2.cpp:205).
+A batch of B sequences is B rows of every MatMulQ (M = B). The prompt is either
+consumed token by token, as the reference's prefill does (tools/run_gpt2.cpp:205),
+or -- prefill="gemm" -- in one pass in which every Linear is a single MatMulQ of
+M = B * P rows (a dense contraction: the cluster GEMV up to 64 rows, the tcgen05
+GEMM above in bf16 mode) and attention is causal over the prompt; the KV caches
+then hold every prompt position and decoding continues from there.
 
 Weights here are random (the architecture of GPT-2 small, N(0, 0.02) for every
 matrix, embedding and bias, LayerNorm gamma 1 and beta 0), seeded per tensor.
@@ -222,11 +226,72 @@ class DeviceDecoder:
             self.next_tok.zero_()
             self.history.zero_()
 
-    def generate(self, prompt, max_new: int, use_graph: bool = True) -> dict:
-        """prompt: int [B, P] token ids. Runs P + max_new - 1 steps (the P prompt
-        positions, then one per generated token after the first) and returns
-        {"tokens": int32 [B, max_new], "prefill_s", "decode_s"} with the step times
-        measured by CUDA events."""
+    # -- the prompt in one pass: every Linear one MatMulQ of M = B * P rows ---------
+    def _prefill_buffers(self, P: int):
+        if getattr(self, "_pf_P", None) == P:
+            return
+        cfg, B = self.cfg, self.B
+        D, F, R = cfg.d_model, cfg.d_ff, self.B * P
+        z = lambda *s: torch.zeros(s, dtype=torch.float32, device=self.dev)
+        self.pf_x, self.pf_h, self.pf_attn = z(R, D), z(R, D), z(R, D)
+        self.pf_qkv, self.pf_mh = z(R, 3 * D), z(R, F)
+        need = max(workspace_bytes(R, K, N, torch.float32, self.mode)
+                   for K, N in [(D, 3 * D), (D, D), (D, F), (F, D)])
+        self.pf_ws = Workspace(self.dev).get(need)
+        self._pf_P = P
+
+    def _mm_ws(self, x, w: PackedWeight, bias, y, ws, epilogue=_lib.EPILOGUE_NONE, residual=None):
+        check(lib().mtrtq_matmul_ex(x.data_ptr(), _lib.DTYPE_F32, x.stride(0), w.packed.data_ptr(),
+                                    w.scale.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                    y.data_ptr(), y.stride(0), x.shape[0], w.K, w.N, MODES[self.mode],
+                                    ws.data_ptr() if ws is not None else None,
+                                    ws.numel() if ws is not None else 0, epilogue,
+                                    residual.data_ptr() if residual is not None else None,
+                                    residual.stride(0) if residual is not None else 0, self._sp),
+              "mtrtq_matmul_ex")
+
+    def _launch_prefill(self, P: int):
+        """Launches the prefill of self.prompt ([B, P]) on self.stream: positions
+        0..P-1 through every layer as M = B * P products, the caches filled, then
+        the LM head and argmax of each sequence's last position, which becomes the
+        first generated token (history[P - 1]); decoding then starts at P."""
+        cfg, B, D, sp, L = self.cfg, self.B, self.cfg.d_model, self._sp, lib()
+        R = B * P
+        ws = self.pf_ws
+        check(L.mtrtq_prefill_embed(self.prompt.data_ptr(), B, P, self.wte.data_ptr(), self.wpe.data_ptr(),
+                                    cfg.n_pos, self.pf_x.data_ptr(), D, cfg.vocab, sp), "prefill_embed")
+        x, h = self.pf_x, self.pf_h
+        for i, ly in enumerate(self.layers):
+            check(L.mtrtq_layernorm(x.data_ptr(), ly["ln1"][0].data_ptr(), ly["ln1"][1].data_ptr(), h.data_ptr(),
+                                    R, D, cfg.eps, sp), "layernorm")
+            self._mm_ws(h, ly["qkv"], ly["bqkv"], self.pf_qkv, ws)
+            check(L.mtrtq_prefill_attention(self.pf_qkv.data_ptr(), self.kc[i].data_ptr(), self.vc[i].data_ptr(),
+                                            self.pf_attn.data_ptr(), B, P, cfg.n_head, cfg.head_dim,
+                                            self.max_ctx, sp), "prefill_attention")
+            self._mm_ws(self.pf_attn, ly["o"], ly["bo"], x, ws, _lib.EPILOGUE_ADD_RESIDUAL, x)
+            check(L.mtrtq_layernorm(x.data_ptr(), ly["ln2"][0].data_ptr(), ly["ln2"][1].data_ptr(), h.data_ptr(),
+                                    R, D, cfg.eps, sp), "layernorm")
+            self._mm_ws(h, ly["fc"], ly["bfc"], self.pf_mh, ws, _lib.EPILOGUE_GELU_TANH)
+            self._mm_ws(self.pf_mh, ly["proj"], ly["bproj"], x, ws, _lib.EPILOGUE_ADD_RESIDUAL, x)
+        # each sequence's last position: rows P-1, 2P-1, ... (a strided view)
+        last = x.view(B, P, D)[:, P - 1, :]
+        check(L.mtrtq_layernorm_strided(last.data_ptr(), last.stride(0), self.ln_f[0].data_ptr(),
+                                        self.ln_f[1].data_ptr(), self.h.data_ptr(), B, D, cfg.eps, sp),
+              "layernorm")
+        self._mm(self.h, self.lm_head, None, self.logits)
+        check(L.mtrtq_argmax_rows(self.logits.data_ptr(), B, cfg.vocab, cfg.vocab, self.best.data_ptr(), sp),
+              "argmax")
+        check(L.mtrtq_decode_next(self.best.data_ptr(), B, self.next_tok.data_ptr(), self.history.data_ptr(),
+                                  self.max_steps, self.pos.data_ptr(), sp), "decode_next")
+
+    def generate(self, prompt, max_new: int, use_graph: bool = True, prefill: str = "tokens") -> dict:
+        """prompt: int [B, P] token ids. prefill "tokens": P + max_new - 1 steps (the P
+        prompt positions, then one per generated token after the first); "gemm": the
+        prompt in one pass of M = B * P products, then max_new - 1 steps. Returns
+        {"tokens": int32 [B, max_new], "prefill_s", "decode_s"} with times measured
+        by CUDA events."""
+        if prefill not in ("tokens", "gemm"):
+            raise ValueError("prefill is 'tokens' or 'gemm'")
         prompt = torch.as_tensor(np.asarray(prompt), dtype=torch.int32)
         B, P = prompt.shape
         if B != self.B:
@@ -234,6 +299,8 @@ class DeviceDecoder:
         steps = P + max_new - 1
         if steps > self.max_ctx or steps > self.max_steps:
             raise ValueError("prompt + max_new exceeds max_ctx")
+        if prefill == "gemm":
+            return self._generate_gemm_prefill(prompt, max_new, use_graph)
         self._reset(prompt)
         if use_graph and self.graph is None:
             # one eager step (per-device setup), then capture one step and reset
@@ -259,3 +326,36 @@ class DeviceDecoder:
         hist = self.history[P - 1:P - 1 + max_new].t().contiguous().cpu().numpy()
         return {"tokens": hist, "prefill_s": ev[0].elapsed_time(ev[1]) / 1e3,
                 "decode_s": ev[1].elapsed_time(ev[2]) / 1e3, "steps": steps}
+
+    def _capture_step(self):
+        with torch.cuda.stream(self.stream):
+            self._launch_step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            self._launch_step()
+        self.graph = g
+
+    def _generate_gemm_prefill(self, prompt, max_new: int, use_graph: bool) -> dict:
+        B, P = prompt.shape
+        self._prefill_buffers(P)
+        self._reset(prompt)
+        if use_graph and self.graph is None:
+            self._capture_step()
+            self._reset(prompt)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        with torch.cuda.stream(self.stream):
+            # the prefill's last position is P - 1: decode_next then records the
+            # first generated token there and moves on to P
+            self.pos.fill_(P - 1)
+            ev[0].record(self.stream)
+            with matmulq.option(_lib.OPT_OVERLAP_LAUNCH, 1 if self.overlap else 0):
+                self._launch_prefill(P)
+            ev[1].record(self.stream)
+            for _ in range(max_new - 1):
+                self.graph.replay() if use_graph else self._launch_step()
+            ev[2].record(self.stream)
+        torch.cuda.synchronize()
+        hist = self.history[P - 1:P - 1 + max_new].t().contiguous().cpu().numpy()
+        return {"tokens": hist, "prefill_s": ev[0].elapsed_time(ev[1]) / 1e3,
+                "decode_s": ev[1].elapsed_time(ev[2]) / 1e3, "steps": max_new}
