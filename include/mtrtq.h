@@ -258,6 +258,66 @@ int64_t mtrtq_gemv_group_workspace_bytes(const mtrtq_gemv_problem* problems, int
 int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype, int mode, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* ---- one MatMulQ split across the GPUs of a node -------------------------------- */
+
+/* The op shards without changing its result: output columns are independent and k
+ * partial sums add (the split the reference's tensor-parallel decoder would use).
+ * Rank r holds one shard of the weights and computes it with the single-GPU
+ * kernels; the exchange is this library's own kernels over peer memory (NVLink
+ * P2P stores and atomics, no NCCL, no multicast):
+ *   MTRTQ_SPLIT_N: rank r holds W[:, n0:n1) and scale[n0:n1) (whole 128-channel
+ *     tiles, mtrtq_shard_range) and stores Y[:, n0:n1) into every rank's Y: after
+ *     the call every rank's Y holds the whole product (an all-gather);
+ *   MTRTQ_SPLIT_K: rank r holds W[k0:k1, :] (whole 64-k units) and the full scale,
+ *     computes the scaled partial over its k range and stores it into its slot of
+ *     every rank's slot buffer; every rank then sums the slots in rank order and
+ *     adds the bias once (an all-reduce; identical bits on every rank).
+ * Each call starts with a barrier (every rank signals every peer and waits for
+ * all), so no rank overwrites a buffer a peer's earlier kernels still read. Waits
+ * are bounded (about a second); one that gives up stores MTRTQ_ERR_TIMEOUT in the
+ * device status word (mtrtq_read_status) and the call's exchange is skipped.
+ *
+ * The peer pointers in mtrtq_shard_comm must be usable from this device: another
+ * process's allocation opened with mtrtq_ipc_import (or the caller's own IPC), or
+ * a peer device's memory in this process with peer access enabled. */
+#define MTRTQ_MAX_WORLD 8
+#define MTRTQ_SHARD_FLAG_BYTES 64   /* per rank, device memory, zero-filled once */
+#define MTRTQ_IPC_HANDLE_BYTES 72
+enum { MTRTQ_SPLIT_N = 0, MTRTQ_SPLIT_K = 1 };
+
+typedef struct mtrtq_shard_comm {
+  int rank, world;                   /* this process's rank, 1 <= world <= 8 */
+  float* y[MTRTQ_MAX_WORLD];         /* split N: every rank's Y (same M, N, ldy) */
+  float* slots[MTRTQ_MAX_WORLD];     /* split K: every rank's slot buffer */
+  int64_t slot_elems;                /* floats in each slot buffer (>= M * N * world) */
+  unsigned* flags[MTRTQ_MAX_WORLD];  /* every rank's flag words */
+} mtrtq_shard_comm;
+
+/* [begin, end) of `rank`'s shard of an extent (N for MTRTQ_SPLIT_N, K for
+ * MTRTQ_SPLIT_K): whole 128-channel tiles or 64-k units, split as evenly as possible,
+ * earlier ranks taking the extra ones. */
+int mtrtq_shard_range(int64_t extent, int split, int rank, int world, int64_t* begin, int64_t* end);
+/* Bytes of one rank's slot buffer for split K; workspace of the local product. */
+int64_t mtrtq_shard_slot_bytes(int64_t M, int64_t N, int world);
+int64_t mtrtq_shard_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int split, int rank,
+                                    int world);
+/* Y (every rank) = X x dequant(W) (+ bias). X: the full [M, K] on every rank;
+ * packed/scale: this rank's shard (packed as an unsplit weight of the shard's
+ * shape; NULL for an empty shard); bias: the full [N] or NULL. epoch: 1 for the
+ * first call on these flags, then +1 per call (every rank the same). Calls on the
+ * same comm must be ordered on one stream per rank. */
+int mtrtq_matmul_sharded(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                         const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
+                         int split, const mtrtq_shard_comm* comm, unsigned epoch, void* workspace,
+                         size_t workspace_bytes, void* stream);
+/* Peer pointers across processes: mtrtq_ipc_export writes MTRTQ_IPC_HANDLE_BYTES
+ * naming the device allocation that holds device_ptr (and the offset into it);
+ * another process's mtrtq_ipc_import opens it (peer access enabled) and returns
+ * the same address in its own space; mtrtq_ipc_close releases it. Set-up calls. */
+int mtrtq_ipc_export(const void* device_ptr, void* handle);
+int mtrtq_ipc_import(const void* handle, void** device_ptr);
+int mtrtq_ipc_close(void* device_ptr);
+
 /* ---- options and diagnostics ----------------------------------------------------- */
 
 /* Process-wide options. Both change how a call is carried out, never its result

@@ -82,6 +82,26 @@ class GemvProblem(ctypes.Structure):
                 ("ldr", _i64)]
 
 
+MAX_WORLD = 8
+SPLIT_N, SPLIT_K = 0, 1
+SHARD_FLAG_BYTES = 64
+IPC_HANDLE_BYTES = 72
+
+
+class ShardComm(ctypes.Structure):
+    """mtrtq_shard_comm (include/mtrtq.h)."""
+    _fields_ = [("rank", _int), ("world", _int), ("y", _vp * MAX_WORLD), ("slots", _vp * MAX_WORLD),
+                ("slot_elems", _i64), ("flags", _vp * MAX_WORLD)]
+
+
+SIGNATURES["mtrtq_shard_range"] = (_int, [_i64, _int, _int, _int, _vp, _vp])
+SIGNATURES["mtrtq_shard_slot_bytes"] = (_i64, [_i64, _i64, _int])
+SIGNATURES["mtrtq_shard_workspace_bytes"] = (_i64, [_i64, _i64, _i64, _int, _int, _int, _int, _int])
+SIGNATURES["mtrtq_matmul_sharded"] = (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int,
+                                             _int, _vp, ctypes.c_uint, _vp, _sz, _vp])
+SIGNATURES["mtrtq_ipc_export"] = (_int, [_vp, _vp])
+SIGNATURES["mtrtq_ipc_import"] = (_int, [_vp, _vp])
+SIGNATURES["mtrtq_ipc_close"] = (_int, [_vp])
 SIGNATURES["mtrtq_gemv_group_workspace_bytes"] = (_i64, [_vp, _int])
 SIGNATURES["mtrtq_gemv_group"] = (_int, [_vp, _int, _int, _int, _vp, _sz, _vp])
 

@@ -308,6 +308,25 @@ int check_device_sm100(DeviceInfo* d) {
 }
 
 }  // namespace
+
+int report_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int report_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
+unsigned* device_status_address(int* rc) {
+  DeviceInfo d;
+  *rc = check_device_sm100(&d);
+  return *rc ? nullptr : d.status;
+}
+
 // (device, kernel) pairs whose shared memory limit has been raised.
 static std::mutex g_smem_mu;
 static std::set<std::pair<int, const void*>> g_smem_done;

@@ -1,0 +1,355 @@
+// MatMulQ split across the GPUs of one node, with the exchange done by this
+// library's own kernels over peer memory (NVLink P2P loads, stores and atomics;
+// no NCCL, no multicast).
+//
+// The op shards without changing its result: output columns are independent
+// (split N) and k partial sums add (split K). Rank r computes its shard with the
+// single-GPU kernels (the planner's choice for the shard's shape), then:
+//   * entry: it tells every peer it has entered call `epoch` and waits until every
+//     peer has too -- a peer's kernels that read the previous call's result ran
+//     before its entry signal on its stream, so no buffer a peer still reads is
+//     overwritten;
+//   * push: one kernel stores this rank's result into every peer's buffer (split
+//     N: the shard's columns of the peer's Y; split K: this rank's slot of the
+//     peer's slot buffer); its last block releases one arrival on every peer's
+//     data flag (gpu-scope tickets among the blocks, a system-scope release
+//     fence, then a relaxed add on the peer's flag);
+//   * finish: split N waits for every peer's arrival; split K waits, then sums the
+//     ranks' slots in rank order (fixed, so every rank gets identical bits) and
+//     adds the bias once.
+// Every wait spins on the rank's own flag with an acquire load, bounded by about
+// a second of SM clock; a wait that gives up stores MTRTQ_ERR_TIMEOUT in the
+// device status word and returns.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <mutex>
+
+#include "../../include/mtrtq.h"
+#include "q8_common.cuh"
+#include "q8_internal.h"
+
+namespace mtrtq {
+
+// abi.cu: the thread's last-error text and the current device's status word.
+int report_error(int code, const char* fmt, ...);
+int report_cuda_error(cudaError_t e, const char* what);
+unsigned* device_status_address(int* rc);
+
+namespace {
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void red_add_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Spins until *flag >= target (bounded). Returns false (and records a timeout)
+// when it gives up.
+__device__ bool wait_flag(const unsigned* flag, unsigned target, unsigned* status) {
+  const long long t0 = clock64();
+  while ((int)(ld_acquire_sys(flag) - target) < 0) {
+    if (clock64() - t0 > kSpinLimitCycles) {
+      atomicExch(status, 6u /* MTRTQ_ERR_TIMEOUT */);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// A rank's flag words: arrivals at the entry barrier and of peers' data, the push
+// kernel's block tickets, and the epoch of a call whose entry wait gave up (its
+// push is then skipped: no store goes to a peer that may not be there).
+constexpr int kFlagEntry = 0, kFlagData = 1, kFlagTicket = 2, kFlagAbort = 3;
+
+struct ShardPeers {
+  unsigned* flags[MTRTQ_MAX_WORLD];
+  float* dst[MTRTQ_MAX_WORLD];  // where this rank's result goes on each rank (null: skip)
+};
+
+// Entry barrier: one thread signals every peer, then waits for all of them.
+__global__ void shard_entry_kernel(ShardPeers peers, int rank, int world, unsigned target, unsigned epoch,
+                                   unsigned* status) {
+  if (threadIdx.x != 0) return;
+  fence_acq_rel_sys();
+  for (int p = 0; p < world; ++p)
+    if (p != rank) red_add_relaxed_sys(peers.flags[p] + kFlagEntry, 1u);
+  if (!wait_flag(peers.flags[rank] + kFlagEntry, target, status)) peers.flags[rank][kFlagAbort] = epoch;
+}
+
+// Copies src [rows, cols] (row stride lds) to every peer's dst (row stride ldd),
+// then the last block to finish releases one arrival on every peer's data flag.
+// vec: cols, lds, ldd and the pointers allow 16-byte accesses.
+__global__ void shard_push_kernel(const float* src, int64_t lds, int64_t rows, int64_t cols, int64_t ldd,
+                                  ShardPeers peers, int rank, int world, bool vec, unsigned epoch) {
+  __shared__ unsigned s_ticket;
+  if (*reinterpret_cast<volatile unsigned*>(peers.flags[rank] + kFlagAbort) == epoch) return;
+  const int64_t total = rows * cols;
+  if (vec) {
+    const int64_t c4 = cols / 4, total4 = rows * c4;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total4;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t r = e / c4, c = (e - r * c4) * 4;
+      const float4 v = *reinterpret_cast<const float4*>(src + r * lds + c);
+      for (int p = 0; p < world; ++p)
+        if (p != rank && peers.dst[p]) *reinterpret_cast<float4*>(peers.dst[p] + r * ldd + c) = v;
+    }
+  } else {
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t r = e / cols, c = e - r * cols;
+      const float v = src[r * lds + c];
+      for (int p = 0; p < world; ++p)
+        if (p != rank && peers.dst[p]) peers.dst[p][r * ldd + c] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // This block's stores (observed through the barrier) are released with the
+    // ticket; the last block acquires every other block's the same way.
+    fence_acq_rel_sys();
+    s_ticket = atomicAdd(peers.flags[rank] + kFlagTicket, 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && s_ticket == gridDim.x - 1) {
+    fence_acq_rel_sys();
+    peers.flags[rank][kFlagTicket] = 0u;
+    for (int p = 0; p < world; ++p)
+      if (p != rank) red_add_relaxed_sys(peers.flags[p] + kFlagData, 1u);
+  }
+}
+
+__global__ void shard_wait_kernel(const unsigned* flag, unsigned target, unsigned* status) {
+  if (threadIdx.x == 0) wait_flag(flag, target, status);
+}
+
+// Split K: waits for every peer's slot, then y[m, n] = sum over ranks in rank
+// order of slots[r][m][n] (+ bias[n]).
+__global__ void shard_reduce_kernel(const float* slots, int64_t M, int64_t N, int world, const float* bias,
+                                    float* Y, int64_t ldy, const unsigned* flag, unsigned target,
+                                    unsigned* status) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = wait_flag(flag, target, status) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  const int64_t total = M * N;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = e / N, n = e - m * N;
+    float s = 0.0f;
+    for (int r = 0; r < world; ++r) s += __ldcg(slots + (int64_t)r * total + e);
+    if (bias) s = __fadd_rn(s, bias[n]);
+    Y[m * ldy + n] = s;
+  }
+}
+
+int grid_for(int64_t work, int sm_count) {
+  const int64_t g = (work + 255) / 256;
+  const int64_t cap = (int64_t)sm_count * 4;
+  return (int)(g < 1 ? 1 : g > cap ? cap : g);
+}
+
+// Imported peer allocations: the pointer handed out -> the base to close.
+std::mutex g_ipc_mu;
+std::map<void*, void*> g_ipc_bases;
+
+struct IpcHandle {
+  cudaIpcMemHandle_t h;
+  uint64_t offset;
+};
+static_assert(sizeof(IpcHandle) <= MTRTQ_IPC_HANDLE_BYTES, "handle size");
+
+}  // namespace
+
+}  // namespace mtrtq
+
+using namespace mtrtq;
+
+extern "C" {
+
+int mtrtq_shard_range(int64_t extent, int split, int rank, int world, int64_t* begin, int64_t* end) {
+  if (!begin || !end || extent <= 0 || world < 1 || world > MTRTQ_MAX_WORLD || rank < 0 || rank >= world ||
+      (split != MTRTQ_SPLIT_N && split != MTRTQ_SPLIT_K))
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_shard_range: extent > 0, 1 <= world <= 8, 0 <= rank < world, split N or K");
+  const int64_t q = split == MTRTQ_SPLIT_N ? kTileN : kBlockK;
+  const int64_t blocks = (extent + q - 1) / q;
+  const int64_t b0 = (int64_t)rank * blocks / world, b1 = (int64_t)(rank + 1) * blocks / world;
+  *begin = b0 * q < extent ? b0 * q : extent;
+  *end = b1 * q < extent ? b1 * q : extent;
+  return MTRTQ_OK;
+}
+
+int mtrtq_ipc_export(const void* device_ptr, void* handle) {
+  if (!device_ptr || !handle) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_ipc_export: null pointer");
+  void* base = nullptr;
+  // The allocation that holds device_ptr (a caching allocator may hand out an
+  // offset into a larger block): the handle names the block, plus the offset.
+  // cuMemGetAddressRange through the runtime's driver entry point (no libcuda link).
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  if (!get_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return report_error(MTRTQ_ERR_CUDA, "mtrtq_ipc_export: cuMemGetAddressRange unavailable");
+    get_range = reinterpret_cast<GetRange>(fn);
+  }
+  CUdeviceptr b = 0;
+  size_t sz = 0;
+  if (get_range(&b, &sz, reinterpret_cast<CUdeviceptr>(device_ptr)) != CUDA_SUCCESS)
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_ipc_export: not a device allocation");
+  base = reinterpret_cast<void*>(b);
+  IpcHandle h;
+  if (cudaError_t e = cudaIpcGetMemHandle(&h.h, base)) return report_cuda_error(e, "cudaIpcGetMemHandle");
+  h.offset = static_cast<uint64_t>(static_cast<const char*>(device_ptr) - static_cast<const char*>(base));
+  *static_cast<IpcHandle*>(handle) = h;
+  return MTRTQ_OK;
+}
+
+int mtrtq_ipc_import(const void* handle, void** device_ptr) {
+  if (!handle || !device_ptr) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_ipc_import: null pointer");
+  IpcHandle h = *static_cast<const IpcHandle*>(handle);
+  void* base = nullptr;
+  if (cudaError_t e = cudaIpcOpenMemHandle(&base, h.h, cudaIpcMemLazyEnablePeerAccess))
+    return report_cuda_error(e, "cudaIpcOpenMemHandle");
+  void* p = static_cast<char*>(base) + h.offset;
+  std::lock_guard<std::mutex> lk(g_ipc_mu);
+  g_ipc_bases[p] = base;
+  *device_ptr = p;
+  return MTRTQ_OK;
+}
+
+int mtrtq_ipc_close(void* device_ptr) {
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    auto it = g_ipc_bases.find(device_ptr);
+    if (it == g_ipc_bases.end()) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_ipc_close: not an imported pointer");
+    base = it->second;
+    g_ipc_bases.erase(it);
+  }
+  if (cudaError_t e = cudaIpcCloseMemHandle(base)) return report_cuda_error(e, "cudaIpcCloseMemHandle");
+  return MTRTQ_OK;
+}
+
+int64_t mtrtq_shard_slot_bytes(int64_t M, int64_t N, int world) {
+  if (M <= 0 || N <= 0 || world < 1 || world > MTRTQ_MAX_WORLD) return -1;
+  return M * N * world * (int64_t)sizeof(float);
+}
+
+int64_t mtrtq_shard_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int split, int rank,
+                                    int world) {
+  int64_t b = 0, e = 0;
+  if (mtrtq_shard_range(split == MTRTQ_SPLIT_N ? N : K, split, rank, world, &b, &e) != MTRTQ_OK) return -1;
+  if (e <= b) return 0;
+  return split == MTRTQ_SPLIT_N ? mtrtq_workspace_bytes(M, K, e - b, x_dtype, mode)
+                                : mtrtq_workspace_bytes(M, e - b, N, x_dtype, mode);
+}
+
+int mtrtq_matmul_sharded(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                         const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
+                         int split, const mtrtq_shard_comm* comm, unsigned epoch, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (!X || !Y || !comm) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: null pointer");
+  const int rank = comm->rank, world = comm->world;
+  if (world < 1 || world > MTRTQ_MAX_WORLD || rank < 0 || rank >= world)
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: 1 <= world <= 8 and 0 <= rank < world");
+  if (split != MTRTQ_SPLIT_N && split != MTRTQ_SPLIT_K)
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split is MTRTQ_SPLIT_N or MTRTQ_SPLIT_K");
+  if (epoch == 0) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: epoch counts calls from 1");
+  if (M <= 0 || K <= 0 || N <= 0 || ldx < K || ldy < N)
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: positive sizes, ldx >= K, ldy >= N");
+  for (int p = 0; p < world; ++p)
+    if (!comm->flags[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: every rank's flags are needed");
+  int64_t b = 0, e = 0;
+  mtrtq_shard_range(split == MTRTQ_SPLIT_N ? N : K, split, rank, world, &b, &e);
+  if (split == MTRTQ_SPLIT_N) {
+    for (int p = 0; p < world; ++p)
+      if (p != rank && !comm->y[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split N needs every peer's Y");
+  } else {
+    for (int p = 0; p < world; ++p)
+      if (!comm->slots[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split K needs every rank's slots");
+    if (comm->slot_elems < M * N * world)
+      return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: slot buffers hold %lld floats < M * N * world",
+                              (long long)comm->slot_elems);
+  }
+  if (!packed && e > b) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: this rank's shard is not empty");
+  int dev = 0;
+  cudaDeviceProp prop;
+  if (cudaError_t er = cudaGetDevice(&dev)) return report_cuda_error(er, "cudaGetDevice");
+  if (cudaError_t er = cudaGetDeviceProperties(&prop, dev)) return report_cuda_error(er, "cudaGetDeviceProperties");
+  int status_rc = 0;
+  unsigned* status = device_status_address(&status_rc);
+  if (status_rc) return status_rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned target = epoch * (unsigned)(world - 1);
+  const size_t esz = x_dtype == MTRTQ_DTYPE_BF16 ? 2 : 4;
+
+  // 1. this rank's shard, with the single-GPU kernels
+  float* local = nullptr;
+  int64_t lds = 0, cols = 0;
+  if (split == MTRTQ_SPLIT_N) {
+    local = Y + b;
+    lds = ldy;
+    cols = e - b;
+    if (e > b) {
+      if (int rc = mtrtq_matmul(X, x_dtype, ldx, packed, scale, bias ? bias + b : nullptr, local, ldy, M, K, e - b,
+                                mode, workspace, workspace_bytes, stream))
+        return rc;
+    }
+  } else {
+    local = comm->slots[rank] + (int64_t)rank * M * N;
+    lds = N;
+    cols = N;
+    if (e > b) {
+      if (int rc = mtrtq_matmul(static_cast<const char*>(X) + b * esz, x_dtype, ldx, packed, scale, nullptr, local, N,
+                                M, e - b, N, mode, workspace, workspace_bytes, stream))
+        return rc;
+    } else if (cudaError_t er = cudaMemsetAsync(local, 0, (size_t)(M * N) * sizeof(float), st)) {
+      return report_cuda_error(er, "clear an empty shard's partial");
+    }
+  }
+  if (world == 1) {
+    if (split == MTRTQ_SPLIT_K)
+      shard_reduce_kernel<<<grid_for(M * N, prop.multiProcessorCount), 256, 0, st>>>(
+          comm->slots[0], M, N, 1, bias, Y, ldy, comm->flags[0] + kFlagData, 0u, status);
+    if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard reduce launch");
+    return MTRTQ_OK;
+  }
+
+  // 2. entry barrier, 3. push + arrival, 4. wait (+ reduce)
+  ShardPeers peers;
+  for (int p = 0; p < MTRTQ_MAX_WORLD; ++p) {
+    peers.flags[p] = p < world ? comm->flags[p] : nullptr;
+    peers.dst[p] = nullptr;
+    if (p < world && p != rank)
+      peers.dst[p] = split == MTRTQ_SPLIT_N ? (cols > 0 ? comm->y[p] + b : nullptr)
+                                            : comm->slots[p] + (int64_t)rank * M * N;
+  }
+  shard_entry_kernel<<<1, 32, 0, st>>>(peers, rank, world, target, epoch, status);
+  const int64_t ldd = split == MTRTQ_SPLIT_N ? ldy : N;
+  bool vec = cols % 4 == 0 && lds % 4 == 0 && ldd % 4 == 0 && ((uintptr_t)local % 16) == 0;
+  for (int p = 0; p < world; ++p)
+    if (peers.dst[p] && ((uintptr_t)peers.dst[p] % 16) != 0) vec = false;
+  shard_push_kernel<<<grid_for(cols > 0 ? M * cols / (vec ? 4 : 1) : 1, prop.multiProcessorCount), 256, 0, st>>>(
+      local, lds, cols > 0 ? M : 0, cols, ldd, peers, rank, world, vec, epoch);
+  if (split == MTRTQ_SPLIT_N) {
+    shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[rank] + kFlagData, target, status);
+  } else {
+    shard_reduce_kernel<<<grid_for(M * N, prop.multiProcessorCount), 256, 0, st>>>(
+        comm->slots[rank], M, N, world, bias, Y, ldy, comm->flags[rank] + kFlagData, target, status);
+  }
+  if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard exchange launch");
+  return MTRTQ_OK;
+}
+
+}  // extern "C"

@@ -14,9 +14,13 @@ independent and k partial sums add:
   reference's separate Add does (src/ops/kernels_elementwise.cpp:31-35). K_r are
   whole 64-k units, which keeps every shard's X view 16-byte aligned.
 
-One process per GPU; the collectives are torch.distributed's (NCCL on GPUs).
-The local product is libmtrtq's matmul_q8; a caller may pass another
-`local_matmul` with the same signature (the CPU tests pass the oracle).
+Two implementations of the exchange:
+* ShardedMatMulQ: torch.distributed collectives (NCCL on GPUs, gloo in the CPU
+  tests); the local product is libmtrtq's matmul_q8, or another `local_matmul`
+  with the same signature (the CPU tests pass the oracle);
+* P2PShardedMatMulQ: mtrtq_matmul_sharded, the library's own kernels over peer
+  memory (every rank's output or slot buffer and flag words opened in every
+  process through CUDA IPC at set-up; no collective library on the data path).
 """
 from __future__ import annotations
 
@@ -138,3 +142,142 @@ class ShardedMatMulQ:
         y = y.contiguous()
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
+
+
+def shard_range(extent: int, split: str, rank: int, world: int) -> tuple[int, int]:
+    """mtrtq_shard_range: [begin, end) of rank's shard (128-channel tiles for "N",
+    64-k units for "K")."""
+    import ctypes
+    from . import _lib
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    _lib.check(_lib.lib().mtrtq_shard_range(extent, _lib.SPLIT_N if split == "N" else _lib.SPLIT_K, rank, world,
+                                            ctypes.byref(b), ctypes.byref(e)), "mtrtq_shard_range")
+    return b.value, e.value
+
+
+class P2PShardedMatMulQ:
+    """Y = MatMulQ(X, W, scale) (+ bias) split across the ranks of a process group,
+    one GPU each, exchanged by mtrtq_matmul_sharded over peer memory.
+
+    Set-up (collective over `group`): each rank packs its shard, allocates its
+    output buffer [max_m, N] (split N) or slot buffer [world, max_m, N] (split K)
+    and 64 bytes of flag words, exports their IPC handles, gathers every rank's
+    handles (torch.distributed object all-gather) and opens the peers'. A call
+    returns a view of this rank's output buffer, the full Y [M, N], valid until
+    the next call."""
+
+    def __init__(self, q: np.ndarray, scale: np.ndarray, bias: np.ndarray | None = None, split: str = "N",
+                 group=None, device=None, mode: str = "bf16", max_m: int = 8, x_dtype=torch.float32):
+        import ctypes
+        from . import _lib
+        from .matmulq import PackedWeight
+        if split not in ("N", "K"):
+            raise ValueError("split must be 'N' or 'K'")
+        self.lib = _lib.lib()
+        self._lib = _lib
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if self.world > _lib.MAX_WORLD:
+            raise ValueError(f"at most {_lib.MAX_WORLD} ranks")
+        self.split, self.mode, self.max_m, self.x_dtype = split, mode, max_m, x_dtype
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        K, N = q.shape
+        self.K, self.N = K, N
+        b, e = shard_range(N if split == "N" else K, split, self.rank, self.world)
+        self.begin, self.end = b, e
+        if e > b:
+            qs = q[:, b:e] if split == "N" else q[b:e, :]
+            ss = scale[b:e] if split == "N" else scale
+            self.w = PackedWeight.from_int8(torch.from_numpy(np.ascontiguousarray(qs)),
+                                            torch.from_numpy(np.ascontiguousarray(ss)), self.device)
+        else:
+            self.w = None
+        self.bias = torch.from_numpy(np.ascontiguousarray(bias)).to(self.device) if bias is not None else None
+        self.flags = torch.zeros(_lib.SHARD_FLAG_BYTES // 4, dtype=torch.int32, device=self.device)
+        if split == "N":
+            self.buf = torch.zeros((max_m, N), dtype=torch.float32, device=self.device)
+        else:
+            self.buf = torch.zeros((self.world, max_m, N), dtype=torch.float32, device=self.device)
+        xd = _lib.DTYPE_BF16 if x_dtype == torch.bfloat16 else _lib.DTYPE_F32
+        from .matmulq import MODES
+        self._xd, self._mode = xd, MODES[mode]
+        ws = self.lib.mtrtq_shard_workspace_bytes(max_m, K, N, xd, self._mode,
+                                                  _lib.SPLIT_N if split == "N" else _lib.SPLIT_K, self.rank,
+                                                  self.world)
+        if ws < 0:
+            raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_shard_workspace_bytes", _lib.last_error())
+        self.ws = torch.zeros(max(ws, 256), dtype=torch.uint8, device=self.device)
+        torch.cuda.synchronize(self.device)
+        # exchange the buffers' and flags' IPC handles
+        mine = []
+        for t in (self.buf, self.flags):
+            h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+            with torch.cuda.device(self.device):
+                _lib.check(self.lib.mtrtq_ipc_export(t.data_ptr(), h), "mtrtq_ipc_export")
+            mine.append(bytes(h))
+        allh = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        self.imported = []
+        comm = _lib.ShardComm()
+        comm.rank, comm.world = self.rank, self.world
+        comm.slot_elems = self.buf.numel() if split == "K" else 0
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs = [self.buf.data_ptr(), self.flags.data_ptr()]
+            else:
+                ptrs = []
+                for hb in allh[r]:
+                    p = ctypes.c_void_p()
+                    h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(hb)
+                    with torch.cuda.device(self.device):
+                        _lib.check(self.lib.mtrtq_ipc_import(h, ctypes.byref(p)), "mtrtq_ipc_import")
+                    self.imported.append(p.value)
+                    ptrs.append(p.value)
+            if split == "N":
+                comm.y[r] = ptrs[0]
+            else:
+                comm.slots[r] = ptrs[0]
+            comm.flags[r] = ptrs[1]
+        self.comm = comm
+        self.epoch = 0
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def __call__(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """x: [M, K] (M <= max_m), the same on every rank. Returns this rank's full Y
+        [M, N] (a view of its buffer, valid until the next call)."""
+        import ctypes
+        _lib = self._lib
+        M = x.shape[0]
+        if x.dim() != 2 or x.shape[1] != self.K or x.stride(1) != 1 or M > self.max_m or x.dtype != self.x_dtype:
+            raise ValueError(f"x must be [M <= {self.max_m}, {self.K}] {self.x_dtype} with unit stride along K")
+        self.epoch += 1
+        if self.split == "N":
+            y = self.buf[:M]
+        else:
+            y = torch.empty((M, self.N), dtype=torch.float32, device=self.device) if not hasattr(self, "_y") \
+                or self._y.shape[0] < M else self._y
+            self._y = y
+            y = y[:M]
+        if self.split == "K":
+            self.comm.slot_elems = self.buf.numel()
+        sp = (stream.cuda_stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream)
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.mtrtq_matmul_sharded(
+                x.data_ptr(), self._xd, x.stride(0), self.w.packed.data_ptr() if self.w is not None else None,
+                self.w.scale.data_ptr() if self.w is not None else None,
+                self.bias.data_ptr() if self.bias is not None else None, y.data_ptr(), y.stride(0), M, self.K,
+                self.N, self._mode, _lib.SPLIT_N if self.split == "N" else _lib.SPLIT_K, ctypes.byref(self.comm),
+                self.epoch, self.ws.data_ptr(), self.ws.numel(), sp), "mtrtq_matmul_sharded")
+        return y
+
+    def close(self):
+        """Closes the peers' buffers (set-up's counterpart)."""
+        for p in self.imported:
+            with torch.cuda.device(self.device):
+                self.lib.mtrtq_ipc_close(p)
+        self.imported = []

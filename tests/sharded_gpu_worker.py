@@ -1,6 +1,8 @@
-"""One rank of the two-GPU sharded MatMulQ test (launched by torch.distributed.run
-from tests/test_sharded.py). Checks the full Y of every case against the oracle and
-prints SHARDED OK."""
+"""One rank of the multi-GPU sharded MatMulQ test (launched by torch.distributed.run
+from tests/test_sharded.py). Checks the full Y of every case against the oracle,
+through the NCCL path (ShardedMatMulQ) and the library's own peer-memory exchange
+(P2PShardedMatMulQ, several calls in a row with new activations each), and prints
+SHARDED OK."""
 import datetime
 import os
 import sys
@@ -38,6 +40,25 @@ def main():
             err = rel_err(y[rows], ref)
             assert np.isfinite(y).all(), f"case {i}: non-finite output"
             assert err <= 1e-4, f"rank {rank} case {i} ({split}, {M}x{K}x{N}): rel err {err:.3e}"
+        for i, (split, M, K, N) in enumerate(CASES):
+            W = wl.weights(K, N, 400 + i)
+            q, s = oracle.quantize_per_channel(W)
+            b = wl.bias(N, 500 + i)
+            op = sharded.P2PShardedMatMulQ(q, s, b, split=split, mode="fp32", max_m=M)
+            rows = np.unique(np.linspace(0, M - 1, min(M, 8)).astype(np.int64))
+            for call in range(3):  # epochs 1..3: the entry barrier guards each call's buffers
+                X = wl.activations(M, K, 600 + 10 * i + call)
+                y = op(torch.from_numpy(X).cuda()).cpu().numpy()
+                assert np.isfinite(y).all(), f"p2p case {i} call {call}: non-finite output"
+                err = rel_err(y[rows], oracle.matmul_q8_rows(X, q, s, rows, b))
+                assert err <= 1e-4, f"rank {rank} p2p case {i} call {call} ({split}, {M}x{K}x{N}): {err:.3e}"
+                # every rank holds the same bits (N: the same columns; K: sums in rank order)
+                t = torch.from_numpy(y).cuda()
+                allt = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+                dist.all_gather(allt, t)
+                assert all(torch.equal(allt[0], a) for a in allt), f"p2p case {i}: ranks disagree"
+            torch.cuda.synchronize()
+            op.close()
         torch.cuda.synchronize()
         assert matmulq.read_device_status() == 0
         print("SHARDED OK", flush=True)

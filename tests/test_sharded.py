@@ -114,3 +114,49 @@ def test_sharded_on_two_gpus():
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("SHARDED OK") == 2, r.stdout[-3000:]
+
+
+@pytest.mark.parametrize("extent,world", [(50257, 2), (50257, 8), (768, 3), (100, 8), (14336, 4), (1, 1)])
+def test_abi_shard_range_matches_host_split(extent, world):
+    """mtrtq_shard_range (the C ABI's split) is the host split the NCCL path uses."""
+    for split, quantum in (("N", sharded.TILE_N), ("K", sharded.UNIT_K)):
+        want = sharded.shard_ranges(extent, world, quantum)
+        got = [sharded.shard_range(extent, split, r, world) for r in range(world)]
+        assert got == want
+
+
+def test_sharded_abi_argument_errors():
+    import ctypes
+    from mini_tensorrt_b200 import _lib
+    lib = _lib.lib()
+    comm = _lib.ShardComm()
+    comm.rank, comm.world = 0, 2
+    x = (ctypes.c_float * 64)()
+    call = lambda c, epoch=1, split=_lib.SPLIT_N: lib.mtrtq_matmul_sharded(
+        x, 0, 8, x, x, None, x, 8, 1, 8, 8, 1, split, ctypes.byref(c), epoch, None, 0, None)
+    assert call(comm) == _lib.ERR_INVALID_ARG                      # no flags
+    assert "flags" in _lib.last_error()
+    assert call(comm, epoch=0) == _lib.ERR_INVALID_ARG             # epochs count from 1
+    comm.world = 9
+    assert call(comm) == _lib.ERR_INVALID_ARG
+    assert lib.mtrtq_matmul_sharded(x, 0, 8, x, x, None, x, 8, 1, 8, 8, 1, 0, None, 1, None, 0, None) \
+        == _lib.ERR_INVALID_ARG
+    assert lib.mtrtq_shard_slot_bytes(4, 10, 2) == 4 * 10 * 2 * 4
+    assert lib.mtrtq_shard_slot_bytes(4, 10, 9) == -1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("split", ["N", "K"])
+def test_p2p_sharded_single_rank(cuda_device, split):
+    """mtrtq_matmul_sharded with one rank (no process group): the local product and,
+    for split K, the slot reduction, against the oracle."""
+    M, K, N = 5, 768, 3000
+    W = wl.weights(K, N, 31)
+    q, s = oracle.quantize_per_channel(W)
+    b = wl.bias(N, 32)
+    op = sharded.P2PShardedMatMulQ(q, s, b, split=split, mode="fp32", max_m=8, device=cuda_device)
+    for call in range(2):
+        X = wl.activations(M, K, 33 + call)
+        y = op(torch.from_numpy(X).to(cuda_device)).cpu().numpy()
+        assert rel_err(y, oracle.matmul_q8(X, q, s, b)) <= 1e-4
+    op.close()
