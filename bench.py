@@ -21,9 +21,12 @@ each call's activations and device->host copy of each output inside the timed
 region. Secondary lines: the prefill tensor-core GEMM (TFLOP/s) at the large
 shapes, and the single-op FFN-up case.
 
-Multi-GPU (torchrun, one process per GPU): each rank runs its own full decode
-GEMV set (data-parallel replicas of the path, no collective on the data path);
-value = all ranks' bytes / the max over ranks of the timed region.
+Multi-GPU (torchrun, one process per GPU): the same decode GEMV set strong-scaled
+over the ranks (each call's output channels split per rank, one grouped launch of
+the shards, one all-gather of the outputs through peer memory by the library's
+own kernels); value = the set's bytes per step x steps / the max over ranks of
+the timed region. --multi replicas: each rank its own full set (weak scaling);
+that figure is also kept in the sharded line's method.replicas.
 
 --impl reference: the reference's own CPU MatMulQ (oracle/_ref, compiled from
 its sources) on the same workload, every call split into row x column-chunk
@@ -78,6 +81,9 @@ def parse():
                          "4 cluster GEMV")
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch every call only after the previous one has finished")
+    ap.add_argument("--multi", choices=["sharded", "replicas"], default="sharded",
+                    help="N > 1: the decode set column-sharded over the ranks (strong scaling, default) or "
+                         "one full set per rank (replicas)")
     ap.add_argument("--step-launch", choices=["group", "hybrid", "calls"], default="group",
                     help="decode set: one grouped launch per step (default); hybrid: the eight smaller "
                          "calls grouped and the two LM heads as their own launches; calls: a launch per call")
@@ -417,6 +423,90 @@ def run_ours(args, torch, rank, world, dev, dist):
         "clocks": clk.summary(),
     }
     return line, calls, stream
+
+
+def run_sharded_decode_set(args, torch, rank, world, dev, dist):
+    """The decode GEMV set strong-scaled over the ranks: every call's output
+    channels split into whole 128-channel tiles per rank (mtrtq_shard_range), a
+    step = one grouped launch of this rank's shards writing straight into its copy
+    of the outputs, then one all-gather of every rank's output segments through
+    peer memory (mtrtq_shard_allgather), so that every rank ends the step with all
+    ten full outputs. Both launches are captured in one CUDA graph per weight
+    rotation (the exchange counts its epochs on the device). value = the unsplit
+    step's algorithmic bytes x steps / the max over ranks of the timed region."""
+    from mini_tensorrt_b200 import _lib, matmulq, sharded, workloads as wl
+    hbm_peak, _, _, peak_kind = peaks()
+    matmulq.set_option(_lib.OPT_OVERLAP_LAUNCH, 0 if args.no_overlap else 1)
+    shapes = [(M, name, K, N) for M in wl.DECODE_M for name, K, N in wl.DECODE_SHAPES]
+    y_elems = sum(M * N for M, _, _, N in shapes)
+    peers = sharded.PeerBuffers(y_elems, 0, device=dev, device_epochs=True)
+    calls, off, step_bytes, my_bytes = [], 0, 0, 0
+    for M, name, K, N in shapes:
+        n0, n1 = sharded.shard_range(N, "N", rank, world)
+        c = {"name": name, "M": M, "K": K, "N": N, "n0": n0, "n1": n1, "off": off,
+             "y": peers.y[off:off + M * N].view(M, N),
+             "x": torch.from_numpy(wl.activations(M, K, wl.shape_seed("x:" + name, M, K))).to(dev)}
+        step_bytes += wl.algorithmic_bytes(M, K, N, 4)
+        if n1 > n0:
+            q, s = matmulq.quantize_per_channel(wl.decode_weight(name, K, N))
+            base = matmulq.PackedWeight.from_int8(torch.from_numpy(np.ascontiguousarray(q[:, n0:n1])),
+                                                  torch.from_numpy(np.ascontiguousarray(s[n0:n1])), dev)
+            c["w"] = [base] + [matmulq.PackedWeight(base.packed.clone(), base.scale.clone(), K, n1 - n0)
+                               for _ in range(WEIGHT_COPIES - 1)]
+            my_bytes += K * (n1 - n0)
+        calls.append(c)
+        off += M * N
+    mine = [c for c in calls if c["n1"] > c["n0"]]
+    segments = [(c["off"] + c["n0"], c["M"], c["n1"] - c["n0"], c["N"]) for c in mine]
+    groups = [matmulq.GemvGroup([{"x": c["x"], "w": c["w"][(g + i) % WEIGHT_COPIES],
+                                  "out": c["y"][:, c["n0"]:c["n1"]]} for i, c in enumerate(mine)], mode=args.mode)
+              for g in range(WEIGHT_COPIES)]
+    stream = torch.cuda.Stream(dev)
+
+    def one(g):
+        groups[g](stream)
+        peers.allgather(segments, stream=stream)
+
+    graphs = []
+    with torch.cuda.stream(stream):
+        one(0)
+        torch.cuda.synchronize()
+        for g in range(WEIGHT_COPIES):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                one(g)
+            graphs.append(graph)
+    torch.cuda.synchronize()
+    dist.barrier()
+    with ClockSampler(dev.index) as clk:
+        dist.barrier()
+        secs = time_graphs(torch, graphs, args.steps, args.warmup, stream)
+        dist.barrier()
+    t = torch.tensor([secs], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    secs = float(t.item())
+    assert matmulq.read_device_status() == 0, "a device wait timed out"
+    # every rank holds the full outputs: check them against this rank's own
+    # unsplit product of the last step's weights (sampled rows of each call)
+    for c in calls:
+        full_q, full_s = matmulq.quantize_per_channel(wl.decode_weight(c["name"], c["K"], c["N"]))
+        pw = matmulq.PackedWeight.from_int8(torch.from_numpy(full_q), torch.from_numpy(full_s), dev)
+        ref = matmulq.matmul_q8(c["x"], pw, mode=args.mode)
+        torch.cuda.synchronize()
+        err = float((c["y"] - ref).abs().max() / ref.abs().max())
+        assert err <= 1e-4, f"sharded step output {c['name']}/M{c['M']} differs from the unsplit product: {err:.3e}"
+    step_us = secs / args.steps * 1e6
+    exch_bytes = sum(c["M"] * c["N"] * 4 for c in calls) * (world - 1) / world  # each rank receives
+    line = {"value": round(step_bytes * args.steps / secs / 1e9, 1), "ms_per_step": round(step_us / 1e3, 4),
+            "scaling": "strong", "clocks": clk.summary(),
+            "rank0_weight_bytes_per_step": my_bytes,
+            "exchange": {"how": "mtrtq_shard_allgather: entry barrier, peer stores, bounded wait (library kernels)",
+                         "bytes_received_per_rank_per_step": int(exch_bytes),
+                         "nvlink_lower_bound_us": round(exch_bytes / 770e9 * 1e6, 3)},
+            "gpu_launches": 4 * args.steps}
+    del graphs
+    peers.close()
+    return line
 
 
 def run_e2e_group(torch, calls, args, dev, stream, dist, world):
@@ -984,9 +1074,26 @@ def main():
         if rank == 0:
             print(json.dumps(line))
         return
+    sharded_line = None
+    if world > 1 and args.multi == "sharded":
+        sharded_line = run_sharded_decode_set(args, torch, rank, world, dev, dist)
+        torch.cuda.empty_cache()
     line, calls, stream = run_ours(args, torch, rank, world, dev, dist)
     del calls
     torch.cuda.empty_cache()
+    if sharded_line is not None:
+        # headline: the strong-scaled decode set; the replicas (each rank its own
+        # full set, no exchange) stay as a secondary figure
+        replicas = {k: line[k] for k in ("value", "ms_per_step", "roofline", "e2e", "gpu_launches")}
+        replicas["scaling"] = "weak"
+        line.update({k: v for k, v in sharded_line.items() if k != "rank0_weight_bytes_per_step"})
+        line["config"]["parallelism"] = f"column-sharded x{world} (strong scaling, peer-memory all-gather)"
+        line["method"]["step_launch"] = ("per rank: one mtrtq_gemv_group launch over its column shards, then "
+                                         "mtrtq_shard_allgather of the output segments; one CUDA graph per step")
+        line["method"]["replicas"] = replicas
+        line["roofline"]["scope"] = "the grouped GEMV on one full set (measured in the replicas run)"
+        line["e2e"]["scope"] = "replicas: each rank its own full set through the grouped API with host buffers"
+        line["method"]["rank0_weight_bytes_per_step"] = sharded_line["rank0_weight_bytes_per_step"]
     if rank == 0 and world == 1 and not args.no_extras:
         line["extras"] = run_extras(torch, dev, args, stream)
         line["extras"]["gpt2_small_decode"] = run_gpt2_decode(args, torch, dev, mode="fp32")

@@ -304,12 +304,37 @@ int64_t mtrtq_shard_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype
 /* Y (every rank) = X x dequant(W) (+ bias). X: the full [M, K] on every rank;
  * packed/scale: this rank's shard (packed as an unsplit weight of the shard's
  * shape; NULL for an empty shard); bias: the full [N] or NULL. epoch: 1 for the
- * first call on these flags, then +1 per call (every rank the same). Calls on the
- * same comm must be ordered on one stream per rank. */
+ * first exchange on these flags, then +1 per exchange (every rank the same); or 0
+ * for every call, and the count is kept on the device (the calls can then be
+ * captured in a CUDA graph and replayed); do not mix the two on the same flags.
+ * Calls on the same comm must be ordered on one stream per rank. */
 int mtrtq_matmul_sharded(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                          const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
                          int split, const mtrtq_shard_comm* comm, unsigned epoch, void* workspace,
                          size_t workspace_bytes, void* stream);
+/* The exchange steps on their own, for callers that compute their shards
+ * themselves (a tensor-parallel layer keeps column-parallel outputs sharded and
+ * reduces only after the row-parallel product). Each call has the entry barrier
+ * and bounded waits described above, and counts as one epoch.
+ * mtrtq_shard_allgather: for each segment (rows x cols floats at `offset` from
+ * the buffer base, row stride ld), this rank's part of the buffers comm->y is
+ * stored into the same place of every peer's buffer; each rank passes the
+ * segments it owns (at most 16), and every rank's buffer then holds all of them.
+ * mtrtq_shard_allreduce: `partial` [M, N] (row stride N; best placed at this
+ * rank's slot, comm->slots[rank] + mtrtq_shard_slot_offset(rank, M, N), which
+ * saves a copy) goes to this rank's slot of every rank's slot buffer; then
+ * Y = sum of the slots in rank order (+ bias[N]) (+ residual, which may be Y),
+ * the same bits on every rank. */
+typedef struct mtrtq_shard_segment {
+  int64_t offset, rows, cols, ld;
+} mtrtq_shard_segment;
+int mtrtq_shard_allgather(const mtrtq_shard_segment* segments, int count, const mtrtq_shard_comm* comm,
+                          unsigned epoch, void* stream);
+int mtrtq_shard_allreduce(const float* partial, const float* bias, const float* residual, int64_t ldr, float* Y,
+                          int64_t ldy, int64_t M, int64_t N, const mtrtq_shard_comm* comm, unsigned epoch,
+                          void* stream);
+int64_t mtrtq_shard_slot_offset(int rank, int64_t M, int64_t N);
+
 /* Peer pointers across processes: mtrtq_ipc_export writes MTRTQ_IPC_HANDLE_BYTES
  * naming the device allocation that holds device_ptr (and the offset into it);
  * another process's mtrtq_ipc_import opens it (peer access enabled) and returns

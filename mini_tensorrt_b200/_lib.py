@@ -99,6 +99,14 @@ SIGNATURES["mtrtq_shard_slot_bytes"] = (_i64, [_i64, _i64, _int])
 SIGNATURES["mtrtq_shard_workspace_bytes"] = (_i64, [_i64, _i64, _i64, _int, _int, _int, _int, _int])
 SIGNATURES["mtrtq_matmul_sharded"] = (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int,
                                              _int, _vp, ctypes.c_uint, _vp, _sz, _vp])
+class ShardSegment(ctypes.Structure):
+    """mtrtq_shard_segment (include/mtrtq.h)."""
+    _fields_ = [("offset", _i64), ("rows", _i64), ("cols", _i64), ("ld", _i64)]
+
+
+SIGNATURES["mtrtq_shard_allgather"] = (_int, [_vp, _int, _vp, ctypes.c_uint, _vp])
+SIGNATURES["mtrtq_shard_allreduce"] = (_int, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, ctypes.c_uint, _vp])
+SIGNATURES["mtrtq_shard_slot_offset"] = (_i64, [_int, _i64, _i64])
 SIGNATURES["mtrtq_ipc_export"] = (_int, [_vp, _vp])
 SIGNATURES["mtrtq_ipc_import"] = (_int, [_vp, _vp])
 SIGNATURES["mtrtq_ipc_close"] = (_int, [_vp])

@@ -68,47 +68,67 @@ __device__ bool wait_flag(const unsigned* flag, unsigned target, unsigned* statu
 // A rank's flag words: arrivals at the entry barrier and of peers' data, the push
 // kernel's block tickets, and the epoch of a call whose entry wait gave up (its
 // push is then skipped: no store goes to a peer that may not be there).
-constexpr int kFlagEntry = 0, kFlagData = 1, kFlagTicket = 2, kFlagAbort = 3;
+constexpr int kFlagEntry = 0, kFlagData = 1, kFlagTicket = 2, kFlagAbort = 3, kFlagEpoch = 4;
+
+// The call's epoch: the caller's, or -- epoch 0 -- the rank's device-side count,
+// which the entry kernel advances (so that a captured graph replays correctly).
+__device__ __forceinline__ unsigned call_epoch(unsigned* own_flags, unsigned epoch) {
+  return epoch != 0 ? epoch : *reinterpret_cast<volatile unsigned*>(own_flags + kFlagEpoch);
+}
 
 struct ShardPeers {
   unsigned* flags[MTRTQ_MAX_WORLD];
-  float* dst[MTRTQ_MAX_WORLD];  // where this rank's result goes on each rank (null: skip)
+  float* dst[MTRTQ_MAX_WORLD];  // each rank's destination base (null: not pushed to)
+};
+
+// Pieces of a rank's result to push: segment k is the rows x cols block at
+// float offset off[k] (row stride ld[k]) from the source base, and goes to the same
+// offset from every peer's destination base.
+constexpr int kMaxSegs = 16;
+struct SegList {
+  int count;
+  int64_t off[kMaxSegs], rows[kMaxSegs], cols[kMaxSegs], ld[kMaxSegs];
+  int64_t first[kMaxSegs + 1];  // prefix of the segments' work items
+  bool vec[kMaxSegs];           // 16-byte items (off, cols, ld multiples of 4)
 };
 
 // Entry barrier: one thread signals every peer, then waits for all of them.
-__global__ void shard_entry_kernel(ShardPeers peers, int rank, int world, unsigned target, unsigned epoch,
-                                   unsigned* status) {
+__global__ void shard_entry_kernel(ShardPeers peers, int rank, int world, unsigned epoch, unsigned* status) {
   if (threadIdx.x != 0) return;
+  if (epoch == 0) {
+    epoch = peers.flags[rank][kFlagEpoch] + 1;
+    peers.flags[rank][kFlagEpoch] = epoch;
+  }
+  const unsigned target = epoch * (unsigned)(world - 1);
   fence_acq_rel_sys();
   for (int p = 0; p < world; ++p)
     if (p != rank) red_add_relaxed_sys(peers.flags[p] + kFlagEntry, 1u);
   if (!wait_flag(peers.flags[rank] + kFlagEntry, target, status)) peers.flags[rank][kFlagAbort] = epoch;
 }
 
-// Copies src [rows, cols] (row stride lds) to every peer's dst (row stride ldd),
-// then the last block to finish releases one arrival on every peer's data flag.
-// vec: cols, lds, ldd and the pointers allow 16-byte accesses.
-__global__ void shard_push_kernel(const float* src, int64_t lds, int64_t rows, int64_t cols, int64_t ldd,
-                                  ShardPeers peers, int rank, int world, bool vec, unsigned epoch) {
+// Stores every segment of src into every peer's destination, then the last block
+// to finish releases one arrival on every peer's data flag.
+__global__ void shard_push_kernel(const float* src, SegList segs, ShardPeers peers, int rank, int world,
+                                  unsigned epoch) {
   __shared__ unsigned s_ticket;
+  epoch = call_epoch(peers.flags[rank], epoch);
   if (*reinterpret_cast<volatile unsigned*>(peers.flags[rank] + kFlagAbort) == epoch) return;
-  const int64_t total = rows * cols;
-  if (vec) {
-    const int64_t c4 = cols / 4, total4 = rows * c4;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total4;
-         e += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t r = e / c4, c = (e - r * c4) * 4;
-      const float4 v = *reinterpret_cast<const float4*>(src + r * lds + c);
+  const int64_t total = segs.first[segs.count];
+  int k = 0;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    while (e >= segs.first[k + 1]) ++k;  // items ascend within a thread
+    const int64_t i = e - segs.first[k];
+    if (segs.vec[k]) {
+      const int64_t c4 = segs.cols[k] / 4, r = i / c4, o = segs.off[k] + r * segs.ld[k] + (i - r * c4) * 4;
+      const float4 v = *reinterpret_cast<const float4*>(src + o);
       for (int p = 0; p < world; ++p)
-        if (p != rank && peers.dst[p]) *reinterpret_cast<float4*>(peers.dst[p] + r * ldd + c) = v;
-    }
-  } else {
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-         e += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t r = e / cols, c = e - r * cols;
-      const float v = src[r * lds + c];
+        if (p != rank && peers.dst[p]) *reinterpret_cast<float4*>(peers.dst[p] + o) = v;
+    } else {
+      const int64_t r = i / segs.cols[k], o = segs.off[k] + r * segs.ld[k] + (i - r * segs.cols[k]);
+      const float v = src[o];
       for (int p = 0; p < world; ++p)
-        if (p != rank && peers.dst[p]) peers.dst[p][r * ldd + c] = v;
+        if (p != rank && peers.dst[p]) peers.dst[p][o] = v;
     }
   }
   __syncthreads();
@@ -127,17 +147,19 @@ __global__ void shard_push_kernel(const float* src, int64_t lds, int64_t rows, i
   }
 }
 
-__global__ void shard_wait_kernel(const unsigned* flag, unsigned target, unsigned* status) {
-  if (threadIdx.x == 0) wait_flag(flag, target, status);
+__global__ void shard_wait_kernel(unsigned* own_flags, int world, unsigned epoch, unsigned* status) {
+  if (threadIdx.x == 0) wait_flag(own_flags + kFlagData, call_epoch(own_flags, epoch) * (unsigned)(world - 1), status);
 }
 
 // Split K: waits for every peer's slot, then y[m, n] = sum over ranks in rank
-// order of slots[r][m][n] (+ bias[n]).
+// order of slots[r][m][n] (+ bias[n]) (+ residual[m, n], which may be Y).
 __global__ void shard_reduce_kernel(const float* slots, int64_t M, int64_t N, int world, const float* bias,
-                                    float* Y, int64_t ldy, const unsigned* flag, unsigned target,
-                                    unsigned* status) {
+                                    const float* residual, int64_t ldr, float* Y, int64_t ldy, unsigned* own_flags,
+                                    unsigned epoch, unsigned* status) {
   __shared__ int s_ok;
-  if (threadIdx.x == 0) s_ok = wait_flag(flag, target, status) ? 1 : 0;
+  if (threadIdx.x == 0)
+    s_ok = world == 1 || wait_flag(own_flags + kFlagData, call_epoch(own_flags, epoch) * (unsigned)(world - 1), status)
+               ? 1 : 0;
   __syncthreads();
   if (!s_ok) return;
   const int64_t total = M * N;
@@ -147,8 +169,38 @@ __global__ void shard_reduce_kernel(const float* slots, int64_t M, int64_t N, in
     float s = 0.0f;
     for (int r = 0; r < world; ++r) s += __ldcg(slots + (int64_t)r * total + e);
     if (bias) s = __fadd_rn(s, bias[n]);
+    if (residual) s = __fadd_rn(residual[m * ldr + n], s);
     Y[m * ldy + n] = s;
   }
+}
+
+int grid_for(int64_t work, int sm_count);
+
+// Entry barrier, then the push of `segs` from src to every peer's dst base.
+cudaError_t launch_exchange(const float* src, const SegList& segs, ShardPeers peers, int rank, int world,
+                            unsigned epoch, unsigned* status, int sm_count, cudaStream_t st) {
+  shard_entry_kernel<<<1, 32, 0, st>>>(peers, rank, world, epoch, status);
+  int64_t items = segs.first[segs.count];
+  shard_push_kernel<<<grid_for(items > 0 ? items : 1, sm_count), 256, 0, st>>>(src, segs, peers, rank, world, epoch);
+  return cudaGetLastError();
+}
+
+// Whether src and every destination base allow 16-byte accesses.
+bool bases_aligned(const float* src, const float* const* bases, int world) {
+  if ((uintptr_t)src % 16) return false;
+  for (int p = 0; p < world; ++p)
+    if (bases[p] && (uintptr_t)bases[p] % 16) return false;
+  return true;
+}
+
+void seg_add(SegList& s, int64_t off, int64_t rows, int64_t cols, int64_t ld, bool base_aligned) {
+  const int k = s.count++;
+  s.off[k] = off;
+  s.rows[k] = rows;
+  s.cols[k] = cols;
+  s.ld[k] = ld;
+  s.vec[k] = base_aligned && off % 4 == 0 && cols % 4 == 0 && ld % 4 == 0;
+  s.first[k + 1] = s.first[k] + rows * (s.vec[k] ? cols / 4 : cols);
 }
 
 int grid_for(int64_t work, int sm_count) {
@@ -255,101 +307,166 @@ int64_t mtrtq_shard_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype
                                 : mtrtq_workspace_bytes(M, e - b, N, x_dtype, mode);
 }
 
+// Checks a comm; *sm_count and *status receive the device's SM count and status word.
+static int check_comm(const mtrtq_shard_comm* comm, unsigned epoch, int* sm_count, unsigned** status) {
+  if (!comm) return report_error(MTRTQ_ERR_INVALID_ARG, "null comm");
+  if (comm->world < 1 || comm->world > MTRTQ_MAX_WORLD || comm->rank < 0 || comm->rank >= comm->world)
+    return report_error(MTRTQ_ERR_INVALID_ARG, "1 <= world <= 8 and 0 <= rank < world");
+  for (int p = 0; p < comm->world; ++p)
+    if (!comm->flags[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "every rank's flags are needed");
+  int rc = 0;
+  *status = device_status_address(&rc);
+  if (rc) return rc;
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return report_cuda_error(e, "cudaGetDevice");
+  if (cudaError_t e = cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, dev))
+    return report_cuda_error(e, "cudaDeviceGetAttribute");
+  return MTRTQ_OK;
+}
+
+static ShardPeers peers_of(const mtrtq_shard_comm* comm, float* const* bases, int64_t base_offset) {
+  ShardPeers peers;
+  for (int p = 0; p < MTRTQ_MAX_WORLD; ++p) {
+    peers.flags[p] = p < comm->world ? comm->flags[p] : nullptr;
+    peers.dst[p] = (p < comm->world && p != comm->rank && bases[p]) ? bases[p] + base_offset : nullptr;
+  }
+  return peers;
+}
+
+// Split K's second half: every rank's slot r of `slots` holds rank r's partial
+// [M, N]; this rank's is pushed to every peer, then Y = sum in rank order
+// (+ bias) (+ residual).
+static int exchange_reduce(const mtrtq_shard_comm* comm, unsigned epoch, int64_t M, int64_t N, const float* bias,
+                           const float* residual, int64_t ldr, float* Y, int64_t ldy, int sm_count, unsigned* status,
+                           cudaStream_t st) {
+  const int rank = comm->rank, world = comm->world;
+  if (world > 1) {
+    SegList segs = {};
+    seg_add(segs, (int64_t)rank * M * N, 1, M * N, M * N, bases_aligned(comm->slots[rank], comm->slots, world));
+    if (cudaError_t er = launch_exchange(comm->slots[rank], segs, peers_of(comm, comm->slots, 0), rank, world, epoch,
+                                         status, sm_count, st))
+      return report_cuda_error(er, "shard exchange launch");
+  }
+  shard_reduce_kernel<<<grid_for(M * N, sm_count), 256, 0, st>>>(comm->slots[rank], M, N, world, bias, residual, ldr,
+                                                                 Y, ldy, comm->flags[rank], epoch, status);
+  if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard reduce launch");
+  return MTRTQ_OK;
+}
+
 int mtrtq_matmul_sharded(const void* X, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                          const float* bias, float* Y, int64_t ldy, int64_t M, int64_t K, int64_t N, int mode,
                          int split, const mtrtq_shard_comm* comm, unsigned epoch, void* workspace,
                          size_t workspace_bytes, void* stream) {
-  if (!X || !Y || !comm) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: null pointer");
-  const int rank = comm->rank, world = comm->world;
-  if (world < 1 || world > MTRTQ_MAX_WORLD || rank < 0 || rank >= world)
-    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: 1 <= world <= 8 and 0 <= rank < world");
+  if (!X || !Y) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: null pointer");
   if (split != MTRTQ_SPLIT_N && split != MTRTQ_SPLIT_K)
     return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split is MTRTQ_SPLIT_N or MTRTQ_SPLIT_K");
-  if (epoch == 0) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: epoch counts calls from 1");
   if (M <= 0 || K <= 0 || N <= 0 || ldx < K || ldy < N)
     return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: positive sizes, ldx >= K, ldy >= N");
-  for (int p = 0; p < world; ++p)
-    if (!comm->flags[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: every rank's flags are needed");
+  int sm_count = 0;
+  unsigned* status = nullptr;
+  if (!comm) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: null comm");
+  const int rank = comm->rank, world = comm->world;
+  if (world >= 1 && world <= MTRTQ_MAX_WORLD && rank >= 0 && rank < world) {
+    if (split == MTRTQ_SPLIT_N) {
+      for (int p = 0; p < world; ++p)
+        if (p != rank && !comm->y[p])
+          return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split N needs every peer's Y");
+    } else {
+      for (int p = 0; p < world; ++p)
+        if (!comm->slots[p])
+          return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split K needs every rank's slots");
+      if (comm->slot_elems < M * N * world)
+        return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: slot buffers hold %lld floats < M*N*world",
+                            (long long)comm->slot_elems);
+    }
+  }
+  if (int rc = check_comm(comm, epoch, &sm_count, &status)) return rc;
   int64_t b = 0, e = 0;
   mtrtq_shard_range(split == MTRTQ_SPLIT_N ? N : K, split, rank, world, &b, &e);
-  if (split == MTRTQ_SPLIT_N) {
-    for (int p = 0; p < world; ++p)
-      if (p != rank && !comm->y[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split N needs every peer's Y");
-  } else {
-    for (int p = 0; p < world; ++p)
-      if (!comm->slots[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: split K needs every rank's slots");
-    if (comm->slot_elems < M * N * world)
-      return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: slot buffers hold %lld floats < M * N * world",
-                              (long long)comm->slot_elems);
-  }
   if (!packed && e > b) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_matmul_sharded: this rank's shard is not empty");
-  int dev = 0;
-  cudaDeviceProp prop;
-  if (cudaError_t er = cudaGetDevice(&dev)) return report_cuda_error(er, "cudaGetDevice");
-  if (cudaError_t er = cudaGetDeviceProperties(&prop, dev)) return report_cuda_error(er, "cudaGetDeviceProperties");
-  int status_rc = 0;
-  unsigned* status = device_status_address(&status_rc);
-  if (status_rc) return status_rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned target = epoch * (unsigned)(world - 1);
   const size_t esz = x_dtype == MTRTQ_DTYPE_BF16 ? 2 : 4;
 
-  // 1. this rank's shard, with the single-GPU kernels
-  float* local = nullptr;
-  int64_t lds = 0, cols = 0;
   if (split == MTRTQ_SPLIT_N) {
-    local = Y + b;
-    lds = ldy;
-    cols = e - b;
+    // the shard's columns of Y, then those columns to every peer's Y
     if (e > b) {
-      if (int rc = mtrtq_matmul(X, x_dtype, ldx, packed, scale, bias ? bias + b : nullptr, local, ldy, M, K, e - b,
+      if (int rc = mtrtq_matmul(X, x_dtype, ldx, packed, scale, bias ? bias + b : nullptr, Y + b, ldy, M, K, e - b,
                                 mode, workspace, workspace_bytes, stream))
         return rc;
     }
-  } else {
-    local = comm->slots[rank] + (int64_t)rank * M * N;
-    lds = N;
-    cols = N;
-    if (e > b) {
-      if (int rc = mtrtq_matmul(static_cast<const char*>(X) + b * esz, x_dtype, ldx, packed, scale, nullptr, local, N,
-                                M, e - b, N, mode, workspace, workspace_bytes, stream))
-        return rc;
-    } else if (cudaError_t er = cudaMemsetAsync(local, 0, (size_t)(M * N) * sizeof(float), st)) {
-      return report_cuda_error(er, "clear an empty shard's partial");
-    }
-  }
-  if (world == 1) {
-    if (split == MTRTQ_SPLIT_K)
-      shard_reduce_kernel<<<grid_for(M * N, prop.multiProcessorCount), 256, 0, st>>>(
-          comm->slots[0], M, N, 1, bias, Y, ldy, comm->flags[0] + kFlagData, 0u, status);
-    if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard reduce launch");
+    if (world == 1) return MTRTQ_OK;
+    SegList segs = {};
+    seg_add(segs, b, e > b ? M : 0, e - b, ldy, bases_aligned(Y, comm->y, world));
+    if (cudaError_t er = launch_exchange(Y, segs, peers_of(comm, comm->y, 0), rank, world, epoch, status, sm_count, st))
+      return report_cuda_error(er, "shard exchange launch");
+    shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[rank], world, epoch, status);
+    if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard wait launch");
     return MTRTQ_OK;
   }
+  // split K: the scaled partial over this rank's k range into its own slot
+  float* local = comm->slots[rank] + (int64_t)rank * M * N;
+  if (e > b) {
+    if (int rc = mtrtq_matmul(static_cast<const char*>(X) + b * esz, x_dtype, ldx, packed, scale, nullptr, local, N,
+                              M, e - b, N, mode, workspace, workspace_bytes, stream))
+      return rc;
+  } else if (cudaError_t er = cudaMemsetAsync(local, 0, (size_t)(M * N) * sizeof(float), st)) {
+    return report_cuda_error(er, "clear an empty shard's partial");
+  }
+  return exchange_reduce(comm, epoch, M, N, bias, nullptr, 0, Y, ldy, sm_count, status, st);
+}
 
-  // 2. entry barrier, 3. push + arrival, 4. wait (+ reduce)
-  ShardPeers peers;
-  for (int p = 0; p < MTRTQ_MAX_WORLD; ++p) {
-    peers.flags[p] = p < world ? comm->flags[p] : nullptr;
-    peers.dst[p] = nullptr;
-    if (p < world && p != rank)
-      peers.dst[p] = split == MTRTQ_SPLIT_N ? (cols > 0 ? comm->y[p] + b : nullptr)
-                                            : comm->slots[p] + (int64_t)rank * M * N;
+int mtrtq_shard_allgather(const mtrtq_shard_segment* segments, int count, const mtrtq_shard_comm* comm,
+                          unsigned epoch, void* stream) {
+  if (!segments || count < 0 || count > kMaxSegs)
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_shard_allgather: 0 to %d segments", kMaxSegs);
+  int sm_count = 0;
+  unsigned* status = nullptr;
+  if (int rc = check_comm(comm, epoch, &sm_count, &status)) return rc;
+  for (int p = 0; p < comm->world; ++p)
+    if (!comm->y[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_shard_allgather: every rank's buffer is needed");
+  SegList segs = {};
+  for (int k = 0; k < count; ++k) {
+    const mtrtq_shard_segment& g = segments[k];
+    if (g.offset < 0 || g.rows < 0 || g.cols < 0 || (g.rows > 1 && g.ld < g.cols))
+      return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_shard_allgather: segment %d: offset, rows, cols >= 0, ld >= cols", k);
+    seg_add(segs, g.offset, g.rows, g.cols, g.rows > 1 ? g.ld : g.cols,
+            bases_aligned(comm->y[comm->rank], comm->y, comm->world));
   }
-  shard_entry_kernel<<<1, 32, 0, st>>>(peers, rank, world, target, epoch, status);
-  const int64_t ldd = split == MTRTQ_SPLIT_N ? ldy : N;
-  bool vec = cols % 4 == 0 && lds % 4 == 0 && ldd % 4 == 0 && ((uintptr_t)local % 16) == 0;
-  for (int p = 0; p < world; ++p)
-    if (peers.dst[p] && ((uintptr_t)peers.dst[p] % 16) != 0) vec = false;
-  shard_push_kernel<<<grid_for(cols > 0 ? M * cols / (vec ? 4 : 1) : 1, prop.multiProcessorCount), 256, 0, st>>>(
-      local, lds, cols > 0 ? M : 0, cols, ldd, peers, rank, world, vec, epoch);
-  if (split == MTRTQ_SPLIT_N) {
-    shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[rank] + kFlagData, target, status);
-  } else {
-    shard_reduce_kernel<<<grid_for(M * N, prop.multiProcessorCount), 256, 0, st>>>(
-        comm->slots[rank], M, N, world, bias, Y, ldy, comm->flags[rank] + kFlagData, target, status);
-  }
-  if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard exchange launch");
+  if (comm->world == 1) return MTRTQ_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaError_t er = launch_exchange(comm->y[comm->rank], segs, peers_of(comm, comm->y, 0), comm->rank, comm->world,
+                                       epoch, status, sm_count, st))
+    return report_cuda_error(er, "shard exchange launch");
+  shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[comm->rank], comm->world, epoch, status);
+  if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard wait launch");
   return MTRTQ_OK;
+}
+
+int mtrtq_shard_allreduce(const float* partial, const float* bias, const float* residual, int64_t ldr, float* Y,
+                          int64_t ldy, int64_t M, int64_t N, const mtrtq_shard_comm* comm, unsigned epoch,
+                          void* stream) {
+  if (!partial || !Y || M <= 0 || N <= 0 || ldy < N || (residual && ldr < N))
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_shard_allreduce: pointers, positive sizes, ldy, ldr >= N");
+  int sm_count = 0;
+  unsigned* status = nullptr;
+  if (int rc = check_comm(comm, epoch, &sm_count, &status)) return rc;
+  for (int p = 0; p < comm->world; ++p)
+    if (!comm->slots[p]) return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_shard_allreduce: every rank's slots are needed");
+  if (comm->slot_elems < M * N * comm->world)
+    return report_error(MTRTQ_ERR_INVALID_ARG, "mtrtq_shard_allreduce: slot buffers hold %lld floats < M*N*world",
+                        (long long)comm->slot_elems);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* local = comm->slots[comm->rank] + (int64_t)comm->rank * M * N;
+  if (partial != local) {
+    if (cudaError_t er = cudaMemcpyAsync(local, partial, (size_t)(M * N) * sizeof(float), cudaMemcpyDeviceToDevice, st))
+      return report_cuda_error(er, "copy the partial into this rank's slot");
+  }
+  return exchange_reduce(comm, epoch, M, N, bias, residual, ldr, Y, ldy, sm_count, status, st);
+}
+
+int64_t mtrtq_shard_slot_offset(int rank, int64_t M, int64_t N) {
+  if (rank < 0 || rank >= MTRTQ_MAX_WORLD || M <= 0 || N <= 0) return -1;
+  return (int64_t)rank * M * N;
 }
 
 }  // extern "C"

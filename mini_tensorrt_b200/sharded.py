@@ -155,63 +155,31 @@ def shard_range(extent: int, split: str, rank: int, world: int) -> tuple[int, in
     return b.value, e.value
 
 
-class P2PShardedMatMulQ:
-    """Y = MatMulQ(X, W, scale) (+ bias) split across the ranks of a process group,
-    one GPU each, exchanged by mtrtq_matmul_sharded over peer memory.
+class PeerBuffers:
+    """Buffers every rank of a process group can store into, and the flag words of
+    the library's exchange (mtrtq_shard_comm), set up collectively: each rank
+    allocates a float buffer of `y_elems` (all-gather target), one of `slot_elems`
+    (all-reduce slots) and MTRTQ_SHARD_FLAG_BYTES of flags, exports their CUDA IPC
+    handles, gathers every rank's (torch.distributed object all-gather) and opens
+    the peers'. The epoch counter advances once per exchange, the same on every
+    rank as long as every rank makes the same calls in the same order."""
 
-    Set-up (collective over `group`): each rank packs its shard, allocates its
-    output buffer [max_m, N] (split N) or slot buffer [world, max_m, N] (split K)
-    and 64 bytes of flag words, exports their IPC handles, gathers every rank's
-    handles (torch.distributed object all-gather) and opens the peers'. A call
-    returns a view of this rank's output buffer, the full Y [M, N], valid until
-    the next call."""
-
-    def __init__(self, q: np.ndarray, scale: np.ndarray, bias: np.ndarray | None = None, split: str = "N",
-                 group=None, device=None, mode: str = "bf16", max_m: int = 8, x_dtype=torch.float32):
+    def __init__(self, y_elems: int, slot_elems: int, group=None, device=None):
         import ctypes
         from . import _lib
-        from .matmulq import PackedWeight
-        if split not in ("N", "K"):
-            raise ValueError("split must be 'N' or 'K'")
-        self.lib = _lib.lib()
-        self._lib = _lib
+        self._lib, self.lib = _lib, _lib.lib()
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         if self.world > _lib.MAX_WORLD:
             raise ValueError(f"at most {_lib.MAX_WORLD} ranks")
-        self.split, self.mode, self.max_m, self.x_dtype = split, mode, max_m, x_dtype
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        K, N = q.shape
-        self.K, self.N = K, N
-        b, e = shard_range(N if split == "N" else K, split, self.rank, self.world)
-        self.begin, self.end = b, e
-        if e > b:
-            qs = q[:, b:e] if split == "N" else q[b:e, :]
-            ss = scale[b:e] if split == "N" else scale
-            self.w = PackedWeight.from_int8(torch.from_numpy(np.ascontiguousarray(qs)),
-                                            torch.from_numpy(np.ascontiguousarray(ss)), self.device)
-        else:
-            self.w = None
-        self.bias = torch.from_numpy(np.ascontiguousarray(bias)).to(self.device) if bias is not None else None
+        z = lambda n: torch.zeros(max(int(n), 64), dtype=torch.float32, device=self.device)
+        self.y, self.slots = z(y_elems), z(slot_elems)
         self.flags = torch.zeros(_lib.SHARD_FLAG_BYTES // 4, dtype=torch.int32, device=self.device)
-        if split == "N":
-            self.buf = torch.zeros((max_m, N), dtype=torch.float32, device=self.device)
-        else:
-            self.buf = torch.zeros((self.world, max_m, N), dtype=torch.float32, device=self.device)
-        xd = _lib.DTYPE_BF16 if x_dtype == torch.bfloat16 else _lib.DTYPE_F32
-        from .matmulq import MODES
-        self._xd, self._mode = xd, MODES[mode]
-        ws = self.lib.mtrtq_shard_workspace_bytes(max_m, K, N, xd, self._mode,
-                                                  _lib.SPLIT_N if split == "N" else _lib.SPLIT_K, self.rank,
-                                                  self.world)
-        if ws < 0:
-            raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_shard_workspace_bytes", _lib.last_error())
-        self.ws = torch.zeros(max(ws, 256), dtype=torch.uint8, device=self.device)
         torch.cuda.synchronize(self.device)
-        # exchange the buffers' and flags' IPC handles
         mine = []
-        for t in (self.buf, self.flags):
+        for t in (self.y, self.slots, self.flags):
             h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
             with torch.cuda.device(self.device):
                 _lib.check(self.lib.mtrtq_ipc_export(t.data_ptr(), h), "mtrtq_ipc_export")
@@ -224,10 +192,10 @@ class P2PShardedMatMulQ:
         self.imported = []
         comm = _lib.ShardComm()
         comm.rank, comm.world = self.rank, self.world
-        comm.slot_elems = self.buf.numel() if split == "K" else 0
+        comm.slot_elems = self.slots.numel()
         for r in range(self.world):
             if r == self.rank:
-                ptrs = [self.buf.data_ptr(), self.flags.data_ptr()]
+                ptrs = [self.y.data_ptr(), self.slots.data_ptr(), self.flags.data_ptr()]
             else:
                 ptrs = []
                 for hb in allh[r]:
@@ -237,47 +205,116 @@ class P2PShardedMatMulQ:
                         _lib.check(self.lib.mtrtq_ipc_import(h, ctypes.byref(p)), "mtrtq_ipc_import")
                     self.imported.append(p.value)
                     ptrs.append(p.value)
-            if split == "N":
-                comm.y[r] = ptrs[0]
-            else:
-                comm.slots[r] = ptrs[0]
-            comm.flags[r] = ptrs[1]
+            comm.y[r], comm.slots[r], comm.flags[r] = ptrs
         self.comm = comm
         self.epoch = 0
+        self.device_epochs = device_epochs
         if self.world > 1:
             dist.barrier(group=group)
 
+    def next_epoch(self) -> int:
+        if self.device_epochs:
+            return 0
+        self.epoch += 1
+        return self.epoch
+
+    def allgather(self, segments, stream=None):
+        """segments: (offset, rows, cols, ld) in floats of self.y that this rank owns;
+        after the call every rank's y holds every rank's segments."""
+        import ctypes
+        _lib = self._lib
+        arr = (_lib.ShardSegment * max(1, len(segments)))(*[_lib.ShardSegment(*g) for g in segments])
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.mtrtq_shard_allgather(arr, len(segments), ctypes.byref(self.comm), self.next_epoch(),
+                                                      _sp(stream, self.device)), "mtrtq_shard_allgather")
+
+    def slot(self, M: int, N: int) -> torch.Tensor:
+        """This rank's slot for an [M, N] partial (write the partial here: no copy)."""
+        off = self.rank * M * N
+        return self.slots[off:off + M * N].view(M, N)
+
+    def allreduce(self, partial: torch.Tensor, out: torch.Tensor, bias=None, residual=None, stream=None):
+        """out = sum over ranks of partial (+ bias) (+ residual), rank order."""
+        import ctypes
+        _lib = self._lib
+        M, N = partial.shape
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.mtrtq_shard_allreduce(
+                partial.data_ptr(), bias.data_ptr() if bias is not None else None,
+                residual.data_ptr() if residual is not None else None,
+                residual.stride(0) if residual is not None else 0, out.data_ptr(), out.stride(0), M, N,
+                ctypes.byref(self.comm), self.next_epoch(), _sp(stream, self.device)), "mtrtq_shard_allreduce")
+        return out
+
+    def close(self):
+        for p in self.imported:
+            with torch.cuda.device(self.device):
+                self.lib.mtrtq_ipc_close(p)
+        self.imported = []
+
+
+def _sp(stream, device):
+    return stream.cuda_stream if stream is not None else torch.cuda.current_stream(device).cuda_stream
+
+
+class P2PShardedMatMulQ:
+    """Y = MatMulQ(X, W, scale) (+ bias) split across the ranks of a process group,
+    one GPU each, exchanged by mtrtq_matmul_sharded over peer memory (PeerBuffers:
+    every rank's output or slot buffer and flag words opened in every process).
+    A call returns the full Y [M, N] on every rank (split N: a view of this rank's
+    peer buffer, valid until the next call)."""
+
+    def __init__(self, q: np.ndarray, scale: np.ndarray, bias: np.ndarray | None = None, split: str = "N",
+                 group=None, device=None, mode: str = "bf16", max_m: int = 8, x_dtype=torch.float32):
+        from . import _lib
+        from .matmulq import MODES, PackedWeight
+        if split not in ("N", "K"):
+            raise ValueError("split must be 'N' or 'K'")
+        self._lib, self.lib = _lib, _lib.lib()
+        self.split, self.mode, self.max_m, self.x_dtype = split, mode, max_m, x_dtype
+        K, N = q.shape
+        self.K, self.N = K, N
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.peers = PeerBuffers(max_m * N if split == "N" else 0, max_m * N * world if split == "K" else 0,
+                                 group=group, device=device)
+        self.rank, self.world, self.device = self.peers.rank, self.peers.world, self.peers.device
+        b, e = shard_range(N if split == "N" else K, split, self.rank, self.world)
+        self.begin, self.end = b, e
+        if e > b:
+            qs = q[:, b:e] if split == "N" else q[b:e, :]
+            ss = scale[b:e] if split == "N" else scale
+            self.w = PackedWeight.from_int8(torch.from_numpy(np.ascontiguousarray(qs)),
+                                            torch.from_numpy(np.ascontiguousarray(ss)), self.device)
+        else:
+            self.w = None
+        self.bias = torch.from_numpy(np.ascontiguousarray(bias)).to(self.device) if bias is not None else None
+        self._xd = _lib.DTYPE_BF16 if x_dtype == torch.bfloat16 else _lib.DTYPE_F32
+        self._mode = MODES[mode]
+        ws = self.lib.mtrtq_shard_workspace_bytes(max_m, K, N, self._xd, self._mode,
+                                                  _lib.SPLIT_N if split == "N" else _lib.SPLIT_K, self.rank,
+                                                  self.world)
+        if ws < 0:
+            raise _lib.MtrtqError(_lib.ERR_INVALID_ARG, "mtrtq_shard_workspace_bytes", _lib.last_error())
+        self.ws = torch.zeros(max(ws, 256), dtype=torch.uint8, device=self.device)
+        self._y = torch.empty((max_m, N), dtype=torch.float32, device=self.device) if split == "K" else None
+
     def __call__(self, x: torch.Tensor, stream=None) -> torch.Tensor:
-        """x: [M, K] (M <= max_m), the same on every rank. Returns this rank's full Y
-        [M, N] (a view of its buffer, valid until the next call)."""
+        """x: [M, K] (M <= max_m), the same on every rank."""
         import ctypes
         _lib = self._lib
         M = x.shape[0]
         if x.dim() != 2 or x.shape[1] != self.K or x.stride(1) != 1 or M > self.max_m or x.dtype != self.x_dtype:
             raise ValueError(f"x must be [M <= {self.max_m}, {self.K}] {self.x_dtype} with unit stride along K")
-        self.epoch += 1
-        if self.split == "N":
-            y = self.buf[:M]
-        else:
-            y = torch.empty((M, self.N), dtype=torch.float32, device=self.device) if not hasattr(self, "_y") \
-                or self._y.shape[0] < M else self._y
-            self._y = y
-            y = y[:M]
-        if self.split == "K":
-            self.comm.slot_elems = self.buf.numel()
-        sp = (stream.cuda_stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream)
+        y = self.peers.y[:M * self.N].view(M, self.N) if self.split == "N" else self._y[:M]
         with torch.cuda.device(self.device):
             _lib.check(self.lib.mtrtq_matmul_sharded(
                 x.data_ptr(), self._xd, x.stride(0), self.w.packed.data_ptr() if self.w is not None else None,
                 self.w.scale.data_ptr() if self.w is not None else None,
                 self.bias.data_ptr() if self.bias is not None else None, y.data_ptr(), y.stride(0), M, self.K,
-                self.N, self._mode, _lib.SPLIT_N if self.split == "N" else _lib.SPLIT_K, ctypes.byref(self.comm),
-                self.epoch, self.ws.data_ptr(), self.ws.numel(), sp), "mtrtq_matmul_sharded")
+                self.N, self._mode, _lib.SPLIT_N if self.split == "N" else _lib.SPLIT_K,
+                ctypes.byref(self.peers.comm), self.peers.next_epoch(), self.ws.data_ptr(), self.ws.numel(),
+                _sp(stream, self.device)), "mtrtq_matmul_sharded")
         return y
 
     def close(self):
-        """Closes the peers' buffers (set-up's counterpart)."""
-        for p in self.imported:
-            with torch.cuda.device(self.device):
-                self.lib.mtrtq_ipc_close(p)
-        self.imported = []
+        self.peers.close()

@@ -59,6 +59,58 @@ def main():
                 assert all(torch.equal(allt[0], a) for a in allt), f"p2p case {i}: ranks disagree"
             torch.cuda.synchronize()
             op.close()
+        # the exchange steps on their own: segments of a peer buffer, partials + residual
+        world = dist.get_world_size()
+        M, N = 5, 37
+        pb = sharded.PeerBuffers(y_elems=4096, slot_elems=M * N * world)
+        for call in range(3):
+            base = torch.arange(4096, dtype=torch.float32, device="cuda") * (call + 1)
+            # rank r owns rows r, r + world, ... of a [24, 100] block at offset 17 (ld 120)
+            segs = []
+            for row in range(rank, 24, world):
+                segs.append((17 + row * 120, 1, 100, 100))
+                pb.y[17 + row * 120:17 + row * 120 + 100] = base[17 + row * 120:17 + row * 120 + 100]
+            pb.allgather(segs)
+            torch.cuda.synchronize()
+            got = pb.y[17:17 + 24 * 120].view(24, 120)[:, :100]
+            assert torch.equal(got, base[17:17 + 24 * 120].view(24, 120)[:, :100]), f"allgather call {call}"
+            g = torch.Generator(device="cuda").manual_seed(100 * call + rank)
+            partial = pb.slot(M, N)
+            partial.copy_(torch.randn(M, N, device="cuda", generator=g))
+            res = torch.full((M, N), float(call), device="cuda")
+            bias = torch.arange(N, dtype=torch.float32, device="cuda")
+            out = torch.empty(M, N, device="cuda")
+            pb.allreduce(partial, out, bias=bias, residual=res)
+            torch.cuda.synchronize()
+            parts = []
+            for r in range(world):
+                gr = torch.Generator(device="cuda").manual_seed(100 * call + r)
+                parts.append(torch.randn(M, N, device="cuda", generator=gr))
+            want = parts[0].clone()
+            for r in range(1, world):
+                want += parts[r]
+            want = res + (want + bias)
+            assert torch.equal(out, want), f"allreduce call {call}: {float((out - want).abs().max())}"
+        pb.close()
+        # device-counted epochs: one all-reduce captured in a CUDA graph, replayed
+        pg = sharded.PeerBuffers(y_elems=64, slot_elems=M * N * world, device_epochs=True)
+        partial, out = pg.slot(M, N), torch.empty(M, N, device="cuda")
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            partial.fill_(1.0)
+            pg.allreduce(partial, out, stream=st)  # epoch 1, eager
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                pg.allreduce(partial, out, stream=st)
+            for call in range(3):
+                partial.fill_(float(rank + call))
+                graph.replay()
+                torch.cuda.synchronize()
+                want = float(sum(r + call for r in range(world)))
+                assert torch.all(out == want), f"graph replay {call}: {out.flatten()[:4].tolist()} != {want}"
+        del graph
+        pg.close()
         torch.cuda.synchronize()
         assert matmulq.read_device_status() == 0
         print("SHARDED OK", flush=True)

@@ -134,9 +134,13 @@ def test_sharded_abi_argument_errors():
     x = (ctypes.c_float * 64)()
     call = lambda c, epoch=1, split=_lib.SPLIT_N: lib.mtrtq_matmul_sharded(
         x, 0, 8, x, x, None, x, 8, 1, 8, 8, 1, split, ctypes.byref(c), epoch, None, 0, None)
-    assert call(comm) == _lib.ERR_INVALID_ARG                      # no flags
+    assert call(comm) == _lib.ERR_INVALID_ARG                      # no peer buffers
+    assert "peer's Y" in _lib.last_error()
+    assert call(comm, split=_lib.SPLIT_K) == _lib.ERR_INVALID_ARG
+    assert "slots" in _lib.last_error()
+    comm.y[1] = 0x1000  # never dereferenced: the flags check fails first
+    assert call(comm) == _lib.ERR_INVALID_ARG
     assert "flags" in _lib.last_error()
-    assert call(comm, epoch=0) == _lib.ERR_INVALID_ARG             # epochs count from 1
     comm.world = 9
     assert call(comm) == _lib.ERR_INVALID_ARG
     assert lib.mtrtq_matmul_sharded(x, 0, 8, x, x, None, x, 8, 1, 8, 8, 1, 0, None, 1, None, 0, None) \
