@@ -162,9 +162,11 @@ class PeerBuffers:
     (all-reduce slots) and MTRTQ_SHARD_FLAG_BYTES of flags, exports their CUDA IPC
     handles, gathers every rank's (torch.distributed object all-gather) and opens
     the peers'. The epoch counter advances once per exchange, the same on every
-    rank as long as every rank makes the same calls in the same order."""
+    rank as long as every rank makes the same calls in the same order; with
+    device_epochs the count lives on the device instead (epoch 0 in every call),
+    so that the exchanges can be captured in a CUDA graph and replayed."""
 
-    def __init__(self, y_elems: int, slot_elems: int, group=None, device=None):
+    def __init__(self, y_elems: int, slot_elems: int, group=None, device=None, device_epochs: bool = False):
         import ctypes
         from . import _lib
         self._lib, self.lib = _lib, _lib.lib()
