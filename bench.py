@@ -242,7 +242,8 @@ def launch_step(calls, step, mode, stream, branches=None, side_streams=()):
 
 
 def time_graphs(torch, graphs, steps, warmup, stream):
-    """Replays graphs round-robin on `stream`; returns seconds for `steps` replays."""
+    """Replays graphs round-robin on `stream` (the timed replays continue the
+    warm-up's order); returns seconds for `steps` replays."""
     with torch.cuda.stream(stream):
         for i in range(warmup):
             graphs[i % len(graphs)].replay()
@@ -250,7 +251,7 @@ def time_graphs(torch, graphs, steps, warmup, stream):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(steps):
+        for i in range(warmup, warmup + steps):
             graphs[i % len(graphs)].replay()
         e1.record(stream)
         torch.cuda.synchronize()
@@ -439,12 +440,14 @@ def run_sharded_decode_set(args, torch, rank, world, dev, dist):
     matmulq.set_option(_lib.OPT_OVERLAP_LAUNCH, 0 if args.no_overlap else 1)
     shapes = [(M, name, K, N) for M in wl.DECODE_M for name, K, N in wl.DECODE_SHAPES]
     y_elems = sum(M * N for M, _, _, N in shapes)
-    peers = sharded.PeerBuffers(y_elems, 0, device=dev, device_epochs=True)
+    # outputs alternate between two copies from one step to the next (graph g
+    # writes copy g % 2; the rotation count is even), so no entry barrier is needed
+    peers = sharded.PeerBuffers(y_elems, 0, device=dev, device_epochs=True, alternating=True)
+    assert WEIGHT_COPIES % 2 == 0
     calls, off, step_bytes, my_bytes = [], 0, 0, 0
     for M, name, K, N in shapes:
         n0, n1 = sharded.shard_range(N, "N", rank, world)
         c = {"name": name, "M": M, "K": K, "N": N, "n0": n0, "n1": n1, "off": off,
-             "y": peers.y[off:off + M * N].view(M, N),
              "x": torch.from_numpy(wl.activations(M, K, wl.shape_seed("x:" + name, M, K))).to(dev)}
         step_bytes += wl.algorithmic_bytes(M, K, N, 4)
         if n1 > n0:
@@ -457,19 +460,27 @@ def run_sharded_decode_set(args, torch, rank, world, dev, dist):
         calls.append(c)
         off += M * N
     mine = [c for c in calls if c["n1"] > c["n0"]]
-    segments = [(c["off"] + c["n0"], c["M"], c["n1"] - c["n0"], c["N"]) for c in mine]
+
+    def out_view(c, g):
+        o = (g % 2) * y_elems + c["off"]
+        return peers.y[o:o + c["M"] * c["N"]].view(c["M"], c["N"])
+
+    segments = [[((g % 2) * y_elems + c["off"] + c["n0"], c["M"], c["n1"] - c["n0"], c["N"]) for c in mine]
+                for g in range(2)]
     groups = [matmulq.GemvGroup([{"x": c["x"], "w": c["w"][(g + i) % WEIGHT_COPIES],
-                                  "out": c["y"][:, c["n0"]:c["n1"]]} for i, c in enumerate(mine)], mode=args.mode)
+                                  "out": out_view(c, g)[:, c["n0"]:c["n1"]]} for i, c in enumerate(mine)],
+                                mode=args.mode)
               for g in range(WEIGHT_COPIES)]
     stream = torch.cuda.Stream(dev)
 
     def one(g):
         groups[g](stream)
-        peers.allgather(segments, stream=stream)
+        peers.allgather(segments[g % 2], stream=stream)
 
     graphs = []
     with torch.cuda.stream(stream):
-        one(0)
+        one(0)  # eager set-up launches, copy 0 then copy 1, so that the replays
+        one(1)  # (graph 0 first) keep alternating
         torch.cuda.synchronize()
         for g in range(WEIGHT_COPIES):
             graph = torch.cuda.CUDAGraph()
@@ -488,12 +499,13 @@ def run_sharded_decode_set(args, torch, rank, world, dev, dist):
     assert matmulq.read_device_status() == 0, "a device wait timed out"
     # every rank holds the full outputs: check them against this rank's own
     # unsplit product of the last step's weights (sampled rows of each call)
+    last = (args.steps + args.warmup - 1) % WEIGHT_COPIES  # the graph of the last step
     for c in calls:
         full_q, full_s = matmulq.quantize_per_channel(wl.decode_weight(c["name"], c["K"], c["N"]))
         pw = matmulq.PackedWeight.from_int8(torch.from_numpy(full_q), torch.from_numpy(full_s), dev)
         ref = matmulq.matmul_q8(c["x"], pw, mode=args.mode)
         torch.cuda.synchronize()
-        err = float((c["y"] - ref).abs().max() / ref.abs().max())
+        err = float((out_view(c, last) - ref).abs().max() / ref.abs().max())
         assert err <= 1e-4, f"sharded step output {c['name']}/M{c['M']} differs from the unsplit product: {err:.3e}"
     step_us = secs / args.steps * 1e6
     exch_bytes = sum(c["M"] * c["N"] * 4 for c in calls) * (world - 1) / world  # each rank receives

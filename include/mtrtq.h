@@ -291,6 +291,12 @@ typedef struct mtrtq_shard_comm {
   float* slots[MTRTQ_MAX_WORLD];     /* split K: every rank's slot buffer */
   int64_t slot_elems;                /* floats in each slot buffer (>= M * N * world) */
   unsigned* flags[MTRTQ_MAX_WORLD];  /* every rank's flag words */
+  int alternating;                   /* 1: the caller's exchanges alternate between two
+                                        destination buffers (and every rank sends to
+                                        every peer in each); the entry barrier is then
+                                        skipped: a peer's data for the previous exchange
+                                        already shows it has finished reading the buffer
+                                        this one writes */
 } mtrtq_shard_comm;
 
 /* [begin, end) of `rank`'s shard of an extent (N for MTRTQ_SPLIT_N, K for

@@ -91,7 +91,7 @@ IPC_HANDLE_BYTES = 72
 class ShardComm(ctypes.Structure):
     """mtrtq_shard_comm (include/mtrtq.h)."""
     _fields_ = [("rank", _int), ("world", _int), ("y", _vp * MAX_WORLD), ("slots", _vp * MAX_WORLD),
-                ("slot_elems", _i64), ("flags", _vp * MAX_WORLD)]
+                ("slot_elems", _i64), ("flags", _vp * MAX_WORLD), ("alternating", _int)]
 
 
 SIGNATURES["mtrtq_shard_range"] = (_int, [_i64, _int, _int, _int, _vp, _vp])

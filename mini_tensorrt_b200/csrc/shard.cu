@@ -12,8 +12,8 @@
 //   * push: one kernel stores this rank's result into every peer's buffer (split
 //     N: the shard's columns of the peer's Y; split K: this rank's slot of the
 //     peer's slot buffer); its last block releases one arrival on every peer's
-//     data flag (gpu-scope tickets among the blocks, a system-scope release
-//     fence, then a relaxed add on the peer's flag);
+//     data flag (gpu-scope acq_rel tickets among the blocks, then one
+//     system-scope fence and a relaxed add on each peer's flag);
 //   * finish: split N waits for every peer's arrival; split K waits, then sums the
 //     ranks' slots in rank order (fixed, so every rank gets identical bits) and
 //     adds the bias once.
@@ -39,12 +39,6 @@ unsigned* device_status_address(int* rc);
 
 namespace {
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __device__ __forceinline__ void red_add_relaxed_sys(unsigned* p, unsigned v) {
@@ -53,15 +47,24 @@ __device__ __forceinline__ void red_add_relaxed_sys(unsigned* p, unsigned v) {
 
 // Spins until *flag >= target (bounded). Returns false (and records a timeout)
 // when it gives up.
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Spins (relaxed loads) until *flag >= target, then one acquire fence orders the
+// caller's later reads after the arrivals it saw. Bounded: returns false (and
+// records a timeout) when it gives up.
 __device__ bool wait_flag(const unsigned* flag, unsigned target, unsigned* status) {
   const long long t0 = clock64();
-  while ((int)(ld_acquire_sys(flag) - target) < 0) {
+  while ((int)(ld_relaxed_sys(flag) - target) < 0) {
     if (clock64() - t0 > kSpinLimitCycles) {
       atomicExch(status, 6u /* MTRTQ_ERR_TIMEOUT */);
       return false;
     }
-    __nanosleep(64);
   }
+  fence_acq_rel_sys();
   return true;
 }
 
@@ -106,6 +109,11 @@ __global__ void shard_entry_kernel(ShardPeers peers, int rank, int world, unsign
   if (!wait_flag(peers.flags[rank] + kFlagEntry, target, status)) peers.flags[rank][kFlagAbort] = epoch;
 }
 
+// Advances the device-side epoch where no entry barrier runs.
+__global__ void shard_epoch_kernel(unsigned* own_flags) {
+  if (threadIdx.x == 0) own_flags[kFlagEpoch] = own_flags[kFlagEpoch] + 1;
+}
+
 // Stores every segment of src into every peer's destination, then the last block
 // to finish releases one arrival on every peer's data flag.
 __global__ void shard_push_kernel(const float* src, SegList segs, ShardPeers peers, int rank, int world,
@@ -133,10 +141,11 @@ __global__ void shard_push_kernel(const float* src, SegList segs, ShardPeers pee
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    // This block's stores (observed through the barrier) are released with the
-    // ticket; the last block acquires every other block's the same way.
-    fence_acq_rel_sys();
-    s_ticket = atomicAdd(peers.flags[rank] + kFlagTicket, 1u);
+    // This block's stores (observed through the barrier) are released to this
+    // GPU with the ticket (gpu scope: every block runs here); the last block
+    // acquires them all and releases them to the peers with one system-scope
+    // fence before it signals (causality carries over from one scope to the next).
+    s_ticket = ticket_acq_rel(peers.flags[rank] + kFlagTicket);
   }
   __syncthreads();
   if (threadIdx.x == 0 && s_ticket == gridDim.x - 1) {
@@ -176,10 +185,15 @@ __global__ void shard_reduce_kernel(const float* slots, int64_t M, int64_t N, in
 
 int grid_for(int64_t work, int sm_count);
 
-// Entry barrier, then the push of `segs` from src to every peer's dst base.
+// Entry barrier (unless the caller's buffers alternate), then the push of `segs`
+// from src to every peer's dst base.
 cudaError_t launch_exchange(const float* src, const SegList& segs, ShardPeers peers, int rank, int world,
-                            unsigned epoch, unsigned* status, int sm_count, cudaStream_t st) {
-  shard_entry_kernel<<<1, 32, 0, st>>>(peers, rank, world, epoch, status);
+                            unsigned epoch, unsigned* status, int sm_count, bool entry, cudaStream_t st) {
+  if (entry) {
+    shard_entry_kernel<<<1, 32, 0, st>>>(peers, rank, world, epoch, status);
+  } else if (epoch == 0) {
+    shard_epoch_kernel<<<1, 32, 0, st>>>(peers.flags[rank]);
+  }
   int64_t items = segs.first[segs.count];
   shard_push_kernel<<<grid_for(items > 0 ? items : 1, sm_count), 256, 0, st>>>(src, segs, peers, rank, world, epoch);
   return cudaGetLastError();
@@ -344,7 +358,7 @@ static int exchange_reduce(const mtrtq_shard_comm* comm, unsigned epoch, int64_t
     SegList segs = {};
     seg_add(segs, (int64_t)rank * M * N, 1, M * N, M * N, bases_aligned(comm->slots[rank], comm->slots, world));
     if (cudaError_t er = launch_exchange(comm->slots[rank], segs, peers_of(comm, comm->slots, 0), rank, world, epoch,
-                                         status, sm_count, st))
+                                         status, sm_count, !comm->alternating, st))
       return report_cuda_error(er, "shard exchange launch");
   }
   shard_reduce_kernel<<<grid_for(M * N, sm_count), 256, 0, st>>>(comm->slots[rank], M, N, world, bias, residual, ldr,
@@ -397,7 +411,8 @@ int mtrtq_matmul_sharded(const void* X, int x_dtype, int64_t ldx, const void* pa
     if (world == 1) return MTRTQ_OK;
     SegList segs = {};
     seg_add(segs, b, e > b ? M : 0, e - b, ldy, bases_aligned(Y, comm->y, world));
-    if (cudaError_t er = launch_exchange(Y, segs, peers_of(comm, comm->y, 0), rank, world, epoch, status, sm_count, st))
+    if (cudaError_t er = launch_exchange(Y, segs, peers_of(comm, comm->y, 0), rank, world, epoch, status, sm_count,
+                                         !comm->alternating, st))
       return report_cuda_error(er, "shard exchange launch");
     shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[rank], world, epoch, status);
     if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard wait launch");
@@ -435,7 +450,7 @@ int mtrtq_shard_allgather(const mtrtq_shard_segment* segments, int count, const 
   if (comm->world == 1) return MTRTQ_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cudaError_t er = launch_exchange(comm->y[comm->rank], segs, peers_of(comm, comm->y, 0), comm->rank, comm->world,
-                                       epoch, status, sm_count, st))
+                                       epoch, status, sm_count, !comm->alternating, st))
     return report_cuda_error(er, "shard exchange launch");
   shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[comm->rank], comm->world, epoch, status);
   if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard wait launch");

@@ -164,9 +164,17 @@ class PeerBuffers:
     the peers'. The epoch counter advances once per exchange, the same on every
     rank as long as every rank makes the same calls in the same order; with
     device_epochs the count lives on the device instead (epoch 0 in every call),
-    so that the exchanges can be captured in a CUDA graph and replayed."""
+    so that the exchanges can be captured in a CUDA graph and replayed.
 
-    def __init__(self, y_elems: int, slot_elems: int, group=None, device=None, device_epochs: bool = False):
+    alternating: the exchanges alternate between two destination buffers, which
+    lets the library skip its entry barrier (MTRTQ_SHARD comm.alternating). The
+    slot buffer is allocated twice and allreduce() switches halves on every call;
+    all-gather callers alternate themselves, between the halves y[:y_elems] and
+    y[y_elems:] of a buffer allocated twice (`half`). Every rank must make the same
+    sequence of exchanges, and a captured graph an even number of them."""
+
+    def __init__(self, y_elems: int, slot_elems: int, group=None, device=None, device_epochs: bool = False,
+                 alternating: bool = False):
         import ctypes
         from . import _lib
         self._lib, self.lib = _lib, _lib.lib()
@@ -177,7 +185,11 @@ class PeerBuffers:
             raise ValueError(f"at most {_lib.MAX_WORLD} ranks")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         z = lambda n: torch.zeros(max(int(n), 64), dtype=torch.float32, device=self.device)
-        self.y, self.slots = z(y_elems), z(slot_elems)
+        copies = 2 if alternating else 1
+        self.alternating = alternating
+        self.half = int(y_elems)
+        self.slot_half = max(int(slot_elems), 64)
+        self.y, self.slots = z(y_elems * copies), z(self.slot_half * copies)
         self.flags = torch.zeros(_lib.SHARD_FLAG_BYTES // 4, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         mine = []
@@ -208,7 +220,18 @@ class PeerBuffers:
                     self.imported.append(p.value)
                     ptrs.append(p.value)
             comm.y[r], comm.slots[r], comm.flags[r] = ptrs
+        comm.alternating = 1 if alternating else 0
         self.comm = comm
+        self._slot_turn = 0
+        if alternating:  # a second comm whose slot buffers are the other halves
+            comm2 = _lib.ShardComm()
+            ctypes.memmove(ctypes.byref(comm2), ctypes.byref(comm), ctypes.sizeof(comm))
+            for r in range(self.world):
+                comm2.slots[r] = comm.slots[r] + 4 * self.slot_half
+            comm.slot_elems = comm2.slot_elems = self.slot_half
+            self.comms = [comm, comm2]
+        else:
+            self.comms = [comm]
         self.epoch = 0
         self.device_epochs = device_epochs
         if self.world > 1:
@@ -231,8 +254,9 @@ class PeerBuffers:
                                                       _sp(stream, self.device)), "mtrtq_shard_allgather")
 
     def slot(self, M: int, N: int) -> torch.Tensor:
-        """This rank's slot for an [M, N] partial (write the partial here: no copy)."""
-        off = self.rank * M * N
+        """This rank's slot for the next all-reduce of an [M, N] partial (write the
+        partial here: no copy)."""
+        off = self._slot_turn * self.slot_half + self.rank * M * N
         return self.slots[off:off + M * N].view(M, N)
 
     def allreduce(self, partial: torch.Tensor, out: torch.Tensor, bias=None, residual=None, stream=None):
@@ -240,12 +264,14 @@ class PeerBuffers:
         import ctypes
         _lib = self._lib
         M, N = partial.shape
+        comm = self.comms[self._slot_turn]
+        self._slot_turn = (self._slot_turn + 1) % len(self.comms)
         with torch.cuda.device(self.device):
             _lib.check(self.lib.mtrtq_shard_allreduce(
                 partial.data_ptr(), bias.data_ptr() if bias is not None else None,
                 residual.data_ptr() if residual is not None else None,
                 residual.stride(0) if residual is not None else 0, out.data_ptr(), out.stride(0), M, N,
-                ctypes.byref(self.comm), self.next_epoch(), _sp(stream, self.device)), "mtrtq_shard_allreduce")
+                ctypes.byref(comm), self.next_epoch(), _sp(stream, self.device)), "mtrtq_shard_allreduce")
         return out
 
     def close(self):

@@ -92,6 +92,17 @@ def main():
             want = res + (want + bias)
             assert torch.equal(out, want), f"allreduce call {call}: {float((out - want).abs().max())}"
         pb.close()
+        # alternating buffers (no entry barrier): all-reduces back to back
+        pa = sharded.PeerBuffers(y_elems=64, slot_elems=M * N * world, alternating=True)
+        for call in range(6):
+            partial = pa.slot(M, N)
+            partial.fill_(float(rank * 10 + call))
+            out = torch.empty(M, N, device="cuda")
+            pa.allreduce(partial, out)
+            torch.cuda.synchronize()
+            want = float(sum(r * 10 + call for r in range(world)))
+            assert torch.all(out == want), f"alternating all-reduce {call}"
+        pa.close()
         # device-counted epochs: one all-reduce captured in a CUDA graph, replayed
         pg = sharded.PeerBuffers(y_elems=64, slot_elems=M * N * world, device_epochs=True)
         partial, out = pg.slot(M, N), torch.empty(M, N, device="cuda")
