@@ -73,7 +73,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--workload", default="decode_set",
-                    help="decode_set (default) or shape:M,K,N (one MatMulQ shape timed alone)")
+                    help="decode_set (default), shape:M,K,N (one MatMulQ shape timed alone), gpt2_decode, "
+                         "tp_decode (GPT-2-XL tensor parallel over the ranks) or sharded:M,K,N,S")
     ap.add_argument("--x-dtype", choices=["f32", "bf16"], default="f32",
                     help="activation type for --workload shape:M,K,N")
     ap.add_argument("--force-path", type=int, default=0, choices=[0, 1, 2, 3, 4],
@@ -81,6 +82,7 @@ def parse():
                          "4 cluster GEMV")
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch every call only after the previous one has finished")
+    ap.add_argument("--tp-layers", type=int, default=48, help="tp_decode: layers of the GPT-2-XL-shaped model")
     ap.add_argument("--multi", choices=["sharded", "replicas"], default="sharded",
                     help="N > 1: the decode set column-sharded over the ranks (strong scaling, default) or "
                          "one full set per rank (replicas)")
@@ -790,6 +792,61 @@ def run_gpt2_decode(args, torch, dev, mode=None):
     return out
 
 
+def run_tp_decode(args, torch, rank, world, dev, dist):
+    """GPT-2-XL-shaped random-init model (48 layers, d 1600, 25 heads, d_ff 6400,
+    vocab 50257), every Linear int8 per channel, tensor-parallel over the ranks
+    (mini_tensorrt_b200.tp: column-split QKV by heads and FFN-up, row-split
+    attn-out and FFN-down with two library all-reduces per layer, vocabulary-split
+    LM head): batch 32, prompts of 128 ids consumed token by token, then 128 greedy
+    tokens; one CUDA graph per step on every rank. Reports decode tokens/s over all
+    sequences (max over ranks of the decode time) and checks that every rank
+    produced the same tokens. --tp-layers shortens the model for quick runs."""
+    import dataclasses
+    from mini_tensorrt_b200 import gpt2, tp
+    from mini_tensorrt_b200.matmulq import set_option
+    from mini_tensorrt_b200 import _lib
+    set_option(_lib.OPT_OVERLAP_LAUNCH, 0 if args.no_overlap else 1)
+    cfg = dataclasses.replace(tp.GPT2_XL, n_layer=args.tp_layers)
+    B, P, new = 32, 128, 128
+    t0 = time.time()
+    w = gpt2.random_weights(cfg, seed=0)
+    setup_s = time.time() - t0
+    dec = tp.TPDecoder(w, B, max_ctx=P + new, mode=args.mode, device=dev)
+    del w
+    prompt = np.random.default_rng(4321).integers(0, cfg.vocab, (B, P), dtype=np.int32)
+    dec.generate(prompt, 8)  # capture + warm-up
+    runs = []
+    for _ in range(2):
+        if world > 1:
+            dist.barrier()
+        runs.append(dec.generate(prompt, new))
+    dsec = min(r["decode_s"] for r in runs)
+    t = torch.tensor([dsec], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dsec = float(t.item())
+    toks = torch.from_numpy(runs[-1]["tokens"]).to(dev)
+    if world > 1:
+        allt = [torch.empty_like(toks) for _ in range(world)]
+        dist.all_gather(allt, toks)
+        assert all(torch.equal(allt[0], a) for a in allt), "ranks generated different tokens"
+    D, F, V, L = cfg.d_model, cfg.d_ff, cfg.vocab, cfg.n_layer
+    step_bytes = L * (D * 3 * D + D * D + D * F + F * D) + D * V
+    nsteps = new - 1
+    digest = int(np.asarray(runs[-1]["tokens"], dtype=np.int64).sum())
+    dec.close()
+    return {"metric": METRIC, "impl": "ours", "workload": "tp_decode", "n_gpus": world, "scaling": "strong",
+            "config": {"model": f"GPT-2-XL shape ({L}L, d 1600, 25 heads, d_ff 6400, vocab 50257), random init",
+                       "batch": B, "prompt_len": P, "max_new": new, "mode": args.mode,
+                       "parallelism": f"tensor parallel x{world} (heads / FFN columns / vocabulary)",
+                       "int8_weight_bytes_per_step": step_bytes},
+            "decode_tok_s": round(B * nsteps / dsec, 1), "decode_ms_per_step": round(dsec / nsteps * 1e3, 4),
+            "decode_weight_gbs": round(step_bytes * nsteps / dsec / 1e9, 1),
+            "weight_bytes_per_rank_per_step": int(step_bytes / world),
+            "exchanges_per_step": 2 * L + 1, "token_digest": digest, "weights_setup_s": round(setup_s, 1),
+            "timing": "CUDA events around the 127 decode steps (graph replays), best of 2, max over ranks"}
+
+
 def run_sharded(args, torch, rank, world, dev, dist):
     """One large MatMulQ split across the ranks (strong scaling: the total work is
     fixed): --workload sharded:M,K,N,S with S = N (column split + all-gather) or
@@ -1077,6 +1134,14 @@ def main():
     if args.workload == "gpt2_decode":
         if rank == 0:
             print(json.dumps({"metric": METRIC, "impl": "ours", "n_gpus": 1, **run_gpt2_decode(args, torch, dev)}))
+        return
+    if args.workload == "tp_decode":
+        line = run_tp_decode(args, torch, rank, world, dev, dist)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(line))
         return
     if args.workload.startswith("sharded:"):
         line = run_sharded(args, torch, rank, world, dev, dist)

@@ -300,8 +300,9 @@ typedef struct mtrtq_shard_comm {
 } mtrtq_shard_comm;
 
 /* [begin, end) of `rank`'s shard of an extent (N for MTRTQ_SPLIT_N, K for
- * MTRTQ_SPLIT_K): whole 128-channel tiles or 64-k units, split as evenly as possible,
- * earlier ranks taking the extra ones. */
+ * MTRTQ_SPLIT_K): whole 128-channel tiles or 64-k units, split as evenly as possible
+ * (rank r starts at unit floor(r * units / world): later ranks take the extra ones;
+ * with fewer units than ranks some shards are empty). */
 int mtrtq_shard_range(int64_t extent, int split, int rank, int world, int64_t* begin, int64_t* end);
 /* Bytes of one rank's slot buffer for split K; workspace of the local product. */
 int64_t mtrtq_shard_slot_bytes(int64_t M, int64_t N, int world);

@@ -36,9 +36,10 @@ UNIT_K = 64    # k per packed unit
 
 
 def shard_ranges(total: int, world: int, quantum: int) -> list[tuple[int, int]]:
-    """[begin, end) of each rank: whole `quantum` blocks split as evenly as possible,
-    earlier ranks taking the extra blocks; the last range ends at `total`. Ranks
-    past the last block get empty ranges."""
+    """[begin, end) of each rank: whole `quantum` blocks split as evenly as possible
+    (rank r starts at block floor(r * blocks / world), so later ranks take the extra
+    blocks); the last range ends at `total`. With fewer blocks than ranks some
+    ranges are empty."""
     blocks = -(-total // quantum)
     out = []
     for r in range(world):

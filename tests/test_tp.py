@@ -66,7 +66,7 @@ def _free_port():
 @pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_tp_on_two_gpus():
-    """Two ranks: a 2-layer GPT-2-XL-shaped model (25 heads split 13 / 12) against
+    """Two ranks: a 2-layer GPT-2-XL-shaped model (25 heads split 12 / 13) against
     the oracle, and GPT-2-small-shaped tokens against the unsplit decoder."""
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
