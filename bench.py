@@ -104,7 +104,7 @@ def peaks():
 
 
 # Kernel (function name) that each plan path launches.
-PATH_KERNELS = {"gemv": "gemv_q8_kernel", "gemm_tc": "gemm_q8_tc_kernel",
+PATH_KERNELS = {"gemv": "gemv_q8_kernel", "gemm_tc": "gemm_q8_tc_kernel", "gemv_stream": "gemv_stream_kernel",
                 "stream_k_tc": "skinny_q8_tc_kernel", "cluster_gemv": "gemv_cluster_kernel"}
 
 # Arithmetic of each path: what the product is computed in.

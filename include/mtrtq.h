@@ -68,6 +68,9 @@ enum { MTRTQ_DTYPE_F32 = 0, MTRTQ_DTYPE_BF16 = 1 };
  *    range, x = (s/127)(d0 + d1/2^7 + d2/2^14) with s the range's max |x|, which
  *    represents it to within 2^-15 s/127 (about 2^-22 of that max); int8 x int8
  *    warp MMAs accumulate exactly in int32, and the digits are combined in fp32.
+ *  - 32 < M <= 64 on weights of at most 8 MiB, either mode: the grouped GEMV
+ *    (mtrtq_gemv_group's kernel) over blocks of 8 tokens that share the weights,
+ *    with the cluster GEMV's arithmetic.
  *  - bf16 mode, M <= 32 otherwise: a stream-K tcgen05 kernel; above, a tiled
  *    tcgen05 GEMM. Weights are dequantized to bf16 exactly, products accumulate in
  *    fp32 in TMEM.
@@ -363,7 +366,8 @@ enum {
                                   mtrtq_plan_info). Otherwise one kernel for every
                                   call: 1 CUDA-core split-K GEMV; 2 tile tcgen05 GEMM;
                                   3 stream-K tcgen05 kernel (M <= 32); 4 cluster
-                                  GEMV (M <= 64).
+                                  GEMV (M <= 64); 5 grouped GEMV over blocks of 8
+                                  tokens (M <= 64, mtrtq_gemv_group's kernel).
                                   2 and 3 need MTRTQ_MODE_BF16. A call the forced
                                   kernel cannot take fails with
                                   MTRTQ_ERR_INVALID_ARG. */

@@ -24,7 +24,7 @@ struct Epilogue {
 // problem alone (and the device's SM count), so the workspace query and the
 // launch always agree.
 struct Plan {
-  enum Kind { kGemv = 0, kGemmTC = 1, kSkinnyTC = 2, kGemvCluster = 3 } kind = kGemv;
+  enum Kind { kGemv = 0, kGemmTC = 1, kSkinnyTC = 2, kGemvCluster = 3, kGemvStream = 4 } kind = kGemv;
   int64_t M = 0, K = 0, N = 0;
   int64_t n_pad = 0, k_pad = 0;    // packed weight extents
   int n_tiles = 0;                 // channel tiles of 128

@@ -149,10 +149,10 @@ def plan_info(M: int, K: int, N: int, x_dtype=torch.float32, mode: str = "bf16")
     xd = _lib.DTYPE_BF16 if x_dtype == torch.bfloat16 else _lib.DTYPE_F32
     info = (ctypes.c_int64 * 6)()
     check(lib().mtrtq_plan_info(M, K, N, xd, MODES[mode], info, 6), "mtrtq_plan_info")
-    path = {0: "gemv", 1: "gemm_tc", 2: "stream_k_tc", 3: "cluster_gemv"}[info[0]]
+    path = {0: "gemv", 1: "gemm_tc", 2: "stream_k_tc", 3: "cluster_gemv", 4: "gemv_stream"}[info[0]]
     out = {"path": path, "tile_m": info[1], "m_tiles": info[2], "n_tiles": info[3],
            "k_per_split": info[5]}
-    out["ctas" if path.startswith("stream_k") else "splits"] = info[4]
+    out["ctas" if path in ("stream_k_tc", "gemv_stream") else "splits"] = info[4]
     return out
 
 

@@ -109,7 +109,7 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.mtrtq_workspace_bytes(0, 64, 64, 0, 0) == -1
     assert lib.mtrtq_workspace_bytes(1, 1 << 31, 64, 0, 0) == -1
     assert lib.mtrtq_set_option(99, 0) == _lib.ERR_INVALID_ARG
-    assert lib.mtrtq_set_option(_lib.OPT_FORCE_PATH, 5) == _lib.ERR_INVALID_ARG
+    assert lib.mtrtq_set_option(_lib.OPT_FORCE_PATH, 6) == _lib.ERR_INVALID_ARG
     assert lib.mtrtq_matmul(None, 0, 64, None, None, None, None, 64, 1, 64, 64, 0, None, 0,
                             None) == _lib.ERR_INVALID_ARG
 
@@ -126,11 +126,12 @@ def test_launch_without_device_fails_loudly():
 @pytest.mark.parametrize("M,K,N,mode,path", [
     (1, 768, 50257, "bf16", "cluster_gemv"), (8, 768, 768, "fp32", "cluster_gemv"),
     (8, 3072, 768, "bf16", "cluster_gemv"), (9, 768, 768, "bf16", "cluster_gemv"),
-    (32, 768, 3072, "bf16", "cluster_gemv"), (33, 768, 3072, "bf16", "cluster_gemv"),
+    (32, 768, 3072, "bf16", "cluster_gemv"), (33, 768, 3072, "bf16", "gemv_stream"),
     (16, 768, 50257, "bf16", "stream_k_tc"), (16, 768, 50257, "fp32", "cluster_gemv"),
-    (64, 768, 3072, "bf16", "cluster_gemv"), (65, 768, 3072, "bf16", "gemm_tc"),
+    (64, 768, 3072, "bf16", "gemv_stream"), (65, 768, 3072, "bf16", "gemm_tc"),
     (64, 4096, 4096, "bf16", "gemm_tc"), (64, 4096, 14336, "fp32", "cluster_gemv"),
-    (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "cluster_gemv"),
+    (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv_stream"),
+    (40, 3072, 768, "fp32", "gemv_stream"),
     (65, 768, 3072, "fp32", "gemv"),
     (1, 768, 200000, "bf16", "cluster_gemv"), (33, 768, 200000, "bf16", "gemm_tc"),
     (8, 24576, 128, "bf16", "stream_k_tc"), (32, 65536, 128, "bf16", "stream_k_tc"),
@@ -145,6 +146,12 @@ def test_planner(M, K, N, mode, path):
         kb = -(-K // 64)
         assert info["ctas"] == max(1, min(148, units // -(-kb // 8)))
         assert matmulq.workspace_bytes(M, K, N, torch.float32, mode) >= 4096 + info["ctas"] * 2 * M * 512
+        return
+    if path == "gemv_stream":
+        # blocks of 8 tokens sharing the weights, three persistent CTAs per SM at most
+        units = info["n_tiles"] * (-(-K // 64)) * (-(-M // 8))
+        assert info["ctas"] == min(148 * 3, units) and info["m_tiles"] == -(-M // 8)
+        assert matmulq.workspace_bytes(M, K, N, torch.float32, mode) == 4096 + info["ctas"] * 8192
         return
     if path == "cluster_gemv":
         # CS ranks take near-equal ranges of the 64-k units; no workspace
@@ -181,7 +188,7 @@ def test_forced_paths_change_the_plan():
         with pytest.raises(_lib.MtrtqError):
             matmulq.plan_info(65, 768, 768)
         with pytest.raises(_lib.MtrtqError):
-            matmulq.set_option(_lib.OPT_FORCE_PATH, 5)
+            matmulq.set_option(_lib.OPT_FORCE_PATH, 6)
     finally:
         matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
 
