@@ -14,9 +14,13 @@
 //     peer's slot buffer); its last block releases one arrival on every peer's
 //     data flag (gpu-scope acq_rel tickets among the blocks, then one
 //     system-scope fence and a relaxed add on each peer's flag);
-//   * finish: split N waits for every peer's arrival; split K waits, then sums the
-//     ranks' slots in rank order (fixed, so every rank gets identical bits) and
-//     adds the bias once.
+//   * finish: split N -- the push kernel's last block, after signalling, waits for
+//     every peer's arrival, so the kernel ends when the rank holds every segment;
+//     split K -- a reduce kernel waits, then sums the ranks' slots in rank order
+//     (fixed, so every rank gets identical bits) and adds the bias once.
+// Where the caller's destinations alternate between two buffers (comm.alternating)
+// the entry barrier is skipped: a peer's data for the previous exchange already
+// shows it has finished reading the buffer this one writes.
 // Every wait spins on the rank's own flag with an acquire load, bounded by about
 // a second of SM clock; a wait that gives up stores MTRTQ_ERR_TIMEOUT in the
 // device status word and returns.
@@ -117,7 +121,7 @@ __global__ void shard_epoch_kernel(unsigned* own_flags) {
 // Stores every segment of src into every peer's destination, then the last block
 // to finish releases one arrival on every peer's data flag.
 __global__ void shard_push_kernel(const float* src, SegList segs, ShardPeers peers, int rank, int world,
-                                  unsigned epoch) {
+                                  unsigned epoch, bool wait_after, unsigned* status) {
   __shared__ unsigned s_ticket;
   epoch = call_epoch(peers.flags[rank], epoch);
   if (*reinterpret_cast<volatile unsigned*>(peers.flags[rank] + kFlagAbort) == epoch) return;
@@ -153,11 +157,11 @@ __global__ void shard_push_kernel(const float* src, SegList segs, ShardPeers pee
     peers.flags[rank][kFlagTicket] = 0u;
     for (int p = 0; p < world; ++p)
       if (p != rank) red_add_relaxed_sys(peers.flags[p] + kFlagData, 1u);
+    // All-gather: the same block then waits for every peer's data (it signalled
+    // its own first, so no rank waits on one that has not signalled); the kernel
+    // ends when this rank holds every segment.
+    if (wait_after) wait_flag(peers.flags[rank] + kFlagData, epoch * (unsigned)(world - 1), status);
   }
-}
-
-__global__ void shard_wait_kernel(unsigned* own_flags, int world, unsigned epoch, unsigned* status) {
-  if (threadIdx.x == 0) wait_flag(own_flags + kFlagData, call_epoch(own_flags, epoch) * (unsigned)(world - 1), status);
 }
 
 // Split K: waits for every peer's slot, then y[m, n] = sum over ranks in rank
@@ -188,14 +192,18 @@ int grid_for(int64_t work, int sm_count);
 // Entry barrier (unless the caller's buffers alternate), then the push of `segs`
 // from src to every peer's dst base.
 cudaError_t launch_exchange(const float* src, const SegList& segs, ShardPeers peers, int rank, int world,
-                            unsigned epoch, unsigned* status, int sm_count, bool entry, cudaStream_t st) {
+                            unsigned epoch, unsigned* status, int sm_count, bool entry, bool wait_after,
+                            cudaStream_t st) {
   if (entry) {
     shard_entry_kernel<<<1, 32, 0, st>>>(peers, rank, world, epoch, status);
   } else if (epoch == 0) {
     shard_epoch_kernel<<<1, 32, 0, st>>>(peers.flags[rank]);
   }
+  // one block per SM at most: few blocks take the (same-address) tickets
   int64_t items = segs.first[segs.count];
-  shard_push_kernel<<<grid_for(items > 0 ? items : 1, sm_count), 256, 0, st>>>(src, segs, peers, rank, world, epoch);
+  int grid = grid_for(items > 0 ? items : 1, sm_count);
+  if (grid > sm_count) grid = sm_count;
+  shard_push_kernel<<<grid, 256, 0, st>>>(src, segs, peers, rank, world, epoch, wait_after, status);
   return cudaGetLastError();
 }
 
@@ -358,7 +366,7 @@ static int exchange_reduce(const mtrtq_shard_comm* comm, unsigned epoch, int64_t
     SegList segs = {};
     seg_add(segs, (int64_t)rank * M * N, 1, M * N, M * N, bases_aligned(comm->slots[rank], comm->slots, world));
     if (cudaError_t er = launch_exchange(comm->slots[rank], segs, peers_of(comm, comm->slots, 0), rank, world, epoch,
-                                         status, sm_count, !comm->alternating, st))
+                                         status, sm_count, !comm->alternating, false, st))
       return report_cuda_error(er, "shard exchange launch");
   }
   shard_reduce_kernel<<<grid_for(M * N, sm_count), 256, 0, st>>>(comm->slots[rank], M, N, world, bias, residual, ldr,
@@ -412,10 +420,8 @@ int mtrtq_matmul_sharded(const void* X, int x_dtype, int64_t ldx, const void* pa
     SegList segs = {};
     seg_add(segs, b, e > b ? M : 0, e - b, ldy, bases_aligned(Y, comm->y, world));
     if (cudaError_t er = launch_exchange(Y, segs, peers_of(comm, comm->y, 0), rank, world, epoch, status, sm_count,
-                                         !comm->alternating, st))
+                                         !comm->alternating, true, st))
       return report_cuda_error(er, "shard exchange launch");
-    shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[rank], world, epoch, status);
-    if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard wait launch");
     return MTRTQ_OK;
   }
   // split K: the scaled partial over this rank's k range into its own slot
@@ -450,10 +456,8 @@ int mtrtq_shard_allgather(const mtrtq_shard_segment* segments, int count, const 
   if (comm->world == 1) return MTRTQ_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cudaError_t er = launch_exchange(comm->y[comm->rank], segs, peers_of(comm, comm->y, 0), comm->rank, comm->world,
-                                       epoch, status, sm_count, !comm->alternating, st))
+                                       epoch, status, sm_count, !comm->alternating, true, st))
     return report_cuda_error(er, "shard exchange launch");
-  shard_wait_kernel<<<1, 32, 0, st>>>(comm->flags[comm->rank], comm->world, epoch, status);
-  if (cudaError_t er = cudaGetLastError()) return report_cuda_error(er, "shard wait launch");
   return MTRTQ_OK;
 }
 
