@@ -18,7 +18,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libmtrtq.so")
-SOURCES = ["abi.cu", "prepack.cu", "gemv.cu", "gemv_cluster.cu", "gemv_stream.cu", "decoder.cu", "gemm_tc.cu",
+SOURCES = ["abi.cu", "prepack.cu", "gemv.cu", "gemv_cluster.cu", "gemv_stream.cu", "gemv_tc.cu", "decoder.cu",
+           "gemm_tc.cu",
            "skinny_tc.cu", "shard.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",

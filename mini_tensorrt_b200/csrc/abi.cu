@@ -152,7 +152,7 @@ static bool stream_plan_fits(int64_t M, int64_t n_tiles) {
   return M <= 64 && ceil_div64(M, 8) * n_tiles <= kStreamMaxTiles;
 }
 
-// force_path: 0 chooses by shape and mode; 1, 2, 3, 4, 5 select a kernel (see
+// force_path: 0 chooses by shape and mode; 1 to 6 select a kernel (see
 // MTRTQ_OPT_FORCE_PATH). Callers pass the process-wide option.
 int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_count, Plan* out,
                 int force_path) {
@@ -191,6 +191,9 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
     if (M > 32 && M <= 64 && small_w && stream_plan_fits(M, p.n_tiles)) path = 5;
   }
   if (force_path != 0) {
+    if (force_path == 6 && (M > kTcMaxTokens || p.n_tiles > kStreamMaxTiles))
+      return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core digit GEMV takes M <= %d and at most %d channel tiles",
+                  kTcMaxTokens, kStreamMaxTiles);
     if ((force_path == 2 || force_path == 3) && mode != MTRTQ_MODE_BF16)
       return fail(MTRTQ_ERR_INVALID_ARG, "the tensor-core kernels compute in MTRTQ_MODE_BF16 only");
     if (force_path == 3 && (M > 32 || p.n_tiles > kMaxSplitTiles))
@@ -212,6 +215,21 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   if (path == 4) {
     gemv_cluster_plan(M, sm_count, &p);
     p.round_x = (mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32);
+    *out = p;
+    return MTRTQ_OK;
+  }
+  if (path == 6) {
+    p.kind = Plan::kGemvTC;
+    p.tile_m = gemv_tc_tokens((int)M);
+    p.m_tiles = 1;
+    p.kunits = (int)(p.k_pad / kBlockK);
+    p.kunits_per_split = p.kunits;
+    const int64_t units = (int64_t)p.n_tiles * p.kunits;
+    p.grid = gemv_tc_grid(units, sm_count, p.tile_m);
+    p.round_x = (mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32);
+    GroupProblem g;
+    g.KB = p.kunits;
+    p.total = gemv_tc_layout(&g, 1, p.grid, p.tile_m).total;
     *out = p;
     return MTRTQ_OK;
   }
@@ -326,6 +344,28 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   return MTRTQ_OK;
 }
 
+// The one problem of a single call as a group of one (the digit GEMV's launch).
+GroupProblem single_problem(const Plan& p, const void* X, int64_t ldx, const void* packed, const float* scale,
+                            const float* bias, float* Y, int64_t ldy, const Epilogue& epi) {
+  GroupProblem g;
+  g.X = X;
+  g.ldx = ldx;
+  g.W = static_cast<const char*>(packed);
+  g.scale = scale;
+  g.bias = bias;
+  g.Y = Y;
+  g.ldy = ldy;
+  g.epi = epi;
+  g.M = (int)p.M;
+  g.K = (int)p.K;
+  g.N = (int)p.N;
+  g.KB = p.kunits;
+  g.n_tiles = p.n_tiles;
+  g.tile_begin = 0;
+  g.unit_begin = 0;
+  return g;
+}
+
 int check_device_sm100(DeviceInfo* d) {
   if (int rc = current_device(d)) return rc;
   if (d->major != 10)
@@ -401,7 +441,7 @@ int mtrtq_set_option(int option, int64_t value) {
       g_opt_gemm_a_source = (int)value;
       return MTRTQ_OK;
     case MTRTQ_OPT_FORCE_PATH:
-      if (value < 0 || value > 5) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0 to 5");
+      if (value < 0 || value > 6) return fail(MTRTQ_ERR_INVALID_ARG, "path is 0 to 6");
       g_opt_force_path = (int)value;
       return MTRTQ_OK;
     case MTRTQ_OPT_OVERLAP_LAUNCH:
@@ -577,6 +617,13 @@ int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed,
     if (e != cudaSuccess) return cuda_fail(e, "grouped GEMV launch");
     return MTRTQ_OK;
   }
+  if (p.kind == Plan::kGemvTC) {
+    const GroupProblem g = single_problem(p, X, ldx, packed, scale, bias, Y, ldy, epi);
+    e = launch_gemv_tc(&g, 1, (int64_t)p.n_tiles * p.kunits, p.grid, p.tile_m, x_dtype, p.round_x, workspace,
+                       status, g_opt_overlap != 0, st);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMV launch");
+    return MTRTQ_OK;
+  }
   if (p.kind == Plan::kGemvCluster) {
     e = launch_gemv_cluster(p, X, x_dtype, ldx, packed, scale, bias, Y, ldy, status,
                             g_opt_overlap != 0, epi, st);
@@ -659,18 +706,27 @@ int mtrtq_matmul_ln_ex(const float* X, int64_t ldx, const float* ln_gamma, const
   if (int rc = check_device_sm100(&d)) return rc;
   Plan p;
   if (int rc = plan_matmul(M, K, N, MTRTQ_DTYPE_F32, mode, d.sm_count, &p, g_opt_force_path)) return rc;
-  if (p.kind != Plan::kGemvCluster)
+  if (p.kind != Plan::kGemvCluster && p.kind != Plan::kGemvTC)
     return fail(MTRTQ_ERR_INVALID_ARG,
-                "the LayerNorm prologue runs on the cluster GEMV only; this call plans another kernel "
-                "(M=%lld K=%lld N=%lld): run mtrtq_layernorm, then mtrtq_matmul_ex",
+                "the LayerNorm prologue runs on the decode GEMVs only (M <= 64); this call plans another "
+                "kernel (M=%lld K=%lld N=%lld): run mtrtq_layernorm, then mtrtq_matmul_ex",
                 (long long)M, (long long)K, (long long)N);
   if (!aligned(packed, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "packed weights must be 256-byte aligned");
   if (!aligned(scale, 4) || (bias && !aligned(bias, 4)) || !aligned(Y, 4) || !aligned(ln_gamma, 4) ||
       !aligned(ln_beta, 4))
     return fail(MTRTQ_ERR_ALIGNMENT, "scale, bias, Y, gamma and beta must be 4-byte aligned");
   if (!aligned(X, 16)) return fail(MTRTQ_ERR_ALIGNMENT, "X must be 16-byte aligned");
-  (void)workspace;
-  (void)workspace_bytes;
+  if (p.kind == Plan::kGemvTC) {
+    if (!workspace || workspace_bytes < p.total)
+      return fail(MTRTQ_ERR_WORKSPACE, "workspace %zu bytes < %zu", workspace_bytes, p.total);
+    if (!aligned(workspace, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    const GroupProblem g = single_problem(p, X, ldx, packed, scale, bias, Y, ldy, epi);
+    cudaError_t e = launch_gemv_tc(&g, 1, (int64_t)p.n_tiles * p.kunits, p.grid, p.tile_m, MTRTQ_DTYPE_F32,
+                                   p.round_x, workspace, d.status, g_opt_overlap != 0,
+                                   static_cast<cudaStream_t>(stream), ln_gamma, ln_beta, ln_eps);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMV launch");
+    return MTRTQ_OK;
+  }
   cudaError_t e = launch_gemv_cluster(p, X, MTRTQ_DTYPE_F32, ldx, packed, scale, bias, Y, ldy, d.status,
                                       g_opt_overlap != 0, epi, static_cast<cudaStream_t>(stream), ln_gamma,
                                       ln_beta, ln_eps);
@@ -803,7 +859,7 @@ namespace {
 // Validates a group and lays its problems out in one unit list; *units and *tiles
 // receive the totals. Device pointers are checked only when check_ptrs is set.
 int group_layout(const mtrtq_gemv_problem* probs, int count, bool check_ptrs, GroupProblem* out,
-                 int64_t* units, int* tiles) {
+                 int64_t* units, int* tiles, int max_m) {
   if (!probs) return fail(MTRTQ_ERR_INVALID_ARG, "null problem list");
   if (count < 1 || count > kGroupMax)
     return fail(MTRTQ_ERR_INVALID_ARG, "a group holds 1 to %d problems (got %d)", kGroupMax, count);
@@ -812,7 +868,8 @@ int group_layout(const mtrtq_gemv_problem* probs, int count, bool check_ptrs, Gr
   for (int i = 0; i < count; ++i) {
     const mtrtq_gemv_problem& q = probs[i];
     if (int rc = check_dims(q.M, q.K, q.N)) return rc;
-    if (q.M > 8) return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: a group takes M <= 8 (M=%lld)", i, (long long)q.M);
+    if (q.M > max_m)
+      return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: a group takes M <= %d (M=%lld)", i, max_m, (long long)q.M);
     if (q.epilogue != MTRTQ_EPILOGUE_NONE && q.epilogue != MTRTQ_EPILOGUE_GELU_TANH &&
         q.epilogue != MTRTQ_EPILOGUE_ADD_RESIDUAL)
       return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: unknown epilogue %d", i, q.epilogue);
@@ -860,6 +917,17 @@ int group_grid(int64_t units, int sm_count) {
   return (int)(units < g ? units : g);
 }
 
+// Groups run on the tensor-core digit GEMV (M <= 64), or on the mma.sync
+// grouped GEMV (M <= 8) when MTRTQ_OPT_FORCE_PATH is 5.
+bool group_on_stream_kernel() { return g_opt_force_path == 5; }
+int group_max_m() { return group_on_stream_kernel() ? 8 : kTcMaxTokens; }
+
+int group_max_tokens(const GroupProblem* gp, int count) {
+  int m = 1;
+  for (int i = 0; i < count; ++i) m = gp[i].M > m ? gp[i].M : m;
+  return m;
+}
+
 }  // namespace
 }  // namespace mtrtq
 
@@ -869,8 +937,13 @@ int64_t mtrtq_gemv_group_workspace_bytes(const mtrtq_gemv_problem* problems, int
   GroupProblem gp[kGroupMax];
   int64_t units = 0;
   int tiles = 0;
-  if (group_layout(problems, count, false, gp, &units, &tiles) != MTRTQ_OK) return -1;
-  return (int64_t)gemv_stream_workspace_bytes(group_grid(units, sm_count_or_default()));
+  if (group_layout(problems, count, false, gp, &units, &tiles, kTcMaxTokens) != MTRTQ_OK) return -1;
+  // Enough for either kernel, so that the option may change between calls.
+  const int sm = sm_count_or_default();
+  const size_t a = gemv_stream_workspace_bytes(group_grid(units, sm));
+  const int nt = gemv_tc_tokens(group_max_tokens(gp, count));
+  const size_t b = gemv_tc_layout(gp, count, gemv_tc_grid(units, sm, nt), nt).total;
+  return (int64_t)(a > b ? a : b);
 }
 
 int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype, int mode, void* workspace,
@@ -884,17 +957,23 @@ int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype,
   GroupProblem gp[kGroupMax];
   int64_t units = 0;
   int tiles = 0;
-  if (int rc = group_layout(problems, count, true, gp, &units, &tiles)) return rc;
+  if (int rc = group_layout(problems, count, true, gp, &units, &tiles, group_max_m())) return rc;
   DeviceInfo d;
   if (int rc = check_device_sm100(&d)) return rc;
-  const int grid = group_grid(units, d.sm_count);
-  const size_t need = gemv_stream_workspace_bytes(grid);
+  const bool on_stream = group_on_stream_kernel();
+  const int nt = gemv_tc_tokens(group_max_tokens(gp, count));
+  const int grid = on_stream ? group_grid(units, d.sm_count) : gemv_tc_grid(units, d.sm_count, nt);
+  const size_t need =
+      on_stream ? gemv_stream_workspace_bytes(grid) : gemv_tc_layout(gp, count, grid, nt).total;
   if (!workspace || workspace_bytes < need)
     return fail(MTRTQ_ERR_WORKSPACE, "workspace %zu bytes < %zu", workspace_bytes, need);
   if (!aligned(workspace, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
   const bool round_x = mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32;
-  cudaError_t e = launch_gemv_stream(gp, count, units, grid, x_dtype, round_x, workspace, d.status,
-                                     g_opt_overlap != 0, g_opt_producers, static_cast<cudaStream_t>(stream));
+  cudaError_t e =
+      on_stream ? launch_gemv_stream(gp, count, units, grid, x_dtype, round_x, workspace, d.status,
+                                     g_opt_overlap != 0, g_opt_producers, static_cast<cudaStream_t>(stream))
+                : launch_gemv_tc(gp, count, units, grid, nt, x_dtype, round_x, workspace, d.status,
+                                 g_opt_overlap != 0, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "grouped GEMV launch");
   return MTRTQ_OK;
 }
@@ -904,11 +983,11 @@ int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int6
   Plan p;
   if (int rc = plan_matmul(M, K, N, x_dtype, mode, sm_count_or_default(), &p, g_opt_force_path))
     return rc;
-  info[0] = p.kind;  // 0 GEMV, 1 tile GEMM, 2 stream-K tcgen05, 3 cluster GEMV, 4 grouped GEMV
+  info[0] = p.kind;  // 0 GEMV, 1 tile GEMM, 2 stream-K tcgen05, 3 cluster GEMV, 4 grouped GEMV, 5 digit tcgen05 GEMV
   info[1] = p.tile_m;
   info[2] = p.m_tiles;
   info[3] = p.n_tiles;
-  info[4] = (p.kind == Plan::kSkinnyTC || p.kind == Plan::kGemvStream) ? p.grid : p.splits;
+  info[4] = (p.kind == Plan::kSkinnyTC || p.kind == Plan::kGemvStream || p.kind == Plan::kGemvTC) ? p.grid : p.splits;
   info[5] = p.kunits_per_split * (p.kind == Plan::kGemv ? kSlabK : kBlockK);
   return MTRTQ_OK;
 }

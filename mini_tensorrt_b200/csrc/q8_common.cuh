@@ -273,6 +273,41 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// K-major operand in shared memory without swizzle ("interleaved" canonical
+// layout): 8 x 16-byte core matrices, the 8 rows of each at 16-byte stride; the
+// two core matrices of one K = 32-byte step lbo bytes apart (leading byte
+// offset), consecutive 8-row groups sbo bytes apart (stride byte offset); version
+// 1 (sm_100), layout type 0 (SWIZZLE_NONE). The packed weight unit (16-k slabs of
+// 128 rows x 16 bytes) is this layout with lbo = 2048 and sbo = 128.
+__device__ __forceinline__ uint64_t umma_desc_interleave(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);    // start address
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;       // leading byte offset
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;       // stride byte offset
+  d |= (uint64_t)1 << 46;                            // descriptor version
+  return d;                                          // base offset 0, SWIZZLE_NONE
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::i8 (s8 inputs, s32 accumulate).
+__device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor: kind::i8, A = B = signed 8-bit, D = s32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_s8(int M, int N) {
+  return (2u << 4)                          // D format s32
+         | (1u << 7)                        // A format signed 8-bit
+         | (1u << 10)                       // B format signed 8-bit
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
 // Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major, M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
   return (1u << 4)                          // D format f32
@@ -308,6 +343,16 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&v)
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
         "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
         "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// 32 lanes x 32 bits, 8 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7])
       : "r"(taddr)
       : "memory");
 }

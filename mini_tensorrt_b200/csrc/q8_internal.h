@@ -24,7 +24,7 @@ struct Epilogue {
 // problem alone (and the device's SM count), so the workspace query and the
 // launch always agree.
 struct Plan {
-  enum Kind { kGemv = 0, kGemmTC = 1, kSkinnyTC = 2, kGemvCluster = 3, kGemvStream = 4 } kind = kGemv;
+  enum Kind { kGemv = 0, kGemmTC = 1, kSkinnyTC = 2, kGemvCluster = 3, kGemvStream = 4, kGemvTC = 5 } kind = kGemv;
   int64_t M = 0, K = 0, N = 0;
   int64_t n_pad = 0, k_pad = 0;    // packed weight extents
   int n_tiles = 0;                 // channel tiles of 128
@@ -96,6 +96,49 @@ inline size_t gemv_stream_workspace_bytes(int grid) {
 cudaError_t launch_gemv_stream(const GroupProblem* probs, int count, int64_t units, int grid, int x_dtype,
                                bool round_x, void* workspace, unsigned* status, bool pdl, int producers,
                                cudaStream_t st);
+
+// Tensor-core digit GEMV (gemv_tc.cu): up to kGroupMax independent problems of
+// M <= kTcMaxTokens tokens in one persistent launch, one CTA per SM, each CTA a
+// contiguous range of the group's 64-k weight units as in the grouped GEMV. A
+// digitize kernel first writes four int8 digits of every activation (per token,
+// scaled by the row's max |x|) in the MMA's operand layout; tcgen05 kind::i8 MMAs
+// then multiply the weight units, straight from the shared memory ring, by the
+// digits into s32 accumulators in tensor memory.
+constexpr int kTcMaxTokens = 64;
+// Tokens per launch (the MMA's N is four digits x this): the smallest of 8, 16,
+// 32 and 64 that holds the largest M of the group.
+inline int gemv_tc_tokens(int max_m) { return max_m <= 8 ? 8 : max_m <= 16 ? 16 : max_m <= 32 ? 32 : 64; }
+// CTAs per SM: two (each with half the shared memory ring and 256 TMEM columns)
+// up to 32 tokens, one at 64 (its two 256-column accumulators fill TMEM).
+inline int gemv_tc_ctas_per_sm(int nt) { return nt == 64 ? 1 : 2; }
+// Persistent CTAs: at most gemv_tc_ctas_per_sm per SM, and none with fewer than
+// four 64-k units (fewer parts for a small problem's cut tiles to add).
+inline int gemv_tc_grid(int64_t units, int sm_count, int nt) {
+  const int64_t by_units = (units + 3) / 4;
+  const int64_t slots = (int64_t)sm_count * gemv_tc_ctas_per_sm(nt);
+  return (int)(by_units < slots ? by_units : slots);
+}
+// Workspace: tickets | per-token scales [kGroupMax][64] | [grid][2][nt][128] fp32
+// partials | each problem's digits, KB units of 256 * nt bytes.
+struct TcLayout {
+  size_t off_scales = 0, off_partials = 0, off_digits = 0, total = 0;
+};
+inline TcLayout gemv_tc_layout(const GroupProblem* probs, int count, int grid, int nt) {
+  TcLayout l;
+  l.off_scales = kStreamCounterBytes;
+  l.off_partials = l.off_scales + (size_t)kGroupMax * kTcMaxTokens * sizeof(float);
+  l.off_digits = l.off_partials + (((size_t)grid * 2 * nt * 128 * sizeof(float) + 255) & ~(size_t)255);
+  size_t d = 0;
+  for (int i = 0; i < count; ++i) d += (size_t)probs[i].KB * 256 * nt;
+  l.total = l.off_digits + d;
+  return l;
+}
+// ln_gamma non-null (one problem, fp32 X): each row of X is layer-normalized
+// (ln_gamma, ln_beta, ln_eps) before the product.
+cudaError_t launch_gemv_tc(const GroupProblem* probs, int count, int64_t units, int grid, int nt, int x_dtype,
+                           bool round_x, void* workspace, unsigned* status, bool pdl, cudaStream_t st,
+                           const float* ln_gamma = nullptr, const float* ln_beta = nullptr,
+                           float ln_eps = 0.0f);
 
 // Cluster GEMV: CTAs resident per SM (registers are capped to allow it) and the
 // shared memory a CTA may use so that they fit, for M <= 8 and for larger M (more

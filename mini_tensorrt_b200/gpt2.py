@@ -171,7 +171,9 @@ class DeviceDecoder:
         check(lib().mtrtq_matmul_ln_ex(x.data_ptr(), x.stride(0), ln[0].data_ptr(), ln[1].data_ptr(),
                                        self.cfg.eps, w.packed.data_ptr(), w.scale.data_ptr(),
                                        bias.data_ptr() if bias is not None else None, y.data_ptr(),
-                                       y.stride(0), x.shape[0], w.K, w.N, MODES[self.mode], None, 0, epilogue,
+                                       y.stride(0), x.shape[0], w.K, w.N, MODES[self.mode],
+                                       self.ws_buf.data_ptr() if self.ws_buf is not None else None,
+                                       self.ws_buf.numel() if self.ws_buf is not None else 0, epilogue,
                                        None, 0, self._sp), "mtrtq_matmul_ln_ex")
 
     def _ln_then(self, name, ln, w, bias, y, epilogue=_lib.EPILOGUE_NONE):

@@ -149,10 +149,10 @@ def plan_info(M: int, K: int, N: int, x_dtype=torch.float32, mode: str = "bf16")
     xd = _lib.DTYPE_BF16 if x_dtype == torch.bfloat16 else _lib.DTYPE_F32
     info = (ctypes.c_int64 * 6)()
     check(lib().mtrtq_plan_info(M, K, N, xd, MODES[mode], info, 6), "mtrtq_plan_info")
-    path = {0: "gemv", 1: "gemm_tc", 2: "stream_k_tc", 3: "cluster_gemv", 4: "gemv_stream"}[info[0]]
+    path = {0: "gemv", 1: "gemm_tc", 2: "stream_k_tc", 3: "cluster_gemv", 4: "gemv_stream", 5: "gemv_tc"}[info[0]]
     out = {"path": path, "tile_m": info[1], "m_tiles": info[2], "n_tiles": info[3],
            "k_per_split": info[5]}
-    out["ctas" if path in ("stream_k_tc", "gemv_stream") else "splits"] = info[4]
+    out["ctas" if path in ("stream_k_tc", "gemv_stream", "gemv_tc") else "splits"] = info[4]
     return out
 
 
@@ -272,8 +272,9 @@ def matmul_q8_ln(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: 
                  bias: torch.Tensor | None = None, out: torch.Tensor | None = None, mode: str = "bf16",
                  stream=None, epilogue: str = "none", residual: torch.Tensor | None = None) -> torch.Tensor:
     """out = epilogue(LayerNorm(x; gamma, beta, eps) @ dequant(w) (+ bias)) in one
-    kernel (mtrtq_matmul_ln_ex). x: float32 CUDA [M, K]; raises MtrtqError when the
-    shape plans a kernel other than the cluster GEMV (check supports_ln first)."""
+    launch sequence (mtrtq_matmul_ln_ex). x: float32 CUDA [M, K]; raises MtrtqError
+    when the shape plans a kernel other than the decode GEMVs (check supports_ln
+    first)."""
     if x.dim() != 2 or x.shape[1] != w.K or x.dtype != torch.float32 or x.stride(1) != 1:
         raise ValueError(f"x must be float32 [M, {w.K}] with unit stride along K")
     M = x.shape[0]
@@ -282,10 +283,13 @@ def matmul_q8_ln(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: 
     epi = EPILOGUES[epilogue]
     if epi == _lib.EPILOGUE_ADD_RESIDUAL and (residual is None or residual.shape != (M, w.N)):
         raise ValueError("the residual epilogue needs residual float32 [M, N]")
+    need = lib().mtrtq_workspace_bytes(M, w.K, w.N, _lib.DTYPE_F32, MODES[mode])
+    ws = default_workspace(x.device).get(need) if need > 0 else None
     with torch.cuda.device(x.device):
         check(lib().mtrtq_matmul_ln_ex(x.data_ptr(), x.stride(0), gamma.data_ptr(), beta.data_ptr(), float(eps),
                                        w.packed.data_ptr(), w.scale.data_ptr(), _ptr(bias), out.data_ptr(),
-                                       out.stride(0), M, w.K, w.N, MODES[mode], None, 0, epi,
+                                       out.stride(0), M, w.K, w.N, MODES[mode], _ptr(ws),
+                                       ws.numel() if ws is not None else 0, epi,
                                        _ptr(residual) if epi == _lib.EPILOGUE_ADD_RESIDUAL else None,
                                        residual.stride(0) if epi == _lib.EPILOGUE_ADD_RESIDUAL else 0,
                                        _stream_ptr(stream)),
@@ -294,8 +298,8 @@ def matmul_q8_ln(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: 
 
 
 def supports_ln(M: int, K: int, N: int, mode: str = "bf16") -> bool:
-    """Whether mtrtq_matmul_ln_ex takes this shape (it plans the cluster GEMV)."""
-    return plan_info(M, K, N, torch.float32, mode)["path"] == "cluster_gemv"
+    """Whether mtrtq_matmul_ln_ex takes this shape (it plans a decode GEMV)."""
+    return plan_info(M, K, N, torch.float32, mode)["path"] in ("cluster_gemv", "gemv_tc")
 
 
 def host_workspace_bytes(M: int, K: int, N: int, mode: str = "bf16") -> int:

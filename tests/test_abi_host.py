@@ -109,7 +109,7 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.mtrtq_workspace_bytes(0, 64, 64, 0, 0) == -1
     assert lib.mtrtq_workspace_bytes(1, 1 << 31, 64, 0, 0) == -1
     assert lib.mtrtq_set_option(99, 0) == _lib.ERR_INVALID_ARG
-    assert lib.mtrtq_set_option(_lib.OPT_FORCE_PATH, 6) == _lib.ERR_INVALID_ARG
+    assert lib.mtrtq_set_option(_lib.OPT_FORCE_PATH, 7) == _lib.ERR_INVALID_ARG
     assert lib.mtrtq_matmul(None, 0, 64, None, None, None, None, 64, 1, 64, 64, 0, None, 0,
                             None) == _lib.ERR_INVALID_ARG
 
@@ -187,8 +187,16 @@ def test_forced_paths_change_the_plan():
         assert matmulq.workspace_bytes(8, 768, 768, torch.float32, "fp32") == 0
         with pytest.raises(_lib.MtrtqError):
             matmulq.plan_info(65, 768, 768)
+        matmulq.set_option(_lib.OPT_FORCE_PATH, 6)
+        info = matmulq.plan_info(40, 768, 3072, mode="fp32")
+        assert info["path"] == "gemv_tc" and info["tile_m"] == 64 and info["ctas"] == _tc_grid(24 * 12, 64) == 72
+        assert matmulq.workspace_bytes(40, 768, 3072, torch.float32, "fp32") == _tc_workspace([(40, 768)], 24 * 12)
+        assert matmulq.plan_info(8, 768, 50257)["ctas"] == 296
+        assert matmulq.plan_info(1, 64, 128)["ctas"] == 1
         with pytest.raises(_lib.MtrtqError):
-            matmulq.set_option(_lib.OPT_FORCE_PATH, 6)
+            matmulq.plan_info(65, 768, 768)
+        with pytest.raises(_lib.MtrtqError):
+            matmulq.set_option(_lib.OPT_FORCE_PATH, 7)
     finally:
         matmulq.set_option(_lib.OPT_FORCE_PATH, 0)
 
@@ -230,21 +238,43 @@ def _problem(M, K, N):
     return p
 
 
+def _tc_grid(units, nt):
+    """The digit GEMV's persistent CTAs: two per SM up to 32 tokens (one at 64), and
+    none with fewer than four 64-k units."""
+    return min(-(-units // 4), 148 * (1 if nt == 64 else 2))
+
+
+def _tc_workspace(problems, units):
+    """The digit GEMV's workspace: part counters (4 KiB), per-token scales (16 x 64
+    fp32), [grid][2][nt][128] fp32 partials (256-byte rounded), and each problem's
+    digits, 256 * nt bytes per 64-k unit; nt = 8, 16, 32 or 64 holds the largest M."""
+    mmax = max(M for M, _ in problems)
+    nt = next(t for t in (8, 16, 32, 64) if mmax <= t)
+    part = -(-(_tc_grid(units, nt) * 2 * nt * 128 * 4) // 256) * 256
+    return 4096 + 16 * 64 * 4 + part + sum(-(-K // 64) * 256 * nt for _, K in problems)
+
+
 def test_group_workspace_and_limits():
-    """mtrtq_gemv_group_workspace_bytes: tickets (4 KiB) + 8 KiB of partials per CTA,
-    three CTAs per SM but never more CTAs than 64-k units; groups of 1..16
-    problems of M <= 8 and at most 1024 channel tiles."""
+    """mtrtq_gemv_group_workspace_bytes: enough for either group kernel -- the digit
+    GEMV (one CTA per SM, at most one per 64-k unit) and the mma.sync grouped GEMV
+    (tickets + 8 KiB of partials per CTA, three CTAs per SM); groups of 1..16
+    problems of M <= 64 and at most 1024 channel tiles."""
     lib = _lib.lib()
     decode = [(M, K, N) for M in (1, 8) for K, N in ((768, 2304), (768, 768), (768, 3072), (3072, 768),
                                                        (768, 50257))]
     arr = (_lib.GemvProblem * 10)(*[_problem(*s) for s in decode])
-    assert lib.mtrtq_gemv_group_workspace_bytes(arr, 10) == 4096 + 148 * 3 * 8192
+    want = max(4096 + 148 * 3 * 8192, _tc_workspace([(M, K) for M, K, _ in decode], 11160))
+    assert lib.mtrtq_gemv_group_workspace_bytes(arr, 10) == want
     one = (_lib.GemvProblem * 1)(_problem(1, 64, 128))
-    assert lib.mtrtq_gemv_group_workspace_bytes(one, 1) == 4096 + 1 * 8192
+    assert lib.mtrtq_gemv_group_workspace_bytes(one, 1) == max(4096 + 1 * 8192, _tc_workspace([(1, 64)], 1))
+    wide_m = (_lib.GemvProblem * 2)(_problem(64, 768, 3072), _problem(9, 100, 300))
+    units = 24 * 12 + 3 * 2
+    assert lib.mtrtq_gemv_group_workspace_bytes(wide_m, 2) == max(
+        4096 + min(units, 444) * 8192, _tc_workspace([(64, 768), (9, 100)], units))
     assert lib.mtrtq_gemv_group_workspace_bytes(arr, 0) == -1
     many = (_lib.GemvProblem * 17)(*[_problem(1, 64, 128)] * 17)
     assert lib.mtrtq_gemv_group_workspace_bytes(many, 17) == -1
-    assert lib.mtrtq_gemv_group_workspace_bytes((_lib.GemvProblem * 1)(_problem(9, 64, 128)), 1) == -1
+    assert lib.mtrtq_gemv_group_workspace_bytes((_lib.GemvProblem * 1)(_problem(65, 64, 128)), 1) == -1
     wide = (_lib.GemvProblem * 3)(*[_problem(1, 64, 50257)] * 3)  # 3 x 393 tiles > 1024
     assert lib.mtrtq_gemv_group_workspace_bytes(wide, 3) == -1
     assert "1024" in _lib.last_error()

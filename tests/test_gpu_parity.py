@@ -595,8 +595,8 @@ def test_layernorm_prologue_refuses_other_kernels(cuda_device):
     pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
     x = torch.zeros((65, 768), device=cuda_device)
     g = torch.ones(768, device=cuda_device)
-    with pytest.raises(_lib.MtrtqError, match="cluster GEMV"):
+    with pytest.raises(_lib.MtrtqError, match="decode GEMVs"):
         matmulq.matmul_q8_ln(x, g, g, 1e-5, pw)  # M = 65: the tile GEMM
     with forced(1):
-        with pytest.raises(_lib.MtrtqError, match="cluster GEMV"):
+        with pytest.raises(_lib.MtrtqError, match="decode GEMVs"):
             matmulq.matmul_q8_ln(x[:4], g, g, 1e-5, pw)
