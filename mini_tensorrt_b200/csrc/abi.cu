@@ -95,6 +95,7 @@ size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 constexpr int64_t kMaxDim = int64_t(1) << 30;
 constexpr size_t kCounterBytes = 4096;                       // fixed ticket region
 constexpr int64_t kMaxSplitTiles = kCounterBytes / sizeof(unsigned);
+constexpr int64_t kDigitTcMinWeights = int64_t(24) << 20;  // K * N from which 8 < M <= 64 runs on it
 // Weight bytes up to which bf16 calls with 8 < M <= 64 take the cluster GEMV.
 constexpr int64_t kClusterWideMaxBytes = 8ll << 20;
 
@@ -189,6 +190,14 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
     // sharing the weights (the cluster GEMV's eight-block instance runs one CTA per
     // SM in two waves there: FFN-up 64 x 768 x 3072 + bias 15.3 us against 23.1 us).
     if (M > 32 && M <= 64 && small_w && stream_plan_fits(M, p.n_tiles)) path = 5;
+    // 8 < M <= 64 (bf16 mode: <= 32) on large weights: the tensor-core digit GEMV,
+    // one pass over the weights for all the tokens (B200, fp32 mode: 16 x 4096 x
+    // 14336 21.5 us against 55.8 on the cluster GEMV, 32 x 768 x 50257 28.0
+    // against 59.5, 64 x 14336 x 4096 61 against 304 on the CUDA-core GEMV; bf16
+    // mode: 16 x 4096 x 14336 22.3 against 27.3 on the stream-K kernel). Below about
+    // 25M weights the other kernels' lower fixed cost wins.
+    const bool digit_tc_w = K * N >= kDigitTcMinWeights && p.n_tiles <= kStreamMaxTiles;
+    if (M > 8 && digit_tc_w && M <= (mode == MTRTQ_MODE_FP32 ? kTcMaxTokens : 32)) path = 6;
   }
   if (force_path != 0) {
     if (force_path == 6 && (M > kTcMaxTokens || p.n_tiles > kStreamMaxTiles))

@@ -431,15 +431,30 @@ __device__ __forceinline__ void tc_epilogue(const TcParams& p, uint32_t tmem, ui
     // The lowest CTA's part of a cut tile is its last segment unless the tile
     // starts its range; every later CTA's part is its first segment.
     const int first_slot = tc_range_start(c_lo, U, G) == T0 ? 0 : 1;
+    // A finisher adds the other CTAs' parts first: every token's load of one CTA's
+    // part in flight at once, the CTAs in order.
+    float s[NT];
+#pragma unroll
+    for (int m = 0; m < NT; ++m) s[m] = 0.0f;
     if (finisher) {
       if (etid == 0) tc_wait_parts(counter, (unsigned)(c_hi - c_lo), s_abort, p.status);
       named_bar_sync(1, kTcEpiThreads);  // the parts are visible to every thread (acquired above)
+      for (int64_t cc = c_lo; cc < c_hi; ++cc) {
+        const float* part = p.partials + ((size_t)(cc * 2 + (cc == c_lo ? first_slot : 0)) * NT) * kTileN + row;
+        float t[NT];
+#pragma unroll
+        for (int m = 0; m < NT; ++m) t[m] = m < P.M ? __ldcg(part + m * kTileN) : 0.0f;
+#pragma unroll
+        for (int m = 0; m < NT; ++m) s[m] += t[m];
+      }
     }
     ok = ok && mbar_wait_bounded(&accf[ab], (uint32_t)(seg / C::kBufs) & 1u, s_abort, p.status);
     tc_fence_after();
     const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ab * C::kAccCols);
     const int groups = (P.M + 7) >> 3;
-    for (int g = 0; g < groups; ++g) {
+#pragma unroll
+    for (int g = 0; g < NT / 8; ++g) {
+      if (g >= groups) break;
       float v8[8];
       if (ok) {
         tc_load8<NT>(ta, g, v8);
@@ -453,26 +468,12 @@ __device__ __forceinline__ void tc_epilogue(const TcParams& p, uint32_t tmem, ui
           if (g * 8 + j < P.M) __stcg(slot + (g * 8 + j) * kTileN + row, v8[j]);
         continue;
       }
-      if (finisher) {
-        float s8[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s8[j] = 0.0f;
-        for (int64_t cc = c_lo; cc < c_hi; ++cc) {
-          const float* part = p.partials + ((size_t)(cc * 2 + (cc == c_lo ? first_slot : 0)) * NT) * kTileN + row;
-          float t8[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) t8[j] = g * 8 + j < P.M ? __ldcg(part + (g * 8 + j) * kTileN) : 0.0f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) s8[j] += t8[j];
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v8[j] = s8[j] + v8[j];
-      }
       if (n < P.N) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int m = g * 8 + j;
-          if (m < P.M) P.Y[(int64_t)m * P.ldy + n] = tc_finish(P, v8[j], __ldg(sc + m), m, n);
+          if (m < P.M)
+            P.Y[(int64_t)m * P.ldy + n] = tc_finish(P, finisher ? s[m] + v8[j] : v8[j], __ldg(sc + m), m, n);
         }
       }
     }

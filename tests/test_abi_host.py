@@ -127,9 +127,12 @@ def test_launch_without_device_fails_loudly():
     (1, 768, 50257, "bf16", "cluster_gemv"), (8, 768, 768, "fp32", "cluster_gemv"),
     (8, 3072, 768, "bf16", "cluster_gemv"), (9, 768, 768, "bf16", "cluster_gemv"),
     (32, 768, 3072, "bf16", "cluster_gemv"), (33, 768, 3072, "bf16", "gemv_stream"),
-    (16, 768, 50257, "bf16", "stream_k_tc"), (16, 768, 50257, "fp32", "cluster_gemv"),
+    (16, 768, 50257, "bf16", "gemv_tc"), (16, 768, 50257, "fp32", "gemv_tc"),
+    (16, 4096, 4096, "bf16", "stream_k_tc"), (16, 4096, 4096, "fp32", "cluster_gemv"),
+    (32, 4096, 14336, "bf16", "gemv_tc"), (64, 14336, 4096, "fp32", "gemv_tc"),
+    (33, 4096, 14336, "bf16", "gemm_tc"), (8, 4096, 14336, "fp32", "cluster_gemv"),
     (64, 768, 3072, "bf16", "gemv_stream"), (65, 768, 3072, "bf16", "gemm_tc"),
-    (64, 4096, 4096, "bf16", "gemm_tc"), (64, 4096, 14336, "fp32", "cluster_gemv"),
+    (64, 4096, 4096, "bf16", "gemm_tc"), (64, 4096, 14336, "fp32", "gemv_tc"),
     (2048, 4096, 14336, "bf16", "gemm_tc"), (64, 768, 3072, "fp32", "gemv_stream"),
     (40, 3072, 768, "fp32", "gemv_stream"),
     (65, 768, 3072, "fp32", "gemv"),
@@ -152,6 +155,12 @@ def test_planner(M, K, N, mode, path):
         units = info["n_tiles"] * (-(-K // 64)) * (-(-M // 8))
         assert info["ctas"] == min(148 * 3, units) and info["m_tiles"] == -(-M // 8)
         assert matmulq.workspace_bytes(M, K, N, torch.float32, mode) == 4096 + info["ctas"] * 8192
+        return
+    if path == "gemv_tc":
+        nt = next(t for t in (8, 16, 32, 64) if M <= t)
+        units = info["n_tiles"] * (-(-K // 64))
+        assert info["tile_m"] == nt and info["ctas"] == _tc_grid(units, nt)
+        assert matmulq.workspace_bytes(M, K, N, torch.float32, mode) == _tc_workspace([(M, K)], units)
         return
     if path == "cluster_gemv":
         # CS ranks take near-equal ranges of the 64-k units; no workspace
