@@ -68,13 +68,21 @@ enum { MTRTQ_DTYPE_F32 = 0, MTRTQ_DTYPE_BF16 = 1 };
  *    range, x = (s/127)(d0 + d1/2^7 + d2/2^14) with s the range's max |x|, which
  *    represents it to within 2^-15 s/127 (about 2^-22 of that max); int8 x int8
  *    warp MMAs accumulate exactly in int32, and the digits are combined in fp32.
- *  - 32 < M <= 64 on weights of at most 8 MiB, either mode: the grouped GEMV
- *    (mtrtq_gemv_group's kernel) over blocks of 8 tokens that share the weights,
- *    with the cluster GEMV's arithmetic.
+ *  - 32 < M <= 64 on weights of at most 8 MiB, either mode: the mma.sync grouped
+ *    GEMV over blocks of 8 tokens that share the weights, with the cluster GEMV's
+ *    arithmetic.
+ *  - 8 < M <= 64 (bf16 mode: <= 32) on 24M weights or more: the tensor-core digit
+ *    GEMV (also mtrtq_gemv_group's kernel). A digitize kernel writes each
+ *    activation row as four int8 digits, x = (s/127)(d0 + d1/2^7 + d2/2^14 +
+ *    d3/2^21) with s the row's max |x| (within 2^-22 s/127); tcgen05 kind::i8 MMAs
+ *    multiply the int8 weights by the digits with exact int32 sums in TMEM, and
+ *    the digit sums are combined in fp32. One pass over the weights for all tokens.
  *  - bf16 mode, M <= 32 otherwise: a stream-K tcgen05 kernel; above, a tiled
- *    tcgen05 GEMM. Weights are dequantized to bf16 exactly, products accumulate in
- *    fp32 in TMEM.
- *  - fp32 mode above M = 32: a CUDA-core split-K GEMV, every product and sum fp32.
+ *    tcgen05 GEMM (persistent, two TMEM accumulators, when it has a 256-token tile
+ *    per SM). Weights are dequantized to bf16 exactly, products accumulate in fp32
+ *    in TMEM.
+ *  - fp32 mode above M = 32 otherwise: a CUDA-core split-K GEMV, every product and
+ *    sum fp32.
  * In every kernel the per-channel scale multiplies the finished sum, then the bias
  * is added, as in the reference (src/ops/kernels_matmul.cpp:66-73). */
 enum { MTRTQ_MODE_BF16 = 0, MTRTQ_MODE_FP32 = 1 };
@@ -224,7 +232,7 @@ int mtrtq_matmul_gemv_noalloc(const void* X, int x_dtype, int64_t ldx, const voi
 /* ---- a group of independent decode products in one launch ------------------------ */
 
 /* One problem of a group: Y = X x dequant(W) (+ bias), then the epilogue, with the
- * arguments of mtrtq_matmul_ex (M <= 8). */
+ * arguments of mtrtq_matmul_ex (M <= 64; M <= 8 under MTRTQ_OPT_FORCE_PATH 5). */
 typedef struct mtrtq_gemv_problem {
   const void* X;          /* [M, ldx], 16-byte aligned, the group's x_dtype */
   int64_t ldx;
@@ -233,7 +241,7 @@ typedef struct mtrtq_gemv_problem {
   const float* bias;      /* [N] or NULL */
   float* Y;               /* [M, ldy] */
   int64_t ldy;
-  int64_t M, K, N;        /* 1 <= M <= 8 */
+  int64_t M, K, N;        /* 1 <= M <= 64 */
   int epilogue;           /* MTRTQ_EPILOGUE_* */
   const float* residual;  /* MTRTQ_EPILOGUE_ADD_RESIDUAL: [M, ldr] (may be Y) */
   int64_t ldr;
@@ -241,22 +249,26 @@ typedef struct mtrtq_gemv_problem {
 
 #define MTRTQ_GROUP_MAX 16
 
-/* Computes `count` (1..MTRTQ_GROUP_MAX) independent decode products in one launch
- * of the persistent grouped GEMV: the problems' 64-k weight units are split into
- * equal contiguous ranges over three CTAs per SM, so every SM streams the same
+/* Computes `count` (1..MTRTQ_GROUP_MAX) independent decode products in one
+ * persistent launch of the tensor-core digit GEMV (after its digitize kernel): the
+ * problems' 64-k weight units are split into equal contiguous ranges over two CTAs
+ * per SM (one when a problem has more than 32 tokens), so every SM streams the same
  * bytes whatever the shapes and the launch's fixed cost is paid once. Results are
- * those of mtrtq_matmul_ex on each problem within its tolerance (the cluster GEMV's
- * arithmetic: int8 weights times three int8 digits of each activation, exact int32
- * sums), deterministic (cut tiles are summed in a fixed order).
+ * those of mtrtq_matmul_ex on each problem within its tolerance (int8 weights times
+ * four int8 digits of each activation row, exact int32 sums), deterministic (the
+ * parts of a tile cut between CTAs are added in a fixed order). Under
+ * MTRTQ_OPT_FORCE_PATH 5 the group runs on the mma.sync grouped GEMV instead (M <= 8,
+ * three CTAs per SM, three digits per value).
  *
  * Replaces a run of independent MatMulQ calls of the reference
  * (src/ops/kernels_matmul.cpp:42-74), such as the Q, K and V projections its KV
  * decoder issues one after another (tools/run_gpt2.cpp:142-150).
  *
  * No Y may overlap another problem's X, Y or residual. At most 1024 channel tiles
- * of 128 in all. workspace: >= mtrtq_gemv_group_workspace_bytes, 256-byte aligned,
- * zero-filled once after allocation (calls leave its tickets at zero); calls
- * sharing it must be stream-ordered. Honours MTRTQ_OPT_OVERLAP_LAUNCH. */
+ * of 128 in all. workspace: >= mtrtq_gemv_group_workspace_bytes (enough for either
+ * kernel), 256-byte aligned, zero-filled once after allocation (calls leave its
+ * counters at zero; after a MTRTQ_ERR_TIMEOUT fill it again); calls sharing it must
+ * be stream-ordered. Honours MTRTQ_OPT_OVERLAP_LAUNCH. */
 int64_t mtrtq_gemv_group_workspace_bytes(const mtrtq_gemv_problem* problems, int count);
 int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype, int mode, void* workspace,
                      size_t workspace_bytes, void* stream);
@@ -359,16 +371,23 @@ int mtrtq_ipc_close(void* device_ptr);
  * beyond fp32 summation order; the workspace size depends on them, so set them
  * before querying mtrtq_workspace_bytes. */
 enum {
-  MTRTQ_OPT_GEMM_A_SOURCE = 1, /* 0 (default): dequantized weights staged in TMEM
-                                  (tcgen05.mma A from tensor memory);
-                                  1: staged in 128-byte-swizzled shared memory */
+  MTRTQ_OPT_GEMM_A_SOURCE = 1, /* tile tcgen05 GEMM. 0 (default): the persistent
+                                  kernel (one CTA per SM, two TMEM accumulators,
+                                  dequantized weights in 128-byte-swizzled shared
+                                  memory) when the plan has at least one 256-token
+                                  tile per SM and no k split, otherwise one tile
+                                  per CTA with the weights staged in TMEM;
+                                  1: one tile per CTA, weights in shared memory;
+                                  2: one tile per CTA, weights in TMEM */
   MTRTQ_OPT_FORCE_PATH = 2,    /* 0 (default): chosen by shape and mode (see
                                   mtrtq_plan_info). Otherwise one kernel for every
                                   call: 1 CUDA-core split-K GEMV; 2 tile tcgen05 GEMM;
                                   3 stream-K tcgen05 kernel (M <= 32); 4 cluster
-                                  GEMV (M <= 64); 5 grouped GEMV over blocks of 8
-                                  tokens (M <= 64, mtrtq_gemv_group's kernel).
-                                  2 and 3 need MTRTQ_MODE_BF16. A call the forced
+                                  GEMV (M <= 64); 5 mma.sync grouped GEMV over
+                                  blocks of 8 tokens (M <= 64; also makes
+                                  mtrtq_gemv_group use it, for M <= 8); 6 tensor-core
+                                  digit GEMV (M <= 64, mtrtq_gemv_group's default
+                                  kernel). 2 and 3 need MTRTQ_MODE_BF16. A call the forced
                                   kernel cannot take fails with
                                   MTRTQ_ERR_INVALID_ARG. */
   MTRTQ_OPT_OVERLAP_LAUNCH = 3 /* 0 (default) or 1: the cluster GEMV is launched with

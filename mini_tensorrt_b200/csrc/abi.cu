@@ -44,7 +44,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 // Process-wide options (mtrtq_set_option).
-int g_opt_gemm_a_source = 0;  // 0: dequantized weights in TMEM, 1: in shared memory
+int g_opt_gemm_a_source = 0;  // 0: automatic, 1: one tile per CTA, A in shared memory, 2: A in TMEM
 int g_opt_force_path = 0;     // 0 auto, else the kernel (MTRTQ_OPT_FORCE_PATH)
 int g_opt_overlap = 0;        // 1: programmatic dependent launch (MTRTQ_OPT_OVERLAP_LAUNCH)
 int g_opt_producers = 1;      // grouped GEMV: bulk-copy issuing lanes (MTRTQ_OPT_PRODUCER_LANES)
@@ -330,6 +330,17 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
     p.splits = (int)ceil_div64(p.kunits, kbps);
     p.x_to_bf16 = (x_dtype == MTRTQ_DTYPE_F32);
     p.ldxb = round_up64(K, 8);
+    // At least three 256-token tiles per SM and no k split: the persistent kernel
+    // (its epilogue overlaps the next tile's MMAs; B200, M = 2048: 4096 x 14336 973
+    // TFLOP/s against 868, 4096 x 11008 995 against 914), unless
+    // MTRTQ_OPT_GEMM_A_SOURCE asks for a one-tile-per-CTA kernel. With fewer tiles
+    // per SM the one-tile-per-CTA kernel, whose dequantized weights sit in TMEM
+    // rather than shared memory, stays ahead (14336 x 4096: 1053 against 984).
+    const int64_t tiles = (int64_t)p.n_tiles * p.m_tiles;
+    if (tm == 256 && p.splits == 1 && tiles >= 3 * (int64_t)sm_count && g_opt_gemm_a_source == 0) {
+      p.persistent = true;
+      p.grid = sm_count;
+    }
   }
 
   // Split-K tickets live in a fixed region at the start of every workspace (each
@@ -409,6 +420,20 @@ static std::set<std::pair<int, const void*>> g_smem_done;
 
 bool overlap_launch_enabled() { return g_opt_overlap != 0; }
 
+// (device, kernel) pairs whose preferred carveout is the largest shared memory.
+static std::set<std::pair<int, const void*>> g_carveout_done;
+
+cudaError_t ensure_max_carveout(const void* kernel) {
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return e;
+  std::lock_guard<std::mutex> lk(g_smem_mu);
+  if (g_carveout_done.count({dev, kernel})) return cudaSuccess;
+  cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) g_carveout_done.insert({dev, kernel});
+  return e;
+}
+
 cudaError_t ensure_smem_limit(const void* kernel, int bytes) {
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return e;
@@ -446,7 +471,7 @@ const char* mtrtq_last_error(void) { return g_last_error.c_str(); }
 int mtrtq_set_option(int option, int64_t value) {
   switch (option) {
     case MTRTQ_OPT_GEMM_A_SOURCE:
-      if (value != 0 && value != 1) return fail(MTRTQ_ERR_INVALID_ARG, "GEMM A source is 0 or 1");
+      if (value < 0 || value > 2) return fail(MTRTQ_ERR_INVALID_ARG, "GEMM A source is 0, 1 or 2");
       g_opt_gemm_a_source = (int)value;
       return MTRTQ_OK;
     case MTRTQ_OPT_FORCE_PATH:
@@ -685,7 +710,7 @@ int mtrtq_matmul_ex(const void* X, int x_dtype, int64_t ldx, const void* packed,
   const int rc = make_x_tensor_map(&xmap, xb, M, K, ldxb, p.tile_m);
   if (rc != 0) return fail(MTRTQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", rc);
   e = launch_gemm_tc(p, xb, ldxb, packed, scale, bias, Y, ldy, workspace, xmap,
-                     g_opt_gemm_a_source == 0 ? 1 : 0, status, epi, st);
+                     g_opt_gemm_a_source == 1 ? 0 : 1, status, epi, st);
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return MTRTQ_OK;
 }

@@ -309,6 +309,227 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---- persistent variant: one CTA per SM over a static tile schedule ----------------
+//
+// For grids of at least one tile per SM and one k split. Ten warps: warp 0 the
+// producer (as above), warp 1 the MMA issuer, warps 2..5 dequantize each weight tile
+// into a 128-byte-swizzled shared memory ring (the A operand), warps 6..9 the
+// epilogue. TMEM holds two 256-column fp32 accumulators: the MMAs of a CTA's next
+// tile run while the epilogue drains the last one, so the per-tile epilogue (128
+// KiB of fp32 Y) and set-up no longer stall the tensor pipe. CTA c takes tiles c,
+// c + G, c + 2G, ..., token tiles fastest, so that the CTAs working at the same time
+// share channel tiles (weights) and every token tile (X) in L2.
+constexpr int kPgThreads = 320;
+constexpr int kPgLoadStages = 4;  // X (32 KiB) + W (8 KiB) per stage
+constexpr int kPgAStages = 2;     // dequantized A, 16 KiB per stage
+
+struct PgCfg {
+  static constexpr int TM = 256;
+  static constexpr int X_STAGE = TM * 128;
+  static constexpr int W_STAGE = kTileN * kBlockK;
+  static constexpr int A_STAGE = kTileN * 128;
+  static constexpr int OFF_X = 0;
+  static constexpr int OFF_A = OFF_X + kPgLoadStages * X_STAGE;
+  static constexpr int OFF_W = OFF_A + kPgAStages * A_STAGE;
+  static constexpr int OFF_BAR = OFF_W + kPgLoadStages * W_STAGE;
+  static constexpr int NUM_BARS = 2 * kPgLoadStages + 2 * kPgAStages + 4 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 32 + 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
+
+__global__ void __launch_bounds__(kPgThreads, 1)
+    gemm_q8_tc_persistent_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p) {
+  using C = PgCfg;
+  constexpr int TM = C::TM;
+  constexpr int SL = kPgLoadStages, SA = kPgAStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;                    // X + W landed: 1 + tx
+  uint64_t* empty = bars + SL;              // load stage free: 4 dequantizing warps + 1 commit
+  uint64_t* a_full = bars + 2 * SL;         // A written: 4 dequantizing warps
+  uint64_t* a_empty = a_full + SA;          // A consumed: 1 commit
+  uint64_t* acc_full = a_empty + SA;        // [2] accumulator final: 1 commit
+  uint64_t* acc_empty = acc_full + 2;       // [2] accumulator drained: 4 epilogue warps
+  uint64_t* done = acc_empty + 2;           // every MMA of this CTA complete
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = p.m_tiles * p.n_tiles;
+  const int KB = p.KB;
+
+  if (tid == 0) {
+    for (int s = 0; s < SL; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 5);
+    }
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&a_full[s], 4);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) prefetch_tensormap(&xmap);
+  if (warp == 1) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int64_t li = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < T; tile += gridDim.x) {
+        const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+        for (int kb = 0; kb < KB; ++kb, ++li) {
+          const int s = (int)(li % SL);
+          if (li >= SL && !mbar_wait_bounded(&empty[s], ((uint32_t)(li / SL) & 1u) ^ 1u, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::X_STAGE + C::W_STAGE);
+          tma_load_2d(smem + C::OFF_X + s * C::X_STAGE, &xmap, kb * kBlockK, mt * TM, &full[s]);
+          bulk_g2s(smem + C::OFF_W + s * C::W_STAGE, p.W + ((int64_t)nt * KB + kb) * (int64_t)C::W_STAGE,
+                   C::W_STAGE, &full[s]);
+        }
+      }
+      for (int64_t j = li - 1; j >= 0 && j >= li - SL; --j) mbar_drain(&full[j % SL], (uint32_t)(j / SL) & 1u, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
+      int64_t li = 0, ai = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < T; tile += gridDim.x, ++it) {
+        const int b = it & 1;
+        if (it >= 2 && !mbar_wait_bounded(&acc_empty[b], (uint32_t)((it >> 1) - 1) & 1u, s_abort, p.status)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem_base + (uint32_t)(b * TM);
+        for (int kb = 0; kb < KB; ++kb, ++li, ++ai) {
+          const int s = (int)(li % SL), sa = (int)(ai % SA);
+          if (!mbar_wait_bounded(&a_full[sa], (uint32_t)(ai / SA) & 1u, s_abort, p.status) ||
+              !mbar_wait_bounded(&full[s], (uint32_t)(li / SL) & 1u, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xaddr = smem_u32(smem + C::OFF_X + s * C::X_STAGE);
+          const uint32_t aaddr = smem_u32(smem + C::OFF_A + sa * C::A_STAGE);
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k)
+            umma_ss(acc, umma_desc_sw128(aaddr + k * 32), umma_desc_sw128(xaddr + k * 32), idesc,
+                    (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+          umma_commit(&a_empty[sa]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[b]);
+      }
+      umma_commit(done);  // MMAs must finish before TMEM is freed
+      mbar_drain(done, 0, p.status);
+    }
+  } else if (warp < 6) {
+    // Dequantize each weight tile: thread = channel row, 64 int8 -> bf16, into a
+    // 128-byte-swizzled row of the A stage.
+    const int r = (warp - 2) * 32 + lane;
+    int64_t li = 0, ai = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < T; tile += gridDim.x) {
+      for (int kb = 0; kb < KB; ++kb, ++li, ++ai) {
+        const int s = (int)(li % SL), sa = (int)(ai % SA);
+        if (!warp_wait(&full[s], (uint32_t)(li / SL) & 1u, s_abort, p.status)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* wst = smem + C::OFF_W + s * C::W_STAGE;
+        uint4 wv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const uint4*>(wst + j * kSlabBytes + r * 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        uint32_t a[32];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          i8x4_to_bf16x4(wv[j].x, a[8 * j + 0], a[8 * j + 1]);
+          i8x4_to_bf16x4(wv[j].y, a[8 * j + 2], a[8 * j + 3]);
+          i8x4_to_bf16x4(wv[j].z, a[8 * j + 4], a[8 * j + 5]);
+          i8x4_to_bf16x4(wv[j].w, a[8 * j + 6], a[8 * j + 7]);
+        }
+        if (ai >= SA && !warp_wait(&a_empty[sa], ((uint32_t)(ai / SA) & 1u) ^ 1u, s_abort, p.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* arow = smem + C::OFF_A + sa * C::A_STAGE + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) =
+              make_uint4(a[4 * c], a[4 * c + 1], a[4 * c + 2], a[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[sa]);
+      }
+    }
+  } else {
+    // Epilogue: thread = channel row = TMEM lane of its quarter.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < T; tile += gridDim.x, ++it) {
+      const int b = it & 1;
+      const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+      const bool ok = warp_wait(&acc_full[b], (uint32_t)(it >> 1) & 1u, s_abort, p.status);
+      tc_fence_after();
+      const int n = nt * kTileN + r;
+      const bool n_ok = n < p.N;
+      const float sc = n_ok ? __ldg(p.scale + n) : 0.0f;
+      const float bs = (n_ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
+      const int m0 = mt * TM;
+      if (ok) {
+        for (int c0 = 0; c0 < TM && m0 + c0 < p.M; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(tmem_base + lane_off + (uint32_t)(b * TM + c0), v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (n_ok && m < p.M) {
+              float y = __fmul_rn(__uint_as_float(v[j]), sc);
+              if (p.bias) y = __fadd_rn(y, bs);
+              p.Y[(int64_t)m * p.ldy + n] = epi_apply(p.epi, y, m, n);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
 template <int TM, bool A_TMEM, int STAGES>
 static cudaError_t launch_cfg(const GemmParams& gp, const CUtensorMap& xmap, cudaStream_t st) {
   using C = GemmCfg<TM, A_TMEM, STAGES>;
@@ -336,6 +557,14 @@ bool gemm_tile_supported(int tile_m) {
   return tile_m == 16 || tile_m == 32 || tile_m == 64 || tile_m == 128 || tile_m == 256;
 }
 
+static cudaError_t launch_persistent(const GemmParams& gp, const CUtensorMap& xmap, int grid, cudaStream_t st) {
+  if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemm_q8_tc_persistent_kernel),
+                                         PgCfg::SMEM_BYTES))
+    return e;
+  gemm_q8_tc_persistent_kernel<<<grid, kPgThreads, PgCfg::SMEM_BYTES, st>>>(xmap, gp);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const void* packed,
                            const float* scale, const float* bias, float* Y, int64_t ldy,
                            void* workspace, const CUtensorMap& xmap, int a_from_tmem,
@@ -361,6 +590,7 @@ cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const vo
   gp.counters = ws ? reinterpret_cast<unsigned*>(ws + p.off_counters) : nullptr;
   gp.partials = ws ? reinterpret_cast<float*>(ws + p.off_partials) : nullptr;
   gp.status = status;
+  if (p.persistent) return launch_persistent(gp, xmap, p.grid, st);
   return a_from_tmem ? launch_tm<true>(p.tile_m, gp, xmap, st)
                      : launch_tm<false>(p.tile_m, gp, xmap, st);
 }

@@ -632,17 +632,16 @@ cudaError_t tc_launch(const TcParams& tp, int x_dtype, bool round_x, bool pdl, c
   dc.stream = st;
   dc.attrs = attr;
   dc.numAttrs = pdl ? 1 : 0;
-  cudaError_t e;
+  void (*dk)(TcParams);
   if (x_dtype == 1)
-    e = cudaLaunchKernelEx(&dc, digitize_kernel<true, false, false>, tp);
+    dk = digitize_kernel<true, false, false>;
   else if (tp.ln_gamma)
-    e = round_x ? cudaLaunchKernelEx(&dc, digitize_kernel<false, true, true>, tp)
-                : cudaLaunchKernelEx(&dc, digitize_kernel<false, false, true>, tp);
-  else if (round_x)
-    e = cudaLaunchKernelEx(&dc, digitize_kernel<false, true, false>, tp);
+    dk = round_x ? digitize_kernel<false, true, true> : digitize_kernel<false, false, true>;
   else
-    e = cudaLaunchKernelEx(&dc, digitize_kernel<false, false, false>, tp);
+    dk = round_x ? digitize_kernel<false, true, false> : digitize_kernel<false, false, false>;
+  cudaError_t e = ensure_max_carveout(reinterpret_cast<const void*>(dk));
   if (e != cudaSuccess) return e;
+  if ((e = cudaLaunchKernelEx(&dc, dk, tp)) != cudaSuccess) return e;
 
   auto kern = gemv_tc_kernel<NT>;
   if ((e = ensure_smem_limit(reinterpret_cast<const void*>(kern), (int)TcCfg<NT>::kSmem))) return e;

@@ -38,6 +38,7 @@ struct Plan {
   int stages = 0;                  // cluster GEMV: shared memory ring stages
   bool x_to_bf16 = false;          // GEMM: X is staged as a bf16 copy in the workspace
   bool round_x = false;            // GEMV: round fp32 X to bf16 before the product
+  bool persistent = false;         // GEMM: one CTA per SM over the tiles (grid CTAs), two accumulators
   // workspace layout (byte offsets)
   size_t off_counters = 0, off_partials = 0, off_xb = 0, total = 0;
   int64_t ldxb = 0;                // row stride (elements) of the bf16 X copy
@@ -61,6 +62,11 @@ struct DeviceInfo {
 // Raises a kernel's dynamic shared memory limit to `bytes` on the current device,
 // once per (device, kernel); later calls only look the pair up.
 cudaError_t ensure_smem_limit(const void* kernel, int bytes);
+// Asks for the largest shared memory carveout for a small kernel that runs
+// between (or overlapped with) kernels using most of an SM's shared memory, so that
+// an SM running it need not change its L1 / shared memory split before their next
+// CTA can start there. Once per (device, kernel).
+cudaError_t ensure_max_carveout(const void* kernel);
 
 // Persistent grouped decode GEMV (gemv_stream.cu): up to kGroupMax independent
 // problems of M <= 8 tokens in one launch, their 64-k weight units split evenly

@@ -91,7 +91,7 @@ def test_decode_gemv_set(cuda_device, case, mode):
     check(Y, X, q, s, mode)
 
 
-@pytest.mark.parametrize("path,a_source", [(0, 0), (2, 0), (2, 1), (3, 0), (1, 0)],
+@pytest.mark.parametrize("path,a_source", [(0, 0), (2, 2), (2, 1), (3, 0), (1, 0)],
                          ids=["auto", "tile_A_tmem", "tile_A_smem", "stream_k", "gemv"])
 @pytest.mark.parametrize("mode", ["bf16", "fp32"])
 def test_single_op_with_bias(cuda_device, mode, path, a_source):
@@ -204,6 +204,49 @@ def test_strided_input_and_output(cuda_device):
         yb = ybig.cpu().numpy()
         assert np.all(yb[:, N:] == 7.0), "wrote outside the [M, N] window"
         check(yb[:, :N], X, q, s, mode, tc=(mode == "bf16"))
+
+
+PERSISTENT = [(2048, 768, 7168), (300, 1000, 60000), (2048, 4096, 14336), (700, 64, 50257)]
+
+
+@pytest.mark.parametrize("M,K,N", PERSISTENT, ids=[f"{M}x{K}x{N}" for M, K, N in PERSISTENT])
+@pytest.mark.parametrize("epilogue", ["none", "gelu", "residual"])
+def test_persistent_gemm(cuda_device, M, K, N, epilogue):
+    """The persistent tile GEMM (one CTA per SM, two TMEM accumulators) against the
+    oracle, and against the one-tile-per-CTA kernel on the same inputs."""
+    if epilogue != "none" and M * N > 2048 * 7168:
+        pytest.skip("epilogues are covered on the smaller shapes")
+    q, s = matmulq.quantize_per_channel(wl.weights(K, N, 1100 + K))
+    X = oracle.round_bf16(wl.activations(M, K, 1101))
+    b = wl.bias(N, 1102)
+    R = wl.activations(M, N, 1103) if epilogue == "residual" else None
+    info = matmulq.plan_info(M, K, N, torch.bfloat16, "bf16")
+    assert info["path"] == "gemm_tc" and info["tile_m"] == 256
+    pw = PackedWeight.from_int8(torch.from_numpy(q), torch.from_numpy(s), cuda_device)
+    xt = torch.from_numpy(X).to(cuda_device).to(torch.bfloat16)
+    bt = torch.from_numpy(b).to(cuda_device)
+    outs = []
+    for a_source in (0, 2):  # persistent (automatic: at least three tiles per SM), then one tile per CTA
+        matmulq.set_option(_lib.OPT_GEMM_A_SOURCE, a_source)
+        try:
+            y = torch.from_numpy(R).to(cuda_device) if R is not None else torch.full((M, N), float("nan"),
+                                                                                       device=cuda_device)
+            matmul_q8(xt, pw, bias=bt, out=y, mode="bf16", epilogue=epilogue,
+                      residual=y if epilogue == "residual" else None)
+            torch.cuda.synchronize()
+        finally:
+            matmulq.set_option(_lib.OPT_GEMM_A_SOURCE, 0)
+        assert matmulq.read_device_status() == 0
+        outs.append(y.cpu().numpy())
+    t = oracle.matmul_q8(X, q, s, b)
+    if epilogue == "gelu":
+        u = t.astype(np.float64)
+        t = (0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))).astype(np.float32)
+    elif epilogue == "residual":
+        t = (R + t).astype(np.float32)
+    assert np.all(np.isfinite(outs[0]))
+    assert rel_err(outs[0], t) <= BF16_SAME_INPUT_TOL_TC
+    assert rel_err(outs[0], outs[1]) <= 1e-6
 
 
 @pytest.mark.parametrize("M", [1, 8, 64, 2048])
