@@ -86,6 +86,9 @@ def parse():
     ap.add_argument("--multi", choices=["sharded", "replicas"], default="sharded",
                     help="N > 1: the decode set column-sharded over the ranks (strong scaling, default) or "
                          "one full set per rank (replicas)")
+    ap.add_argument("--exchange", choices=["fused", "separate"], default="fused",
+                    help="N > 1, sharded decode set: the all-gather fused into the grouped GEMV (default) or run "
+                         "after it (mtrtq_shard_allgather)")
     ap.add_argument("--step-launch", choices=["group", "hybrid", "calls"], default="group",
                     help="decode set: one grouped launch per step (default); hybrid: the eight smaller "
                          "calls grouped and the two LM heads as their own launches; calls: a launch per call")
@@ -483,8 +486,11 @@ def run_sharded_decode_set(args, torch, rank, world, dev, dist):
     stream = torch.cuda.Stream(dev)
 
     def one(g):
-        groups[g](stream)
-        peers.allgather(segments[g % 2], stream=stream)
+        if args.exchange == "fused":  # one call: the group's kernel stores to every rank
+            peers.group_allgather(groups[g], stream=stream)
+        else:
+            groups[g](stream)
+            peers.allgather(segments[g % 2], stream=stream)
 
     graphs = []
     with torch.cuda.stream(stream):
@@ -521,12 +527,17 @@ def run_sharded_decode_set(args, torch, rank, world, dev, dist):
     line = {"value": round(step_bytes * args.steps / secs / 1e9, 1), "ms_per_step": round(step_us / 1e3, 4),
             "scaling": "strong", "clocks": clk.summary(),
             "rank0_weight_bytes_per_step": my_bytes,
-            "exchange": {"how": "mtrtq_shard_allgather: entry barrier, peer stores, bounded wait (library kernels)",
+            "exchange": {"how": ("mtrtq_gemv_group_allgather: the grouped GEMV's epilogue stores every output to "
+                                 "every rank over NVLink; its last CTA signals the peers and waits, bounded, for "
+                                 "theirs (one call per step)") if args.exchange == "fused" else
+                                ("mtrtq_shard_allgather after the group: peer stores, bounded wait (library "
+                                 "kernels)"),
                          "bytes_received_per_rank_per_step": int(exch_bytes),
                          "nvlink_lower_bound_us": round(exch_bytes / 770e9 * 1e6, 3)},
-            # per step: the digitize kernel and the grouped GEMV, then the
-            # all-gather's epoch kernel (device-counted epochs) and push kernel
-            "gpu_launches": 4 * args.steps}
+            # per step: the digitize kernel and the grouped GEMV (fused: it also
+            # stores to the peers), or those, then the all-gather's epoch kernel
+            # (device-counted epochs) and push kernel
+            "gpu_launches": (2 if args.exchange == "fused" else 4) * args.steps}
     del graphs
     peers.close()
     return line

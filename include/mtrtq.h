@@ -314,6 +314,21 @@ typedef struct mtrtq_shard_comm {
                                         this one writes */
 } mtrtq_shard_comm;
 
+/* mtrtq_gemv_group with its all-gather fused in (split N across the ranks): each
+ * problem's Y lies in this rank's comm->y[rank] buffer (its column shard of an
+ * output every rank lays out the same way), and every output element is also stored
+ * at the same offset in every peer's buffer by the kernel that computes it (stores
+ * over NVLink); the launch's last CTA then signals every peer and waits, bounded,
+ * for their shards, so the call ends when every rank holds every rank's outputs.
+ * Needs comm->alternating = 1 (no entry barrier: successive calls must alternate
+ * between two output buffers) and every rank making the same calls in the same
+ * order; epoch as for mtrtq_shard_allgather (0: device-counted, for CUDA graphs).
+ * world = 1: mtrtq_gemv_group. Replaces the split-N step's product and all-gather
+ * pair (one MatMulQ, src/ops/kernels_matmul.cpp:42-74, per rank, then the gather). */
+int mtrtq_gemv_group_allgather(const mtrtq_gemv_problem* problems, int count, int x_dtype, int mode,
+                               void* workspace, size_t workspace_bytes, const mtrtq_shard_comm* comm,
+                               unsigned epoch, void* stream);
+
 /* [begin, end) of `rank`'s shard of an extent (N for MTRTQ_SPLIT_N, K for
  * MTRTQ_SPLIT_K): whole 128-channel tiles or 64-k units, split as evenly as possible
  * (rank r starts at unit floor(r * units / world): later ranks take the extra ones;

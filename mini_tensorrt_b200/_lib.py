@@ -112,6 +112,7 @@ SIGNATURES["mtrtq_ipc_import"] = (_int, [_vp, _vp])
 SIGNATURES["mtrtq_ipc_close"] = (_int, [_vp])
 SIGNATURES["mtrtq_gemv_group_workspace_bytes"] = (_i64, [_vp, _int])
 SIGNATURES["mtrtq_gemv_group"] = (_int, [_vp, _int, _int, _int, _vp, _sz, _vp])
+SIGNATURES["mtrtq_gemv_group_allgather"] = (_int, [_vp, _int, _int, _int, _vp, _sz, _vp, ctypes.c_uint, _vp])
 
 
 class MtrtqError(RuntimeError):

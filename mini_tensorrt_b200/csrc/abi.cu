@@ -1012,6 +1012,58 @@ int mtrtq_gemv_group(const mtrtq_gemv_problem* problems, int count, int x_dtype,
   return MTRTQ_OK;
 }
 
+int mtrtq_gemv_group_allgather(const mtrtq_gemv_problem* problems, int count, int x_dtype, int mode,
+                               void* workspace, size_t workspace_bytes, const mtrtq_shard_comm* comm,
+                               unsigned epoch, void* stream) {
+  if (!comm) return fail(MTRTQ_ERR_INVALID_ARG, "null communicator");
+  if (comm->world < 1 || comm->world > MTRTQ_MAX_WORLD || comm->rank < 0 || comm->rank >= comm->world)
+    return fail(MTRTQ_ERR_INVALID_ARG, "rank %d / world %d out of range", comm->rank, comm->world);
+  if (comm->world == 1) return mtrtq_gemv_group(problems, count, x_dtype, mode, workspace, workspace_bytes, stream);
+  if (!comm->alternating)
+    return fail(MTRTQ_ERR_INVALID_ARG,
+                "the fused all-gather needs alternating output buffers (comm->alternating = 1): it has no entry "
+                "barrier; run mtrtq_gemv_group, then mtrtq_shard_allgather");
+  if (group_on_stream_kernel())
+    return fail(MTRTQ_ERR_INVALID_ARG, "the fused all-gather runs on the digit GEMV (MTRTQ_OPT_FORCE_PATH 5 is set)");
+  for (int r = 0; r < comm->world; ++r)
+    if (!comm->y[r] || !comm->flags[r]) return fail(MTRTQ_ERR_INVALID_ARG, "rank %d: null output or flag buffer", r);
+  if (x_dtype != MTRTQ_DTYPE_F32 && x_dtype != MTRTQ_DTYPE_BF16)
+    return fail(MTRTQ_ERR_INVALID_ARG, "x_dtype must be MTRTQ_DTYPE_F32 or MTRTQ_DTYPE_BF16");
+  if (mode != MTRTQ_MODE_BF16 && mode != MTRTQ_MODE_FP32)
+    return fail(MTRTQ_ERR_INVALID_ARG, "mode must be MTRTQ_MODE_BF16 or MTRTQ_MODE_FP32");
+  if (mode == MTRTQ_MODE_FP32 && x_dtype == MTRTQ_DTYPE_BF16)
+    return fail(MTRTQ_ERR_INVALID_ARG, "MTRTQ_MODE_FP32 needs fp32 activations");
+  GroupProblem gp[kGroupMax];
+  int64_t units = 0;
+  int tiles = 0;
+  if (int rc = group_layout(problems, count, true, gp, &units, &tiles, kTcMaxTokens)) return rc;
+  for (int i = 0; i < count; ++i)
+    if (reinterpret_cast<const char*>(gp[i].Y) < reinterpret_cast<const char*>(comm->y[comm->rank]))
+      return fail(MTRTQ_ERR_INVALID_ARG, "problem %d: Y lies below this rank's output buffer", i);
+  DeviceInfo d;
+  if (int rc = check_device_sm100(&d)) return rc;
+  const int nt = gemv_tc_tokens(group_max_tokens(gp, count));
+  const int grid = gemv_tc_grid(units, d.sm_count, nt);
+  const size_t need = gemv_tc_layout(gp, count, grid, nt).total;
+  if (!workspace || workspace_bytes < need)
+    return fail(MTRTQ_ERR_WORKSPACE, "workspace %zu bytes < %zu", workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(MTRTQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  TcExchange xc;
+  xc.world = comm->world;
+  xc.rank = comm->rank;
+  xc.own_base = reinterpret_cast<const char*>(comm->y[comm->rank]);
+  for (int r = 0; r < comm->world; ++r) {
+    xc.peer_base[r] = reinterpret_cast<char*>(comm->y[r]);
+    xc.flags[r] = comm->flags[r];
+  }
+  xc.epoch = epoch;
+  const bool round_x = mode == MTRTQ_MODE_BF16 && x_dtype == MTRTQ_DTYPE_F32;
+  cudaError_t e = launch_gemv_tc(gp, count, units, grid, nt, x_dtype, round_x, workspace, d.status,
+                                 g_opt_overlap != 0, static_cast<cudaStream_t>(stream), nullptr, nullptr, 0.0f, &xc);
+  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMV launch (fused all-gather)");
+  return MTRTQ_OK;
+}
+
 int mtrtq_plan_info(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int64_t* info, int n_info) {
   if (!info || n_info < 6) return fail(MTRTQ_ERR_INVALID_ARG, "info needs 6 slots");
   Plan p;

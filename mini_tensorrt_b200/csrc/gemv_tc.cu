@@ -98,6 +98,7 @@ struct TcParams {
   const float* ln_gamma;  // non-null: the rows of X (fp32, one problem) are layer-normalized first
   const float* ln_beta;
   float ln_eps;
+  TcExchange xc;          // the fused all-gather (xc.world > 1)
 };
 
 __host__ __device__ __forceinline__ int64_t tc_range_start(int64_t c, int64_t U, int64_t G) { return c * U / G; }
@@ -171,6 +172,10 @@ __global__ void __launch_bounds__(kDigitizeThreads) digitize_kernel(const __grid
   const int nt = p.nt;
   grid_launch_dependents();
   grid_dependency_wait();  // X comes from the grid ahead; the digits may still be read by it
+  if (p.xc.world > 1 && p.xc.epoch == 0 && m == 0 && pi == 0 && tid == 0) {
+    unsigned* e = p.xc.flags[p.xc.rank] + kShardFlagEpoch;  // this call's count, read by the GEMV's last CTA
+    *e = *e + 1u;
+  }
   const bool live = m < P.M;
   const int groups = P.KB * 16;  // 4-element groups over the padded row
   const bool vec = (P.ldx & 3) == 0;
@@ -348,6 +353,55 @@ __device__ __forceinline__ float tc_finish(const GroupProblem& P, float v, float
   return epi_apply(P.epi, y, m, n);
 }
 
+// Y[m, n] = y here, and at the same offset in every peer's output buffer when the
+// group's all-gather is fused (stores over NVLink, released by the last CTA).
+__device__ __forceinline__ void tc_store(const TcParams& p, const GroupProblem& P, int m, int n, float y) {
+  float* dst = P.Y + (int64_t)m * P.ldy + n;
+  *dst = y;
+  if (p.xc.world > 1) {
+    const int64_t off = reinterpret_cast<const char*>(dst) - p.xc.own_base;
+    for (int r = 0; r < p.xc.world; ++r)
+      if (r != p.xc.rank) *reinterpret_cast<float*>(p.xc.peer_base[r] + off) = y;
+  }
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys_tc() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_add_relaxed_sys_tc(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_relaxed_sys_tc(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The fused all-gather's end, by one thread of each CTA after all its stores
+// (a barrier of the threads that made them comes first): the CTA's stores are
+// released to this GPU with the rank's ticket; the last CTA acquires them all,
+// releases them to the peers with one system-scope fence, adds one arrival to every
+// peer's data flag, then waits, bounded, until every peer's arrival for this call is
+// in its own (it signalled first, so no rank waits on one that has not signalled).
+// The launch ends when this rank holds every rank's outputs.
+__device__ __noinline__ void tc_exchange_end(const TcParams& p) {
+  const TcExchange& xc = p.xc;
+  unsigned* own = xc.flags[xc.rank];
+  if (ticket_acq_rel(own + kShardFlagTicket) != (unsigned)(p.grid - 1)) return;
+  fence_acq_rel_sys_tc();
+  own[kShardFlagTicket] = 0u;
+  const unsigned epoch = xc.epoch != 0 ? xc.epoch : *reinterpret_cast<volatile unsigned*>(own + kShardFlagEpoch);
+  for (int r = 0; r < xc.world; ++r)
+    if (r != xc.rank) red_add_relaxed_sys_tc(xc.flags[r] + kShardFlagData, 1u);
+  const unsigned target = epoch * (unsigned)(xc.world - 1);
+  const long long t0 = clock64();
+  while ((int)(ld_relaxed_sys_tc(own + kShardFlagData) - target) < 0) {
+    if (clock64() - t0 > kSpinLimitCycles) {
+      atomicExch(p.status, 6u /* MTRTQ_ERR_TIMEOUT */);
+      return;
+    }
+  }
+  fence_acq_rel_sys_tc();
+}
+
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -472,8 +526,7 @@ __device__ __forceinline__ void tc_epilogue(const TcParams& p, uint32_t tmem, ui
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int m = g * 8 + j;
-          if (m < P.M)
-            P.Y[(int64_t)m * P.ldy + n] = tc_finish(P, finisher ? s[m] + v8[j] : v8[j], __ldg(sc + m), m, n);
+          if (m < P.M) tc_store(p, P, m, n, tc_finish(P, finisher ? s[m] + v8[j] : v8[j], __ldg(sc + m), m, n));
         }
       }
     }
@@ -488,6 +541,10 @@ __device__ __forceinline__ void tc_epilogue(const TcParams& p, uint32_t tmem, ui
     }
     w.advance(p, nu);
     ++seg;
+  }
+  if (p.xc.world > 1) {
+    named_bar_sync(1, kTcEpiThreads);  // every store of this CTA is made
+    if (etid == 0) tc_exchange_end(p);
   }
 }
 
@@ -659,9 +716,10 @@ cudaError_t tc_launch(const TcParams& tp, int x_dtype, bool round_x, bool pdl, c
 
 cudaError_t launch_gemv_tc(const GroupProblem* probs, int count, int64_t units, int grid, int nt, int x_dtype,
                            bool round_x, void* workspace, unsigned* status, bool pdl, cudaStream_t st,
-                           const float* ln_gamma, const float* ln_beta, float ln_eps) {
+                           const float* ln_gamma, const float* ln_beta, float ln_eps, const TcExchange* xc) {
   if (ln_gamma && (count != 1 || x_dtype != 0)) return cudaErrorInvalidValue;
   TcParams tp;
+  tp.xc = xc ? *xc : TcExchange();
   tp.ln_gamma = ln_gamma;
   tp.ln_beta = ln_beta;
   tp.ln_eps = ln_eps;

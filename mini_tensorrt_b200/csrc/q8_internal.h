@@ -103,6 +103,25 @@ cudaError_t launch_gemv_stream(const GroupProblem* probs, int count, int64_t uni
                                bool round_x, void* workspace, unsigned* status, bool pdl, int producers,
                                cudaStream_t st);
 
+// A rank's flag words in peer-memory exchanges (shard.cu, and the digit GEMV's
+// fused all-gather): arrivals at the entry barrier and of peers' data, the
+// last-block ticket, the epoch of a call whose entry wait gave up, and the
+// device-side call count (epoch 0).
+constexpr int kShardFlagEntry = 0, kShardFlagData = 1, kShardFlagTicket = 2, kShardFlagAbort = 3,
+              kShardFlagEpoch = 4;
+constexpr int kShardMaxWorld = 8;
+
+// The fused all-gather of a digit GEMV group: every output element is also stored
+// at the same byte offset from each peer's output base; the last CTA then signals
+// every peer's data flag and waits for theirs. world <= 1: no exchange.
+struct TcExchange {
+  int world = 1, rank = 0;
+  const char* own_base = nullptr;           // this rank's output buffer
+  char* peer_base[kShardMaxWorld] = {};     // each rank's output buffer (mapped here)
+  unsigned* flags[kShardMaxWorld] = {};     // each rank's flag words
+  unsigned epoch = 0;                       // 0: device-counted (advanced by the digitize kernel)
+};
+
 // Tensor-core digit GEMV (gemv_tc.cu): up to kGroupMax independent problems of
 // M <= kTcMaxTokens tokens in one persistent launch, one CTA per SM, each CTA a
 // contiguous range of the group's 64-k weight units as in the grouped GEMV. A
@@ -144,7 +163,7 @@ inline TcLayout gemv_tc_layout(const GroupProblem* probs, int count, int grid, i
 cudaError_t launch_gemv_tc(const GroupProblem* probs, int count, int64_t units, int grid, int nt, int x_dtype,
                            bool round_x, void* workspace, unsigned* status, bool pdl, cudaStream_t st,
                            const float* ln_gamma = nullptr, const float* ln_beta = nullptr,
-                           float ln_eps = 0.0f);
+                           float ln_eps = 0.0f, const TcExchange* xc = nullptr);
 
 // Cluster GEMV: CTAs resident per SM (registers are capped to allow it) and the
 // shared memory a CTA may use so that they fit, for M <= 8 and for larger M (more

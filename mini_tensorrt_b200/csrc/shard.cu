@@ -75,7 +75,8 @@ __device__ bool wait_flag(const unsigned* flag, unsigned target, unsigned* statu
 // A rank's flag words: arrivals at the entry barrier and of peers' data, the push
 // kernel's block tickets, and the epoch of a call whose entry wait gave up (its
 // push is then skipped: no store goes to a peer that may not be there).
-constexpr int kFlagEntry = 0, kFlagData = 1, kFlagTicket = 2, kFlagAbort = 3, kFlagEpoch = 4;
+constexpr int kFlagEntry = kShardFlagEntry, kFlagData = kShardFlagData, kFlagTicket = kShardFlagTicket,
+              kFlagAbort = kShardFlagAbort, kFlagEpoch = kShardFlagEpoch;
 
 // The call's epoch: the caller's, or -- epoch 0 -- the rank's device-side count,
 // which the entry kernel advances (so that a captured graph replays correctly).

@@ -254,6 +254,21 @@ class PeerBuffers:
             _lib.check(self.lib.mtrtq_shard_allgather(arr, len(segments), ctypes.byref(self.comm), self.next_epoch(),
                                                       _sp(stream, self.device)), "mtrtq_shard_allgather")
 
+    def group_allgather(self, group, stream=None):
+        """Runs a GemvGroup whose outputs are this rank's column shards inside one
+        half of self.y, with the all-gather fused into the kernel
+        (mtrtq_gemv_group_allgather): after the call every rank's buffer holds every
+        rank's shards. Needs alternating=True; callers alternate the halves."""
+        import ctypes
+        from .matmulq import MODES
+        if not self.alternating:
+            raise ValueError("the fused all-gather needs alternating buffers")
+        with torch.cuda.device(self.device):
+            self._lib.check(self.lib.mtrtq_gemv_group_allgather(
+                group.problems, len(group.items), group.x_dtype, MODES[group.mode], group.workspace.data_ptr(),
+                group.workspace.numel(), ctypes.byref(self.comm), self.next_epoch(), _sp(stream, self.device)),
+                "mtrtq_gemv_group_allgather")
+
     def slot(self, M: int, N: int) -> torch.Tensor:
         """This rank's slot for the next all-reduce of an [M, N] partial (write the
         partial here: no copy)."""

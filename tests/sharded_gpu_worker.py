@@ -103,6 +103,72 @@ def main():
             want = float(sum(r * 10 + call for r in range(world)))
             assert torch.all(out == want), f"alternating all-reduce {call}"
         pa.close()
+        # the grouped GEMV with its all-gather fused in: every rank computes its column
+        # shard of three problems straight into its half of the output buffer and
+        # the peers'; eager calls (host epochs) alternate the halves, then a captured
+        # pair of calls (device epochs) is replayed
+        fused_shapes = [(8, 768, 2304), (1, 768, 50257), (3, 100, 300), (40, 1000, 1500)]
+        y_elems = sum(M_ * N_ for M_, _, N_ in fused_shapes)
+        for device_epochs in (False, True):
+            pf = sharded.PeerBuffers(y_elems, 0, device_epochs=device_epochs, alternating=True)
+            probs, off = [], 0
+            for j, (M_, K_, N_) in enumerate(fused_shapes):
+                q_, s_ = oracle.quantize_per_channel(wl.weights(K_, N_, 700 + j))
+                n0, n1 = sharded.shard_range(N_, "N", rank, world)
+                w_ = matmulq.PackedWeight.from_int8(torch.from_numpy(np.ascontiguousarray(q_[:, n0:n1])),
+                                                    torch.from_numpy(np.ascontiguousarray(s_[n0:n1])), "cuda")
+                probs.append((M_, K_, N_, q_, s_, n0, n1, w_, off))
+                off += M_ * N_
+
+            def make_group(h, xs):
+                items = []
+                for (M_, K_, N_, q_, s_, n0, n1, w_, o), x in zip(probs, xs):
+                    if n1 > n0:
+                        yv = pf.y[h * y_elems + o:h * y_elems + o + M_ * N_].view(M_, N_)
+                        items.append({"x": x, "w": w_, "out": yv[:, n0:n1]})
+                return matmulq.GemvGroup(items, mode="fp32")
+
+            def check_half(h, xs_host, tag):
+                for (M_, K_, N_, q_, s_, n0, n1, w_, o), X_ in zip(probs, xs_host):
+                    got = pf.y[h * y_elems + o:h * y_elems + o + M_ * N_].view(M_, N_).cpu().numpy()
+                    rows = np.unique(np.linspace(0, M_ - 1, min(M_, 4)).astype(np.int64))
+                    err = rel_err(got[rows], oracle.matmul_q8_rows(X_, q_, s_, rows))
+                    assert np.isfinite(got).all() and err <= 1e-4, f"fused all-gather {tag} {M_}x{K_}x{N_}: {err:.3e}"
+
+            xs_host = [[wl.activations(M_, K_, 800 + 10 * h + j) for j, (M_, K_, N_) in enumerate(fused_shapes)]
+                       for h in range(2)]
+            xs = [[torch.from_numpy(a).cuda() for a in xs_host[h]] for h in range(2)]
+            groups = [make_group(h, xs[h]) for h in range(2)]
+            if not device_epochs:
+                for call in range(4):
+                    h = call % 2
+                    pf.y[h * y_elems:(h + 1) * y_elems].fill_(float("nan"))
+                    dist.barrier()
+                    pf.group_allgather(groups[h])
+                    torch.cuda.synchronize()
+                    check_half(h, xs_host[h], f"call {call}")
+                    dist.barrier()
+            else:
+                st = torch.cuda.Stream()
+                with torch.cuda.stream(st):
+                    pf.group_allgather(groups[0], stream=st)
+                    pf.group_allgather(groups[1], stream=st)
+                    torch.cuda.synchronize()
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=st):
+                        pf.group_allgather(groups[0], stream=st)
+                        pf.group_allgather(groups[1], stream=st)
+                    for call in range(3):
+                        pf.y.fill_(float("nan"))
+                        torch.cuda.synchronize()
+                        dist.barrier()
+                        graph.replay()
+                        torch.cuda.synchronize()
+                        check_half(0, xs_host[0], f"graph replay {call} half 0")
+                        check_half(1, xs_host[1], f"graph replay {call} half 1")
+                        dist.barrier()
+                del graph
+            pf.close()
         # device-counted epochs: one all-reduce captured in a CUDA graph, replayed
         pg = sharded.PeerBuffers(y_elems=64, slot_elems=M * N * world, device_epochs=True)
         partial, out = pg.slot(M, N), torch.empty(M, N, device="cuda")

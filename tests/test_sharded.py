@@ -149,6 +149,26 @@ def test_sharded_abi_argument_errors():
     assert lib.mtrtq_shard_slot_bytes(4, 10, 9) == -1
 
 
+def test_group_allgather_argument_errors():
+    """mtrtq_gemv_group_allgather refuses, before any device work: a null or
+    out-of-range communicator, a non-alternating one (it has no entry barrier),
+    and missing peer buffers."""
+    import ctypes
+    from mini_tensorrt_b200 import _lib
+    lib = _lib.lib()
+    probs = (_lib.GemvProblem * 1)()
+    call = lambda c: lib.mtrtq_gemv_group_allgather(probs, 1, _lib.DTYPE_F32, _lib.MODE_FP32, None, 0,
+                                                    ctypes.byref(c) if c is not None else None, 0, None)
+    assert call(None) == _lib.ERR_INVALID_ARG
+    comm = _lib.ShardComm()
+    comm.rank, comm.world = 2, 2
+    assert call(comm) == _lib.ERR_INVALID_ARG and "out of range" in _lib.last_error()
+    comm.rank = 0
+    assert call(comm) == _lib.ERR_INVALID_ARG and "alternating" in _lib.last_error()
+    comm.alternating = 1
+    assert call(comm) == _lib.ERR_INVALID_ARG and "null output or flag" in _lib.last_error()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("split", ["N", "K"])
 def test_p2p_sharded_single_rank(cuda_device, split):
