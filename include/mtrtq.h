@@ -393,7 +393,11 @@ enum {
                                   tile per SM and no k split, otherwise one tile
                                   per CTA with the weights staged in TMEM;
                                   1: one tile per CTA, weights in shared memory;
-                                  2: one tile per CTA, weights in TMEM */
+                                  2: one tile per CTA, weights in TMEM;
+                                  3: the persistent kernel in stream-K form (equal
+                                  runs of tile x k-block iterations per CTA, cut
+                                  tiles added by their last CTA), from one tile per
+                                  SM, no k split */
   MTRTQ_OPT_FORCE_PATH = 2,    /* 0 (default): chosen by shape and mode (see
                                   mtrtq_plan_info). Otherwise one kernel for every
                                   call: 1 CUDA-core split-K GEMV; 2 tile tcgen05 GEMM;

@@ -341,6 +341,11 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
       p.persistent = true;
       p.grid = sm_count;
     }
+    if (tm == 256 && p.splits == 1 && tiles >= sm_count && g_opt_gemm_a_source == 3) {
+      p.persistent = true;
+      p.stream_k = true;
+      p.grid = sm_count;
+    }
   }
 
   // Split-K tickets live in a fixed region at the start of every workspace (each
@@ -358,8 +363,16 @@ int plan_matmul(int64_t M, int64_t K, int64_t N, int x_dtype, int mode, int sm_c
   if (p.splits > 1) off += round256((size_t)p.splits * (size_t)M * (size_t)p.n_pad * sizeof(float));
   p.off_xb = off;
   if (p.x_to_bf16) off += round256((size_t)M * (size_t)p.ldxb * 2);
+  if (p.stream_k) {
+    // stream-K GEMM: [grid][2][256 tokens][128 channels] fp32 parts of cut tiles,
+    // then one part counter per tile (its own, left at zero by each call).
+    p.off_partials = off;
+    off += round256((size_t)p.grid * 2 * 256 * kTileN * sizeof(float));
+    p.off_counters = off;
+    off += round256((size_t)p.n_tiles * p.m_tiles * sizeof(unsigned));
+  }
   // A single-split GEMV needs no workspace at all.
-  p.total = (p.splits > 1 || p.x_to_bf16) ? off : 0;
+  p.total = (p.splits > 1 || p.x_to_bf16 || p.stream_k) ? off : 0;
   *out = p;
   return MTRTQ_OK;
 }
@@ -471,7 +484,7 @@ const char* mtrtq_last_error(void) { return g_last_error.c_str(); }
 int mtrtq_set_option(int option, int64_t value) {
   switch (option) {
     case MTRTQ_OPT_GEMM_A_SOURCE:
-      if (value < 0 || value > 2) return fail(MTRTQ_ERR_INVALID_ARG, "GEMM A source is 0, 1 or 2");
+      if (value < 0 || value > 3) return fail(MTRTQ_ERR_INVALID_ARG, "GEMM A source is 0 to 3");
       g_opt_gemm_a_source = (int)value;
       return MTRTQ_OK;
     case MTRTQ_OPT_FORCE_PATH:

@@ -530,6 +530,332 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   }
 }
 
+// ---- stream-K variant of the persistent kernel ---------------------------------------
+//
+// The same roles, but CTA c takes the contiguous run [c I / G, (c + 1) I / G) of the
+// I = tiles x k-blocks iterations (tile-major, k fastest, token tiles fastest among
+// tiles), so every SM gets the same number of MMAs whatever the tile count: no wave
+// quantization (4096 x 4096 at M = 2048 is 256 tiles on 148 SMs). A run is a
+// sequence of segments (its part of one tile); each segment accumulates in one of the
+// two TMEM accumulators. A segment that is a whole tile is finished in place; of a
+// tile cut between CTAs, the CTA holding its last k-block (the finisher) waits,
+// bounded, for the other CTAs' fp32 parts (each stores its part to its workspace slot
+// and counts it on the tile's counter with one release) and adds them in CTA order
+// ahead of its own. A CTA takes the last segment of its run first (the tile it shares
+// with the next CTA), so parts are ready early; all CTAs are resident (one per SM)
+// and a finisher only waits for lower-numbered CTAs.
+struct SkWalk {
+  int tile, kb;         // the segment's tile and first k-block
+  int64_t u, rem;       // its first iteration; iterations left in this part of the run
+  int64_t next_b, next_e;
+  __device__ __forceinline__ void start(int64_t b, int64_t e, int KB) {
+    u = b;
+    rem = e - b;
+    tile = (int)(b / KB);
+    kb = (int)(b - (int64_t)tile * KB);
+  }
+  __device__ __forceinline__ void init(int64_t ub, int64_t ue, int KB) {
+    const int64_t last_tile_start = (ue - 1) / KB * KB;
+    const int64_t ls = last_tile_start > ub ? last_tile_start : ub;
+    start(ls, ue, KB);
+    next_b = ub;
+    next_e = ls;
+  }
+  __device__ __forceinline__ int seg_len(int KB) const {
+    const int64_t left = KB - kb;
+    return (int)(left < rem ? left : rem);
+  }
+  __device__ __forceinline__ void advance(int n, int KB) {
+    u += n;
+    rem -= n;
+    kb += n;
+    if (rem == 0 && next_b < next_e) {
+      start(next_b, next_e, KB);
+      next_b = next_e;
+      return;
+    }
+    if (kb == KB) {
+      kb = 0;
+      ++tile;
+    }
+  }
+};
+
+__device__ __forceinline__ int64_t sk_range_start(int64_t c, int64_t I, int64_t G) { return c * I / G; }
+__device__ __forceinline__ int64_t sk_cta_of(int64_t u, int64_t I, int64_t G) { return ((u + 1) * G + I - 1) / I - 1; }
+
+__device__ __forceinline__ void sk_red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned sk_ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __noinline__ void sk_wait_parts(const unsigned* counter, unsigned want, volatile int* abort_flag,
+                                           unsigned* status) {
+  const long long t0 = clock64();
+  while (sk_ld_acquire(counter) < want) {
+    if (*abort_flag) return;
+    if (clock64() - t0 > kSpinLimitCycles) {
+      *abort_flag = 1;
+      atomicExch(status, 6u /* MTRTQ_ERR_TIMEOUT */);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+__global__ void __launch_bounds__(kPgThreads, 1)
+    gemm_q8_tc_streamk_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p) {
+  using C = PgCfg;
+  constexpr int TM = C::TM;
+  constexpr int SL = kPgLoadStages, SA = kPgAStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + SL;
+  uint64_t* a_full = bars + 2 * SL;
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* acc_full = a_empty + SA;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* done = acc_empty + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KB = p.KB;
+  const int64_t I = (int64_t)p.m_tiles * p.n_tiles * KB, G = gridDim.x, cta = blockIdx.x;
+  const int64_t ub = sk_range_start(cta, I, G), ue = sk_range_start(cta + 1, I, G);
+
+  if (tid == 0) {
+    for (int s = 0; s < SL; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 5);
+    }
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&a_full[s], 4);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) prefetch_tensormap(&xmap);
+  if (warp == 1) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      SkWalk w;
+      w.init(ub, ue, KB);
+      int64_t li = 0;
+      bool ok = true;
+      while (ok && w.rem > 0) {
+        const int n = w.seg_len(KB);
+        const int mt = w.tile % p.m_tiles, nt = w.tile / p.m_tiles;
+        for (int q = 0; q < n; ++q, ++li) {
+          const int s = (int)(li % SL);
+          if (li >= SL && !mbar_wait_bounded(&empty[s], ((uint32_t)(li / SL) & 1u) ^ 1u, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+          const int kb = w.kb + q;
+          mbar_arrive_expect_tx(&full[s], C::X_STAGE + C::W_STAGE);
+          tma_load_2d(smem + C::OFF_X + s * C::X_STAGE, &xmap, kb * kBlockK, mt * TM, &full[s]);
+          bulk_g2s(smem + C::OFF_W + s * C::W_STAGE, p.W + ((int64_t)nt * KB + kb) * (int64_t)C::W_STAGE,
+                   C::W_STAGE, &full[s]);
+        }
+        w.advance(n, KB);
+      }
+      for (int64_t j = li - 1; j >= 0 && j >= li - SL; --j) mbar_drain(&full[j % SL], (uint32_t)(j / SL) & 1u, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kTileN, TM);
+      SkWalk w;
+      w.init(ub, ue, KB);
+      int64_t li = 0;
+      int seg = 0;
+      bool ok = true;
+      while (ok && w.rem > 0) {
+        const int n = w.seg_len(KB);
+        const int b = seg & 1;
+        if (seg >= 2 && !mbar_wait_bounded(&acc_empty[b], (uint32_t)((seg >> 1) - 1) & 1u, s_abort, p.status)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem_base + (uint32_t)(b * TM);
+        for (int q = 0; q < n; ++q, ++li) {
+          const int s = (int)(li % SL), sa = (int)(li % SA);
+          if (!mbar_wait_bounded(&a_full[sa], (uint32_t)(li / SA) & 1u, s_abort, p.status) ||
+              !mbar_wait_bounded(&full[s], (uint32_t)(li / SL) & 1u, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xaddr = smem_u32(smem + C::OFF_X + s * C::X_STAGE);
+          const uint32_t aaddr = smem_u32(smem + C::OFF_A + sa * C::A_STAGE);
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k)
+            umma_ss(acc, umma_desc_sw128(aaddr + k * 32), umma_desc_sw128(xaddr + k * 32), idesc,
+                    (q > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+          umma_commit(&a_empty[sa]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[b]);
+        w.advance(n, KB);
+        ++seg;
+      }
+      umma_commit(done);
+      mbar_drain(done, 0, p.status);
+    }
+  } else if (warp < 6) {
+    const int r = (warp - 2) * 32 + lane;
+    SkWalk w;
+    w.init(ub, ue, KB);
+    int64_t li = 0;
+    bool ok = true;
+    while (ok && w.rem > 0) {
+      const int n = w.seg_len(KB);
+      for (int q = 0; q < n; ++q, ++li) {
+        const int s = (int)(li % SL), sa = (int)(li % SA);
+        if (!warp_wait(&full[s], (uint32_t)(li / SL) & 1u, s_abort, p.status)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* wst = smem + C::OFF_W + s * C::W_STAGE;
+        uint4 wv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const uint4*>(wst + j * kSlabBytes + r * 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        uint32_t a[32];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          i8x4_to_bf16x4(wv[j].x, a[8 * j + 0], a[8 * j + 1]);
+          i8x4_to_bf16x4(wv[j].y, a[8 * j + 2], a[8 * j + 3]);
+          i8x4_to_bf16x4(wv[j].z, a[8 * j + 4], a[8 * j + 5]);
+          i8x4_to_bf16x4(wv[j].w, a[8 * j + 6], a[8 * j + 7]);
+        }
+        if (li >= SA && !warp_wait(&a_empty[sa], ((uint32_t)(li / SA) & 1u) ^ 1u, s_abort, p.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* arow = smem + C::OFF_A + sa * C::A_STAGE + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) =
+              make_uint4(a[4 * c], a[4 * c + 1], a[4 * c + 2], a[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[sa]);
+      }
+      w.advance(n, KB);
+    }
+  } else {
+    // Epilogue: thread = channel row = TMEM lane of its quarter.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int etid = tid - 192;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    SkWalk w;
+    w.init(ub, ue, KB);
+    int seg = 0;
+    bool ok = true;
+    while (w.rem > 0) {
+      const int nlen = w.seg_len(KB);
+      const int b = seg & 1;
+      const int mt = w.tile % p.m_tiles, nt = w.tile / p.m_tiles;
+      const bool whole = w.kb == 0 && nlen == KB;
+      const bool finisher = !whole && w.kb + nlen == KB;
+      unsigned* counter = p.counters + w.tile;
+      const int64_t T0 = (int64_t)w.tile * KB;
+      const int64_t c_lo = sk_cta_of(T0, I, G), c_hi = sk_cta_of(T0 + KB - 1, I, G);
+      const int first_slot = sk_range_start(c_lo, I, G) == T0 ? 0 : 1;
+      float* slot = p.partials + (size_t)(cta * 2 + (w.u == ub ? 0 : 1)) * TM * kTileN;
+      if (finisher) {
+        if (etid == 0) sk_wait_parts(counter, (unsigned)(c_hi - c_lo), s_abort, p.status);
+        named_bar_sync(1, 128);
+      }
+      ok = ok && warp_wait(&acc_full[b], (uint32_t)(seg >> 1) & 1u, s_abort, p.status);
+      tc_fence_after();
+      const int n = nt * kTileN + r;
+      const bool n_ok = n < p.N;
+      const float sc = n_ok ? __ldg(p.scale + n) : 0.0f;
+      const float bs = (n_ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
+      const int m0 = mt * TM;
+      for (int c0 = 0; c0 < TM && m0 + c0 < p.M; c0 += 16) {
+        uint32_t v[16];
+        if (ok) {
+          tmem_ld_32x32b_x16(tmem_base + lane_off + (uint32_t)(b * TM + c0), v);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0u;
+        }
+        if (!whole && !finisher) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(slot + (c0 + j) * kTileN + r, __uint_as_float(v[j]));
+          continue;
+        }
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+        if (finisher) {
+          for (int64_t cc = c_lo; cc < c_hi; ++cc) {
+            const float* part =
+                p.partials + (size_t)(cc * 2 + (cc == c_lo ? first_slot : 0)) * TM * kTileN + (size_t)c0 * kTileN + r;
+            float t[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) t[j] = __ldcg(part + j * kTileN);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] += t[j];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + c0 + j;
+          if (n_ok && m < p.M) {
+            float y = __fmul_rn(acc[j] + __uint_as_float(v[j]), sc);
+            if (p.bias) y = __fadd_rn(y, bs);
+            p.Y[(int64_t)m * p.ldy + n] = epi_apply(p.epi, y, m, n);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (!whole && !finisher) {
+        named_bar_sync(1, 128);  // every part of this CTA is stored
+        if (etid == 0) sk_red_release_add(counter, 1u);
+      } else if (finisher && etid == 0) {
+        *counter = 0u;  // left at zero for the next call
+      }
+      w.advance(nlen, KB);
+      ++seg;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
 template <int TM, bool A_TMEM, int STAGES>
 static cudaError_t launch_cfg(const GemmParams& gp, const CUtensorMap& xmap, cudaStream_t st) {
   using C = GemmCfg<TM, A_TMEM, STAGES>;
@@ -557,11 +883,15 @@ bool gemm_tile_supported(int tile_m) {
   return tile_m == 16 || tile_m == 32 || tile_m == 64 || tile_m == 128 || tile_m == 256;
 }
 
-static cudaError_t launch_persistent(const GemmParams& gp, const CUtensorMap& xmap, int grid, cudaStream_t st) {
-  if (cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gemm_q8_tc_persistent_kernel),
-                                         PgCfg::SMEM_BYTES))
-    return e;
-  gemm_q8_tc_persistent_kernel<<<grid, kPgThreads, PgCfg::SMEM_BYTES, st>>>(xmap, gp);
+static cudaError_t launch_persistent(const GemmParams& gp, const CUtensorMap& xmap, int grid, bool stream_k,
+                                     cudaStream_t st) {
+  const void* k = stream_k ? reinterpret_cast<const void*>(gemm_q8_tc_streamk_kernel)
+                           : reinterpret_cast<const void*>(gemm_q8_tc_persistent_kernel);
+  if (cudaError_t e = ensure_smem_limit(k, PgCfg::SMEM_BYTES)) return e;
+  if (stream_k)
+    gemm_q8_tc_streamk_kernel<<<grid, kPgThreads, PgCfg::SMEM_BYTES, st>>>(xmap, gp);
+  else
+    gemm_q8_tc_persistent_kernel<<<grid, kPgThreads, PgCfg::SMEM_BYTES, st>>>(xmap, gp);
   return cudaGetLastError();
 }
 
@@ -590,7 +920,7 @@ cudaError_t launch_gemm_tc(const Plan& p, const void* Xb, int64_t ldxb, const vo
   gp.counters = ws ? reinterpret_cast<unsigned*>(ws + p.off_counters) : nullptr;
   gp.partials = ws ? reinterpret_cast<float*>(ws + p.off_partials) : nullptr;
   gp.status = status;
-  if (p.persistent) return launch_persistent(gp, xmap, p.grid, st);
+  if (p.persistent) return launch_persistent(gp, xmap, p.grid, p.stream_k, st);
   return a_from_tmem ? launch_tm<true>(p.tile_m, gp, xmap, st)
                      : launch_tm<false>(p.tile_m, gp, xmap, st);
 }

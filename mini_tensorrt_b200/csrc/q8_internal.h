@@ -39,6 +39,7 @@ struct Plan {
   bool x_to_bf16 = false;          // GEMM: X is staged as a bf16 copy in the workspace
   bool round_x = false;            // GEMV: round fp32 X to bf16 before the product
   bool persistent = false;         // GEMM: one CTA per SM over the tiles (grid CTAs), two accumulators
+  bool stream_k = false;           // persistent GEMM: equal runs of (tile, k-block) iterations per CTA
   // workspace layout (byte offsets)
   size_t off_counters = 0, off_partials = 0, off_xb = 0, total = 0;
   int64_t ldxb = 0;                // row stride (elements) of the bf16 X copy

@@ -212,8 +212,9 @@ PERSISTENT = [(2048, 768, 7168), (300, 1000, 60000), (2048, 4096, 14336), (700, 
 @pytest.mark.parametrize("M,K,N", PERSISTENT, ids=[f"{M}x{K}x{N}" for M, K, N in PERSISTENT])
 @pytest.mark.parametrize("epilogue", ["none", "gelu", "residual"])
 def test_persistent_gemm(cuda_device, M, K, N, epilogue):
-    """The persistent tile GEMM (one CTA per SM, two TMEM accumulators) against the
-    oracle, and against the one-tile-per-CTA kernel on the same inputs."""
+    """The persistent tile GEMM (one CTA per SM, two TMEM accumulators) and its
+    stream-K form against the oracle, and against the one-tile-per-CTA kernel on the
+    same inputs."""
     if epilogue != "none" and M * N > 2048 * 7168:
         pytest.skip("epilogues are covered on the smaller shapes")
     q, s = matmulq.quantize_per_channel(wl.weights(K, N, 1100 + K))
@@ -226,7 +227,8 @@ def test_persistent_gemm(cuda_device, M, K, N, epilogue):
     xt = torch.from_numpy(X).to(cuda_device).to(torch.bfloat16)
     bt = torch.from_numpy(b).to(cuda_device)
     outs = []
-    for a_source in (0, 2):  # persistent (automatic: at least three tiles per SM), then one tile per CTA
+    # persistent (automatic: at least three tiles per SM), one tile per CTA, stream-K
+    for a_source in (0, 2, 3):
         matmulq.set_option(_lib.OPT_GEMM_A_SOURCE, a_source)
         try:
             y = torch.from_numpy(R).to(cuda_device) if R is not None else torch.full((M, N), float("nan"),
@@ -238,15 +240,22 @@ def test_persistent_gemm(cuda_device, M, K, N, epilogue):
             matmulq.set_option(_lib.OPT_GEMM_A_SOURCE, 0)
         assert matmulq.read_device_status() == 0
         outs.append(y.cpu().numpy())
-    t = oracle.matmul_q8(X, q, s, b)
+    # the oracle on sampled rows (first and last token tiles included); the kernels
+    # against each other on every element
+    rows = np.unique(np.concatenate([np.arange(min(M, 8)), np.linspace(0, M - 1, 12).astype(np.int64),
+                                     np.arange(max(0, M - 4), M)]))
+    t = oracle.matmul_q8_rows(X, q, s, rows, b)
     if epilogue == "gelu":
         u = t.astype(np.float64)
         t = (0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))).astype(np.float32)
     elif epilogue == "residual":
-        t = (R + t).astype(np.float32)
+        t = (R[rows] + t).astype(np.float32)
     assert np.all(np.isfinite(outs[0]))
-    assert rel_err(outs[0], t) <= BF16_SAME_INPUT_TOL_TC
+    assert rel_err(outs[0][rows], t) <= BF16_SAME_INPUT_TOL_TC
     assert rel_err(outs[0], outs[1]) <= 1e-6
+    # stream-K adds the fp32 parts of a cut tile (a different summation order)
+    assert np.all(np.isfinite(outs[2])) and rel_err(outs[2][rows], t) <= BF16_SAME_INPUT_TOL_TC
+    assert rel_err(outs[2], outs[1]) <= 1e-5
 
 
 @pytest.mark.parametrize("M", [1, 8, 64, 2048])
