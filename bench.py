@@ -265,6 +265,35 @@ def time_graphs(torch, graphs, steps, warmup, stream):
     return e0.elapsed_time(e1) / 1e3
 
 
+def time_step_graphs(torch, singles, pairs, steps, warmup, stream):
+    """Like time_graphs over the rotation, but every two consecutive steps that start
+    at an even rotation offset replay as one graph holding both (pairs[g // 2] is
+    steps g and g + 1); a step left over replays alone. Every step still runs its
+    full launch sequence on its own weight copy."""
+    n = len(singles)
+
+    def run(i0, count):
+        i = i0
+        while i < i0 + count:
+            if i % 2 == 0 and i + 1 < i0 + count:
+                pairs[(i % n) // 2].replay()
+                i += 2
+            else:
+                singles[i % n].replay()
+                i += 1
+
+    with torch.cuda.stream(stream):
+        run(0, warmup)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run(warmup, steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3
+
+
 def run_ours(args, torch, rank, world, dev, dist):
     from mini_tensorrt_b200 import _lib, matmulq, workloads as wl
     hbm_peak, tc_peak, tc_sust, peak_kind = peaks()
@@ -308,7 +337,7 @@ def run_ours(args, torch, rank, world, dev, dist):
                 c = calls[i]
                 matmulq.matmul_q8(c["x"], c["w"][(g + i) % WEIGHT_COPIES], out=c["y"], mode=args.mode,
                                   workspace=c["ws"], stream=stream)
-        out = []
+        out, pairs = [], []
         with torch.cuda.stream(stream):
             one(0)
             torch.cuda.synchronize()
@@ -317,12 +346,21 @@ def run_ours(args, torch, rank, world, dev, dist):
                 with torch.cuda.graph(graph, stream=stream):
                     one(g)
                 out.append(graph)
+            # two consecutive steps per graph: inside a graph the second step's
+            # launches overlap the first's tail (programmatic dependent launch);
+            # between graph replays they cannot
+            for g in range(0, WEIGHT_COPIES, 2):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    one(g)
+                    one(g + 1)
+                pairs.append(graph)
         torch.cuda.synchronize()
-        return out, groups
+        return out, groups, pairs
 
-    groups = None
+    groups, pairs = None, None
     if args.step_launch in ("group", "hybrid"):
-        graphs, groups = capture_group()
+        graphs, groups, pairs = capture_group()
     else:
         graphs = capture_calls()
 
@@ -332,9 +370,17 @@ def run_ours(args, torch, rank, world, dev, dist):
     with ClockSampler(dev.index) as clk:
         if world > 1:
             dist.barrier()
-        secs = time_graphs(torch, graphs, args.steps, args.warmup, stream)
+        if pairs is not None:
+            secs = time_step_graphs(torch, graphs, pairs, args.steps, args.warmup, stream)
+        else:
+            secs = time_graphs(torch, graphs, args.steps, args.warmup, stream)
         if world > 1:
             dist.barrier()
+    single_step = None
+    if pairs is not None:
+        s1 = time_graphs(torch, graphs, args.steps, args.warmup, stream)
+        single_step = {"value": round(step_bytes * args.steps * world / s1 / 1e9, 1),
+                       "ms_per_step": round(s1 / args.steps * 1e3, 4)}
     torch.cuda.synchronize()
     t = torch.tensor([secs], dtype=torch.float64, device=dev)
     if world > 1:
@@ -391,8 +437,8 @@ def run_ours(args, torch, rank, world, dev, dist):
                     "traffic": committed_traffic(f"gemv_tc_decode_set_{args.mode}"),
                     "kernel": "gemv_tc_kernel (the whole decode GEMV set, one launch, after its digitize_kernel)",
                     "peak_kind": f"{peak_kind} hbm_gbs", "per_launch_us": round(step_us, 3),
-                    "per_launch_timing": "CUDA events around graph replays of the step (digitize + grouped GEMV), "
-                                         f"weights rotated over {WEIGHT_COPIES} copies",
+                    "per_launch_timing": "CUDA events around graph replays of two steps each (digitize + grouped "
+                                         f"GEMV per step), weights rotated over {WEIGHT_COPIES} copies",
                     "algorithmic_bytes_per_launch": step_bytes,
                     "lm_head_per_call": lm_head}
     else:
@@ -418,7 +464,10 @@ def run_ours(args, torch, rank, world, dev, dist):
         "dtype": PATH_DTYPES["gemv_tc" if args.step_launch == "group" else "cluster_gemv"],
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantized per channel)",
         "config": decode_set_config(args, world, step_bytes),
-        "method": {"timing": "CUDA graphs of one step, CUDA events on the launching stream",
+        "method": {"timing": ("CUDA graphs of two consecutive steps (a step left over alone), CUDA events on "
+                              "the launching stream" if pairs is not None else
+                              "CUDA graphs of one step, CUDA events on the launching stream"),
+                   "one_step_per_graph": single_step,
                    "overlap_launch": not args.no_overlap,
                    "step_launch": {"group": "one mtrtq_gemv_group call for the ten calls (a digitize kernel and "
                                              "the tensor-core digit GEMV)",
